@@ -1,0 +1,477 @@
+// tcgen05 GEMM for sm_100a: D[M,N] = epilogue(A[M,K] * B[N,K]^T).
+//
+// One persistent, warp-specialised kernel serves the three contractions of a
+// GPT-2 linear layer (reference gpt2/cuda/matmul.cu:223-449):
+//   forward  out  = inp * W^T      A = inp  (K-major),  B = W    (K-major)
+//   dinp     dinp = dout * W       A = dout (K-major),  B = W    (N-major)
+//   dweight  dW   = dout^T * inp   A = dout (M-major),  B = inp  (N-major)
+// Operand majorness is a template parameter; the smem descriptors and the
+// instruction descriptor's transpose bits absorb it, so no operand is ever
+// transposed in memory.
+//
+// CTA = 6 warps: warp 0 issues TMA loads into a kStages-deep ring of 128B-
+// swizzled smem stages, warp 1 owns TMEM and issues tcgen05.mma (one thread),
+// warps 2..5 drain the double-buffered TMEM accumulator (tcgen05.ld) through
+// the fused epilogue (bias, residual add, GELU, GELU-backward, accumulate)
+// while the next tile's mainloop runs. Split-K writes fp32 partial tiles to a
+// caller workspace, reduced deterministically by gemm_splitk_reduce.
+#include <algorithm>
+#include <cstdio>
+
+#include "ptx.cuh"
+#include "runtime.h"
+
+namespace llmk {
+namespace {
+
+struct EpiParams {
+  void* D;
+  long long ldd;
+  int d_bf16;
+  const float* bias;
+  const float* residual;
+  long long ldr;
+  __nv_bfloat16* aux;
+  long long ldaux;
+  int flags;
+  float* partial;  // split-K: fp32 [splits][M][N] workspace (raw accumulators)
+};
+
+template <bool kTF32, bool kAMN, bool kBMN, int kBN>
+struct Cfg {
+  static constexpr int kElem = kTF32 ? 4 : 2;
+  static constexpr int BM = 128;
+  static constexpr int BK = 128 / kElem;           // K per stage (one 128-byte swizzle row)
+  static constexpr int kAtomMN = 128 / kElem;      // M/N elements per 128-byte atom (MN-major)
+  static constexpr int kStages = (kBN == 256) ? 4 : 6;
+  static constexpr int A_BYTES = BM * 128;
+  static constexpr int B_BYTES = kBN * 128;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int kRowsPerMma = 32 / kElem;   // K of one MMA (16 bf16, 8 tf32)
+  static constexpr int kKSteps = BK / kRowsPerMma; // 4
+  static constexpr int kTmemCols = 2 * kBN;        // two accumulators
+  // MN-major operands: tf32 needs the 32-byte-atom 128B swizzle (4-row
+  // groups, 512 B apart); bf16 the plain 128B swizzle (8-row groups, 1024 B).
+  static constexpr uint32_t kMNLayout = kTF32 ? kLayoutSW128Base32 : kLayoutSW128;
+  static constexpr uint32_t kMNSbo = kTF32 ? 512 : 1024;
+  static constexpr int kThreads = 192;
+  static constexpr size_t SMEM = size_t(kStages) * STAGE_BYTES + 1024 + 256;
+  static_assert(kBN == 128 || kBN == 256, "BN");
+};
+
+__device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& m_blk, int& n_blk, int& split) {
+  const int per_split = num_m * num_n;
+  split = t / per_split;
+  t -= split * per_split;
+  constexpr int G = 8;  // m-blocks per raster group: consecutive tiles share B panels in L2
+  const int per_group = G * num_n;
+  const int g = t / per_group;
+  const int r = t - g * per_group;
+  const int m_first = g * G;
+  const int gs = min(G, num_m - m_first);
+  m_blk = m_first + r % gs;
+  n_blk = r / gs;
+}
+
+__device__ __forceinline__ void load8(const float* p, float* v) {
+  float4 a = reinterpret_cast<const float4*>(p)[0];
+  float4 b = reinterpret_cast<const float4*>(p)[1];
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+__device__ __forceinline__ void load8_bf16(const __nv_bfloat16* p, float* v) {
+  uint4 u = *reinterpret_cast<const uint4*>(p);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 f = __bfloat1622float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+__device__ __forceinline__ void store8(float* p, const float* v) {
+  reinterpret_cast<float4*>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
+  reinterpret_cast<float4*>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
+}
+__device__ __forceinline__ void store8_bf16(__nv_bfloat16* p, const float* v) {
+  uint4 u;
+  u.x = pack_bf16x2(v[0], v[1]);
+  u.y = pack_bf16x2(v[2], v[3]);
+  u.z = pack_bf16x2(v[4], v[5]);
+  u.w = pack_bf16x2(v[6], v[7]);
+  *reinterpret_cast<uint4*>(p) = u;
+}
+
+// Applies the epilogue to 8 consecutive columns [gn, gn+8) of row gm, all in
+// bounds. Shared by the direct epilogue and the split-K reduction.
+__device__ __forceinline__ void epi_apply8(const EpiParams& ep, long long gm, int gn, float* v) {
+  float t[8];
+  if (ep.bias) {
+    load8(ep.bias + gn, t);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] += t[j];
+  }
+  if (ep.residual) {
+    load8(ep.residual + gm * ep.ldr + gn, t);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] += t[j];
+  }
+  if (ep.flags & LLMK_EPI_GELU) {
+    if (ep.aux) store8_bf16(ep.aux + gm * ep.ldaux + gn, v);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = gelu_tanh(v[j]);
+  } else if (ep.flags & LLMK_EPI_GELU_BWD) {
+    load8_bf16(ep.aux + gm * ep.ldaux + gn, t);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] *= gelu_tanh_grad(t[j]);
+  }
+  if (ep.d_bf16) {
+    __nv_bfloat16* dp = static_cast<__nv_bfloat16*>(ep.D) + gm * ep.ldd + gn;
+    if (ep.flags & LLMK_EPI_ACCUMULATE) {
+      load8_bf16(dp, t);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] += t[j];
+    }
+    store8_bf16(dp, v);
+  } else {
+    float* dp = static_cast<float*>(ep.D) + gm * ep.ldd + gn;
+    if (ep.flags & LLMK_EPI_ACCUMULATE) {
+      load8(dp, t);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] += t[j];
+    }
+    store8(dp, v);
+  }
+}
+
+template <bool kTF32, bool kAMN, bool kBMN, int kBN>
+__global__ void __launch_bounds__(192, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, EpiParams ep,
+                   int M, int N, int K, int splits, unsigned int* status) {
+  using C = Cfg<kTF32, kAMN, kBMN, kBN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kStages * C::STAGE_BYTES);
+  uint64_t* empty = full + C::kStages;
+  uint64_t* accf = empty + C::kStages;
+  uint64_t* acce = accf + 2;
+  uint64_t* done = acce + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(full + s, 1);
+      mbar_init(empty + s, 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(accf + a, 1);
+      mbar_init(acce + a, 128);
+    }
+    mbar_init(done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int num_m = (M + C::BM - 1) / C::BM;
+  const int num_n = (N + kBN - 1) / kBN;
+  const int num_tiles = num_m * num_n * splits;
+  const int num_kb = (K + C::BK - 1) / C::BK;
+  const int kb_per = (num_kb + splits - 1) / splits;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+        int mb, nb, sp;
+        tile_coords(tile, num_m, num_n, mb, nb, sp);
+        const int m0 = mb * C::BM, n0 = nb * kBN;
+        const int kb0 = sp * kb_per, kb1 = min(num_kb, kb0 + kb_per);
+        bool ok = true;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(empty + stage, phase ^ 1u, status, abort_flag)) { ok = false; break; }
+          uint8_t* sA = smem + stage * C::STAGE_BYTES;
+          uint8_t* sB = sA + C::A_BYTES;
+          mbar_arrive_expect_tx(full + stage, C::STAGE_BYTES);
+          const int k0 = kb * C::BK;
+          if (!kAMN) {
+            tma_load_2d(sA, &tmA, full + stage, k0, m0);
+          } else {
+#pragma unroll
+            for (int j = 0; j < C::BM / C::kAtomMN; ++j)
+              tma_load_2d(sA + j * C::BK * 128, &tmA, full + stage, m0 + j * C::kAtomMN, k0);
+          }
+          if (!kBMN) {
+            tma_load_2d(sB, &tmB, full + stage, k0, n0);
+          } else {
+#pragma unroll
+            for (int j = 0; j < kBN / C::kAtomMN; ++j)
+              tma_load_2d(sB + j * C::BK * 128, &tmB, full + stage, n0 + j * C::kAtomMN, k0);
+          }
+          if (++stage == C::kStages) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = idesc_f32acc(128, kBN, kTF32 ? kFmtTF32 : kFmtBF16, kAMN, kBMN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
+        int mb, nb, sp;
+        tile_coords(tile, num_m, num_n, mb, nb, sp);
+        const int kb0 = sp * kb_per, kb1 = min(num_kb, kb0 + kb_per);
+        const int acc = local & 1;
+        const uint32_t aphase = (local >> 1) & 1;
+        if (!mbar_wait(acce + acc, aphase ^ 1u, status, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * kBN;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(full + stage, phase, status, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t sA = smem_u32(smem + stage * C::STAGE_BYTES);
+          const uint32_t sB = sA + C::A_BYTES;
+#pragma unroll
+          for (int ks = 0; ks < C::kKSteps; ++ks) {
+            uint64_t adesc, bdesc;
+            if (!kAMN) adesc = sdesc_sw128(sA + ks * 32, 16, 1024);
+            else adesc = sdesc_sw128(sA + ks * C::kRowsPerMma * 128, C::BK * 128, C::kMNSbo, C::kMNLayout);
+            if (!kBMN) bdesc = sdesc_sw128(sB + ks * 32, 16, 1024);
+            else bdesc = sdesc_sw128(sB + ks * C::kRowsPerMma * 128, C::BK * 128, C::kMNSbo, C::kMNLayout);
+            const uint32_t accum = (kb > kb0 || ks > 0) ? 1u : 0u;
+            if (kTF32) mma_tf32_ss(d_tmem, adesc, bdesc, idesc, accum);
+            else mma_f16_ss(d_tmem, adesc, bdesc, idesc, accum);
+          }
+          mma_commit(empty + stage);
+          if (++stage == C::kStages) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+        mma_commit(accf + acc);
+      }
+      // All MMAs issued by this thread complete before TMEM is released.
+      mma_commit(done);
+      mbar_wait(done, 0, status, nullptr);
+    }
+    __syncwarp();
+  } else {
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    int local = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+      int mb, nb, sp;
+      tile_coords(tile, num_m, num_n, mb, nb, sp);
+      const int m0 = mb * C::BM, n0 = nb * kBN;
+      const int acc = local & 1;
+      const uint32_t aphase = (local >> 1) & 1;
+      bool ok = mbar_wait(accf + acc, aphase, status, abort_flag);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      tc_fence_after();
+      const long long gm = m0 + q * 32 + lane;
+      const bool row_ok = gm < M;
+#pragma unroll 1
+      for (int c = 0; c < kBN / 32; ++c) {
+        const int gn0 = n0 + c * 32;
+        if (gn0 >= N) break;
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * kBN + c * 32, r);
+        tmem_ld_wait();
+        if (!row_ok) continue;
+        const int nvalid = min(32, N - gn0);
+        if (ep.partial) {
+          float* pp = ep.partial + (static_cast<long long>(sp) * M + gm) * N + gn0;
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            if (g * 8 < nvalid) {
+              float v[8];
+#pragma unroll
+              for (int j = 0; j < 8; ++j) v[j] = __uint_as_float(r[g * 8 + j]);
+              store8(pp + g * 8, v);
+            }
+          }
+        } else {
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            if (g * 8 < nvalid) {
+              float v[8];
+#pragma unroll
+              for (int j = 0; j < 8; ++j) v[j] = __uint_as_float(r[g * 8 + j]);
+              epi_apply8(ep, gm, gn0 + g * 8, v);
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(acce + acc);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::kTmemCols);
+  }
+}
+
+// out = epilogue(sum_s partial[s]) over 8-column groups; grid-stride.
+__global__ void gemm_splitk_reduce(EpiParams ep, int M, int N, int splits) {
+  const long long groups = static_cast<long long>(M) * (N / 8);
+  const long long plane = static_cast<long long>(M) * N;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < groups;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long gm = i / (N / 8);
+    const int gn = static_cast<int>(i - gm * (N / 8)) * 8;
+    float v[8], t[8];
+    load8(ep.partial + gm * N + gn, v);
+    for (int s = 1; s < splits; ++s) {
+      load8(ep.partial + s * plane + gm * N + gn, t);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] += t[j];
+    }
+    epi_apply8(ep, gm, gn, v);
+  }
+}
+
+template <bool kTF32, bool kAMN, bool kBMN, int kBN>
+int launch_gemm(const void* A, long long lda, const void* B, long long ldb, int M, int N, int K, EpiParams ep,
+                int splits, cudaStream_t stream) {
+  using C = Cfg<kTF32, kAMN, kBMN, kBN>;
+  auto kern = gemm_tc_kernel<kTF32, kAMN, kBMN, kBN>;
+  static bool attr_done[64] = {};
+  int dev = 0;
+  LLMK_CUDA(cudaGetDevice(&dev));
+  if (dev < 64 && !attr_done[dev]) {
+    LLMK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(C::SMEM)));
+    attr_done[dev] = true;
+  }
+  const CUtensorMapDataType dt = kTF32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  CUtensorMap ta, tb;
+  const CUtensorMapSwizzle mn_swz = kTF32 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B;
+  if (!kAMN) LLMK_TRY(make_tmap_2d(&ta, A, dt, K, M, lda * C::kElem, C::BK, C::BM));
+  else LLMK_TRY(make_tmap_2d(&ta, A, dt, M, K, lda * C::kElem, C::kAtomMN, C::BK, mn_swz));
+  if (!kBMN) LLMK_TRY(make_tmap_2d(&tb, B, dt, K, N, ldb * C::kElem, C::BK, kBN));
+  else LLMK_TRY(make_tmap_2d(&tb, B, dt, N, K, ldb * C::kElem, C::kAtomMN, C::BK, mn_swz));
+  const int num_tiles = ((M + C::BM - 1) / C::BM) * ((N + kBN - 1) / kBN) * splits;
+  const int grid = std::min(num_tiles, num_sms());
+  unsigned int* st = device_status_ptr();
+  kern<<<grid, C::kThreads, C::SMEM, static_cast<cudaStream_t>(stream)>>>(ta, tb, ep, M, N, K, splits, st);
+  count_launch();
+  LLMK_CUDA(cudaGetLastError());
+  return LLMK_OK;
+}
+
+template <bool kTF32, int kBN>
+int dispatch_major(int a_trans, int b_trans, const void* A, long long lda, const void* B, long long ldb, int M,
+                   int N, int K, const EpiParams& ep, int splits, cudaStream_t s) {
+  if (!a_trans && !b_trans) return launch_gemm<kTF32, false, false, kBN>(A, lda, B, ldb, M, N, K, ep, splits, s);
+  if (!a_trans && b_trans) return launch_gemm<kTF32, false, true, kBN>(A, lda, B, ldb, M, N, K, ep, splits, s);
+  if (a_trans && b_trans) return launch_gemm<kTF32, true, true, kBN>(A, lda, B, ldb, M, N, K, ep, splits, s);
+  return launch_gemm<kTF32, true, false, kBN>(A, lda, B, ldb, M, N, K, ep, splits, s);
+}
+
+}  // namespace
+
+// Chooses BN and the split-K factor. Split-K only when the output tile grid
+// leaves most SMs idle and K is long (the dweight GEMMs: M,N = layer width,
+// K = B*T tokens).
+static void plan_gemm(int M, int N, int K, int elem, int* bn, int* splits) {
+  const int sms = num_sms();
+  const int num_m = (M + 127) / 128;
+  const int t256 = num_m * ((N + 255) / 256), t128 = num_m * ((N + 127) / 128);
+  const long long w256 = (t256 + sms - 1) / sms, w128 = (t128 + sms - 1) / sms;
+  // A 128-wide tile costs ~half a 256-wide one plus a smem-bandwidth penalty.
+  *bn = (w256 * 256 * 10 <= w128 * 128 * 11) ? 256 : 128;
+  const int tiles = (*bn == 256) ? t256 : t128;
+  const int bk = 128 / elem;
+  const int num_kb = (K + bk - 1) / bk;
+  int s = 1;
+  while (tiles * s < sms && num_kb / (s * 2) >= 8) s *= 2;
+  // Every split must own at least one K block (an empty split would publish
+  // a stale accumulator).
+  while (s > 1 && ((num_kb + s - 1) / s) * (s - 1) >= num_kb) s /= 2;
+  *splits = s;
+}
+
+}  // namespace llmk
+
+using namespace llmk;
+
+static int gemm_impl(void* D, llmk_dtype d_dtype, long long ldd, const void* A, int a_trans, long long lda,
+                     const void* B, int b_trans, long long ldb, llmk_math math, int M, int N, int K,
+                     const llmk_epilogue* epi, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!D || !A || !B) return fail(LLMK_ERR_INVALID_ARG, "gemm: null operand");
+  if (M <= 0 || N <= 0 || K <= 0) return fail(LLMK_ERR_INVALID_ARG, "gemm: non-positive size");
+  if (math != LLMK_MATH_BF16 && math != LLMK_MATH_TF32) return fail(LLMK_ERR_INVALID_ARG, "gemm: bad math mode");
+  const int elem = (math == LLMK_MATH_TF32) ? 4 : 2;
+  const int d_elem = (d_dtype == LLMK_BF16) ? 2 : 4;
+  if (!aligned16(A) || !aligned16(B) || !aligned16(D) || (lda * elem) % 16 || (ldb * elem) % 16 ||
+      (ldd * d_elem) % 16 || N % 8)
+    return fail(LLMK_ERR_UNSUPPORTED, "gemm: operands need 16-byte aligned bases/row strides and N % 8 == 0");
+  EpiParams ep{};
+  ep.D = D;
+  ep.ldd = ldd;
+  ep.d_bf16 = d_dtype == LLMK_BF16;
+  if (epi) {
+    ep.bias = epi->bias;
+    ep.residual = epi->residual;
+    ep.ldr = epi->ldr;
+    ep.aux = static_cast<__nv_bfloat16*>(epi->aux);
+    ep.ldaux = epi->ldaux;
+    ep.flags = epi->flags;
+    if ((ep.bias && !aligned16(ep.bias)) || (ep.residual && (!aligned16(ep.residual) || ep.ldr % 4)) ||
+        (ep.aux && (!aligned16(ep.aux) || ep.ldaux % 8)))
+      return fail(LLMK_ERR_UNSUPPORTED, "gemm: epilogue operands need 16-byte alignment");
+    if ((ep.flags & LLMK_EPI_GELU_BWD) && !ep.aux) return fail(LLMK_ERR_INVALID_ARG, "gemm: GELU_BWD needs aux");
+  }
+  int bn, splits;
+  plan_gemm(M, N, K, elem, &bn, &splits);
+  const size_t need = static_cast<size_t>(splits) * M * N * sizeof(float);
+  if (splits > 1 && (!workspace || workspace_bytes < need || !aligned16(workspace))) splits = 1;
+  if (splits > 1) ep.partial = static_cast<float*>(workspace);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int rc;
+  if (elem == 4) rc = bn == 256 ? dispatch_major<true, 256>(a_trans, b_trans, A, lda, B, ldb, M, N, K, ep, splits, s)
+                                : dispatch_major<true, 128>(a_trans, b_trans, A, lda, B, ldb, M, N, K, ep, splits, s);
+  else rc = bn == 256 ? dispatch_major<false, 256>(a_trans, b_trans, A, lda, B, ldb, M, N, K, ep, splits, s)
+                      : dispatch_major<false, 128>(a_trans, b_trans, A, lda, B, ldb, M, N, K, ep, splits, s);
+  if (rc != LLMK_OK || splits == 1) return rc;
+  const long long groups = static_cast<long long>(M) * (N / 8);
+  const int grid = static_cast<int>(std::min<long long>((groups + 255) / 256, num_sms() * 8LL));
+  gemm_splitk_reduce<<<grid, 256, 0, s>>>(ep, M, N, splits);
+  count_launch();
+  LLMK_CUDA(cudaGetLastError());
+  return LLMK_OK;
+}
+
+extern "C" {
+
+size_t llmk_gemm_workspace(int M, int N, int K, llmk_math math) {
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  int bn, splits;
+  plan_gemm(M, N, K, math == LLMK_MATH_TF32 ? 4 : 2, &bn, &splits);
+  return splits > 1 ? static_cast<size_t>(splits) * M * N * sizeof(float) : 0;
+}
+
+int llmk_gemm(void* D, llmk_dtype d_dtype, long long ldd, const void* A, int a_trans, long long lda, const void* B,
+              int b_trans, long long ldb, llmk_math math, int M, int N, int K, const llmk_epilogue* epi,
+              void* workspace, size_t workspace_bytes, void* stream) {
+  return gemm_impl(D, d_dtype, ldd, A, a_trans, lda, B, b_trans, ldb, math, M, N, K, epi, workspace,
+                   workspace_bytes, stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,133 @@
+"""ctypes binding of libllmk.so — the C ABI declared in include/llmk.h.
+
+This is the Python-side FFI stub a host program uses to call the sm_100a
+kernels (tests and bench.py go through it). It only moves pointers and sizes:
+device memory comes from the caller (torch tensors here), and every call
+raises LlmkError when the library returns a non-zero status. There is no
+fallback: if libllmk.so is missing, importing this module raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(os.path.dirname(_HERE), "libllmk.so")
+
+F32, BF16 = 0, 1
+MATH_BF16, MATH_TF32 = 1, 2
+EPI_ACCUMULATE, EPI_GELU, EPI_GELU_BWD = 1, 2, 4
+ACCUM_DINP, ACCUM_DWEIGHT, ACCUM_DBIAS = 1, 2, 4
+DEV_TIMEOUT = 1
+
+STATUS = {0: "ok", 1: "invalid argument", 2: "unsupported", 3: "cuda error", 4: "device wait timed out",
+          5: "workspace missing or too small", 6: "nccl error", 7: "no sm_100 device"}
+
+
+class LlmkError(RuntimeError):
+    def __init__(self, fn: str, code: int, detail: str):
+        super().__init__(f"{fn} -> {code} ({STATUS.get(code, '?')}): {detail}")
+        self.code = code
+
+
+class Epilogue(C.Structure):
+    _fields_ = [("bias", C.c_void_p), ("residual", C.c_void_p), ("ldr", C.c_longlong), ("aux", C.c_void_p),
+                ("ldaux", C.c_longlong), ("flags", C.c_int)]
+
+
+class GPT2Config(C.Structure):
+    _fields_ = [("max_seq_len", C.c_int), ("vocab_size", C.c_int), ("padded_vocab_size", C.c_int),
+                ("num_layers", C.c_int), ("num_heads", C.c_int), ("channels", C.c_int)]
+
+
+vp, i32, i64, sz, f32, u32p = C.c_void_p, C.c_int, C.c_longlong, C.c_size_t, C.c_float, C.POINTER(C.c_uint)
+
+# name -> (restype, argtypes); restype c_int means "status code, check it".
+SIGNATURES: dict[str, tuple] = {
+    "llmk_status_string": (C.c_char_p, [i32]),
+    "llmk_last_error": (C.c_char_p, []),
+    "llmk_version": (C.c_char_p, []),
+    "llmk_device_status": (i32, [u32p, i32]),
+    "llmk_launch_count": (C.c_ulonglong, []),
+    "llmk_gemm_workspace": (sz, [i32, i32, i32, i32]),
+    "llmk_gemm": (i32, [vp, i32, i64, vp, i32, i64, vp, i32, i64, i32, i32, i32, i32, C.POINTER(Epilogue), vp, sz,
+                        vp]),
+    "llmk_matmul_forward": (i32, [vp, i32, vp, vp, vp, i32, i32, i32, i32, vp]),
+    "llmk_matmul_backward_workspace": (sz, [i32, i32, i32, i32]),
+    "llmk_matmul_backward": (i32, [vp, i32, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, vp, sz, vp]),
+    "llmk_colsum_workspace": (sz, [i32, i32]),
+    "llmk_colsum": (i32, [vp, vp, i32, i32, i32, i32, vp, sz, vp]),
+}
+
+_lib = None
+
+
+def lib():
+    """Loads libllmk.so once (raises OSError when it has not been built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise OSError(f"{LIB_PATH} not built: run `python llm.cpp_b200/build.py`")
+        L = C.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def exported_symbols() -> list[str]:
+    return list(SIGNATURES)
+
+
+def check(name: str, rc: int) -> None:
+    if rc != 0:
+        raise LlmkError(name, rc, lib().llmk_last_error().decode(errors="replace"))
+
+
+def call(name: str, *args) -> None:
+    check(name, getattr(lib(), name)(*args))
+
+
+def ptr(t) -> int | None:
+    """Device pointer of a torch tensor (None for None)."""
+    return None if t is None else t.data_ptr()
+
+
+def stream_ptr(stream=None) -> int | None:
+    import torch
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return s.cuda_stream
+
+
+def dtype_code(t) -> int:
+    import torch
+    if t.dtype == torch.bfloat16:
+        return BF16
+    if t.dtype == torch.float32:
+        return F32
+    raise TypeError(f"unsupported dtype {t.dtype}")
+
+
+def device_status(reset: bool = True) -> int:
+    v = C.c_uint(0)
+    call("llmk_device_status", C.byref(v), 1 if reset else 0)
+    return v.value
+
+
+# ----------------------------------------------------------------- helpers
+def gemm(D, A, B, *, a_trans=False, b_trans=False, math=MATH_BF16, bias=None, residual=None, aux=None, flags=0,
+         workspace=None, stream=None, M=None, N=None, K=None):
+    """D[M,N] = epi(A x B^T); shapes inferred from the storage layouts."""
+    if M is None:
+        M = A.shape[1] if a_trans else A.shape[0]
+    if K is None:
+        K = A.shape[0] if a_trans else A.shape[1]
+    if N is None:
+        N = B.shape[1] if b_trans else B.shape[0]
+    ep = Epilogue(ptr(bias), ptr(residual), residual.stride(0) if residual is not None else 0, ptr(aux),
+                  aux.stride(0) if aux is not None else 0, flags)
+    ws_bytes = workspace.numel() * workspace.element_size() if workspace is not None else 0
+    call("llmk_gemm", ptr(D), dtype_code(D), D.stride(0), ptr(A), int(a_trans), A.stride(0), ptr(B), int(b_trans),
+         B.stride(0), math, M, N, K, C.byref(ep), ptr(workspace), ws_bytes, stream_ptr(stream))
