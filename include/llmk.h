@@ -117,6 +117,96 @@ size_t llmk_colsum_workspace(int M, int N);
 int llmk_colsum(float* dbias, const void* x, llmk_dtype x_dtype, int M, int N, int accumulate, void* workspace,
                 size_t workspace_bytes, void* stream);
 
+/* ------------------------------------------------------------ attention */
+/* Causal multi-head attention, head size 64, bf16 in/out, fp32 softmax and
+ * accumulation. qkv: (B, T, C3) bf16, Q|K|V blocks of C = C3/3 columns, head
+ * h at columns h*64 of each block. out: (B, T, C) bf16. lse: (B, NH, T) fp32
+ * natural-log logsumexp of the scaled scores (scale 1/8). Any T >= 1.
+ * Replaces gpt2cuda::BatchCausalAttentionForward, gpt2/cuda/attention.cu:119-133
+ * (AttentionForwardCUDA, kernel/flash_attn/flash_fwd_launch.cuh:18-68, which
+ * requires T % 128 == 0). */
+int llmk_attention_forward(void* out, float* lse, const void* qkv, int B, int T, int C3, int NH, void* stream);
+
+/* Gradient of llmk_attention_forward. dqkv (B, T, C3) bf16 is OVERWRITTEN
+ * (dQ, dK and dV); the reference accumulates dQ and overwrites dK/dV
+ * (flash_bwd_kernel.cuh:377-472) on buffers its callers zero first.
+ * workspace >= llmk_attention_backward_workspace(): D = rowsum(dO * O) and an
+ * fp32 dQ accumulator.
+ * Replaces gpt2cuda::BatchCausalAttentionBackward, gpt2/cuda/attention.cu:135-148. */
+size_t llmk_attention_backward_workspace(int B, int T, int C3, int NH);
+int llmk_attention_backward(void* dqkv, const void* dout, const void* out, const void* qkv, const float* lse, int B,
+                            int T, int C3, int NH, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------ layernorm */
+/* out = (inp - mean) * rstd * gamma + beta over rows of C (eps 1e-5, two-pass
+ * variance as the reference CPU path gpt2/layernorm.cpp:16-23). inp fp32,
+ * out fp32 or bf16; mean/rstd (N) may be NULL.
+ * Replaces gpt2cuda::BatchLayerNormForward, gpt2/cuda/layernorm.cu:348-350. */
+int llmk_layernorm_forward(void* out, llmk_dtype out_dtype, float* mean, float* rstd, const float* inp,
+                           const float* gamma, const float* beta, int N, int C, void* stream);
+
+/* dinp (+)= LN backward (LLMK_ACCUM_DINP selects +=); dgamma, dbeta (+)=
+ * (LLMK_ACCUM_DPARAM selects +=, as the reference). dinp_bf16 (optional)
+ * receives a bf16 copy of the final dinp. dout fp32 or bf16.
+ * workspace >= llmk_layernorm_backward_workspace(N, C) (per-block partials,
+ * reduced in a fixed order: deterministic).
+ * Replaces gpt2cuda::BatchLayerNormBackward, gpt2/cuda/layernorm.cu:351-353. */
+#define LLMK_ACCUM_DPARAM 8
+size_t llmk_layernorm_backward_workspace(int N, int C);
+int llmk_layernorm_backward(float* dinp, void* dinp_bf16, float* dgamma, float* dbeta, const void* dout,
+                            llmk_dtype dout_dtype, const float* inp, const float* gamma, const float* mean,
+                            const float* rstd, int N, int C, int flags, void* workspace, size_t workspace_bytes,
+                            void* stream);
+
+/* --------------------------------------------------- elementwise helpers */
+/* GELU (tanh form, gpt2/gelu.h:7-8) forward / backward over n elements
+ * (n % 4 == 0). Replaces gpt2cuda::BatchGeluForward/Backward, gpt2/cuda/gelu.cu:85-90. */
+int llmk_gelu_forward(void* out, const void* inp, llmk_dtype dtype, long long n, void* stream);
+int llmk_gelu_backward(void* dinp, const void* dout, const void* inp, llmk_dtype dtype, long long n, int accumulate,
+                       void* stream);
+/* out = a + b; backward da (+)= dy, db (+)= dy.
+ * Replaces gpt2cuda::BatchResidualForward/Backward, gpt2/cuda/residual.cu:74-81. */
+int llmk_residual_forward(void* out, const void* a, const void* b, llmk_dtype dtype, long long n, void* stream);
+int llmk_residual_backward(void* da, void* db, const void* dy, llmk_dtype dtype, long long n, int accumulate,
+                           void* stream);
+/* dtype conversion (f32 <-> bf16), n % 4 == 0. New helper. */
+int llmk_cast(void* out, llmk_dtype out_dtype, const void* in, llmk_dtype in_dtype, long long n, void* stream);
+
+/* --------------------------------------------------------------- encoder */
+/* out[b,t,:] = wte[tokens[b,t],:] + wpe[t,:] (fp32).
+ * Replaces gpt2cuda::BatchEncoderForward, gpt2/cuda/encoder.cu:92-99. */
+int llmk_encoder_forward(float* out, const int* tokens, const float* wte, const float* wpe, int B, int T, int C,
+                         void* stream);
+/* dwte[tokens[b,t],:] += dout[b,t,:]; dwpe[t,:] += sum_b dout[b,t,:]. Summed
+ * in position order (deterministic; the reference scatters with float
+ * atomicAdd, encoder.cu:17-25). workspace >= llmk_encoder_backward_workspace(B,T). */
+size_t llmk_encoder_backward_workspace(int B, int T);
+int llmk_encoder_backward(float* dwte, float* dwpe, const float* dout, const int* tokens, int B, int T, int C,
+                          void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------ softmax + cross-entropy */
+/* Per row of logits (BT, Vp) over the first V columns: losses[row] =
+ * logsumexp - logit[target]; when dlogits != NULL it receives
+ * (softmax - onehot(target)) * dscale on columns < V and 0 on [V, Vp)
+ * (dlogits may alias logits). Fuses the reference's BatchSoftmaxForward +
+ * BatchCrossEntropyForward + BatchCrossEntropySoftmaxBackward
+ * (gpt2/cuda/softmax.cu:13-91, cross_entropy.cu:7-32; call sites
+ * gpt2/cuda/gpt2cuda.cu:325,342,398). */
+int llmk_softmax_crossentropy(float* losses, void* dlogits, const void* logits, llmk_dtype dtype, const int* targets,
+                              int BT, int V, int Vp, float dscale, void* stream);
+/* *out = mean(x[0..n)) on the device, fixed reduction order. */
+int llmk_mean(float* out, const float* x, int n, void* stream);
+
+/* ----------------------------------------------------------------- AdamW */
+/* One launch over a flat parameter buffer: g' = g * grad_scale,
+ * m = b1 m + (1-b1) g', v = b2 v + (1-b2) g'^2,
+ * p -= lr (m/(1-b1^t) / (sqrt(v/(1-b2^t)) + eps) + wd p); params_bf16
+ * (optional) receives bf16(p). n % 4 == 0.
+ * Replaces gpt2cuda::AdamW (gpt2/cuda/adamw.cu:66-69), launched once per
+ * parameter tensor by GPT2::Update (gpt2/cuda/gpt2cuda.cu:434-441). */
+int llmk_adamw(float* params, void* params_bf16, const float* grads, float* m, float* v, long long n, float lr,
+               float beta1, float beta2, float eps, float weight_decay, int t, float grad_scale, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,713 @@
+// Causal flash attention (head size 64, bf16 in / fp32 accumulate) on tcgen05.
+//
+// Reference: gpt2cuda::BatchCausalAttentionForward / Backward
+// (gpt2/cuda/attention.cu:119-148) -> FA-2 CuTe kernels on mma.sync with one
+// CTA per (batch, head) walking every query tile (kernel/flash_attn/
+// flash_fwd_kernel.cuh:11-400, flash_bwd_kernel.cuh:94-480).
+//
+// Layout: qkv is the packed (B, T, 3C) activation; head h of Q/K/V is the
+// 64-column slice at h*64 of the first/second/third C block. One 3D TMA map
+// {3C, T, B} with a {64, 128, 1} box serves Q, K, V, dO and O tiles: rows past
+// T of a batch read as zeros.
+//
+// Forward: one CTA per (128-query tile, head, batch), heaviest tiles first.
+// warp 0 = TMA, warp 1 = tcgen05 issuer (S = Q K^T into TMEM, O_part = P V),
+// warps 2..5 = softmax (thread = query row): exp2 online softmax, P -> smem
+// (bf16, 128B-swizzled K-major), O accumulated in registers from O_part.
+// S and O_part are double-buffered in TMEM so the MMAs of tile j+1 overlap the
+// softmax of tile j.
+//
+// Backward: one CTA per (128-key tile, head, batch) walking query tiles from
+// the diagonal down. S^T = K Q^T and dP^T = V dO^T land in TMEM; softmax warps
+// (thread = key row) form P^T and dS^T = P^T (dP^T - D) in smem; then
+// dV += P^T dO and dK += dS^T Q accumulate in TMEM and dQ_i = dS K is added
+// to an fp32 workspace with vector reductions. D = rowsum(dO * O) and the
+// final dQ scaling run as small pre/post kernels.
+#include <algorithm>
+
+#include "ptx.cuh"
+#include "runtime.h"
+
+namespace llmk {
+namespace {
+
+constexpr int HD = 64;          // head size
+constexpr int TILE = 128;       // query / key tile
+constexpr int TILE_BYTES = TILE * HD * 2;  // 16 KB: one [128 x 64] bf16 tile, 128B rows
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Byte offset of 16-byte chunk `c` (0..7) of row `r` inside a 1024B-aligned
+// 128B-swizzled atom column (TMA SWIZZLE_128B / UMMA SWIZZLE_128B pattern).
+__device__ __forceinline__ uint32_t sw128(int r, int c) { return r * 128 + ((c ^ (r & 7)) << 4); }
+
+// Writes 8 fp32 as bf16 into row r, chunk c of a [128 x 128] bf16 K-major
+// tile stored as two 16 KB atom columns.
+__device__ __forceinline__ void st_tile_chunk(uint8_t* tile, int r, int chunk, const float* v) {
+  uint4 u;
+  u.x = pack_bf16x2(v[0], v[1]);
+  u.y = pack_bf16x2(v[2], v[3]);
+  u.z = pack_bf16x2(v[4], v[5]);
+  u.w = pack_bf16x2(v[6], v[7]);
+  *reinterpret_cast<uint4*>(tile + (chunk >> 3) * TILE_BYTES + sw128(r, chunk & 7)) = u;
+}
+
+// ------------------------------------------------------------------ forward
+struct FwdSmem {
+  static constexpr int kStages = 2;
+  static constexpr int Q_OFF = 0;
+  static constexpr int KV_OFF = TILE_BYTES;                          // stages x (K, V)
+  static constexpr int P_OFF = KV_OFF + kStages * 2 * TILE_BYTES;    // 2 x [128 x 128] bf16
+  static constexpr int BAR_OFF = P_OFF + 2 * 2 * TILE_BYTES;
+  static constexpr size_t BYTES = BAR_OFF + 256 + 1024;
+};
+
+__global__ void __launch_bounds__(192, 1)
+    attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, __nv_bfloat16* __restrict__ out,
+                    float* __restrict__ lse, int B, int T, int NH, int C, unsigned int* status) {
+  using S = FwdSmem;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem + S::Q_OFF;
+  uint8_t* sKV = smem + S::KV_OFF;
+  uint8_t* sP = smem + S::P_OFF;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::BAR_OFF);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = bars + 1;                  // [2]
+  uint64_t* kv_empty = kv_full + S::kStages;     // [2]
+  uint64_t* s_full = kv_empty + S::kStages;      // [2]
+  uint64_t* p_full = s_full + 2;                 // [2]
+  uint64_t* o_full = p_full + 2;                 // [2]
+  uint64_t* done = o_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int nq = (T + TILE - 1) / TILE;
+  const int bh_count = B * NH;
+  const int qt = nq - 1 - static_cast<int>(blockIdx.x) / bh_count;  // heaviest first
+  const int bh = static_cast<int>(blockIdx.x) % bh_count;
+  const int b = bh / NH, h = bh % NH;
+  const int q0 = qt * TILE;
+  const int n_kv = qt + 1;
+
+  const int warp = warp_id(), lane = lane_id();
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < S::kStages; ++s) {
+      mbar_init(kv_full + s, 1);
+      mbar_init(kv_empty + s, 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(s_full + i, 1);
+      mbar_init(p_full + i, 128);
+      mbar_init(o_full + i, 1);
+    }
+    mbar_init(done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  // TMEM columns: S[0] 0..127, S[1] 128..255, O_part[0] 256..319, O_part[1] 320..383
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_qkv);
+      mbar_arrive_expect_tx(q_full, TILE_BYTES);
+      tma_load_3d(sQ, &tm_qkv, q_full, h * HD, q0, b);
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int j = 0; j < n_kv; ++j) {
+        if (!mbar_wait(kv_empty + stage, phase ^ 1u, status, abort_flag, 1)) break;
+        uint8_t* sK = sKV + stage * 2 * TILE_BYTES;
+        mbar_arrive_expect_tx(kv_full + stage, 2 * TILE_BYTES);
+        tma_load_3d(sK, &tm_qkv, kv_full + stage, C + h * HD, j * TILE, b);
+        tma_load_3d(sK + TILE_BYTES, &tm_qkv, kv_full + stage, 2 * C + h * HD, j * TILE, b);
+        if (++stage == S::kStages) { stage = 0; phase ^= 1u; }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // S = Q K^T: M=128 queries, N=128 keys, both K-major (hd contiguous).
+      const uint32_t idesc_s = idesc_f32acc(128, 128, kFmtBF16, false, false);
+      // O_part = P V: M=128 queries, N=64 hd, K=128 keys; V is [keys][hd] = N-major.
+      const uint32_t idesc_o = idesc_f32acc(128, HD, kFmtBF16, false, true);
+      const uint32_t q_addr = smem_u32(sQ);
+      bool ok = mbar_wait(q_full, 0, status, abort_flag, 2);
+      auto issue_s = [&](int j, int st) {
+        const uint32_t k_addr = smem_u32(sKV + st * 2 * TILE_BYTES);
+        const uint32_t d = tmem + (j & 1) * 128;
+#pragma unroll
+        for (int ks = 0; ks < HD / 16; ++ks)
+          mma_f16_ss(d, sdesc_sw128(q_addr + ks * 32, 16, 1024), sdesc_sw128(k_addr + ks * 32, 16, 1024), idesc_s,
+                     ks > 0);
+        mma_commit(s_full + (j & 1));
+      };
+      int stage = 0;
+      uint32_t phase = 0;
+      if (ok) ok = mbar_wait(kv_full + 0, 0, status, abort_flag, 3);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0, 0);
+      }
+      for (int j = 0; j < n_kv && ok; ++j) {
+        const int st = stage;
+        const int nst = (stage + 1 == S::kStages) ? 0 : stage + 1;
+        const uint32_t nph = (stage + 1 == S::kStages) ? (phase ^ 1u) : phase;
+        if (j + 1 < n_kv) {
+          if (!mbar_wait(kv_full + nst, nph, status, abort_flag, 3)) { ok = false; break; }
+          tc_fence_after();
+          issue_s(j + 1, nst);
+        }
+        if (!mbar_wait(p_full + (j & 1), (j >> 1) & 1, status, abort_flag, 4)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t p_addr = smem_u32(sP + (j & 1) * 2 * TILE_BYTES);
+        const uint32_t v_addr = smem_u32(sKV + st * 2 * TILE_BYTES + TILE_BYTES);
+        const uint32_t d = tmem + 256 + (j & 1) * HD;
+#pragma unroll
+        for (int ks = 0; ks < TILE / 16; ++ks) {
+          const uint64_t a = sdesc_sw128(p_addr + (ks >> 2) * TILE_BYTES + (ks & 3) * 32, 16, 1024);
+          const uint64_t bd = sdesc_sw128(v_addr + ks * 2048, TILE_BYTES, 1024);
+          mma_f16_ss(d, a, bd, idesc_o, ks > 0);
+        }
+        mma_commit(o_full + (j & 1));
+        mma_commit(kv_empty + st);
+        stage = nst;
+        phase = nph;
+      }
+      mma_commit(done);
+      mbar_wait(done, 0, status, nullptr, 5);
+    }
+    __syncwarp();
+  } else {
+    const int q = warp & 3;
+    const int r = q * 32 + lane;  // query row within the tile (= TMEM lane)
+    const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
+    const float sl2 = 0.125f * 1.4426950408889634f;  // softmax scale * log2(e)
+    float m = -INFINITY, l = 0.f, alpha_prev = 0.f;
+    float o[HD];
+#pragma unroll
+    for (int i = 0; i < HD; ++i) o[i] = 0.f;
+    bool ok = true;
+    auto consume_o = [&](int jj, float alpha) -> bool {
+      bool w = mbar_wait(o_full + (jj & 1), (jj >> 1) & 1, status, abort_flag, 7);
+      if (!__all_sync(0xffffffffu, w)) return false;
+      tc_fence_after();
+      uint32_t v[32];
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        tmem_ld_32x32b_x32(tmem + lane_base + 256 + (jj & 1) * HD + half * 32, v);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) o[half * 32 + i] = o[half * 32 + i] * alpha + __uint_as_float(v[i]);
+      }
+      return true;
+    };
+    for (int j = 0; j < n_kv; ++j) {
+      bool w = mbar_wait(s_full + (j & 1), (j >> 1) & 1, status, abort_flag, 6);
+      if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
+      tc_fence_after();
+      float s[TILE];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tmem + lane_base + (j & 1) * 128 + c * 32, v);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(v[i]) * sl2;
+      }
+      if (j == qt) {  // diagonal tile: key index > query index is masked
+#pragma unroll
+        for (int i = 0; i < TILE; ++i)
+          if (i > r) s[i] = -INFINITY;
+      }
+      float mx = m;
+#pragma unroll
+      for (int i = 0; i < TILE; ++i) mx = fmaxf(mx, s[i]);
+      const float alpha = ex2(m - mx);  // 0 on the first tile (m = -inf)
+      float rs = 0.f;
+#pragma unroll
+      for (int i = 0; i < TILE; ++i) {
+        s[i] = ex2(s[i] - mx);
+        rs += s[i];
+      }
+      l = l * alpha + rs;
+      m = mx;
+      uint8_t* pt = sP + (j & 1) * 2 * TILE_BYTES;
+#pragma unroll
+      for (int ch = 0; ch < TILE / 8; ++ch) st_tile_chunk(pt, r, ch, s + ch * 8);
+      fence_async_smem();
+      tc_fence_before();
+      mbar_arrive(p_full + (j & 1));
+      if (j > 0 && !consume_o(j - 1, alpha_prev)) { ok = false; break; }
+      alpha_prev = alpha;
+    }
+    if (ok && consume_o(n_kv - 1, alpha_prev)) {
+      const int t = q0 + r;
+      if (t < T) {
+        const float inv = 1.0f / l;
+        __nv_bfloat16* dst = out + (static_cast<long long>(b) * T + t) * C + h * HD;
+#pragma unroll
+        for (int ch = 0; ch < HD / 8; ++ch) {
+          uint4 u;
+          u.x = pack_bf16x2(o[ch * 8 + 0] * inv, o[ch * 8 + 1] * inv);
+          u.y = pack_bf16x2(o[ch * 8 + 2] * inv, o[ch * 8 + 3] * inv);
+          u.z = pack_bf16x2(o[ch * 8 + 4] * inv, o[ch * 8 + 5] * inv);
+          u.w = pack_bf16x2(o[ch * 8 + 6] * inv, o[ch * 8 + 7] * inv);
+          reinterpret_cast<uint4*>(dst)[ch] = u;
+        }
+        // natural-log LSE: (m2 + log2 l) * ln 2
+        lse[(static_cast<long long>(b) * NH + h) * T + t] = (m + __log2f(l)) * 0.6931471805599453f;
+      }
+    }
+    tc_fence_before();
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ----------------------------------------------------------------- backward
+// D[b,h,t] = sum_i dO[b,t,h*64+i] * O[b,t,h*64+i]; zeroes dq_acc for the row.
+__global__ void attn_bwd_pre_kernel(float* __restrict__ D, float* __restrict__ dq_acc,
+                                    const __nv_bfloat16* __restrict__ dout, const __nv_bfloat16* __restrict__ o,
+                                    int B, int T, int NH, int C) {
+  const long long idx = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;  // (b, t, h)
+  if (idx >= static_cast<long long>(B) * T * NH) return;
+  const int h = static_cast<int>(idx % NH);
+  const long long bt = idx / NH;
+  const int b = static_cast<int>(bt / T), t = static_cast<int>(bt % T);
+  const uint4* pd = reinterpret_cast<const uint4*>(dout + bt * C + h * HD);
+  const uint4* po = reinterpret_cast<const uint4*>(o + bt * C + h * HD);
+  float s = 0.f;
+#pragma unroll
+  for (int k = 0; k < HD / 8; ++k) {
+    uint4 a = pd[k], c = po[k];
+    const __nv_bfloat162* x = reinterpret_cast<const __nv_bfloat162*>(&a);
+    const __nv_bfloat162* y = reinterpret_cast<const __nv_bfloat162*>(&c);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float2 u = __bfloat1622float2(x[i]), v = __bfloat1622float2(y[i]);
+      s += u.x * v.x + u.y * v.y;
+    }
+  }
+  D[(static_cast<long long>(b) * NH + h) * T + t] = s;
+  float4* z = reinterpret_cast<float4*>(dq_acc + bt * C + h * HD);
+#pragma unroll
+  for (int k = 0; k < HD / 4; ++k) z[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+}
+
+// dqkv[:, :, 0:C] = bf16(dq_acc * scale)
+__global__ void attn_bwd_post_kernel(__nv_bfloat16* __restrict__ dqkv, const float* __restrict__ dq_acc, int BT, int C,
+                                     float scale) {
+  const long long n8 = static_cast<long long>(BT) * C / 8;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n8;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long e = i * 8;
+    const long long bt = e / C;
+    const int c = static_cast<int>(e - bt * C);
+    const float4* p = reinterpret_cast<const float4*>(dq_acc + e);
+    float4 a = p[0], bb = p[1];
+    uint4 u;
+    u.x = pack_bf16x2(a.x * scale, a.y * scale);
+    u.y = pack_bf16x2(a.z * scale, a.w * scale);
+    u.z = pack_bf16x2(bb.x * scale, bb.y * scale);
+    u.w = pack_bf16x2(bb.z * scale, bb.w * scale);
+    *reinterpret_cast<uint4*>(dqkv + bt * 3 * C + c) = u;
+  }
+}
+
+struct BwdSmem {
+  static constexpr int kStages = 2;
+  static constexpr int K_OFF = 0;
+  static constexpr int V_OFF = TILE_BYTES;
+  static constexpr int QD_OFF = 2 * TILE_BYTES;                       // stages x (Q_i, dO_i)
+  static constexpr int P_OFF = QD_OFF + kStages * 2 * TILE_BYTES;      // P^T [128 keys x 128 q]
+  static constexpr int DS_OFF = P_OFF + 2 * TILE_BYTES;                // dS^T [128 keys x 128 q]
+  static constexpr int LD_OFF = DS_OFF + 2 * TILE_BYTES;               // stages x (LSE2[128], D[128]) fp32
+  static constexpr int BAR_OFF = LD_OFF + kStages * 2 * TILE * 4;
+  static constexpr size_t BYTES = BAR_OFF + 256 + 1024;
+};
+
+__device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d)
+               : "memory");
+}
+
+__global__ void __launch_bounds__(192, 1)
+    attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_do,
+                    __nv_bfloat16* __restrict__ dqkv, float* __restrict__ dq_acc, const float* __restrict__ lse,
+                    const float* __restrict__ Dvec, int B, int T, int NH, int C, unsigned int* status) {
+  using S = BwdSmem;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sK = smem + S::K_OFF;
+  uint8_t* sV = smem + S::V_OFF;
+  uint8_t* sQD = smem + S::QD_OFF;
+  uint8_t* sP = smem + S::P_OFF;
+  uint8_t* sDS = smem + S::DS_OFF;
+  float* sLD = reinterpret_cast<float*>(smem + S::LD_OFF);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::BAR_OFF);
+  uint64_t* kv_full = bars;                       // K, V loaded
+  uint64_t* qd_full = bars + 1;                   // [2] Q_i, dO_i (+ LSE/D by the TMA warp's lanes)
+  uint64_t* qd_empty = qd_full + S::kStages;      // [2]
+  uint64_t* sdp_full = qd_empty + S::kStages;     // S^T and dP^T in TMEM
+  uint64_t* ps_full = sdp_full + 1;               // P^T, dS^T in smem (128 arrivals)
+  uint64_t* grad_done = ps_full + 1;              // dV, dK, dQ MMAs of this tile done
+  uint64_t* dq_free = grad_done + 1;              // dQ TMEM read (128 arrivals)
+  uint64_t* ld_full = dq_free + 1;                // [2] LSE/D staged (32 arrivals)
+  uint64_t* done = ld_full + S::kStages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int nk = (T + TILE - 1) / TILE;
+  const int bh_count = B * NH;
+  const int kt = static_cast<int>(blockIdx.x) / bh_count;  // lightest last: kt=0 has the most q tiles
+  const int bh = static_cast<int>(blockIdx.x) % bh_count;
+  const int b = bh / NH, h = bh % NH;
+  const int k0 = kt * TILE;
+  const int nqi = nk - kt;  // query tiles kt..nk-1
+  const int warp = warp_id(), lane = lane_id();
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int s = 0; s < S::kStages; ++s) {
+      mbar_init(qd_full + s, 1);
+      mbar_init(qd_empty + s, 1);
+      mbar_init(ld_full + s, 32);
+    }
+    mbar_init(sdp_full, 1);
+    mbar_init(ps_full, 128);
+    mbar_init(grad_done, 1);
+    mbar_init(dq_free, 128);
+    mbar_init(done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  // TMEM columns: S^T 0..127, dP^T 128..255, dV 256..319, dK 320..383, dQ 384..447
+
+  if (warp == 0) {
+    // lane 0 issues TMA; all 32 lanes stage LSE (log2 units) and D for each q tile.
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_qkv);
+      tma_prefetch_desc(&tm_do);
+      mbar_arrive_expect_tx(kv_full, 2 * TILE_BYTES);
+      tma_load_3d(sK, &tm_qkv, kv_full, C + h * HD, k0, b);
+      tma_load_3d(sV, &tm_qkv, kv_full, 2 * C + h * HD, k0, b);
+    }
+    int stage = 0;
+    uint32_t phase = 0;
+    const float* lse_bh = lse + static_cast<long long>(bh) * T;
+    const float* d_bh = Dvec + static_cast<long long>(bh) * T;
+    for (int i = 0; i < nqi; ++i) {
+      const int q0 = (kt + i) * TILE;
+      bool w = mbar_wait(qd_empty + stage, phase ^ 1u, status, abort_flag, 8);
+      if (!__all_sync(0xffffffffu, w)) break;
+      if (lane == 0) {
+        uint8_t* sq = sQD + stage * 2 * TILE_BYTES;
+        mbar_arrive_expect_tx(qd_full + stage, 2 * TILE_BYTES);
+        tma_load_3d(sq, &tm_qkv, qd_full + stage, h * HD, q0, b);
+        tma_load_3d(sq + TILE_BYTES, &tm_do, qd_full + stage, h * HD, q0, b);
+      }
+      float* ld = sLD + stage * 2 * TILE;
+      for (int k = lane; k < TILE; k += 32) {
+        const int t = q0 + k;
+        ld[k] = t < T ? lse_bh[t] * 1.4426950408889634f : 0.f;
+        ld[TILE + k] = t < T ? d_bh[t] : 0.f;
+      }
+      mbar_arrive(ld_full + stage);
+      if (++stage == S::kStages) { stage = 0; phase ^= 1u; }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // S^T = K Q^T and dP^T = V dO^T: M=128 keys, N=128 q, K=64 (all K-major).
+      const uint32_t idesc_s = idesc_f32acc(128, 128, kFmtBF16, false, false);
+      // dV += P^T dO, dK += dS^T Q: M=128 keys, N=64, K=128 q; B is [q][hd] = N-major.
+      const uint32_t idesc_kv = idesc_f32acc(128, HD, kFmtBF16, false, true);
+      // dQ = dS K: M=128 q, N=64, K=128 keys; A = dS^T stored [keys][q] = M-major;
+      // B = K stored [keys][hd] = N-major.
+      const uint32_t idesc_q = idesc_f32acc(128, HD, kFmtBF16, true, true);
+      const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV);
+      const uint32_t p_addr = smem_u32(sP), ds_addr = smem_u32(sDS);
+      bool ok = mbar_wait(kv_full, 0, status, abort_flag, 9);
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int i = 0; i < nqi && ok; ++i) {
+        if (!mbar_wait(qd_full + stage, phase, status, abort_flag, 10)) { ok = false; break; }
+        // S^T / dP^T TMEM is free once the softmax warps published the previous P^T/dS^T.
+        if (i > 0 && !mbar_wait(ps_full, (i - 1) & 1, status, abort_flag, 11)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t q_addr = smem_u32(sQD + stage * 2 * TILE_BYTES);
+        const uint32_t do_addr = q_addr + TILE_BYTES;
+#pragma unroll
+        for (int ks = 0; ks < HD / 16; ++ks)
+          mma_f16_ss(tmem + 0, sdesc_sw128(k_addr + ks * 32, 16, 1024), sdesc_sw128(q_addr + ks * 32, 16, 1024),
+                     idesc_s, ks > 0);
+#pragma unroll
+        for (int ks = 0; ks < HD / 16; ++ks)
+          mma_f16_ss(tmem + 128, sdesc_sw128(v_addr + ks * 32, 16, 1024), sdesc_sw128(do_addr + ks * 32, 16, 1024),
+                     idesc_s, ks > 0);
+        mma_commit(sdp_full);
+        // P^T and dS^T of this tile written to smem
+        if (!mbar_wait(ps_full, i & 1, status, abort_flag, 12)) { ok = false; break; }
+        // dQ TMEM free (previous tile's dQ read by the epilogue warps)
+        if (i > 0 && !mbar_wait(dq_free, (i - 1) & 1, status, abort_flag, 13)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int ks = 0; ks < TILE / 16; ++ks) {
+          const uint32_t koff = (ks >> 2) * TILE_BYTES + (ks & 3) * 32;  // K (= q) offset in a [128 x 128] K-major tile
+          mma_f16_ss(tmem + 256, sdesc_sw128(p_addr + koff, 16, 1024),
+                     sdesc_sw128(do_addr + ks * 2048, TILE_BYTES, 1024), idesc_kv, (i > 0 || ks > 0));
+          mma_f16_ss(tmem + 320, sdesc_sw128(ds_addr + koff, 16, 1024),
+                     sdesc_sw128(q_addr + ks * 2048, TILE_BYTES, 1024), idesc_kv, (i > 0 || ks > 0));
+        }
+        // dQ = dS K: A = dS^T as M-major (q atoms 16 KB apart, key groups 1 KB apart), K-step = 16 keys.
+#pragma unroll
+        for (int ks = 0; ks < TILE / 16; ++ks)
+          mma_f16_ss(tmem + 384, sdesc_sw128(ds_addr + ks * 2048, TILE_BYTES, 1024),
+                     sdesc_sw128(k_addr + ks * 2048, TILE_BYTES, 1024), idesc_q, ks > 0);
+        mma_commit(grad_done);
+        mma_commit(qd_empty + stage);
+        if (++stage == S::kStages) { stage = 0; phase ^= 1u; }
+      }
+      mma_commit(done);
+      mbar_wait(done, 0, status, nullptr, 5);
+    }
+    __syncwarp();
+  } else {
+    const int q = warp & 3;
+    const int r = q * 32 + lane;  // key row within the tile for S^T/dP^T/dK/dV; query row for dQ
+    const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
+    const float sl2 = 0.125f * 1.4426950408889634f;
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int i = 0; i < nqi; ++i) {
+      const int qt = kt + i;
+      bool w = mbar_wait(ld_full + stage, phase, status, abort_flag, 15) &&
+               mbar_wait(sdp_full, i & 1, status, abort_flag, 16);
+      // previous tile's dV/dK/dQ MMAs read P^T/dS^T: wait before overwriting them
+      if (i > 0) w = w && mbar_wait(grad_done, (i - 1) & 1, status, abort_flag, 17);
+      if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
+      tc_fence_after();
+      if (i > 0) {
+        // dQ of the previous q tile: TMEM lane = query row
+        const int tq = (qt - 1) * TILE + r;
+        uint32_t v[32];
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          tmem_ld_32x32b_x32(tmem + lane_base + 384 + half * 32, v);
+          tmem_ld_wait();
+          if (tq < T) {
+            float* dst = dq_acc + (static_cast<long long>(b) * T + tq) * C + h * HD + half * 32;
+#pragma unroll
+            for (int k = 0; k < 8; ++k)
+              red_add_v4(dst + 4 * k, __uint_as_float(v[4 * k]), __uint_as_float(v[4 * k + 1]),
+                         __uint_as_float(v[4 * k + 2]), __uint_as_float(v[4 * k + 3]));
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(dq_free);
+      }
+      const float* ld = sLD + stage * 2 * TILE;
+      const int key = k0 + r;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t sv[32], dv[32];
+        tmem_ld_32x32b_x32(tmem + lane_base + c * 32, sv);
+        tmem_ld_32x32b_x32(tmem + lane_base + 128 + c * 32, dv);
+        tmem_ld_wait();
+        float p[32], ds[32];
+#pragma unroll
+        for (int k = 0; k < 32; ++k) {
+          const int qi = c * 32 + k;
+          const int tq = qt * TILE + qi;
+          float pv = ex2(__uint_as_float(sv[k]) * sl2 - ld[qi]);
+          if (tq < key || tq >= T) pv = 0.f;  // causal (query before key) and padded queries
+          p[k] = pv;
+          ds[k] = pv * (__uint_as_float(dv[k]) - ld[TILE + qi]);
+        }
+#pragma unroll
+        for (int ch = 0; ch < 4; ++ch) {
+          st_tile_chunk(sP, r, c * 4 + ch, p + ch * 8);
+          st_tile_chunk(sDS, r, c * 4 + ch, ds + ch * 8);
+        }
+      }
+      fence_async_smem();
+      tc_fence_before();
+      mbar_arrive(ps_full);
+      if (++stage == S::kStages) { stage = 0; phase ^= 1u; }
+    }
+    if (ok) {
+      bool w = mbar_wait(grad_done, (nqi - 1) & 1, status, abort_flag, 18);
+      if (__all_sync(0xffffffffu, w)) {
+        tc_fence_after();
+        uint32_t v[32];
+        // last dQ
+        const int tq = (kt + nqi - 1) * TILE + r;
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          tmem_ld_32x32b_x32(tmem + lane_base + 384 + half * 32, v);
+          tmem_ld_wait();
+          if (tq < T) {
+            float* dst = dq_acc + (static_cast<long long>(b) * T + tq) * C + h * HD + half * 32;
+#pragma unroll
+            for (int k = 0; k < 8; ++k)
+              red_add_v4(dst + 4 * k, __uint_as_float(v[4 * k]), __uint_as_float(v[4 * k + 1]),
+                         __uint_as_float(v[4 * k + 2]), __uint_as_float(v[4 * k + 3]));
+          }
+        }
+        // dK (scaled) and dV: TMEM lane = key row
+        const int tk = k0 + r;
+        if (tk < T) {
+          __nv_bfloat16* dk = dqkv + (static_cast<long long>(b) * T + tk) * 3 * C + C + h * HD;
+          __nv_bfloat16* dvp = dk + C;
+#pragma unroll
+          for (int half = 0; half < 2; ++half) {
+            tmem_ld_32x32b_x32(tmem + lane_base + 320 + half * 32, v);
+            tmem_ld_wait();
+#pragma unroll
+            for (int ch = 0; ch < 4; ++ch) {
+              uint4 u;
+              u.x = pack_bf16x2(__uint_as_float(v[ch * 8 + 0]) * 0.125f, __uint_as_float(v[ch * 8 + 1]) * 0.125f);
+              u.y = pack_bf16x2(__uint_as_float(v[ch * 8 + 2]) * 0.125f, __uint_as_float(v[ch * 8 + 3]) * 0.125f);
+              u.z = pack_bf16x2(__uint_as_float(v[ch * 8 + 4]) * 0.125f, __uint_as_float(v[ch * 8 + 5]) * 0.125f);
+              u.w = pack_bf16x2(__uint_as_float(v[ch * 8 + 6]) * 0.125f, __uint_as_float(v[ch * 8 + 7]) * 0.125f);
+              reinterpret_cast<uint4*>(dk + half * 32)[ch] = u;
+            }
+            tmem_ld_32x32b_x32(tmem + lane_base + 256 + half * 32, v);
+            tmem_ld_wait();
+#pragma unroll
+            for (int ch = 0; ch < 4; ++ch) {
+              uint4 u;
+              u.x = pack_bf16x2(__uint_as_float(v[ch * 8 + 0]), __uint_as_float(v[ch * 8 + 1]));
+              u.y = pack_bf16x2(__uint_as_float(v[ch * 8 + 2]), __uint_as_float(v[ch * 8 + 3]));
+              u.z = pack_bf16x2(__uint_as_float(v[ch * 8 + 4]), __uint_as_float(v[ch * 8 + 5]));
+              u.w = pack_bf16x2(__uint_as_float(v[ch * 8 + 6]), __uint_as_float(v[ch * 8 + 7]));
+              reinterpret_cast<uint4*>(dvp + half * 32)[ch] = u;
+            }
+          }
+        } else {
+          // keep the collective tcgen05.ld pattern uniform across the warp
+#pragma unroll
+          for (int half = 0; half < 2; ++half) {
+            tmem_ld_32x32b_x32(tmem + lane_base + 320 + half * 32, v);
+            tmem_ld_32x32b_x32(tmem + lane_base + 256 + half * 32, v);
+            tmem_ld_wait();
+          }
+        }
+      }
+    }
+    tc_fence_before();
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+int set_smem(const void* k, size_t bytes) {
+  static bool done_fwd[64] = {}, done_bwd[64] = {};
+  int dev = 0;
+  LLMK_CUDA(cudaGetDevice(&dev));
+  bool* d = (k == reinterpret_cast<const void*>(attn_fwd_kernel)) ? done_fwd : done_bwd;
+  if (dev < 64 && !d[dev]) {
+    LLMK_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes)));
+    d[dev] = true;
+  }
+  return LLMK_OK;
+}
+
+int check_shapes(int B, int T, int C3, int NH) {
+  if (B <= 0 || T <= 0 || C3 <= 0 || NH <= 0 || C3 % 3) return fail(LLMK_ERR_INVALID_ARG, "attention: bad shape");
+  const int C = C3 / 3;
+  if (C % NH || C / NH != HD) return fail(LLMK_ERR_UNSUPPORTED, "attention: head size must be 64");
+  return LLMK_OK;
+}
+
+}  // namespace
+}  // namespace llmk
+
+using namespace llmk;
+
+extern "C" {
+
+int llmk_attention_forward(void* out, float* lse, const void* qkv, int B, int T, int C3, int NH, void* stream) {
+  if (!out || !lse || !qkv) return fail(LLMK_ERR_INVALID_ARG, "attention_forward: null pointer");
+  LLMK_TRY(check_shapes(B, T, C3, NH));
+  if (!aligned16(out) || !aligned16(qkv)) return fail(LLMK_ERR_UNSUPPORTED, "attention_forward: alignment");
+  const int C = C3 / 3;
+  CUtensorMap tm;
+  LLMK_TRY(make_tmap_3d(&tm, qkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, C3, T, B, static_cast<uint64_t>(C3) * 2,
+                        static_cast<uint64_t>(T) * C3 * 2, HD, TILE, 1));
+  LLMK_TRY(set_smem(reinterpret_cast<const void*>(attn_fwd_kernel), FwdSmem::BYTES));
+  const int nq = (T + TILE - 1) / TILE;
+  attn_fwd_kernel<<<nq * B * NH, 192, FwdSmem::BYTES, static_cast<cudaStream_t>(stream)>>>(
+      tm, static_cast<__nv_bfloat16*>(out), lse, B, T, NH, C, device_status_ptr());
+  count_launch();
+  LLMK_CUDA(cudaGetLastError());
+  return LLMK_OK;
+}
+
+size_t llmk_attention_backward_workspace(int B, int T, int C3, int NH) {
+  if (B <= 0 || T <= 0 || C3 <= 0 || NH <= 0) return 0;
+  const size_t d = static_cast<size_t>(B) * NH * T * sizeof(float);
+  const size_t dq = static_cast<size_t>(B) * T * (C3 / 3) * sizeof(float);
+  return ((d + 255) / 256) * 256 + dq;
+}
+
+int llmk_attention_backward(void* dqkv, const void* dout, const void* out, const void* qkv, const float* lse, int B,
+                            int T, int C3, int NH, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!dqkv || !dout || !out || !qkv || !lse) return fail(LLMK_ERR_INVALID_ARG, "attention_backward: null pointer");
+  LLMK_TRY(check_shapes(B, T, C3, NH));
+  if (!aligned16(dqkv) || !aligned16(dout) || !aligned16(out) || !aligned16(qkv))
+    return fail(LLMK_ERR_UNSUPPORTED, "attention_backward: alignment");
+  if (!workspace || workspace_bytes < llmk_attention_backward_workspace(B, T, C3, NH) || !aligned16(workspace))
+    return fail(LLMK_ERR_WORKSPACE, "attention_backward: workspace too small");
+  const int C = C3 / 3;
+  float* Dv = static_cast<float*>(workspace);
+  float* dq = reinterpret_cast<float*>(static_cast<char*>(workspace) +
+                                       ((static_cast<size_t>(B) * NH * T * sizeof(float) + 255) / 256) * 256);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const long long rows = static_cast<long long>(B) * T * NH;
+  attn_bwd_pre_kernel<<<static_cast<int>((rows + 127) / 128), 128, 0, s>>>(
+      Dv, dq, static_cast<const __nv_bfloat16*>(dout), static_cast<const __nv_bfloat16*>(out), B, T, NH, C);
+  CUtensorMap tq, td;
+  LLMK_TRY(make_tmap_3d(&tq, qkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, C3, T, B, static_cast<uint64_t>(C3) * 2,
+                        static_cast<uint64_t>(T) * C3 * 2, HD, TILE, 1));
+  LLMK_TRY(make_tmap_3d(&td, dout, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, C, T, B, static_cast<uint64_t>(C) * 2,
+                        static_cast<uint64_t>(T) * C * 2, HD, TILE, 1));
+  LLMK_TRY(set_smem(reinterpret_cast<const void*>(attn_bwd_kernel), BwdSmem::BYTES));
+  const int nk = (T + TILE - 1) / TILE;
+  attn_bwd_kernel<<<nk * B * NH, 192, BwdSmem::BYTES, s>>>(tq, td, static_cast<__nv_bfloat16*>(dqkv), dq, lse, Dv, B,
+                                                            T, NH, C, device_status_ptr());
+  const long long n8 = static_cast<long long>(B) * T * C / 8;
+  attn_bwd_post_kernel<<<static_cast<int>(std::min<long long>((n8 + 255) / 256, 148LL * 16)), 256, 0, s>>>(
+      static_cast<__nv_bfloat16*>(dqkv), dq, B * T, C, 0.125f);
+  count_launch(3);
+  LLMK_CUDA(cudaGetLastError());
+  return LLMK_OK;
+}
+
+}  // extern "C"

@@ -55,7 +55,11 @@ struct Cfg {
   static constexpr uint32_t kMNLayout = kTF32 ? kLayoutSW128Base32 : kLayoutSW128;
   static constexpr uint32_t kMNSbo = kTF32 ? 512 : 1024;
   static constexpr int kThreads = 192;
-  static constexpr size_t SMEM = size_t(kStages) * STAGE_BYTES + 1024 + 256;
+  // Epilogue staging for TMA stores: 4 warps x 2 buffers x [32 rows x 128 B].
+  static constexpr int STAGING_OFF = kStages * STAGE_BYTES;
+  static constexpr int STAGING_BYTES = 4 * 2 * 4096;
+  static constexpr int BAR_OFF = STAGING_OFF + STAGING_BYTES;
+  static constexpr size_t SMEM = size_t(BAR_OFF) + 256 + 1024;
   static_assert(kBN == 128 || kBN == 256, "BN");
 };
 
@@ -101,8 +105,40 @@ __device__ __forceinline__ void store8_bf16(__nv_bfloat16* p, const float* v) {
   *reinterpret_cast<uint4*>(p) = u;
 }
 
+// Epilogue operations on 8 consecutive columns [gn, gn+8) of row gm (all in
+// bounds) except the final store: bias, residual, GELU (+ pre-activation
+// store) / GELU-backward, accumulate onto the old D.
+__device__ __forceinline__ void epi_ops8(const EpiParams& ep, long long gm, int gn, float* v) {
+  float t[8];
+  if (ep.bias) {
+    load8(ep.bias + gn, t);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] += t[j];
+  }
+  if (ep.residual) {
+    load8(ep.residual + gm * ep.ldr + gn, t);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] += t[j];
+  }
+  if (ep.flags & LLMK_EPI_GELU) {
+    if (ep.aux) store8_bf16(ep.aux + gm * ep.ldaux + gn, v);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = gelu_tanh(v[j]);
+  } else if (ep.flags & LLMK_EPI_GELU_BWD) {
+    load8_bf16(ep.aux + gm * ep.ldaux + gn, t);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] *= gelu_tanh_grad(t[j]);
+  }
+  if (ep.flags & LLMK_EPI_ACCUMULATE) {
+    if (ep.d_bf16) load8_bf16(static_cast<const __nv_bfloat16*>(ep.D) + gm * ep.ldd + gn, t);
+    else load8(static_cast<const float*>(ep.D) + gm * ep.ldd + gn, t);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] += t[j];
+  }
+}
+
 // Applies the epilogue to 8 consecutive columns [gn, gn+8) of row gm, all in
-// bounds. Shared by the direct epilogue and the split-K reduction.
+// bounds, and stores them (split-K reduction path).
 __device__ __forceinline__ void epi_apply8(const EpiParams& ep, long long gm, int gn, float* v) {
   float t[8];
   if (ep.bias) {
@@ -145,12 +181,13 @@ __device__ __forceinline__ void epi_apply8(const EpiParams& ep, long long gm, in
 
 template <bool kTF32, bool kAMN, bool kBMN, int kBN>
 __global__ void __launch_bounds__(192, 1)
-    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, EpiParams ep,
-                   int M, int N, int K, int splits, unsigned int* status) {
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmD, EpiParams ep, int M, int N, int K, int splits,
+                   unsigned int* status) {
   using C = Cfg<kTF32, kAMN, kBMN, kBN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kStages * C::STAGE_BYTES);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
   uint64_t* empty = full + C::kStages;
   uint64_t* accf = empty + C::kStages;
   uint64_t* acce = accf + 2;
@@ -284,42 +321,76 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_after();
       const long long gm = m0 + q * 32 + lane;
       const bool row_ok = gm < M;
+      // 64-column groups: two TMEM loads, epilogue ops in registers, then the
+      // row is written 128B-swizzled into this warp's staging buffer and one
+      // lane issues a TMA store of the warp's [32 x 32] fp32 or [32 x 64] bf16
+      // block (rows / columns past M / N are clipped by the tensor map).
+      uint8_t* stg = smem + C::STAGING_OFF + (q * 2) * 4096;
+      const bool bf16_out = ep.d_bf16 && !ep.partial;
 #pragma unroll 1
-      for (int c = 0; c < kBN / 32; ++c) {
-        const int gn0 = n0 + c * 32;
+      for (int g = 0; g < kBN / 64; ++g) {
+        const int gn0 = n0 + g * 64;
         if (gn0 >= N) break;
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * kBN + c * 32, r);
-        tmem_ld_wait();
-        if (!row_ok) continue;
-        const int nvalid = min(32, N - gn0);
-        if (ep.partial) {
-          float* pp = ep.partial + (static_cast<long long>(sp) * M + gm) * N + gn0;
+        float v[64];
+        {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * kBN + g * 64, r);
+          tmem_ld_wait();
 #pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            if (g * 8 < nvalid) {
-              float v[8];
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+          tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * kBN + g * 64 + 32, r);
+          tmem_ld_wait();
 #pragma unroll
-              for (int j = 0; j < 8; ++j) v[j] = __uint_as_float(r[g * 8 + j]);
-              store8(pp + g * 8, v);
-            }
+          for (int j = 0; j < 32; ++j) v[32 + j] = __uint_as_float(r[j]);
+        }
+        if (row_ok && !ep.partial) {
+#pragma unroll
+          for (int k = 0; k < 8; ++k)
+            if (gn0 + k * 8 < N) epi_ops8(ep, gm, gn0 + k * 8, v + k * 8);
+        }
+        // the previous group's stores must have read the staging buffers
+        if (lane == 0) bulk_wait_read0();
+        __syncwarp();
+        const int r7 = lane & 7;
+        if (bf16_out) {
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            uint4 u;
+            u.x = pack_bf16x2(v[k * 8 + 0], v[k * 8 + 1]);
+            u.y = pack_bf16x2(v[k * 8 + 2], v[k * 8 + 3]);
+            u.z = pack_bf16x2(v[k * 8 + 4], v[k * 8 + 5]);
+            u.w = pack_bf16x2(v[k * 8 + 6], v[k * 8 + 7]);
+            *reinterpret_cast<uint4*>(stg + lane * 128 + ((k ^ r7) << 4)) = u;
           }
         } else {
 #pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            if (g * 8 < nvalid) {
-              float v[8];
+          for (int h = 0; h < 2; ++h)
 #pragma unroll
-              for (int j = 0; j < 8; ++j) v[j] = __uint_as_float(r[g * 8 + j]);
-              epi_apply8(ep, gm, gn0 + g * 8, v);
-            }
+            for (int k = 0; k < 8; ++k)
+              *reinterpret_cast<float4*>(stg + h * 4096 + lane * 128 + ((k ^ r7) << 4)) =
+                  make_float4(v[h * 32 + k * 4], v[h * 32 + k * 4 + 1], v[h * 32 + k * 4 + 2], v[h * 32 + k * 4 + 3]);
+        }
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          const int y = m0 + q * 32;
+          if (bf16_out) {
+            tma_store_2d(&tmD, stg, gn0, y);
+          } else if (ep.partial) {
+            tma_store_3d(&tmD, stg, gn0, y, sp);
+            if (gn0 + 32 < N) tma_store_3d(&tmD, stg + 4096, gn0 + 32, y, sp);
+          } else {
+            tma_store_2d(&tmD, stg, gn0, y);
+            if (gn0 + 32 < N) tma_store_2d(&tmD, stg + 4096, gn0 + 32, y);
           }
+          bulk_commit();
         }
       }
       tc_fence_before();
       mbar_arrive(acce + acc);
     }
   }
+  if (warp >= 2 && lane == 0) bulk_wait0();  // stores complete before the CTA retires
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -366,10 +437,19 @@ int launch_gemm(const void* A, long long lda, const void* B, long long ldb, int 
   else LLMK_TRY(make_tmap_2d(&ta, A, dt, M, K, lda * C::kElem, C::kAtomMN, C::BK, mn_swz));
   if (!kBMN) LLMK_TRY(make_tmap_2d(&tb, B, dt, K, N, ldb * C::kElem, C::BK, kBN));
   else LLMK_TRY(make_tmap_2d(&tb, B, dt, N, K, ldb * C::kElem, C::kAtomMN, C::BK, mn_swz));
+  CUtensorMap td;
+  if (ep.partial) {
+    LLMK_TRY(make_tmap_3d(&td, ep.partial, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, N, M, splits, static_cast<uint64_t>(N) * 4,
+                          static_cast<uint64_t>(M) * N * 4, 32, 32, 1));
+  } else if (ep.d_bf16) {
+    LLMK_TRY(make_tmap_2d(&td, ep.D, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, N, M, ep.ldd * 2, 64, 32));
+  } else {
+    LLMK_TRY(make_tmap_2d(&td, ep.D, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, N, M, ep.ldd * 4, 32, 32));
+  }
   const int num_tiles = ((M + C::BM - 1) / C::BM) * ((N + kBN - 1) / kBN) * splits;
   const int grid = std::min(num_tiles, num_sms());
   unsigned int* st = device_status_ptr();
-  kern<<<grid, C::kThreads, C::SMEM, static_cast<cudaStream_t>(stream)>>>(ta, tb, ep, M, N, K, splits, st);
+  kern<<<grid, C::kThreads, C::SMEM, static_cast<cudaStream_t>(stream)>>>(ta, tb, td, ep, M, N, K, splits, st);
   count_launch();
   LLMK_CUDA(cudaGetLastError());
   return LLMK_OK;

@@ -1,0 +1,669 @@
+// Native GPT-2 trainer on the llmk ops: the B200 counterpart of the
+// reference's gpt2cuda::GPT2 and gpt2cuda::Layer (gpt2/cuda/gpt2cuda.h:34-190,
+// gpt2/cuda/layer.cuh:5-102) with replicated data parallelism over NCCL.
+//
+// Precision: fp32 master parameters, gradients and AdamW state; a bf16 copy
+// of the parameters feeds the tensor-core GEMMs; activations that feed GEMMs
+// or attention are bf16, the residual stream and its gradient are fp32.
+//
+// Memory layout (HBM): parameters live LAYER-MAJOR in one flat buffer —
+// [wte | wpe | layer 0 {ln1w ln1b qkvw qkvb attprojw attprojb ln2w ln2b fcw
+// fcb fcprojw fcprojb} | ... | layer L-1 {...} | lnfw lnfb] — so each layer's
+// gradients are one contiguous bucket for the data-parallel all-reduce, which
+// is issued on a communication stream as soon as that layer's backward is
+// done and overlaps the backward of the layers below. The llm.c v3 checkpoint
+// order (tensor-major) is used only at the host boundary
+// (llmk_gpt2_{load,read}_parameters).
+//
+// Per-step data flow mirrors gpt2/cuda/gpt2cuda.cu:304-459 and
+// gpt2/cuda/layer.cu:151-266, with bias, residual add, GELU and GELU-backward
+// fused into the GEMM epilogues and softmax + cross-entropy fused into one
+// pass that turns logits into dlogits in place.
+#include <nccl.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "llmk.h"
+#include "llmk_gpt2.h"
+#include "runtime.h"
+
+namespace llmk {
+namespace {
+
+enum Tensor { WTE = 0, WPE, LN1W, LN1B, QKVW, QKVB, ATTPROJW, ATTPROJB, LN2W, LN2B, FCW, FCB, FCPROJW, FCPROJB, LNFW, LNFB };
+
+// Sizes of the 16 llm.c tensors (gpt2/gpt2.cpp:112-230 read order); per-layer
+// tensors are L times the per-layer size.
+void tensor_sizes(const llmk_gpt2_config& c, size_t s[16]) {
+  const size_t C = c.channels, L = c.num_layers;
+  s[WTE] = static_cast<size_t>(c.padded_vocab_size) * C;
+  s[WPE] = static_cast<size_t>(c.max_seq_len) * C;
+  s[LN1W] = s[LN1B] = L * C;
+  s[QKVW] = L * 3 * C * C;
+  s[QKVB] = L * 3 * C;
+  s[ATTPROJW] = L * C * C;
+  s[ATTPROJB] = L * C;
+  s[LN2W] = s[LN2B] = L * C;
+  s[FCW] = L * 4 * C * C;
+  s[FCB] = L * 4 * C;
+  s[FCPROJW] = L * 4 * C * C;
+  s[FCPROJB] = L * C;
+  s[LNFW] = s[LNFB] = C;
+}
+
+template <typename T>
+int dalloc(T** p, size_t n) {
+  return cuda_check(cudaMalloc(reinterpret_cast<void**>(p), std::max<size_t>(n, 1) * sizeof(T)), "cudaMalloc");
+}
+
+}  // namespace
+}  // namespace llmk
+
+using llmk::fail;
+
+struct LayerParams {
+  // offsets (elements) into the flat layer-major parameter buffer
+  size_t ln1w, ln1b, qkvw, qkvb, attprojw, attprojb, ln2w, ln2b, fcw, fcb, fcprojw, fcprojb, begin, end;
+};
+
+struct LayerActs {
+  float *ln1_mean, *ln1_rstd, *ln2_mean, *ln2_rstd, *lse, *res2, *res3;
+  __nv_bfloat16 *ln1, *qkv, *atty, *ln2, *fch_pre, *fch_gelu;
+};
+
+struct llmk_gpt2 {
+  llmk_gpt2_config cfg{};
+  int B = 0, T = 0, device = 0;
+  cudaStream_t stream = nullptr, comm_stream = nullptr;
+  bool own_stream = false;
+  size_t nparams = 0;
+  size_t tsize[16] = {};
+  size_t off_wte = 0, off_wpe = 0, off_lnfw = 0, off_lnfb = 0;
+  std::vector<LayerParams> lp;
+  float *params = nullptr, *grads = nullptr, *m = nullptr, *v = nullptr;
+  __nv_bfloat16* params_bf16 = nullptr;
+  // activations
+  float* encoded = nullptr;
+  std::vector<LayerActs> acts;
+  float *lnf_mean = nullptr, *lnf_rstd = nullptr, *losses = nullptr, *loss = nullptr;
+  __nv_bfloat16 *lnf = nullptr, *logits = nullptr;
+  // backward scratch
+  float *dres = nullptr, *dln = nullptr;
+  __nv_bfloat16 *dres_bf16 = nullptr, *datty = nullptr, *dqkv = nullptr, *dfch = nullptr;
+  void* workspace = nullptr;
+  size_t workspace_bytes = 0;
+  int *inputs = nullptr, *targets = nullptr;
+  int *h_inputs = nullptr, *h_targets = nullptr;  // pinned staging
+  float* h_loss = nullptr;
+  bool have_targets = false;
+  // data parallel
+  ncclComm_t comm = nullptr;
+  int rank = 0, world = 1;
+  std::vector<cudaEvent_t> layer_done;
+  cudaEvent_t embed_done = nullptr, comm_done = nullptr;
+  unsigned long long steps = 0;
+};
+
+namespace {
+
+int ensure_device(llmk_gpt2* g) { return llmk::cuda_check(cudaSetDevice(g->device), "cudaSetDevice"); }
+
+int nccl_check(ncclResult_t r, const char* what) {
+  if (r == ncclSuccess) return LLMK_OK;
+  return fail(LLMK_ERR_NCCL, std::string(what) + ": " + ncclGetErrorString(r));
+}
+
+void layout(llmk_gpt2* g) {
+  const size_t C = g->cfg.channels, L = g->cfg.num_layers;
+  llmk::tensor_sizes(g->cfg, g->tsize);
+  size_t o = 0;
+  g->off_wte = o;
+  o += g->tsize[llmk::WTE];
+  g->off_wpe = o;
+  o += g->tsize[llmk::WPE];
+  g->lp.resize(L);
+  for (size_t l = 0; l < L; ++l) {
+    LayerParams& p = g->lp[l];
+    p.begin = o;
+    p.ln1w = o; o += C;
+    p.ln1b = o; o += C;
+    p.qkvw = o; o += 3 * C * C;
+    p.qkvb = o; o += 3 * C;
+    p.attprojw = o; o += C * C;
+    p.attprojb = o; o += C;
+    p.ln2w = o; o += C;
+    p.ln2b = o; o += C;
+    p.fcw = o; o += 4 * C * C;
+    p.fcb = o; o += 4 * C;
+    p.fcprojw = o; o += 4 * C * C;
+    p.fcprojb = o; o += C;
+    p.end = o;
+  }
+  g->off_lnfw = o;
+  o += C;
+  g->off_lnfb = o;
+  o += C;
+  g->nparams = o;
+}
+
+// Maps llm.c tensor-major order <-> layer-major order on the host.
+// dir = 0: src is llm.c order, dst layer-major; dir = 1: the reverse.
+void permute_params(const llmk_gpt2* g, const float* src, float* dst, int dir) {
+  const size_t C = g->cfg.channels, L = g->cfg.num_layers;
+  const size_t per[12] = {C, C, 3 * C * C, 3 * C, C * C, C, C, C, 4 * C * C, 4 * C, 4 * C * C, C};
+  size_t llmc_off[16];
+  size_t o = 0;
+  for (int i = 0; i < 16; ++i) {
+    llmc_off[i] = o;
+    o += g->tsize[i];
+  }
+  auto copy = [&](size_t lm, size_t lay, size_t n) {
+    if (dir == 0) std::memcpy(dst + lay, src + lm, n * sizeof(float));
+    else std::memcpy(dst + lm, src + lay, n * sizeof(float));
+  };
+  copy(llmc_off[llmk::WTE], g->off_wte, g->tsize[llmk::WTE]);
+  copy(llmc_off[llmk::WPE], g->off_wpe, g->tsize[llmk::WPE]);
+  for (size_t l = 0; l < L; ++l) {
+    const LayerParams& p = g->lp[l];
+    const size_t lay[12] = {p.ln1w, p.ln1b, p.qkvw, p.qkvb, p.attprojw, p.attprojb,
+                            p.ln2w, p.ln2b, p.fcw, p.fcb, p.fcprojw, p.fcprojb};
+    for (int t = 0; t < 12; ++t) copy(llmc_off[2 + t] + l * per[t], lay[t], per[t]);
+  }
+  copy(llmc_off[llmk::LNFW], g->off_lnfw, C);
+  copy(llmc_off[llmk::LNFB], g->off_lnfb, C);
+}
+
+void free_all(llmk_gpt2* g) {
+  auto f = [](void* p) {
+    if (p) cudaFree(p);
+  };
+  f(g->params); f(g->grads); f(g->m); f(g->v); f(g->params_bf16); f(g->encoded);
+  for (auto& a : g->acts) {
+    f(a.ln1_mean); f(a.ln1_rstd); f(a.ln2_mean); f(a.ln2_rstd); f(a.lse); f(a.res2); f(a.res3);
+    f(a.ln1); f(a.qkv); f(a.atty); f(a.ln2); f(a.fch_pre); f(a.fch_gelu);
+  }
+  f(g->lnf_mean); f(g->lnf_rstd); f(g->losses); f(g->loss); f(g->lnf); f(g->logits);
+  f(g->dres); f(g->dln); f(g->dres_bf16); f(g->datty); f(g->dqkv); f(g->dfch); f(g->workspace);
+  f(g->inputs); f(g->targets);
+  if (g->h_inputs) cudaFreeHost(g->h_inputs);
+  if (g->h_targets) cudaFreeHost(g->h_targets);
+  if (g->h_loss) cudaFreeHost(g->h_loss);
+  for (auto e : g->layer_done) cudaEventDestroy(e);
+  if (g->embed_done) cudaEventDestroy(g->embed_done);
+  if (g->comm_done) cudaEventDestroy(g->comm_done);
+  if (g->comm) ncclCommDestroy(g->comm);
+  if (g->comm_stream) cudaStreamDestroy(g->comm_stream);
+  if (g->own_stream && g->stream) cudaStreamDestroy(g->stream);
+}
+
+int alloc_all(llmk_gpt2* g) {
+  using llmk::dalloc;
+  const size_t B = g->B, T = g->T, C = g->cfg.channels, L = g->cfg.num_layers, NH = g->cfg.num_heads;
+  const size_t BT = B * T, Vp = g->cfg.padded_vocab_size;
+  LLMK_TRY(dalloc(&g->params, g->nparams));
+  LLMK_TRY(dalloc(&g->grads, g->nparams));
+  LLMK_TRY(dalloc(&g->m, g->nparams));
+  LLMK_TRY(dalloc(&g->v, g->nparams));
+  LLMK_TRY(dalloc(&g->params_bf16, g->nparams));
+  LLMK_CUDA(cudaMemset(g->m, 0, g->nparams * sizeof(float)));
+  LLMK_CUDA(cudaMemset(g->v, 0, g->nparams * sizeof(float)));
+  LLMK_CUDA(cudaMemset(g->grads, 0, g->nparams * sizeof(float)));
+  LLMK_TRY(dalloc(&g->encoded, BT * C));
+  g->acts.resize(L);
+  for (auto& a : g->acts) {
+    LLMK_TRY(dalloc(&a.ln1_mean, BT)); LLMK_TRY(dalloc(&a.ln1_rstd, BT));
+    LLMK_TRY(dalloc(&a.ln2_mean, BT)); LLMK_TRY(dalloc(&a.ln2_rstd, BT));
+    LLMK_TRY(dalloc(&a.lse, B * NH * T));
+    LLMK_TRY(dalloc(&a.res2, BT * C)); LLMK_TRY(dalloc(&a.res3, BT * C));
+    LLMK_TRY(dalloc(&a.ln1, BT * C)); LLMK_TRY(dalloc(&a.qkv, BT * 3 * C)); LLMK_TRY(dalloc(&a.atty, BT * C));
+    LLMK_TRY(dalloc(&a.ln2, BT * C)); LLMK_TRY(dalloc(&a.fch_pre, BT * 4 * C)); LLMK_TRY(dalloc(&a.fch_gelu, BT * 4 * C));
+  }
+  LLMK_TRY(dalloc(&g->lnf_mean, BT)); LLMK_TRY(dalloc(&g->lnf_rstd, BT));
+  LLMK_TRY(dalloc(&g->losses, BT)); LLMK_TRY(dalloc(&g->loss, 1));
+  LLMK_TRY(dalloc(&g->lnf, BT * C)); LLMK_TRY(dalloc(&g->logits, BT * Vp));
+  LLMK_TRY(dalloc(&g->dres, BT * C)); LLMK_TRY(dalloc(&g->dln, BT * C));
+  LLMK_TRY(dalloc(&g->dres_bf16, BT * C)); LLMK_TRY(dalloc(&g->datty, BT * C));
+  LLMK_TRY(dalloc(&g->dqkv, BT * 3 * C)); LLMK_TRY(dalloc(&g->dfch, BT * 4 * C));
+  LLMK_TRY(dalloc(&g->inputs, BT)); LLMK_TRY(dalloc(&g->targets, BT));
+  LLMK_CUDA(cudaMallocHost(reinterpret_cast<void**>(&g->h_inputs), BT * sizeof(int)));
+  LLMK_CUDA(cudaMallocHost(reinterpret_cast<void**>(&g->h_targets), BT * sizeof(int)));
+  LLMK_CUDA(cudaMallocHost(reinterpret_cast<void**>(&g->h_loss), sizeof(float)));
+  // one workspace, sized for the largest consumer
+  const int iC = static_cast<int>(C), iBT = static_cast<int>(BT), iVp = static_cast<int>(Vp);
+  size_t ws = 0;
+  for (int oc : {3 * iC, iC, 4 * iC}) ws = std::max(ws, llmk_matmul_backward_workspace(iBT, iC, oc, LLMK_MATH_BF16));
+  ws = std::max(ws, llmk_matmul_backward_workspace(iBT, 4 * iC, iC, LLMK_MATH_BF16));
+  ws = std::max(ws, llmk_gemm_workspace(iVp, iC, iBT, LLMK_MATH_BF16));
+  ws = std::max(ws, llmk_layernorm_backward_workspace(iBT, iC));
+  ws = std::max(ws, llmk_attention_backward_workspace(g->B, g->T, 3 * iC, static_cast<int>(NH)));
+  ws = std::max(ws, llmk_encoder_backward_workspace(g->B, g->T));
+  g->workspace_bytes = ws;
+  LLMK_CUDA(cudaMalloc(&g->workspace, std::max<size_t>(ws, 256)));
+  g->layer_done.resize(L);
+  for (auto& e : g->layer_done) LLMK_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+  LLMK_CUDA(cudaEventCreateWithFlags(&g->embed_done, cudaEventDisableTiming));
+  LLMK_CUDA(cudaEventCreateWithFlags(&g->comm_done, cudaEventDisableTiming));
+  return LLMK_OK;
+}
+
+llmk_epilogue epi(const float* bias = nullptr, const float* residual = nullptr, long long ldr = 0, void* aux = nullptr,
+                  long long ldaux = 0, int flags = 0) {
+  llmk_epilogue e{};
+  e.bias = bias;
+  e.residual = residual;
+  e.ldr = ldr;
+  e.aux = aux;
+  e.ldaux = ldaux;
+  e.flags = flags;
+  return e;
+}
+
+// Gradient all-reduce of one contiguous bucket on the comm stream, after `ev`.
+int allreduce_bucket(llmk_gpt2* g, cudaEvent_t ev, size_t begin, size_t end) {
+  if (g->world <= 1) return LLMK_OK;
+  LLMK_CUDA(cudaEventRecord(ev, g->stream));
+  LLMK_CUDA(cudaStreamWaitEvent(g->comm_stream, ev, 0));
+  return nccl_check(ncclAllReduce(g->grads + begin, g->grads + begin, end - begin, ncclFloat, ncclSum, g->comm,
+                                  g->comm_stream),
+                    "ncclAllReduce");
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t llmk_gpt2_num_parameters(const llmk_gpt2_config* cfg) {
+  if (!cfg) return 0;
+  size_t s[16];
+  llmk::tensor_sizes(*cfg, s);
+  size_t n = 0;
+  for (size_t x : s) n += x;
+  return n;
+}
+
+int llmk_gpt2_create(llmk_gpt2** out, const llmk_gpt2_config* cfg, int B, int T, void* stream) {
+  if (!out || !cfg || B <= 0 || T <= 0) return fail(LLMK_ERR_INVALID_ARG, "gpt2_create: bad arguments");
+  if (T > cfg->max_seq_len || cfg->channels % cfg->num_heads || cfg->channels / cfg->num_heads != 64 ||
+      cfg->padded_vocab_size < cfg->vocab_size || cfg->padded_vocab_size % 8 || cfg->channels % 64)
+    return fail(LLMK_ERR_UNSUPPORTED, "gpt2_create: needs head size 64, C % 64 == 0, Vp % 8 == 0, T <= maxT");
+  auto* g = new llmk_gpt2();
+  g->cfg = *cfg;
+  g->B = B;
+  g->T = T;
+  int rc = llmk::cuda_check(cudaGetDevice(&g->device), "cudaGetDevice");
+  if (rc == LLMK_OK) {
+    if (stream) {
+      g->stream = static_cast<cudaStream_t>(stream);
+    } else {
+      rc = llmk::cuda_check(cudaStreamCreateWithFlags(&g->stream, cudaStreamNonBlocking), "cudaStreamCreate");
+      g->own_stream = true;
+    }
+  }
+  if (rc == LLMK_OK)
+    rc = llmk::cuda_check(cudaStreamCreateWithFlags(&g->comm_stream, cudaStreamNonBlocking), "cudaStreamCreate");
+  if (rc == LLMK_OK) {
+    layout(g);
+    rc = alloc_all(g);
+  }
+  if (rc != LLMK_OK) {
+    free_all(g);
+    delete g;
+    return rc;
+  }
+  *out = g;
+  return LLMK_OK;
+}
+
+int llmk_gpt2_destroy(llmk_gpt2* g) {
+  if (!g) return LLMK_OK;
+  cudaSetDevice(g->device);
+  cudaStreamSynchronize(g->stream);
+  cudaStreamSynchronize(g->comm_stream);
+  free_all(g);
+  delete g;
+  return LLMK_OK;
+}
+
+size_t llmk_gpt2_parameter_count(const llmk_gpt2* g) { return g ? g->nparams : 0; }
+
+int llmk_gpt2_load_parameters(llmk_gpt2* g, const float* host_params, size_t n) {
+  if (!g || !host_params || n != g->nparams) return fail(LLMK_ERR_INVALID_ARG, "gpt2_load_parameters: size mismatch");
+  LLMK_TRY(ensure_device(g));
+  std::vector<float> tmp(n);
+  permute_params(g, host_params, tmp.data(), 0);
+  LLMK_CUDA(cudaMemcpy(g->params, tmp.data(), n * sizeof(float), cudaMemcpyHostToDevice));
+  LLMK_TRY(llmk_cast(g->params_bf16, LLMK_BF16, g->params, LLMK_F32, static_cast<long long>(n), g->stream));
+  LLMK_CUDA(cudaMemsetAsync(g->m, 0, n * sizeof(float), g->stream));
+  LLMK_CUDA(cudaMemsetAsync(g->v, 0, n * sizeof(float), g->stream));
+  LLMK_CUDA(cudaStreamSynchronize(g->stream));
+  return LLMK_OK;
+}
+
+static int read_flat(llmk_gpt2* g, const float* dev, float* host_out, size_t n) {
+  if (!g || !host_out || n != g->nparams) return fail(LLMK_ERR_INVALID_ARG, "gpt2_read: size mismatch");
+  LLMK_TRY(ensure_device(g));
+  std::vector<float> tmp(n);
+  LLMK_CUDA(cudaStreamSynchronize(g->stream));
+  LLMK_CUDA(cudaStreamSynchronize(g->comm_stream));
+  LLMK_CUDA(cudaMemcpy(tmp.data(), dev, n * sizeof(float), cudaMemcpyDeviceToHost));
+  permute_params(g, tmp.data(), host_out, 1);
+  return LLMK_OK;
+}
+
+int llmk_gpt2_read_parameters(llmk_gpt2* g, float* host_out, size_t n) { return read_flat(g, g ? g->params : nullptr, host_out, n); }
+int llmk_gpt2_read_gradients(llmk_gpt2* g, float* host_out, size_t n) { return read_flat(g, g ? g->grads : nullptr, host_out, n); }
+
+int llmk_gpt2_forward(llmk_gpt2* g, const int* d_inputs, const int* d_targets) {
+  if (!g || !d_inputs) return fail(LLMK_ERR_INVALID_ARG, "gpt2_forward: null argument");
+  const int B = g->B, T = g->T, C = g->cfg.channels, NH = g->cfg.num_heads, L = g->cfg.num_layers;
+  const int V = g->cfg.vocab_size, Vp = g->cfg.padded_vocab_size, BT = B * T;
+  cudaStream_t s = g->stream;
+  const float* P = g->params;
+  const __nv_bfloat16* Pb = g->params_bf16;
+  if (d_inputs != g->inputs) LLMK_CUDA(cudaMemcpyAsync(g->inputs, d_inputs, BT * sizeof(int), cudaMemcpyDeviceToDevice, s));
+  g->have_targets = d_targets != nullptr;
+  if (d_targets && d_targets != g->targets)
+    LLMK_CUDA(cudaMemcpyAsync(g->targets, d_targets, BT * sizeof(int), cudaMemcpyDeviceToDevice, s));
+  // encoder (gpt2cuda.cu:313)
+  LLMK_TRY(llmk_encoder_forward(g->encoded, g->inputs, P + g->off_wte, P + g->off_wpe, B, T, C, s));
+  const float* x = g->encoded;
+  for (int l = 0; l < L; ++l) {
+    // Layer::Forward (gpt2/cuda/layer.cu:151-177)
+    const LayerParams& p = g->lp[l];
+    LayerActs& a = g->acts[l];
+    LLMK_TRY(llmk_layernorm_forward(a.ln1, LLMK_BF16, a.ln1_mean, a.ln1_rstd, x, P + p.ln1w, P + p.ln1b, BT, C, s));
+    llmk_epilogue e1 = epi(P + p.qkvb);
+    LLMK_TRY(llmk_gemm(a.qkv, LLMK_BF16, 3 * C, a.ln1, 0, C, Pb + p.qkvw, 0, C, LLMK_MATH_BF16, BT, 3 * C, C, &e1,
+                       nullptr, 0, s));
+    LLMK_TRY(llmk_attention_forward(a.atty, a.lse, a.qkv, B, T, 3 * C, NH, s));
+    llmk_epilogue e2 = epi(P + p.attprojb, x, C);  // residual add fused
+    LLMK_TRY(llmk_gemm(a.res2, LLMK_F32, C, a.atty, 0, C, Pb + p.attprojw, 0, C, LLMK_MATH_BF16, BT, C, C, &e2,
+                       nullptr, 0, s));
+    LLMK_TRY(llmk_layernorm_forward(a.ln2, LLMK_BF16, a.ln2_mean, a.ln2_rstd, a.res2, P + p.ln2w, P + p.ln2b, BT, C, s));
+    llmk_epilogue e3 = epi(P + p.fcb, nullptr, 0, a.fch_pre, 4 * C, LLMK_EPI_GELU);  // GELU fused, pre-activation kept
+    LLMK_TRY(llmk_gemm(a.fch_gelu, LLMK_BF16, 4 * C, a.ln2, 0, C, Pb + p.fcw, 0, C, LLMK_MATH_BF16, BT, 4 * C, C, &e3,
+                       nullptr, 0, s));
+    llmk_epilogue e4 = epi(P + p.fcprojb, a.res2, C);
+    LLMK_TRY(llmk_gemm(a.res3, LLMK_F32, C, a.fch_gelu, 0, 4 * C, Pb + p.fcprojw, 0, 4 * C, LLMK_MATH_BF16, BT, C,
+                       4 * C, &e4, nullptr, 0, s));
+    x = a.res3;
+  }
+  LLMK_TRY(llmk_layernorm_forward(g->lnf, LLMK_BF16, g->lnf_mean, g->lnf_rstd, x, P + g->off_lnfw, P + g->off_lnfb, BT,
+                                  C, s));
+  // tied lm_head (gpt2cuda.cu:323): logits[BT, Vp] = lnf * wte^T, no bias
+  LLMK_TRY(llmk_gemm(g->logits, LLMK_BF16, Vp, g->lnf, 0, C, Pb + g->off_wte, 0, C, LLMK_MATH_BF16, BT, Vp, C, nullptr,
+                     nullptr, 0, s));
+  if (g->have_targets) {
+    // softmax + cross-entropy + its backward in one pass; dlogits overwrite the
+    // logits in place with scale 1/(B*T) (gpt2cuda.cu:398)
+    LLMK_TRY(llmk_softmax_crossentropy(g->losses, g->logits, g->logits, LLMK_BF16, g->targets, BT, V, Vp,
+                                       1.0f / static_cast<float>(BT), s));
+    LLMK_TRY(llmk_mean(g->loss, g->losses, BT, s));
+  }
+  return LLMK_OK;
+}
+
+int llmk_gpt2_zero_grad(llmk_gpt2* g) {
+  // Every gradient is overwritten by its producer in llmk_gpt2_backward except
+  // dwpe (accumulated by the encoder backward); the reference memsets all of
+  // them (gpt2cuda.cu:514-565).
+  if (!g) return fail(LLMK_ERR_INVALID_ARG, "gpt2_zero_grad");
+  LLMK_CUDA(cudaMemsetAsync(g->grads + g->off_wpe, 0, g->tsize[llmk::WPE] * sizeof(float), g->stream));
+  return LLMK_OK;
+}
+
+int llmk_gpt2_backward(llmk_gpt2* g) {
+  if (!g || !g->have_targets) return fail(LLMK_ERR_INVALID_ARG, "gpt2_backward: forward with targets first");
+  const int B = g->B, T = g->T, C = g->cfg.channels, NH = g->cfg.num_heads, L = g->cfg.num_layers;
+  const int Vp = g->cfg.padded_vocab_size, BT = B * T;
+  cudaStream_t s = g->stream;
+  const float* P = g->params;
+  const __nv_bfloat16* Pb = g->params_bf16;
+  float* G = g->grads;
+  void* ws = g->workspace;
+  const size_t wsb = g->workspace_bytes;
+  LLMK_TRY(llmk_gpt2_zero_grad(g));
+  // lm_head backward (gpt2cuda.cu:402): dlnf = dlogits * wte; dwte = dlogits^T * lnf
+  LLMK_TRY(llmk_gemm(g->dln, LLMK_F32, C, g->logits, 0, Vp, Pb + g->off_wte, 1, C, LLMK_MATH_BF16, BT, C, Vp, nullptr,
+                     nullptr, 0, s));
+  LLMK_TRY(llmk_gemm(G + g->off_wte, LLMK_F32, C, g->logits, 1, Vp, g->lnf, 1, C, LLMK_MATH_BF16, Vp, C, BT, nullptr,
+                     ws, wsb, s));
+  const float* xL = L > 0 ? g->acts[L - 1].res3 : g->encoded;
+  LLMK_TRY(llmk_layernorm_backward(g->dres, g->dres_bf16, G + g->off_lnfw, G + g->off_lnfb, g->dln, LLMK_F32, xL,
+                                   P + g->off_lnfw, g->lnf_mean, g->lnf_rstd, BT, C, 0, ws, wsb, s));
+  for (int l = L - 1; l >= 0; --l) {
+    // Layer::Backward (gpt2/cuda/layer.cu:180-266); dres = d(layer output)
+    const LayerParams& p = g->lp[l];
+    LayerActs& a = g->acts[l];
+    const float* x = l > 0 ? g->acts[l - 1].res3 : g->encoded;
+    // fcproj: dW = dres^T fch_gelu, db = colsum(dres), dfch = (dres Wfcproj) * gelu'(fch_pre)
+    LLMK_TRY(llmk_gemm(G + p.fcprojw, LLMK_F32, 4 * C, g->dres_bf16, 1, C, a.fch_gelu, 1, 4 * C, LLMK_MATH_BF16, C,
+                       4 * C, BT, nullptr, ws, wsb, s));
+    LLMK_TRY(llmk_colsum(G + p.fcprojb, g->dres, LLMK_F32, BT, C, 0, ws, wsb, s));
+    llmk_epilogue eg = epi(nullptr, nullptr, 0, a.fch_pre, 4 * C, LLMK_EPI_GELU_BWD);
+    LLMK_TRY(llmk_gemm(g->dfch, LLMK_BF16, 4 * C, g->dres_bf16, 0, C, Pb + p.fcprojw, 1, 4 * C, LLMK_MATH_BF16, BT,
+                       4 * C, C, &eg, nullptr, 0, s));
+    // fc: dW = dfch^T ln2, db = colsum(dfch), dln2 = dfch Wfc
+    LLMK_TRY(llmk_gemm(G + p.fcw, LLMK_F32, C, g->dfch, 1, 4 * C, a.ln2, 1, C, LLMK_MATH_BF16, 4 * C, C, BT, nullptr,
+                       ws, wsb, s));
+    LLMK_TRY(llmk_colsum(G + p.fcb, g->dfch, LLMK_BF16, BT, 4 * C, 0, ws, wsb, s));
+    LLMK_TRY(llmk_gemm(g->dln, LLMK_F32, C, g->dfch, 0, 4 * C, Pb + p.fcw, 1, C, LLMK_MATH_BF16, BT, C, 4 * C, nullptr,
+                       nullptr, 0, s));
+    // ln2: dres += LN2 backward (dres becomes d(res2))
+    LLMK_TRY(llmk_layernorm_backward(g->dres, g->dres_bf16, G + p.ln2w, G + p.ln2b, g->dln, LLMK_F32, a.res2,
+                                     P + p.ln2w, a.ln2_mean, a.ln2_rstd, BT, C, LLMK_ACCUM_DINP, ws, wsb, s));
+    // attproj: dW = dres^T atty, db = colsum(dres), datty = dres Wproj
+    LLMK_TRY(llmk_gemm(G + p.attprojw, LLMK_F32, C, g->dres_bf16, 1, C, a.atty, 1, C, LLMK_MATH_BF16, C, C, BT, nullptr,
+                       ws, wsb, s));
+    LLMK_TRY(llmk_colsum(G + p.attprojb, g->dres, LLMK_F32, BT, C, 0, ws, wsb, s));
+    LLMK_TRY(llmk_gemm(g->datty, LLMK_BF16, C, g->dres_bf16, 0, C, Pb + p.attprojw, 1, C, LLMK_MATH_BF16, BT, C, C,
+                       nullptr, nullptr, 0, s));
+    // attention
+    LLMK_TRY(llmk_attention_backward(g->dqkv, g->datty, a.atty, a.qkv, a.lse, B, T, 3 * C, NH, ws, wsb, s));
+    // qkv: dW = dqkv^T ln1, db = colsum(dqkv), dln1 = dqkv Wqkv
+    LLMK_TRY(llmk_gemm(G + p.qkvw, LLMK_F32, C, g->dqkv, 1, 3 * C, a.ln1, 1, C, LLMK_MATH_BF16, 3 * C, C, BT, nullptr,
+                       ws, wsb, s));
+    LLMK_TRY(llmk_colsum(G + p.qkvb, g->dqkv, LLMK_BF16, BT, 3 * C, 0, ws, wsb, s));
+    LLMK_TRY(llmk_gemm(g->dln, LLMK_F32, C, g->dqkv, 0, 3 * C, Pb + p.qkvw, 1, C, LLMK_MATH_BF16, BT, C, 3 * C, nullptr,
+                       nullptr, 0, s));
+    // ln1: dres += LN1 backward (dres becomes d(layer input))
+    LLMK_TRY(llmk_layernorm_backward(g->dres, g->dres_bf16, G + p.ln1w, G + p.ln1b, g->dln, LLMK_F32, x, P + p.ln1w,
+                                     a.ln1_mean, a.ln1_rstd, BT, C, LLMK_ACCUM_DINP, ws, wsb, s));
+    // this layer's gradients are final: reduce them while the layers below run
+    LLMK_TRY(allreduce_bucket(g, g->layer_done[l], p.begin, p.end));
+  }
+  // encoder backward (gpt2cuda.cu:413): dwte += scatter, dwpe += sum over batch
+  LLMK_TRY(llmk_encoder_backward(G + g->off_wte, G + g->off_wpe, g->dres, g->inputs, B, T, C, ws, wsb, s));
+  // wte/wpe bucket, then lnf bucket
+  LLMK_TRY(allreduce_bucket(g, g->embed_done, g->off_wte, g->off_wpe + g->tsize[llmk::WPE]));
+  if (g->world > 1) {
+    LLMK_TRY(nccl_check(ncclAllReduce(G + g->off_lnfw, G + g->off_lnfw, 2 * C, ncclFloat, ncclSum, g->comm,
+                                      g->comm_stream),
+                        "ncclAllReduce"));
+    LLMK_CUDA(cudaEventRecord(g->comm_done, g->comm_stream));
+    LLMK_CUDA(cudaStreamWaitEvent(s, g->comm_done, 0));
+  }
+  return LLMK_OK;
+}
+
+int llmk_gpt2_update(llmk_gpt2* g, float lr, float beta1, float beta2, float eps, float weight_decay, int t) {
+  if (!g || t < 1) return fail(LLMK_ERR_INVALID_ARG, "gpt2_update");
+  // one multi-tensor launch over the flat buffer (the reference launches one
+  // AdamW per tensor, gpt2cuda.cu:434-441); gradients are averaged over ranks
+  const float scale = 1.0f / static_cast<float>(g->world);
+  LLMK_TRY(llmk_adamw(g->params, g->params_bf16, g->grads, g->m, g->v, static_cast<long long>(g->nparams), lr, beta1,
+                      beta2, eps, weight_decay, t, scale, g->stream));
+  ++g->steps;
+  return LLMK_OK;
+}
+
+int llmk_gpt2_set_train_data(llmk_gpt2* g, const int* host_inputs, const int* host_targets) {
+  if (!g || !host_inputs) return fail(LLMK_ERR_INVALID_ARG, "gpt2_set_train_data");
+  const size_t BT = static_cast<size_t>(g->B) * g->T;
+  std::memcpy(g->h_inputs, host_inputs, BT * sizeof(int));
+  LLMK_CUDA(cudaMemcpyAsync(g->inputs, g->h_inputs, BT * sizeof(int), cudaMemcpyHostToDevice, g->stream));
+  if (host_targets) {
+    std::memcpy(g->h_targets, host_targets, BT * sizeof(int));
+    LLMK_CUDA(cudaMemcpyAsync(g->targets, g->h_targets, BT * sizeof(int), cudaMemcpyHostToDevice, g->stream));
+  }
+  return LLMK_OK;
+}
+
+int llmk_gpt2_loss(llmk_gpt2* g, float* host_loss) {
+  if (!g || !host_loss) return fail(LLMK_ERR_INVALID_ARG, "gpt2_loss");
+  LLMK_CUDA(cudaMemcpyAsync(g->h_loss, g->loss, sizeof(float), cudaMemcpyDeviceToHost, g->stream));
+  LLMK_CUDA(cudaStreamSynchronize(g->stream));
+  *host_loss = *g->h_loss;
+  return LLMK_OK;
+}
+
+int llmk_gpt2_device_loss(llmk_gpt2* g, const float** d_loss) {
+  if (!g || !d_loss) return fail(LLMK_ERR_INVALID_ARG, "gpt2_device_loss");
+  *d_loss = g->loss;
+  return LLMK_OK;
+}
+
+int llmk_gpt2_step_device(llmk_gpt2* g, const int* d_inputs, const int* d_targets, float lr, float beta1, float beta2,
+                          float eps, float weight_decay, int t) {
+  LLMK_TRY(llmk_gpt2_forward(g, d_inputs, d_targets));
+  LLMK_TRY(llmk_gpt2_backward(g));
+  return llmk_gpt2_update(g, lr, beta1, beta2, eps, weight_decay, t);
+}
+
+int llmk_gpt2_train_step(llmk_gpt2* g, const int* host_inputs, const int* host_targets, float lr, float beta1,
+                         float beta2, float eps, float weight_decay, int t, float* host_loss) {
+  if (!g || !host_inputs || !host_targets) return fail(LLMK_ERR_INVALID_ARG, "gpt2_train_step");
+  LLMK_TRY(ensure_device(g));
+  LLMK_TRY(llmk_gpt2_set_train_data(g, host_inputs, host_targets));
+  LLMK_TRY(llmk_gpt2_step_device(g, g->inputs, g->targets, lr, beta1, beta2, eps, weight_decay, t));
+  if (host_loss) return llmk_gpt2_loss(g, host_loss);
+  return LLMK_OK;
+}
+
+int llmk_gpt2_stream(llmk_gpt2* g, void** stream) {
+  if (!g || !stream) return fail(LLMK_ERR_INVALID_ARG, "gpt2_stream");
+  *stream = g->stream;
+  return LLMK_OK;
+}
+
+int llmk_gpt2_buffers(llmk_gpt2* g, int** d_inputs, int** d_targets) {
+  if (!g) return fail(LLMK_ERR_INVALID_ARG, "gpt2_buffers");
+  if (d_inputs) *d_inputs = g->inputs;
+  if (d_targets) *d_targets = g->targets;
+  return LLMK_OK;
+}
+
+/* ----------------------------------------------------- data parallelism */
+// Host-only planning helpers (no device needed): the gradient buckets in the
+// order llmk_gpt2_backward all-reduces them, and the llm.c <-> layer-major
+// parameter permutation.
+int llmk_gpt2_dp_buckets(const llmk_gpt2_config* cfg, size_t* ranges, int max_buckets) {
+  if (!cfg || cfg->num_layers < 0) return -1;
+  llmk_gpt2 tmp;
+  tmp.cfg = *cfg;
+  layout(&tmp);
+  const int L = cfg->num_layers;
+  const int n = L + 2;
+  if (ranges && max_buckets >= n) {
+    int k = 0;
+    for (int l = L - 1; l >= 0; --l, ++k) {
+      ranges[2 * k] = tmp.lp[l].begin;
+      ranges[2 * k + 1] = tmp.lp[l].end;
+    }
+    ranges[2 * k] = tmp.off_wte;
+    ranges[2 * k + 1] = tmp.off_wpe + tmp.tsize[llmk::WPE];
+    ++k;
+    ranges[2 * k] = tmp.off_lnfw;
+    ranges[2 * k + 1] = tmp.off_lnfw + 2 * static_cast<size_t>(cfg->channels);
+  }
+  return n;
+}
+
+int llmk_gpt2_to_layer_major(const llmk_gpt2_config* cfg, const float* src, float* dst, int reverse) {
+  if (!cfg || !src || !dst) return fail(LLMK_ERR_INVALID_ARG, "gpt2_to_layer_major");
+  llmk_gpt2 tmp;
+  tmp.cfg = *cfg;
+  layout(&tmp);
+  permute_params(&tmp, src, dst, reverse ? 1 : 0);
+  return LLMK_OK;
+}
+
+int llmk_nccl_unique_id(void* out, size_t bytes) {
+  if (!out || bytes < sizeof(ncclUniqueId)) return fail(LLMK_ERR_INVALID_ARG, "nccl_unique_id: need 128 bytes");
+  ncclUniqueId id;
+  LLMK_TRY(nccl_check(ncclGetUniqueId(&id), "ncclGetUniqueId"));
+  std::memcpy(out, &id, sizeof(id));
+  return LLMK_OK;
+}
+
+int llmk_gpt2_enable_dp(llmk_gpt2* g, const void* unique_id, size_t bytes, int rank, int world) {
+  if (!g || !unique_id || bytes < sizeof(ncclUniqueId) || world < 1 || rank < 0 || rank >= world)
+    return fail(LLMK_ERR_INVALID_ARG, "gpt2_enable_dp: bad arguments");
+  LLMK_TRY(ensure_device(g));
+  if (world == 1) return LLMK_OK;
+  ncclUniqueId id;
+  std::memcpy(&id, unique_id, sizeof(id));
+  LLMK_TRY(nccl_check(ncclCommInitRank(&g->comm, world, id, rank), "ncclCommInitRank"));
+  g->rank = rank;
+  g->world = world;
+  return LLMK_OK;
+}
+
+int llmk_gpt2_broadcast_parameters(llmk_gpt2* g, int root) {
+  if (!g) return fail(LLMK_ERR_INVALID_ARG, "gpt2_broadcast_parameters");
+  if (g->world <= 1) return LLMK_OK;
+  LLMK_TRY(nccl_check(ncclBroadcast(g->params, g->params, g->nparams, ncclFloat, root, g->comm, g->stream),
+                      "ncclBroadcast"));
+  LLMK_TRY(llmk_cast(g->params_bf16, LLMK_BF16, g->params, LLMK_F32, static_cast<long long>(g->nparams), g->stream));
+  LLMK_CUDA(cudaStreamSynchronize(g->stream));
+  return LLMK_OK;
+}
+
+// Waits (host side, bounded) for the step's device work and checks the NCCL
+// communicator for asynchronous errors; aborts the communicator on error or
+// timeout so the other ranks' pending collectives fail instead of hanging.
+int llmk_gpt2_synchronize(llmk_gpt2* g, int timeout_ms) {
+  if (!g) return fail(LLMK_ERR_INVALID_ARG, "gpt2_synchronize");
+  LLMK_TRY(ensure_device(g));
+  cudaEvent_t ev;
+  LLMK_CUDA(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+  cudaEventRecord(ev, g->stream);
+  const auto t0 = std::chrono::steady_clock::now();
+  int rc = LLMK_OK;
+  while (true) {
+    cudaError_t q = cudaEventQuery(ev);
+    if (q == cudaSuccess) break;
+    if (q != cudaErrorNotReady) {
+      rc = llmk::cuda_check(q, "step");
+      break;
+    }
+    if (g->comm) {
+      ncclResult_t ar = ncclSuccess;
+      ncclCommGetAsyncError(g->comm, &ar);
+      if (ar != ncclSuccess && ar != ncclInProgress) {
+        ncclCommAbort(g->comm);
+        g->comm = nullptr;
+        rc = fail(LLMK_ERR_NCCL, std::string("nccl async error: ") + ncclGetErrorString(ar));
+        break;
+      }
+    }
+    const auto ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+    if (timeout_ms > 0 && ms > timeout_ms) {
+      if (g->comm) {
+        ncclCommAbort(g->comm);
+        g->comm = nullptr;
+      }
+      rc = fail(LLMK_ERR_DEVICE_TIMEOUT, "gpt2_synchronize: step did not finish in time");
+      break;
+    }
+  }
+  cudaEventDestroy(ev);
+  return rc;
+}
+
+}  // extern "C"

@@ -57,15 +57,17 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
 
 // Bounded wait for completion of the phase with the given parity. `abort` is a
 // CTA-shared flag: once any role of the CTA gave up, the others stop waiting.
+// `site` (0..23) names the wait in the status word (bit 8 + site) so a timeout
+// report says which barrier never completed.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int* status,
-                                          volatile int* abort_flag) {
+                                          volatile int* abort_flag, int site = 0) {
   if (mbar_test(bar, parity)) return true;
   unsigned long long t0 = global_timer_ns();
   while (true) {
     if (mbar_test(bar, parity)) return true;
     if (abort_flag != nullptr && *abort_flag) return false;
     if (global_timer_ns() - t0 > kWaitLimitNs) {
-      if (status) atomicOr(status, LLMK_DEV_TIMEOUT);
+      if (status) atomicOr(status, LLMK_DEV_TIMEOUT | (1u << (8 + (site & 23))));
       if (abort_flag) *abort_flag = 1;
       return false;
     }
@@ -91,6 +93,26 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
       : "memory");
 }
+
+// TMA stores (shared -> global), tracked per issuing thread by bulk groups.
+// Rows / columns outside the tensor map's extent are not written.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(src)), "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* src, int x, int y, int z) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Waits until the source smem of every committed bulk store was read.
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// Waits until every committed bulk store completed.
+__device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 // ---------------------------------------------------------------- tcgen05
 __device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {

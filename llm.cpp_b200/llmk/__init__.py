@@ -17,7 +17,7 @@ LIB_PATH = os.path.join(os.path.dirname(_HERE), "libllmk.so")
 F32, BF16 = 0, 1
 MATH_BF16, MATH_TF32 = 1, 2
 EPI_ACCUMULATE, EPI_GELU, EPI_GELU_BWD = 1, 2, 4
-ACCUM_DINP, ACCUM_DWEIGHT, ACCUM_DBIAS = 1, 2, 4
+ACCUM_DINP, ACCUM_DWEIGHT, ACCUM_DBIAS, ACCUM_DPARAM = 1, 2, 4, 8
 DEV_TIMEOUT = 1
 
 STATUS = {0: "ok", 1: "invalid argument", 2: "unsupported", 3: "cuda error", 4: "device wait timed out",
@@ -57,6 +57,48 @@ SIGNATURES: dict[str, tuple] = {
     "llmk_matmul_backward": (i32, [vp, i32, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, vp, sz, vp]),
     "llmk_colsum_workspace": (sz, [i32, i32]),
     "llmk_colsum": (i32, [vp, vp, i32, i32, i32, i32, vp, sz, vp]),
+    "llmk_attention_forward": (i32, [vp, vp, vp, i32, i32, i32, i32, vp]),
+    "llmk_attention_backward_workspace": (sz, [i32, i32, i32, i32]),
+    "llmk_attention_backward": (i32, [vp, vp, vp, vp, vp, i32, i32, i32, i32, vp, sz, vp]),
+    "llmk_layernorm_forward": (i32, [vp, i32, vp, vp, vp, vp, vp, i32, i32, vp]),
+    "llmk_layernorm_backward_workspace": (sz, [i32, i32]),
+    "llmk_layernorm_backward": (i32, [vp, vp, vp, vp, vp, i32, vp, vp, vp, vp, i32, i32, i32, vp, sz, vp]),
+    "llmk_gelu_forward": (i32, [vp, vp, i32, i64, vp]),
+    "llmk_gelu_backward": (i32, [vp, vp, vp, i32, i64, i32, vp]),
+    "llmk_residual_forward": (i32, [vp, vp, vp, i32, i64, vp]),
+    "llmk_residual_backward": (i32, [vp, vp, vp, i32, i64, i32, vp]),
+    "llmk_cast": (i32, [vp, i32, vp, i32, i64, vp]),
+    "llmk_encoder_forward": (i32, [vp, vp, vp, vp, i32, i32, i32, vp]),
+    "llmk_encoder_backward_workspace": (sz, [i32, i32]),
+    "llmk_encoder_backward": (i32, [vp, vp, vp, vp, i32, i32, i32, vp, sz, vp]),
+    "llmk_softmax_crossentropy": (i32, [vp, vp, vp, i32, vp, i32, i32, i32, f32, vp]),
+    "llmk_mean": (i32, [vp, vp, i32, vp]),
+    "llmk_adamw": (i32, [vp, vp, vp, vp, vp, i64, f32, f32, f32, f32, f32, i32, f32, vp]),
+    # model (include/llmk_gpt2.h)
+    "llmk_gpt2_num_parameters": (sz, [C.POINTER(GPT2Config)]),
+    "llmk_gpt2_parameter_count": (sz, [vp]),
+    "llmk_gpt2_create": (i32, [C.POINTER(vp), C.POINTER(GPT2Config), i32, i32, vp]),
+    "llmk_gpt2_destroy": (i32, [vp]),
+    "llmk_gpt2_stream": (i32, [vp, C.POINTER(vp)]),
+    "llmk_gpt2_buffers": (i32, [vp, C.POINTER(vp), C.POINTER(vp)]),
+    "llmk_gpt2_load_parameters": (i32, [vp, vp, sz]),
+    "llmk_gpt2_read_parameters": (i32, [vp, vp, sz]),
+    "llmk_gpt2_read_gradients": (i32, [vp, vp, sz]),
+    "llmk_gpt2_set_train_data": (i32, [vp, vp, vp]),
+    "llmk_gpt2_forward": (i32, [vp, vp, vp]),
+    "llmk_gpt2_zero_grad": (i32, [vp]),
+    "llmk_gpt2_backward": (i32, [vp]),
+    "llmk_gpt2_update": (i32, [vp, f32, f32, f32, f32, f32, i32]),
+    "llmk_gpt2_loss": (i32, [vp, C.POINTER(f32)]),
+    "llmk_gpt2_device_loss": (i32, [vp, C.POINTER(vp)]),
+    "llmk_gpt2_step_device": (i32, [vp, vp, vp, f32, f32, f32, f32, f32, i32]),
+    "llmk_gpt2_train_step": (i32, [vp, vp, vp, f32, f32, f32, f32, f32, i32, C.POINTER(f32)]),
+    "llmk_gpt2_dp_buckets": (i32, [C.POINTER(GPT2Config), C.POINTER(sz), i32]),
+    "llmk_gpt2_to_layer_major": (i32, [C.POINTER(GPT2Config), vp, vp, i32]),
+    "llmk_nccl_unique_id": (i32, [vp, sz]),
+    "llmk_gpt2_enable_dp": (i32, [vp, vp, sz, i32, i32]),
+    "llmk_gpt2_broadcast_parameters": (i32, [vp, i32]),
+    "llmk_gpt2_synchronize": (i32, [vp, i32]),
 }
 
 _lib = None
@@ -131,3 +173,99 @@ def gemm(D, A, B, *, a_trans=False, b_trans=False, math=MATH_BF16, bias=None, re
     ws_bytes = workspace.numel() * workspace.element_size() if workspace is not None else 0
     call("llmk_gemm", ptr(D), dtype_code(D), D.stride(0), ptr(A), int(a_trans), A.stride(0), ptr(B), int(b_trans),
          B.stride(0), math, M, N, K, C.byref(ep), ptr(workspace), ws_bytes, stream_ptr(stream))
+
+
+class GPT2:
+    """Handle to the native trainer (include/llmk_gpt2.h)."""
+
+    def __init__(self, B: int, T: int, max_seq_len=1024, vocab_size=50257, padded_vocab_size=50304, num_layers=12,
+                 num_heads=12, channels=768, stream=None):
+        self.cfg = GPT2Config(max_seq_len, vocab_size, padded_vocab_size, num_layers, num_heads, channels)
+        self.B, self.T = B, T
+        h = C.c_void_p()
+        call("llmk_gpt2_create", C.byref(h), C.byref(self.cfg), B, T, stream)
+        self.h = h
+        self.n = lib().llmk_gpt2_parameter_count(self.h)
+
+    @property
+    def stream(self) -> int:
+        s = C.c_void_p()
+        call("llmk_gpt2_stream", self.h, C.byref(s))
+        return s.value
+
+    def buffers(self) -> tuple[int, int]:
+        a, b = C.c_void_p(), C.c_void_p()
+        call("llmk_gpt2_buffers", self.h, C.byref(a), C.byref(b))
+        return a.value, b.value
+
+    def load_parameters(self, params) -> None:
+        import numpy as np
+        p = np.ascontiguousarray(params, dtype=np.float32)
+        assert p.size == self.n, (p.size, self.n)
+        call("llmk_gpt2_load_parameters", self.h, p.ctypes.data, p.size)
+
+    def read_parameters(self):
+        import numpy as np
+        out = np.empty(self.n, np.float32)
+        call("llmk_gpt2_read_parameters", self.h, out.ctypes.data, self.n)
+        return out
+
+    def read_gradients(self):
+        import numpy as np
+        out = np.empty(self.n, np.float32)
+        call("llmk_gpt2_read_gradients", self.h, out.ctypes.data, self.n)
+        return out
+
+    def train_step(self, inputs, targets, lr, t, b1=0.9, b2=0.999, eps=1e-8, wd=0.0, want_loss=True):
+        """Host tokens in, host loss out (None when want_loss is False)."""
+        import numpy as np
+        i = np.ascontiguousarray(inputs, dtype=np.int32)
+        g = np.ascontiguousarray(targets, dtype=np.int32)
+        loss = C.c_float(0.0)
+        call("llmk_gpt2_train_step", self.h, i.ctypes.data, g.ctypes.data, lr, b1, b2, eps, wd, t,
+             C.byref(loss) if want_loss else None)
+        return loss.value if want_loss else None
+
+    def step_device(self, d_inputs: int, d_targets: int, lr, t, b1=0.9, b2=0.999, eps=1e-8, wd=0.0):
+        call("llmk_gpt2_step_device", self.h, d_inputs, d_targets, lr, b1, b2, eps, wd, t)
+
+    def forward(self, d_inputs: int, d_targets: int | None):
+        call("llmk_gpt2_forward", self.h, d_inputs, d_targets)
+
+    def backward(self):
+        call("llmk_gpt2_backward", self.h)
+
+    def update(self, lr, t, b1=0.9, b2=0.999, eps=1e-8, wd=0.0):
+        call("llmk_gpt2_update", self.h, lr, b1, b2, eps, wd, t)
+
+    def loss(self) -> float:
+        v = C.c_float(0.0)
+        call("llmk_gpt2_loss", self.h, C.byref(v))
+        return v.value
+
+    def enable_dp(self, unique_id: bytes, rank: int, world: int):
+        buf = C.create_string_buffer(bytes(unique_id), len(unique_id))
+        call("llmk_gpt2_enable_dp", self.h, C.cast(buf, C.c_void_p), len(unique_id), rank, world)
+
+    def broadcast_parameters(self, root=0):
+        call("llmk_gpt2_broadcast_parameters", self.h, root)
+
+    def synchronize(self, timeout_ms=0):
+        call("llmk_gpt2_synchronize", self.h, timeout_ms)
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().llmk_gpt2_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def nccl_unique_id() -> bytes:
+    buf = C.create_string_buffer(128)
+    call("llmk_nccl_unique_id", C.cast(buf, C.c_void_p), 128)
+    return buf.raw

@@ -42,17 +42,24 @@ def cuda_dev(llmk_lib):
     return torch.device("cuda:0")
 
 
+def _as_double(x):
+    import numpy as np
+    import torch
+    if isinstance(x, np.ndarray):
+        return torch.from_numpy(np.ascontiguousarray(x)).double()
+    return x.detach().double().cpu()
+
+
 def max_rel_err(x, y) -> float:
     """max_i |x_i - y_i| / max_j |y_j| (the parity metric of the hot path)."""
-    import torch
-    x = x.double()
-    y = y.double()
+    x = _as_double(x)
+    y = _as_double(y)
     den = y.abs().max().item()
     return (x - y).abs().max().item() / max(den, 1e-30)
 
 
 def norm_rel_err(x, y) -> float:
     """||x - y||_2 / ||y||_2 (the reference tests' Eigen isApprox metric)."""
-    x = x.double()
-    y = y.double()
+    x = _as_double(x)
+    y = _as_double(y)
     return ((x - y).norm() / max(y.norm().item(), 1e-30)).item()

@@ -1,0 +1,95 @@
+"""tcgen05 causal flash attention vs the oracle (reference CPU algorithm).
+
+Inputs are seeded N(0,1) from the oracle's generator, rounded to bf16 for
+the device; the oracle consumes the same rounded values in fp32. Tolerance:
+max relative error 1e-2 (the BF16 bar of the hot path) on O, LSE, dQ, dK, dV.
+"""
+import numpy as np
+import pytest
+
+import oracle as O
+from conftest import max_rel_err
+
+pytestmark = pytest.mark.gpu
+
+
+def _bf16_round(x):
+    import torch
+    return torch.from_numpy(x).bfloat16().float().numpy()
+
+
+def _run_gpu(qkv_np, dout_np, B, T, C, NH, dev):
+    import torch
+    import llmk
+    qkv = torch.from_numpy(qkv_np).to(dev).bfloat16().contiguous()
+    dout = torch.from_numpy(dout_np).to(dev).bfloat16().contiguous()
+    out = torch.full((B, T, C), float("nan"), device=dev, dtype=torch.bfloat16)
+    lse = torch.full((B, NH, T), float("nan"), device=dev)
+    s = llmk.stream_ptr()
+    llmk.call("llmk_attention_forward", out.data_ptr(), lse.data_ptr(), qkv.data_ptr(), B, T, 3 * C, NH, s)
+    ws_b = llmk.lib().llmk_attention_backward_workspace(B, T, 3 * C, NH)
+    ws = torch.empty(ws_b // 4 + 64, device=dev)
+    dqkv = torch.full((B, T, 3 * C), float("nan"), device=dev, dtype=torch.bfloat16)
+    llmk.call("llmk_attention_backward", dqkv.data_ptr(), dout.data_ptr(), out.data_ptr(), qkv.data_ptr(),
+              lse.data_ptr(), B, T, 3 * C, NH, ws.data_ptr(), ws_b, s)
+    torch.cuda.synchronize()
+    assert llmk.device_status() == 0
+    return out.float().cpu().numpy(), lse.cpu().numpy(), dqkv.float().cpu().numpy()
+
+
+@pytest.mark.parametrize("B,T,NH", [(1, 128, 1), (2, 256, 2), (1, 200, 3), (2, 64, 2), (1, 384, 2), (1, 1, 1)])
+def test_attention_vs_oracle(cuda_dev, B, T, NH):
+    C = 64 * NH
+    qkv = _bf16_round(O.normal((B, T, 3 * C), 100 + T))
+    dout = _bf16_round(O.normal((B, T, C), 200 + T))
+    out_g, lse_g, dqkv_g = _run_gpu(qkv, dout, B, T, C, NH, cuda_dev)
+    out_o = np.zeros((B, T, C), np.float32)
+    att = np.zeros((B, NH, T, T), np.float32)
+    lse_o = np.zeros((B, NH, T), np.float32)
+    O.orc().orc_attention_forward(out_o, att, lse_o.ctypes.data, O.f32a(qkv), B, T, C, NH)
+    dqkv_o = np.zeros((B, T, 3 * C), np.float32)
+    # the backward's dO.O uses the device's bf16 O, as the kernel does
+    O.orc().orc_attention_backward(dqkv_o, O.f32a(dout), O.f32a(qkv), att, B, T, C, NH)
+    assert max_rel_err(out_g, out_o) < 1e-2, max_rel_err(out_g, out_o)
+    assert max_rel_err(lse_g, lse_o) < 1e-2
+    for name, sl in (("dq", slice(0, C)), ("dk", slice(C, 2 * C)), ("dv", slice(2 * C, 3 * C))):
+        e = max_rel_err(dqkv_g[..., sl], dqkv_o[..., sl])
+        assert e < 1e-2, f"{name} max_rel={e:.3e}"
+
+
+def test_attention_config2_vs_torch(cuda_dev):
+    """Config 2 shape (B=8, NH=12, T=1024, hd=64) against an fp32 PyTorch reference on the GPU."""
+    import torch
+    B, NH, T, C = 8, 12, 1024, 768
+    qkv_np = O.normal((B, T, 3 * C), 7)
+    dout_np = O.normal((B, T, C), 8)
+    out_g, lse_g, dqkv_g = _run_gpu(qkv_np, dout_np, B, T, C, NH, cuda_dev)
+    qkv = torch.from_numpy(qkv_np).to(cuda_dev).bfloat16().float().requires_grad_(True)
+    q, k, v = qkv.split(C, dim=2)
+    q = q.view(B, T, NH, 64).transpose(1, 2)
+    k = k.view(B, T, NH, 64).transpose(1, 2)
+    v = v.view(B, T, NH, 64).transpose(1, 2)
+    s = (q @ k.transpose(-1, -2)) * 0.125
+    mask = torch.ones(T, T, device=cuda_dev, dtype=torch.bool).tril()
+    s = s.masked_fill(~mask, float("-inf"))
+    lse = torch.logsumexp(s, dim=-1)
+    y = (torch.softmax(s, dim=-1) @ v).transpose(1, 2).reshape(B, T, C)
+    y.backward(torch.from_numpy(dout_np).to(cuda_dev).bfloat16().float())
+    assert max_rel_err(torch.from_numpy(out_g), y.detach().cpu()) < 1e-2
+    assert max_rel_err(torch.from_numpy(lse_g), lse.detach().cpu()) < 1e-2
+    g = qkv.grad.cpu()
+    for name, sl in (("dq", slice(0, C)), ("dk", slice(C, 2 * C)), ("dv", slice(2 * C, 3 * C))):
+        e = max_rel_err(torch.from_numpy(dqkv_g[..., sl]), g[..., sl])
+        assert e < 1e-2, f"{name} max_rel={e:.3e}"
+
+
+def test_attention_rejects_head_size(cuda_dev):
+    import torch
+    import llmk
+    qkv = torch.zeros(1, 128, 3 * 96, device=cuda_dev, dtype=torch.bfloat16)
+    out = torch.zeros(1, 128, 96, device=cuda_dev, dtype=torch.bfloat16)
+    lse = torch.zeros(1, 3, 128, device=cuda_dev)
+    with pytest.raises(llmk.LlmkError) as e:
+        llmk.call("llmk_attention_forward", out.data_ptr(), lse.data_ptr(), qkv.data_ptr(), 1, 128, 288, 3,
+                  llmk.stream_ptr())
+    assert e.value.code == 2

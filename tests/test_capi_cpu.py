@@ -1,0 +1,123 @@
+"""C ABI checks that need no GPU: the library loads, every function declared
+in include/*.h is exported, argument validation fails cleanly, and the
+host-only planning helpers (workspace sizes, DP buckets, parameter layout)
+are consistent."""
+import ctypes as C
+import os
+import re
+
+import numpy as np
+import pytest
+
+import oracle as O
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_functions():
+    names = []
+    for h in ("llmk.h", "llmk_gpt2.h"):
+        src = open(os.path.join(ROOT, "include", h)).read()
+        src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+        names += re.findall(r"^\s*(?:const\s+)?[\w\s\*]+?\b(llmk_\w+)\s*\(", src, flags=re.M)
+    return sorted(set(names))
+
+
+def test_every_declared_symbol_is_exported(llmk_lib):
+    import llmk
+    decl = declared_functions()
+    assert len(decl) >= 40, decl
+    L = C.CDLL(llmk.LIB_PATH)
+    missing = [n for n in decl if not hasattr(L, n)]
+    assert not missing, missing
+    # and the Python FFI stub binds every one of them
+    assert sorted(set(decl) - set(llmk.exported_symbols())) == []
+
+
+def test_argument_validation_without_gpu(llmk_lib):
+    import llmk
+    L = llmk.lib()
+    assert L.llmk_gemm(None, 0, 0, None, 0, 0, None, 0, 0, llmk.MATH_BF16, 1, 1, 1, None, None, 0, None) == 1
+    assert L.llmk_attention_forward(None, None, None, 1, 64, 192, 1, None) == 1
+    assert b"null" in L.llmk_last_error()
+    assert L.llmk_status_string(4) == b"device wait timed out"
+    assert L.llmk_matmul_backward_workspace(8192, 768, 2304, llmk.MATH_BF16) > 0
+    assert L.llmk_attention_backward_workspace(8, 1024, 2304, 12) == 8 * 12 * 1024 * 4 + 8 * 1024 * 768 * 4
+    assert L.llmk_layernorm_backward_workspace(16384, 768) > 0
+
+
+def test_dp_buckets_partition_parameters(llmk_lib):
+    import llmk
+    cfg = llmk.GPT2Config(1024, 50257, 50304, 12, 12, 768)
+    n = llmk.lib().llmk_gpt2_dp_buckets(C.byref(cfg), None, 0)
+    assert n == 14
+    arr = (C.c_size_t * (2 * n))()
+    assert llmk.lib().llmk_gpt2_dp_buckets(C.byref(cfg), arr, n) == n
+    ranges = sorted((arr[2 * i], arr[2 * i + 1]) for i in range(n))
+    total = llmk.lib().llmk_gpt2_num_parameters(C.byref(cfg))
+    assert total == 124475904
+    pos = 0
+    for b, e in ranges:
+        assert b == pos and e > b
+        pos = e
+    assert pos == total
+
+
+def test_layer_major_permutation_roundtrip(llmk_lib):
+    import llmk
+    cfgo = O.config(max_seq_len=64, vocab_size=100, padded_vocab_size=128, num_layers=3, num_heads=2, channels=128)
+    cfg = llmk.GPT2Config(64, 100, 128, 3, 2, 128)
+    n = llmk.lib().llmk_gpt2_num_parameters(C.byref(cfg))
+    assert n == sum(O.param_sizes(cfgo))
+    src = np.arange(n, dtype=np.float32)
+    lm = np.empty_like(src)
+    back = np.empty_like(src)
+    llmk.call("llmk_gpt2_to_layer_major", C.byref(cfg), src.ctypes.data, lm.ctypes.data, 0)
+    llmk.call("llmk_gpt2_to_layer_major", C.byref(cfg), lm.ctypes.data, back.ctypes.data, 1)
+    assert np.array_equal(back, src)
+    assert not np.array_equal(lm, src)
+    assert np.array_equal(np.sort(lm), src)
+
+
+def test_adapter_compiles_and_links(llmk_lib, tmp_path):
+    """include/llmk_gpt2cuda.hpp (the reference's gpt2cuda:: API over the C ABI)
+    compiles against a DevVecf-like type and links against libllmk.so."""
+    import shutil
+    import subprocess
+    import llmk
+    gxx = shutil.which("g++")
+    if gxx is None:
+        pytest.skip("g++ not available")
+    src = tmp_path / "adapter.cpp"
+    src.write_text(r'''
+#include "llmk_gpt2cuda.hpp"
+struct DevVecf { float* p = nullptr; size_t n = 0; float* data() const { return p; } size_t size() const { return n; } };
+struct DevVeci { int* p = nullptr; size_t n = 0; int* data() const { return p; } size_t size() const { return n; } };
+int main() {
+  DevVecf a, b, c, d, e, g; DevVeci t; cudaStream_t s = nullptr;
+  try {
+    gpt2cuda::BatchMatmulNTForward(a, b, c, d, 1, 1, 8, 8, s);
+    gpt2cuda::BatchMatmulNTBackward(a, b, c, d, e, g, 1, 1, 8, 8, s);
+    gpt2cuda::BatchCausalAttentionForward(a, b, c, 1, 64, 192, 1, s);
+    gpt2cuda::BatchCausalAttentionBackward(a, b, c, d, e, g, 1, 64, 192, 1, s);
+    gpt2cuda::BatchLayerNormForward(a, b, c, d, e, g, 1, 1, 8, s);
+    gpt2cuda::BatchLayerNormBackward(a, b, c, d, e, g, b, c, 1, 1, 8, s);
+    gpt2cuda::BatchGeluForward(a, b, 1, 1, 8, s);
+    gpt2cuda::BatchGeluBackward(a, b, c, 1, 1, 8, s);
+    gpt2cuda::BatchResidualForward(a, b, c, 1, 1, 8, s);
+    gpt2cuda::BatchResidualBackward(a, b, c, 1, 1, 8, s);
+    gpt2cuda::BatchEncoderForward(a, t, b, c, 1, 1, 8, 8, 8, s);
+    gpt2cuda::BatchEncoderBackward(a, b, c, t, 1, 1, 8, 8, 8, s);
+    gpt2cuda::AdamW(a, b, c, d, 8, gpt2cuda::AdamWConfig{1e-3f, .9f, .999f, 1e-8f, 0.f, 1}, s);
+  } catch (const std::invalid_argument&) { return 0; }  // null buffers: rejected as the reference would
+  return 0;
+}
+''')
+    exe = tmp_path / "adapter"
+    lib_dir = os.path.dirname(llmk.LIB_PATH)
+    r = subprocess.run([gxx, "-std=c++17", "-I", os.path.join(ROOT, "include"), "-I", "/usr/local/cuda/include",
+                        str(src), "-o", str(exe), "-L", lib_dir, "-l:libllmk.so", f"-Wl,-rpath,{lib_dir}",
+                        "-L", "/usr/local/cuda/lib64", "-lcudart"], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
+    assert r.returncode == 0, r.stderr
