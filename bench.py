@@ -185,7 +185,15 @@ def reference_step_time(threads: int, steps: int = 3) -> dict:
         O.write_checkpoint(ck, cfg, params)
         losses = np.zeros(steps, np.float32)
         ms = np.zeros(steps, np.float64)
-        O.ref().ref_gpt2_train(ck.encode(), Bs, Ts, toks[:-1].copy(), toks[1:].copy(), steps, LR, losses, ms)
+        # the reference prints its model config on stdout: keep stdout for the JSON line
+        sys.stdout.flush()
+        saved = os.dup(1)
+        os.dup2(2, 1)
+        try:
+            O.ref().ref_gpt2_train(ck.encode(), Bs, Ts, toks[:-1].copy(), toks[1:].copy(), steps, LR, losses, ms)
+        finally:
+            os.dup2(saved, 1)
+            os.close(saved)
     per_step = [Bs * Ts / (x / 1e3) for x in ms]
     return {"value": statistics.median(per_step), "per_step": per_step, "step_s": statistics.median(ms) / 1e3,
             "sample": f"{steps} reference training steps of GPT-2 124M at B={Bs}, T={Ts} ({Bs * Ts} tokens each), "

@@ -51,11 +51,12 @@ unsigned long long llmk_launch_count(void);
 /* ------------------------------------------------------------ GEMM core */
 /* Epilogue applied to the fp32 accumulator of D[M,N] = A[M,K] * B[N,K]^T,
  * in this order: + bias[n]; + residual[m,n]; GELU (pre-activation stored to
- * aux as bf16 when aux != NULL); * gelu'(aux[m,n]) (GELU_BWD, aux = bf16
- * pre-activation); + D_old[m,n] (ACCUMULATE). */
+ * aux when aux != NULL); * gelu'(aux[m,n]) (GELU_BWD, aux = pre-activation);
+ * + D_old[m,n] (ACCUMULATE). aux is bf16, or fp32 with LLMK_EPI_AUX_F32. */
 #define LLMK_EPI_ACCUMULATE 1
 #define LLMK_EPI_GELU 2
 #define LLMK_EPI_GELU_BWD 4
+#define LLMK_EPI_AUX_F32 8 /* aux is fp32 instead of bf16 */
 typedef struct llmk_epilogue {
   const float* bias;     /* [N] fp32 or NULL */
   const float* residual; /* fp32 [M, ldr] or NULL */

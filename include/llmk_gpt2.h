@@ -34,10 +34,14 @@ typedef struct llmk_gpt2 llmk_gpt2;
 size_t llmk_gpt2_num_parameters(const llmk_gpt2_config* cfg);
 size_t llmk_gpt2_parameter_count(const llmk_gpt2* model);
 
-/* Allocates a model for micro-batch B x T on the current device. stream:
- * the cudaStream_t to run on, or NULL for a private one. Head size must be
- * 64. Replaces gpt2cuda::GPT2 construction + Init (gpt2/cuda/gpt2cuda.cu:168-302). */
-int llmk_gpt2_create(llmk_gpt2** out, const llmk_gpt2_config* cfg, int B, int T, void* stream);
+/* Allocates a model for micro-batch B x T on the current device. math:
+ * LLMK_MATH_BF16 (bf16 GEMM operands and activations, fp32 residual stream,
+ * master weights and optimizer: the throughput mode) or LLMK_MATH_TF32 (fp32
+ * activations, TF32 GEMMs, the reference GPU path's precision; attention
+ * still runs on bf16 copies). stream: the cudaStream_t to run on, or NULL
+ * for a private one. Head size must be 64.
+ * Replaces gpt2cuda::GPT2 construction + Init (gpt2/cuda/gpt2cuda.cu:168-302). */
+int llmk_gpt2_create(llmk_gpt2** out, const llmk_gpt2_config* cfg, int B, int T, int math, void* stream);
 int llmk_gpt2_destroy(llmk_gpt2* model);
 int llmk_gpt2_stream(llmk_gpt2* model, void** stream);
 /* Device token buffers the model reads (B*T int32 each). */

@@ -577,43 +577,31 @@ __global__ void __launch_bounds__(192, 1)
                          __uint_as_float(v[4 * k + 2]), __uint_as_float(v[4 * k + 3]));
           }
         }
-        // dK (scaled) and dV: TMEM lane = key row
+        // dK (scaled) and dV: TMEM lane = key row. tcgen05.ld is warp-collective
+        // (.sync.aligned): every lane loads, only lanes of keys < T store.
         const int tk = k0 + r;
-        if (tk < T) {
-          __nv_bfloat16* dk = dqkv + (static_cast<long long>(b) * T + tk) * 3 * C + C + h * HD;
-          __nv_bfloat16* dvp = dk + C;
+        const bool key_ok = tk < T;
+        __nv_bfloat16* dk = dqkv + (static_cast<long long>(b) * T + (key_ok ? tk : 0)) * 3 * C + C + h * HD;
+        __nv_bfloat16* dvp = dk + C;
 #pragma unroll
-          for (int half = 0; half < 2; ++half) {
-            tmem_ld_32x32b_x32(tmem + lane_base + 320 + half * 32, v);
+        for (int half = 0; half < 2; ++half) {
+#pragma unroll
+          for (int which = 0; which < 2; ++which) {  // 0: dK (cols 320..383, scaled), 1: dV (cols 256..319)
+            const float sc = which == 0 ? 0.125f : 1.0f;
+            tmem_ld_32x32b_x32(tmem + lane_base + (which == 0 ? 320 : 256) + half * 32, v);
             tmem_ld_wait();
+            if (key_ok) {
+              __nv_bfloat16* dst = (which == 0 ? dk : dvp) + half * 32;
 #pragma unroll
-            for (int ch = 0; ch < 4; ++ch) {
-              uint4 u;
-              u.x = pack_bf16x2(__uint_as_float(v[ch * 8 + 0]) * 0.125f, __uint_as_float(v[ch * 8 + 1]) * 0.125f);
-              u.y = pack_bf16x2(__uint_as_float(v[ch * 8 + 2]) * 0.125f, __uint_as_float(v[ch * 8 + 3]) * 0.125f);
-              u.z = pack_bf16x2(__uint_as_float(v[ch * 8 + 4]) * 0.125f, __uint_as_float(v[ch * 8 + 5]) * 0.125f);
-              u.w = pack_bf16x2(__uint_as_float(v[ch * 8 + 6]) * 0.125f, __uint_as_float(v[ch * 8 + 7]) * 0.125f);
-              reinterpret_cast<uint4*>(dk + half * 32)[ch] = u;
+              for (int ch = 0; ch < 4; ++ch) {
+                uint4 u;
+                u.x = pack_bf16x2(__uint_as_float(v[ch * 8 + 0]) * sc, __uint_as_float(v[ch * 8 + 1]) * sc);
+                u.y = pack_bf16x2(__uint_as_float(v[ch * 8 + 2]) * sc, __uint_as_float(v[ch * 8 + 3]) * sc);
+                u.z = pack_bf16x2(__uint_as_float(v[ch * 8 + 4]) * sc, __uint_as_float(v[ch * 8 + 5]) * sc);
+                u.w = pack_bf16x2(__uint_as_float(v[ch * 8 + 6]) * sc, __uint_as_float(v[ch * 8 + 7]) * sc);
+                reinterpret_cast<uint4*>(dst)[ch] = u;
+              }
             }
-            tmem_ld_32x32b_x32(tmem + lane_base + 256 + half * 32, v);
-            tmem_ld_wait();
-#pragma unroll
-            for (int ch = 0; ch < 4; ++ch) {
-              uint4 u;
-              u.x = pack_bf16x2(__uint_as_float(v[ch * 8 + 0]), __uint_as_float(v[ch * 8 + 1]));
-              u.y = pack_bf16x2(__uint_as_float(v[ch * 8 + 2]), __uint_as_float(v[ch * 8 + 3]));
-              u.z = pack_bf16x2(__uint_as_float(v[ch * 8 + 4]), __uint_as_float(v[ch * 8 + 5]));
-              u.w = pack_bf16x2(__uint_as_float(v[ch * 8 + 6]), __uint_as_float(v[ch * 8 + 7]));
-              reinterpret_cast<uint4*>(dvp + half * 32)[ch] = u;
-            }
-          }
-        } else {
-          // keep the collective tcgen05.ld pattern uniform across the warp
-#pragma unroll
-          for (int half = 0; half < 2; ++half) {
-            tmem_ld_32x32b_x32(tmem + lane_base + 320 + half * 32, v);
-            tmem_ld_32x32b_x32(tmem + lane_base + 256 + half * 32, v);
-            tmem_ld_wait();
           }
         }
       }

@@ -121,11 +121,15 @@ __device__ __forceinline__ void epi_ops8(const EpiParams& ep, long long gm, int 
     for (int j = 0; j < 8; ++j) v[j] += t[j];
   }
   if (ep.flags & LLMK_EPI_GELU) {
-    if (ep.aux) store8_bf16(ep.aux + gm * ep.ldaux + gn, v);
+    if (ep.aux) {
+      if (ep.flags & LLMK_EPI_AUX_F32) store8(reinterpret_cast<float*>(ep.aux) + gm * ep.ldaux + gn, v);
+      else store8_bf16(ep.aux + gm * ep.ldaux + gn, v);
+    }
 #pragma unroll
     for (int j = 0; j < 8; ++j) v[j] = gelu_tanh(v[j]);
   } else if (ep.flags & LLMK_EPI_GELU_BWD) {
-    load8_bf16(ep.aux + gm * ep.ldaux + gn, t);
+    if (ep.flags & LLMK_EPI_AUX_F32) load8(reinterpret_cast<const float*>(ep.aux) + gm * ep.ldaux + gn, t);
+    else load8_bf16(ep.aux + gm * ep.ldaux + gn, t);
 #pragma unroll
     for (int j = 0; j < 8; ++j) v[j] *= gelu_tanh_grad(t[j]);
   }
@@ -152,11 +156,15 @@ __device__ __forceinline__ void epi_apply8(const EpiParams& ep, long long gm, in
     for (int j = 0; j < 8; ++j) v[j] += t[j];
   }
   if (ep.flags & LLMK_EPI_GELU) {
-    if (ep.aux) store8_bf16(ep.aux + gm * ep.ldaux + gn, v);
+    if (ep.aux) {
+      if (ep.flags & LLMK_EPI_AUX_F32) store8(reinterpret_cast<float*>(ep.aux) + gm * ep.ldaux + gn, v);
+      else store8_bf16(ep.aux + gm * ep.ldaux + gn, v);
+    }
 #pragma unroll
     for (int j = 0; j < 8; ++j) v[j] = gelu_tanh(v[j]);
   } else if (ep.flags & LLMK_EPI_GELU_BWD) {
-    load8_bf16(ep.aux + gm * ep.ldaux + gn, t);
+    if (ep.flags & LLMK_EPI_AUX_F32) load8(reinterpret_cast<const float*>(ep.aux) + gm * ep.ldaux + gn, t);
+    else load8_bf16(ep.aux + gm * ep.ldaux + gn, t);
 #pragma unroll
     for (int j = 0; j < 8; ++j) v[j] *= gelu_tanh_grad(t[j]);
   }
@@ -514,7 +522,7 @@ static int gemm_impl(void* D, llmk_dtype d_dtype, long long ldd, const void* A, 
     ep.ldaux = epi->ldaux;
     ep.flags = epi->flags;
     if ((ep.bias && !aligned16(ep.bias)) || (ep.residual && (!aligned16(ep.residual) || ep.ldr % 4)) ||
-        (ep.aux && (!aligned16(ep.aux) || ep.ldaux % 8)))
+        (ep.aux && (!aligned16(ep.aux) || ep.ldaux % ((ep.flags & LLMK_EPI_AUX_F32) ? 4 : 8))))
       return fail(LLMK_ERR_UNSUPPORTED, "gemm: epilogue operands need 16-byte alignment");
     if ((ep.flags & LLMK_EPI_GELU_BWD) && !ep.aux) return fail(LLMK_ERR_INVALID_ARG, "gemm: GELU_BWD needs aux");
   }

@@ -73,7 +73,10 @@ struct LayerParams {
 
 struct LayerActs {
   float *ln1_mean, *ln1_rstd, *ln2_mean, *ln2_rstd, *lse, *res2, *res3;
-  __nv_bfloat16 *ln1, *qkv, *atty, *ln2, *fch_pre, *fch_gelu;
+  // GEMM operands in the activation dtype (bf16, or fp32 in tf32 mode)
+  void *ln1, *qkv, *atty, *ln2, *fch_pre, *fch_gelu;
+  // tf32 mode only: bf16 copies of the attention operands
+  __nv_bfloat16 *qkv16, *atty16;
 };
 
 struct llmk_gpt2 {
@@ -85,16 +88,21 @@ struct llmk_gpt2 {
   size_t tsize[16] = {};
   size_t off_wte = 0, off_wpe = 0, off_lnfw = 0, off_lnfb = 0;
   std::vector<LayerParams> lp;
+  llmk_math math = LLMK_MATH_BF16;
+  llmk_dtype adt = LLMK_BF16;  // activation dtype of GEMM operands
+  size_t ae = 2;               // its element size
   float *params = nullptr, *grads = nullptr, *m = nullptr, *v = nullptr;
-  __nv_bfloat16* params_bf16 = nullptr;
+  __nv_bfloat16* params_bf16 = nullptr;  // bf16 mode only
   // activations
   float* encoded = nullptr;
   std::vector<LayerActs> acts;
   float *lnf_mean = nullptr, *lnf_rstd = nullptr, *losses = nullptr, *loss = nullptr;
-  __nv_bfloat16 *lnf = nullptr, *logits = nullptr;
+  void *lnf = nullptr, *logits = nullptr;
   // backward scratch
   float *dres = nullptr, *dln = nullptr;
-  __nv_bfloat16 *dres_bf16 = nullptr, *datty = nullptr, *dqkv = nullptr, *dfch = nullptr;
+  __nv_bfloat16* dres_bf16 = nullptr;  // bf16 mode: GEMM copy of dres
+  void *datty = nullptr, *dqkv = nullptr, *dfch = nullptr;
+  __nv_bfloat16 *datty16 = nullptr, *dqkv16 = nullptr;  // tf32 mode: attention-side copies
   void* workspace = nullptr;
   size_t workspace_bytes = 0;
   int *inputs = nullptr, *targets = nullptr;
@@ -185,10 +193,11 @@ void free_all(llmk_gpt2* g) {
   f(g->params); f(g->grads); f(g->m); f(g->v); f(g->params_bf16); f(g->encoded);
   for (auto& a : g->acts) {
     f(a.ln1_mean); f(a.ln1_rstd); f(a.ln2_mean); f(a.ln2_rstd); f(a.lse); f(a.res2); f(a.res3);
-    f(a.ln1); f(a.qkv); f(a.atty); f(a.ln2); f(a.fch_pre); f(a.fch_gelu);
+    f(a.ln1); f(a.qkv); f(a.atty); f(a.ln2); f(a.fch_pre); f(a.fch_gelu); f(a.qkv16); f(a.atty16);
   }
   f(g->lnf_mean); f(g->lnf_rstd); f(g->losses); f(g->loss); f(g->lnf); f(g->logits);
   f(g->dres); f(g->dln); f(g->dres_bf16); f(g->datty); f(g->dqkv); f(g->dfch); f(g->workspace);
+  f(g->datty16); f(g->dqkv16);
   f(g->inputs); f(g->targets);
   if (g->h_inputs) cudaFreeHost(g->h_inputs);
   if (g->h_targets) cudaFreeHost(g->h_targets);
@@ -209,7 +218,12 @@ int alloc_all(llmk_gpt2* g) {
   LLMK_TRY(dalloc(&g->grads, g->nparams));
   LLMK_TRY(dalloc(&g->m, g->nparams));
   LLMK_TRY(dalloc(&g->v, g->nparams));
-  LLMK_TRY(dalloc(&g->params_bf16, g->nparams));
+  const bool bf = g->math == LLMK_MATH_BF16;
+  const size_t ae = g->ae;
+  auto aalloc = [&](void** p, size_t n) {
+    return llmk::cuda_check(cudaMalloc(p, std::max<size_t>(n, 1) * ae), "cudaMalloc");
+  };
+  if (bf) LLMK_TRY(dalloc(&g->params_bf16, g->nparams));
   LLMK_CUDA(cudaMemset(g->m, 0, g->nparams * sizeof(float)));
   LLMK_CUDA(cudaMemset(g->v, 0, g->nparams * sizeof(float)));
   LLMK_CUDA(cudaMemset(g->grads, 0, g->nparams * sizeof(float)));
@@ -220,15 +234,24 @@ int alloc_all(llmk_gpt2* g) {
     LLMK_TRY(dalloc(&a.ln2_mean, BT)); LLMK_TRY(dalloc(&a.ln2_rstd, BT));
     LLMK_TRY(dalloc(&a.lse, B * NH * T));
     LLMK_TRY(dalloc(&a.res2, BT * C)); LLMK_TRY(dalloc(&a.res3, BT * C));
-    LLMK_TRY(dalloc(&a.ln1, BT * C)); LLMK_TRY(dalloc(&a.qkv, BT * 3 * C)); LLMK_TRY(dalloc(&a.atty, BT * C));
-    LLMK_TRY(dalloc(&a.ln2, BT * C)); LLMK_TRY(dalloc(&a.fch_pre, BT * 4 * C)); LLMK_TRY(dalloc(&a.fch_gelu, BT * 4 * C));
+    a.qkv16 = a.atty16 = nullptr;
+    LLMK_TRY(aalloc(&a.ln1, BT * C)); LLMK_TRY(aalloc(&a.qkv, BT * 3 * C)); LLMK_TRY(aalloc(&a.atty, BT * C));
+    LLMK_TRY(aalloc(&a.ln2, BT * C)); LLMK_TRY(aalloc(&a.fch_pre, BT * 4 * C)); LLMK_TRY(aalloc(&a.fch_gelu, BT * 4 * C));
+    if (!bf) {
+      LLMK_TRY(dalloc(&a.qkv16, BT * 3 * C));
+      LLMK_TRY(dalloc(&a.atty16, BT * C));
+    }
   }
   LLMK_TRY(dalloc(&g->lnf_mean, BT)); LLMK_TRY(dalloc(&g->lnf_rstd, BT));
   LLMK_TRY(dalloc(&g->losses, BT)); LLMK_TRY(dalloc(&g->loss, 1));
-  LLMK_TRY(dalloc(&g->lnf, BT * C)); LLMK_TRY(dalloc(&g->logits, BT * Vp));
+  LLMK_TRY(aalloc(&g->lnf, BT * C)); LLMK_TRY(aalloc(&g->logits, BT * Vp));
   LLMK_TRY(dalloc(&g->dres, BT * C)); LLMK_TRY(dalloc(&g->dln, BT * C));
-  LLMK_TRY(dalloc(&g->dres_bf16, BT * C)); LLMK_TRY(dalloc(&g->datty, BT * C));
-  LLMK_TRY(dalloc(&g->dqkv, BT * 3 * C)); LLMK_TRY(dalloc(&g->dfch, BT * 4 * C));
+  if (bf) LLMK_TRY(dalloc(&g->dres_bf16, BT * C));
+  LLMK_TRY(aalloc(&g->datty, BT * C)); LLMK_TRY(aalloc(&g->dqkv, BT * 3 * C)); LLMK_TRY(aalloc(&g->dfch, BT * 4 * C));
+  if (!bf) {
+    LLMK_TRY(dalloc(&g->datty16, BT * C));
+    LLMK_TRY(dalloc(&g->dqkv16, BT * 3 * C));
+  }
   LLMK_TRY(dalloc(&g->inputs, BT)); LLMK_TRY(dalloc(&g->targets, BT));
   LLMK_CUDA(cudaMallocHost(reinterpret_cast<void**>(&g->h_inputs), BT * sizeof(int)));
   LLMK_CUDA(cudaMallocHost(reinterpret_cast<void**>(&g->h_targets), BT * sizeof(int)));
@@ -236,9 +259,9 @@ int alloc_all(llmk_gpt2* g) {
   // one workspace, sized for the largest consumer
   const int iC = static_cast<int>(C), iBT = static_cast<int>(BT), iVp = static_cast<int>(Vp);
   size_t ws = 0;
-  for (int oc : {3 * iC, iC, 4 * iC}) ws = std::max(ws, llmk_matmul_backward_workspace(iBT, iC, oc, LLMK_MATH_BF16));
-  ws = std::max(ws, llmk_matmul_backward_workspace(iBT, 4 * iC, iC, LLMK_MATH_BF16));
-  ws = std::max(ws, llmk_gemm_workspace(iVp, iC, iBT, LLMK_MATH_BF16));
+  for (int oc : {3 * iC, iC, 4 * iC}) ws = std::max(ws, llmk_matmul_backward_workspace(iBT, iC, oc, g->math));
+  ws = std::max(ws, llmk_matmul_backward_workspace(iBT, 4 * iC, iC, g->math));
+  ws = std::max(ws, llmk_gemm_workspace(iVp, iC, iBT, g->math));
   ws = std::max(ws, llmk_layernorm_backward_workspace(iBT, iC));
   ws = std::max(ws, llmk_attention_backward_workspace(g->B, g->T, 3 * iC, static_cast<int>(NH)));
   ws = std::max(ws, llmk_encoder_backward_workspace(g->B, g->T));
@@ -286,13 +309,19 @@ size_t llmk_gpt2_num_parameters(const llmk_gpt2_config* cfg) {
   return n;
 }
 
-int llmk_gpt2_create(llmk_gpt2** out, const llmk_gpt2_config* cfg, int B, int T, void* stream) {
+int llmk_gpt2_create(llmk_gpt2** out, const llmk_gpt2_config* cfg, int B, int T, int math_mode, void* stream) {
   if (!out || !cfg || B <= 0 || T <= 0) return fail(LLMK_ERR_INVALID_ARG, "gpt2_create: bad arguments");
+  if (math_mode != LLMK_MATH_BF16 && math_mode != LLMK_MATH_TF32)
+    return fail(LLMK_ERR_INVALID_ARG, "gpt2_create: math mode");
+  const llmk_math math = static_cast<llmk_math>(math_mode);
   if (T > cfg->max_seq_len || cfg->channels % cfg->num_heads || cfg->channels / cfg->num_heads != 64 ||
       cfg->padded_vocab_size < cfg->vocab_size || cfg->padded_vocab_size % 8 || cfg->channels % 64)
     return fail(LLMK_ERR_UNSUPPORTED, "gpt2_create: needs head size 64, C % 64 == 0, Vp % 8 == 0, T <= maxT");
   auto* g = new llmk_gpt2();
   g->cfg = *cfg;
+  g->math = math;
+  g->adt = math == LLMK_MATH_BF16 ? LLMK_BF16 : LLMK_F32;
+  g->ae = math == LLMK_MATH_BF16 ? 2 : 4;
   g->B = B;
   g->T = T;
   int rc = llmk::cuda_check(cudaGetDevice(&g->device), "cudaGetDevice");
@@ -337,7 +366,8 @@ int llmk_gpt2_load_parameters(llmk_gpt2* g, const float* host_params, size_t n) 
   std::vector<float> tmp(n);
   permute_params(g, host_params, tmp.data(), 0);
   LLMK_CUDA(cudaMemcpy(g->params, tmp.data(), n * sizeof(float), cudaMemcpyHostToDevice));
-  LLMK_TRY(llmk_cast(g->params_bf16, LLMK_BF16, g->params, LLMK_F32, static_cast<long long>(n), g->stream));
+  if (g->params_bf16)
+    LLMK_TRY(llmk_cast(g->params_bf16, LLMK_BF16, g->params, LLMK_F32, static_cast<long long>(n), g->stream));
   LLMK_CUDA(cudaMemsetAsync(g->m, 0, n * sizeof(float), g->stream));
   LLMK_CUDA(cudaMemsetAsync(g->v, 0, n * sizeof(float), g->stream));
   LLMK_CUDA(cudaStreamSynchronize(g->stream));
@@ -364,7 +394,14 @@ int llmk_gpt2_forward(llmk_gpt2* g, const int* d_inputs, const int* d_targets) {
   const int V = g->cfg.vocab_size, Vp = g->cfg.padded_vocab_size, BT = B * T;
   cudaStream_t s = g->stream;
   const float* P = g->params;
-  const __nv_bfloat16* Pb = g->params_bf16;
+  const llmk_math mm = g->math;
+  const llmk_dtype adt = g->adt;
+  const bool bf = mm == LLMK_MATH_BF16;
+  // GEMM weights: the bf16 mirror in bf16 mode, the fp32 master in tf32 mode
+  auto W = [&](size_t off) -> const void* {
+    return bf ? static_cast<const void*>(g->params_bf16 + off) : static_cast<const void*>(P + off);
+  };
+  const int aux_f32 = bf ? 0 : LLMK_EPI_AUX_F32;
   if (d_inputs != g->inputs) LLMK_CUDA(cudaMemcpyAsync(g->inputs, d_inputs, BT * sizeof(int), cudaMemcpyDeviceToDevice, s));
   g->have_targets = d_targets != nullptr;
   if (d_targets && d_targets != g->targets)
@@ -376,32 +413,35 @@ int llmk_gpt2_forward(llmk_gpt2* g, const int* d_inputs, const int* d_targets) {
     // Layer::Forward (gpt2/cuda/layer.cu:151-177)
     const LayerParams& p = g->lp[l];
     LayerActs& a = g->acts[l];
-    LLMK_TRY(llmk_layernorm_forward(a.ln1, LLMK_BF16, a.ln1_mean, a.ln1_rstd, x, P + p.ln1w, P + p.ln1b, BT, C, s));
+    LLMK_TRY(llmk_layernorm_forward(a.ln1, adt, a.ln1_mean, a.ln1_rstd, x, P + p.ln1w, P + p.ln1b, BT, C, s));
     llmk_epilogue e1 = epi(P + p.qkvb);
-    LLMK_TRY(llmk_gemm(a.qkv, LLMK_BF16, 3 * C, a.ln1, 0, C, Pb + p.qkvw, 0, C, LLMK_MATH_BF16, BT, 3 * C, C, &e1,
-                       nullptr, 0, s));
-    LLMK_TRY(llmk_attention_forward(a.atty, a.lse, a.qkv, B, T, 3 * C, NH, s));
+    LLMK_TRY(llmk_gemm(a.qkv, adt, 3 * C, a.ln1, 0, C, W(p.qkvw), 0, C, mm, BT, 3 * C, C, &e1, nullptr, 0, s));
+    if (bf) {
+      LLMK_TRY(llmk_attention_forward(a.atty, a.lse, a.qkv, B, T, 3 * C, NH, s));
+    } else {
+      // the attention kernels are bf16: round the fp32 operands once, widen the output
+      LLMK_TRY(llmk_cast(a.qkv16, LLMK_BF16, a.qkv, LLMK_F32, static_cast<long long>(BT) * 3 * C, s));
+      LLMK_TRY(llmk_attention_forward(a.atty16, a.lse, a.qkv16, B, T, 3 * C, NH, s));
+      LLMK_TRY(llmk_cast(a.atty, LLMK_F32, a.atty16, LLMK_BF16, static_cast<long long>(BT) * C, s));
+    }
     llmk_epilogue e2 = epi(P + p.attprojb, x, C);  // residual add fused
-    LLMK_TRY(llmk_gemm(a.res2, LLMK_F32, C, a.atty, 0, C, Pb + p.attprojw, 0, C, LLMK_MATH_BF16, BT, C, C, &e2,
-                       nullptr, 0, s));
-    LLMK_TRY(llmk_layernorm_forward(a.ln2, LLMK_BF16, a.ln2_mean, a.ln2_rstd, a.res2, P + p.ln2w, P + p.ln2b, BT, C, s));
-    llmk_epilogue e3 = epi(P + p.fcb, nullptr, 0, a.fch_pre, 4 * C, LLMK_EPI_GELU);  // GELU fused, pre-activation kept
-    LLMK_TRY(llmk_gemm(a.fch_gelu, LLMK_BF16, 4 * C, a.ln2, 0, C, Pb + p.fcw, 0, C, LLMK_MATH_BF16, BT, 4 * C, C, &e3,
-                       nullptr, 0, s));
+    LLMK_TRY(llmk_gemm(a.res2, LLMK_F32, C, a.atty, 0, C, W(p.attprojw), 0, C, mm, BT, C, C, &e2, nullptr, 0, s));
+    LLMK_TRY(llmk_layernorm_forward(a.ln2, adt, a.ln2_mean, a.ln2_rstd, a.res2, P + p.ln2w, P + p.ln2b, BT, C, s));
+    // GELU fused, pre-activation kept for the backward
+    llmk_epilogue e3 = epi(P + p.fcb, nullptr, 0, a.fch_pre, 4 * C, LLMK_EPI_GELU | aux_f32);
+    LLMK_TRY(llmk_gemm(a.fch_gelu, adt, 4 * C, a.ln2, 0, C, W(p.fcw), 0, C, mm, BT, 4 * C, C, &e3, nullptr, 0, s));
     llmk_epilogue e4 = epi(P + p.fcprojb, a.res2, C);
-    LLMK_TRY(llmk_gemm(a.res3, LLMK_F32, C, a.fch_gelu, 0, 4 * C, Pb + p.fcprojw, 0, 4 * C, LLMK_MATH_BF16, BT, C,
-                       4 * C, &e4, nullptr, 0, s));
+    LLMK_TRY(llmk_gemm(a.res3, LLMK_F32, C, a.fch_gelu, 0, 4 * C, W(p.fcprojw), 0, 4 * C, mm, BT, C, 4 * C, &e4,
+                       nullptr, 0, s));
     x = a.res3;
   }
-  LLMK_TRY(llmk_layernorm_forward(g->lnf, LLMK_BF16, g->lnf_mean, g->lnf_rstd, x, P + g->off_lnfw, P + g->off_lnfb, BT,
-                                  C, s));
+  LLMK_TRY(llmk_layernorm_forward(g->lnf, adt, g->lnf_mean, g->lnf_rstd, x, P + g->off_lnfw, P + g->off_lnfb, BT, C, s));
   // tied lm_head (gpt2cuda.cu:323): logits[BT, Vp] = lnf * wte^T, no bias
-  LLMK_TRY(llmk_gemm(g->logits, LLMK_BF16, Vp, g->lnf, 0, C, Pb + g->off_wte, 0, C, LLMK_MATH_BF16, BT, Vp, C, nullptr,
-                     nullptr, 0, s));
+  LLMK_TRY(llmk_gemm(g->logits, adt, Vp, g->lnf, 0, C, W(g->off_wte), 0, C, mm, BT, Vp, C, nullptr, nullptr, 0, s));
   if (g->have_targets) {
     // softmax + cross-entropy + its backward in one pass; dlogits overwrite the
     // logits in place with scale 1/(B*T) (gpt2cuda.cu:398)
-    LLMK_TRY(llmk_softmax_crossentropy(g->losses, g->logits, g->logits, LLMK_BF16, g->targets, BT, V, Vp,
+    LLMK_TRY(llmk_softmax_crossentropy(g->losses, g->logits, g->logits, adt, g->targets, BT, V, Vp,
                                        1.0f / static_cast<float>(BT), s));
     LLMK_TRY(llmk_mean(g->loss, g->losses, BT, s));
   }
@@ -423,18 +463,25 @@ int llmk_gpt2_backward(llmk_gpt2* g) {
   const int Vp = g->cfg.padded_vocab_size, BT = B * T;
   cudaStream_t s = g->stream;
   const float* P = g->params;
-  const __nv_bfloat16* Pb = g->params_bf16;
+  const llmk_math mm = g->math;
+  const llmk_dtype adt = g->adt;
+  const bool bf = mm == LLMK_MATH_BF16;
+  auto W = [&](size_t off) -> const void* {
+    return bf ? static_cast<const void*>(g->params_bf16 + off) : static_cast<const void*>(P + off);
+  };
+  // the residual gradient as a GEMM operand: its bf16 mirror, or itself in tf32 mode
+  const void* dres_op = bf ? static_cast<const void*>(g->dres_bf16) : static_cast<const void*>(g->dres);
+  void* dres_mirror = bf ? g->dres_bf16 : nullptr;
+  const int aux_f32 = bf ? 0 : LLMK_EPI_AUX_F32;
   float* G = g->grads;
   void* ws = g->workspace;
   const size_t wsb = g->workspace_bytes;
   LLMK_TRY(llmk_gpt2_zero_grad(g));
   // lm_head backward (gpt2cuda.cu:402): dlnf = dlogits * wte; dwte = dlogits^T * lnf
-  LLMK_TRY(llmk_gemm(g->dln, LLMK_F32, C, g->logits, 0, Vp, Pb + g->off_wte, 1, C, LLMK_MATH_BF16, BT, C, Vp, nullptr,
-                     nullptr, 0, s));
-  LLMK_TRY(llmk_gemm(G + g->off_wte, LLMK_F32, C, g->logits, 1, Vp, g->lnf, 1, C, LLMK_MATH_BF16, Vp, C, BT, nullptr,
-                     ws, wsb, s));
+  LLMK_TRY(llmk_gemm(g->dln, LLMK_F32, C, g->logits, 0, Vp, W(g->off_wte), 1, C, mm, BT, C, Vp, nullptr, nullptr, 0, s));
+  LLMK_TRY(llmk_gemm(G + g->off_wte, LLMK_F32, C, g->logits, 1, Vp, g->lnf, 1, C, mm, Vp, C, BT, nullptr, ws, wsb, s));
   const float* xL = L > 0 ? g->acts[L - 1].res3 : g->encoded;
-  LLMK_TRY(llmk_layernorm_backward(g->dres, g->dres_bf16, G + g->off_lnfw, G + g->off_lnfb, g->dln, LLMK_F32, xL,
+  LLMK_TRY(llmk_layernorm_backward(g->dres, dres_mirror, G + g->off_lnfw, G + g->off_lnfb, g->dln, LLMK_F32, xL,
                                    P + g->off_lnfw, g->lnf_mean, g->lnf_rstd, BT, C, 0, ws, wsb, s));
   for (int l = L - 1; l >= 0; --l) {
     // Layer::Backward (gpt2/cuda/layer.cu:180-266); dres = d(layer output)
@@ -442,37 +489,37 @@ int llmk_gpt2_backward(llmk_gpt2* g) {
     LayerActs& a = g->acts[l];
     const float* x = l > 0 ? g->acts[l - 1].res3 : g->encoded;
     // fcproj: dW = dres^T fch_gelu, db = colsum(dres), dfch = (dres Wfcproj) * gelu'(fch_pre)
-    LLMK_TRY(llmk_gemm(G + p.fcprojw, LLMK_F32, 4 * C, g->dres_bf16, 1, C, a.fch_gelu, 1, 4 * C, LLMK_MATH_BF16, C,
-                       4 * C, BT, nullptr, ws, wsb, s));
-    LLMK_TRY(llmk_colsum(G + p.fcprojb, g->dres, LLMK_F32, BT, C, 0, ws, wsb, s));
-    llmk_epilogue eg = epi(nullptr, nullptr, 0, a.fch_pre, 4 * C, LLMK_EPI_GELU_BWD);
-    LLMK_TRY(llmk_gemm(g->dfch, LLMK_BF16, 4 * C, g->dres_bf16, 0, C, Pb + p.fcprojw, 1, 4 * C, LLMK_MATH_BF16, BT,
-                       4 * C, C, &eg, nullptr, 0, s));
-    // fc: dW = dfch^T ln2, db = colsum(dfch), dln2 = dfch Wfc
-    LLMK_TRY(llmk_gemm(G + p.fcw, LLMK_F32, C, g->dfch, 1, 4 * C, a.ln2, 1, C, LLMK_MATH_BF16, 4 * C, C, BT, nullptr,
+    LLMK_TRY(llmk_gemm(G + p.fcprojw, LLMK_F32, 4 * C, dres_op, 1, C, a.fch_gelu, 1, 4 * C, mm, C, 4 * C, BT, nullptr,
                        ws, wsb, s));
-    LLMK_TRY(llmk_colsum(G + p.fcb, g->dfch, LLMK_BF16, BT, 4 * C, 0, ws, wsb, s));
-    LLMK_TRY(llmk_gemm(g->dln, LLMK_F32, C, g->dfch, 0, 4 * C, Pb + p.fcw, 1, C, LLMK_MATH_BF16, BT, C, 4 * C, nullptr,
-                       nullptr, 0, s));
+    LLMK_TRY(llmk_colsum(G + p.fcprojb, g->dres, LLMK_F32, BT, C, 0, ws, wsb, s));
+    llmk_epilogue eg = epi(nullptr, nullptr, 0, a.fch_pre, 4 * C, LLMK_EPI_GELU_BWD | aux_f32);
+    LLMK_TRY(llmk_gemm(g->dfch, adt, 4 * C, dres_op, 0, C, W(p.fcprojw), 1, 4 * C, mm, BT, 4 * C, C, &eg, nullptr, 0,
+                       s));
+    // fc: dW = dfch^T ln2, db = colsum(dfch), dln2 = dfch Wfc
+    LLMK_TRY(llmk_gemm(G + p.fcw, LLMK_F32, C, g->dfch, 1, 4 * C, a.ln2, 1, C, mm, 4 * C, C, BT, nullptr, ws, wsb, s));
+    LLMK_TRY(llmk_colsum(G + p.fcb, g->dfch, adt, BT, 4 * C, 0, ws, wsb, s));
+    LLMK_TRY(llmk_gemm(g->dln, LLMK_F32, C, g->dfch, 0, 4 * C, W(p.fcw), 1, C, mm, BT, C, 4 * C, nullptr, nullptr, 0, s));
     // ln2: dres += LN2 backward (dres becomes d(res2))
-    LLMK_TRY(llmk_layernorm_backward(g->dres, g->dres_bf16, G + p.ln2w, G + p.ln2b, g->dln, LLMK_F32, a.res2,
+    LLMK_TRY(llmk_layernorm_backward(g->dres, dres_mirror, G + p.ln2w, G + p.ln2b, g->dln, LLMK_F32, a.res2,
                                      P + p.ln2w, a.ln2_mean, a.ln2_rstd, BT, C, LLMK_ACCUM_DINP, ws, wsb, s));
     // attproj: dW = dres^T atty, db = colsum(dres), datty = dres Wproj
-    LLMK_TRY(llmk_gemm(G + p.attprojw, LLMK_F32, C, g->dres_bf16, 1, C, a.atty, 1, C, LLMK_MATH_BF16, C, C, BT, nullptr,
-                       ws, wsb, s));
+    LLMK_TRY(llmk_gemm(G + p.attprojw, LLMK_F32, C, dres_op, 1, C, a.atty, 1, C, mm, C, C, BT, nullptr, ws, wsb, s));
     LLMK_TRY(llmk_colsum(G + p.attprojb, g->dres, LLMK_F32, BT, C, 0, ws, wsb, s));
-    LLMK_TRY(llmk_gemm(g->datty, LLMK_BF16, C, g->dres_bf16, 0, C, Pb + p.attprojw, 1, C, LLMK_MATH_BF16, BT, C, C,
-                       nullptr, nullptr, 0, s));
+    LLMK_TRY(llmk_gemm(g->datty, adt, C, dres_op, 0, C, W(p.attprojw), 1, C, mm, BT, C, C, nullptr, nullptr, 0, s));
     // attention
-    LLMK_TRY(llmk_attention_backward(g->dqkv, g->datty, a.atty, a.qkv, a.lse, B, T, 3 * C, NH, ws, wsb, s));
+    if (bf) {
+      LLMK_TRY(llmk_attention_backward(g->dqkv, g->datty, a.atty, a.qkv, a.lse, B, T, 3 * C, NH, ws, wsb, s));
+    } else {
+      LLMK_TRY(llmk_cast(g->datty16, LLMK_BF16, g->datty, LLMK_F32, static_cast<long long>(BT) * C, s));
+      LLMK_TRY(llmk_attention_backward(g->dqkv16, g->datty16, a.atty16, a.qkv16, a.lse, B, T, 3 * C, NH, ws, wsb, s));
+      LLMK_TRY(llmk_cast(g->dqkv, LLMK_F32, g->dqkv16, LLMK_BF16, static_cast<long long>(BT) * 3 * C, s));
+    }
     // qkv: dW = dqkv^T ln1, db = colsum(dqkv), dln1 = dqkv Wqkv
-    LLMK_TRY(llmk_gemm(G + p.qkvw, LLMK_F32, C, g->dqkv, 1, 3 * C, a.ln1, 1, C, LLMK_MATH_BF16, 3 * C, C, BT, nullptr,
-                       ws, wsb, s));
-    LLMK_TRY(llmk_colsum(G + p.qkvb, g->dqkv, LLMK_BF16, BT, 3 * C, 0, ws, wsb, s));
-    LLMK_TRY(llmk_gemm(g->dln, LLMK_F32, C, g->dqkv, 0, 3 * C, Pb + p.qkvw, 1, C, LLMK_MATH_BF16, BT, C, 3 * C, nullptr,
-                       nullptr, 0, s));
+    LLMK_TRY(llmk_gemm(G + p.qkvw, LLMK_F32, C, g->dqkv, 1, 3 * C, a.ln1, 1, C, mm, 3 * C, C, BT, nullptr, ws, wsb, s));
+    LLMK_TRY(llmk_colsum(G + p.qkvb, g->dqkv, adt, BT, 3 * C, 0, ws, wsb, s));
+    LLMK_TRY(llmk_gemm(g->dln, LLMK_F32, C, g->dqkv, 0, 3 * C, W(p.qkvw), 1, C, mm, BT, C, 3 * C, nullptr, nullptr, 0, s));
     // ln1: dres += LN1 backward (dres becomes d(layer input))
-    LLMK_TRY(llmk_layernorm_backward(g->dres, g->dres_bf16, G + p.ln1w, G + p.ln1b, g->dln, LLMK_F32, x, P + p.ln1w,
+    LLMK_TRY(llmk_layernorm_backward(g->dres, dres_mirror, G + p.ln1w, G + p.ln1b, g->dln, LLMK_F32, x, P + p.ln1w,
                                      a.ln1_mean, a.ln1_rstd, BT, C, LLMK_ACCUM_DINP, ws, wsb, s));
     // this layer's gradients are final: reduce them while the layers below run
     LLMK_TRY(allreduce_bucket(g, g->layer_done[l], p.begin, p.end));
@@ -619,7 +666,8 @@ int llmk_gpt2_broadcast_parameters(llmk_gpt2* g, int root) {
   if (g->world <= 1) return LLMK_OK;
   LLMK_TRY(nccl_check(ncclBroadcast(g->params, g->params, g->nparams, ncclFloat, root, g->comm, g->stream),
                       "ncclBroadcast"));
-  LLMK_TRY(llmk_cast(g->params_bf16, LLMK_BF16, g->params, LLMK_F32, static_cast<long long>(g->nparams), g->stream));
+  if (g->params_bf16)
+    LLMK_TRY(llmk_cast(g->params_bf16, LLMK_BF16, g->params, LLMK_F32, static_cast<long long>(g->nparams), g->stream));
   LLMK_CUDA(cudaStreamSynchronize(g->stream));
   return LLMK_OK;
 }

@@ -2,7 +2,7 @@
 // tcgen05 (TMEM alloc / MMA / commit / ld) and the shared-memory and
 // instruction descriptors the tcgen05 MMAs consume.
 //
-// Every wait in this file is bounded: a spin that exceeds kWaitLimitNs sets
+// Every wait in this file is bounded: a spin that exceeds kWaitLimitCycles sets
 // LLMK_DEV_TIMEOUT in the caller's device status word and returns false so the
 // kernel can unwind (free TMEM, return) instead of hanging the GPU.
 #pragma once
@@ -16,8 +16,10 @@
 
 namespace llmk {
 
-// ~1 s: far above any legitimate wait inside one kernel launch.
-constexpr unsigned long long kWaitLimitNs = 1000ull * 1000ull * 1000ull;
+// ~1 s at B200 clocks (2e9 SM cycles), or 2^24 polls: far above any
+// legitimate wait inside one kernel launch.
+constexpr long long kWaitLimitCycles = 2000ll * 1000ll * 1000ll;
+constexpr unsigned int kWaitLimitIters = 1u << 24;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -62,11 +64,13 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int* status,
                                           volatile int* abort_flag, int site = 0) {
   if (mbar_test(bar, parity)) return true;
-  unsigned long long t0 = global_timer_ns();
-  while (true) {
+  // Two independent bounds: SM cycles (clock64 always advances) and an
+  // iteration count, so the wait ends even if one counter misbehaves.
+  const long long c0 = clock64();
+  for (unsigned int it = 0;; ++it) {
     if (mbar_test(bar, parity)) return true;
     if (abort_flag != nullptr && *abort_flag) return false;
-    if (global_timer_ns() - t0 > kWaitLimitNs) {
+    if (clock64() - c0 > kWaitLimitCycles || it > kWaitLimitIters) {
       if (status) atomicOr(status, LLMK_DEV_TIMEOUT | (1u << (8 + (site & 23))));
       if (abort_flag) *abort_flag = 1;
       return false;

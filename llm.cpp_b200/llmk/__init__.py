@@ -16,7 +16,7 @@ LIB_PATH = os.path.join(os.path.dirname(_HERE), "libllmk.so")
 
 F32, BF16 = 0, 1
 MATH_BF16, MATH_TF32 = 1, 2
-EPI_ACCUMULATE, EPI_GELU, EPI_GELU_BWD = 1, 2, 4
+EPI_ACCUMULATE, EPI_GELU, EPI_GELU_BWD, EPI_AUX_F32 = 1, 2, 4, 8
 ACCUM_DINP, ACCUM_DWEIGHT, ACCUM_DBIAS, ACCUM_DPARAM = 1, 2, 4, 8
 DEV_TIMEOUT = 1
 
@@ -77,7 +77,7 @@ SIGNATURES: dict[str, tuple] = {
     # model (include/llmk_gpt2.h)
     "llmk_gpt2_num_parameters": (sz, [C.POINTER(GPT2Config)]),
     "llmk_gpt2_parameter_count": (sz, [vp]),
-    "llmk_gpt2_create": (i32, [C.POINTER(vp), C.POINTER(GPT2Config), i32, i32, vp]),
+    "llmk_gpt2_create": (i32, [C.POINTER(vp), C.POINTER(GPT2Config), i32, i32, i32, vp]),
     "llmk_gpt2_destroy": (i32, [vp]),
     "llmk_gpt2_stream": (i32, [vp, C.POINTER(vp)]),
     "llmk_gpt2_buffers": (i32, [vp, C.POINTER(vp), C.POINTER(vp)]),
@@ -179,11 +179,11 @@ class GPT2:
     """Handle to the native trainer (include/llmk_gpt2.h)."""
 
     def __init__(self, B: int, T: int, max_seq_len=1024, vocab_size=50257, padded_vocab_size=50304, num_layers=12,
-                 num_heads=12, channels=768, stream=None):
+                 num_heads=12, channels=768, math=MATH_BF16, stream=None):
         self.cfg = GPT2Config(max_seq_len, vocab_size, padded_vocab_size, num_layers, num_heads, channels)
         self.B, self.T = B, T
         h = C.c_void_p()
-        call("llmk_gpt2_create", C.byref(h), C.byref(self.cfg), B, T, stream)
+        call("llmk_gpt2_create", C.byref(h), C.byref(self.cfg), B, T, math, stream)
         self.h = h
         self.n = lib().llmk_gpt2_parameter_count(self.h)
 

@@ -52,8 +52,11 @@ def test_attention_vs_oracle(cuda_dev, B, T, NH):
     O.orc().orc_attention_backward(dqkv_o, O.f32a(dout), O.f32a(qkv), att, B, T, C, NH)
     assert max_rel_err(out_g, out_o) < 1e-2, max_rel_err(out_g, out_o)
     assert max_rel_err(lse_g, lse_o) < 1e-2
+    # relative to the largest gradient entry of dQ|dK|dV: for T = 1 the true dQ
+    # and dK are exactly zero (softmax over one key), so a per-part scale is empty
+    scale = np.abs(dqkv_o).max()
     for name, sl in (("dq", slice(0, C)), ("dk", slice(C, 2 * C)), ("dv", slice(2 * C, 3 * C))):
-        e = max_rel_err(dqkv_g[..., sl], dqkv_o[..., sl])
+        e = np.abs(dqkv_g[..., sl] - dqkv_o[..., sl]).max() / scale
         assert e < 1e-2, f"{name} max_rel={e:.3e}"
 
 

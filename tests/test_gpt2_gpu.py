@@ -3,8 +3,11 @@
 test_config0_loss_trajectory: configuration 0 of the benchmark spec (GPT-2
 124M, B=4, T=64, seed 1337, AdamW lr 3e-4, 20 steps on one fixed batch).
 The expected losses are the reference's own (llm.cpp gpt2/*.cpp compiled and
-run by tests/golden/make_fixtures.py); the bar is |L_gpu - L_ref| / L_ref <=
-0.5% at every step.
+run by tests/golden/make_fixtures.py). In TF32 mode (fp32 activations, TF32
+GEMMs: the reference GPU path's precision) the bar is |L_gpu - L_ref| / L_ref
+<= 0.5% at every step. The bf16 mode (bf16 GEMM operands and activations) is
+held to 2%: this run overfits one batch from loss 11 to 2 in 20 steps, and
+bf16 rounding of every activation compounds over the steps.
 """
 import json
 import os
@@ -19,14 +22,16 @@ pytestmark = pytest.mark.gpu
 HERE = os.path.dirname(os.path.abspath(__file__))
 
 
-def _model(llmk, cfg, B, T):
+def _model(llmk, cfg, B, T, math):
     return llmk.GPT2(B, T, max_seq_len=cfg.max_seq_len, vocab_size=cfg.vocab_size,
                      padded_vocab_size=cfg.padded_vocab_size, num_layers=cfg.num_layers, num_heads=cfg.num_heads,
-                     channels=cfg.channels)
+                     channels=cfg.channels, math=math)
 
 
-def test_config0_loss_trajectory(cuda_dev):
+@pytest.mark.parametrize("mathname,bar", [("tf32", 5e-3), ("bf16", 2e-2)])
+def test_config0_loss_trajectory(cuda_dev, mathname, bar):
     import llmk
+    math = llmk.MATH_TF32 if mathname == "tf32" else llmk.MATH_BF16
     fx = json.load(open(os.path.join(HERE, "golden", "gpt2_124m_b4t64_losses.json")))
     cfg = O.config()
     B, T, steps = fx["B"], fx["T"], fx["steps"]
@@ -35,22 +40,25 @@ def test_config0_loss_trajectory(cuda_dev):
     toks = O.tokens(B * T + 1, cfg.vocab_size, fx["seed"])
     assert toks[:8].tolist() == fx["tokens_head"]
     inp, tgt = toks[:-1], toks[1:]
-    m = _model(llmk, cfg, B, T)
+    m = _model(llmk, cfg, B, T, math)
     m.load_parameters(params)
     losses = [m.train_step(inp, tgt, fx["lr"], t=s + 1) for s in range(steps)]
     ref = fx["losses"]
     rel = [abs(a - b) / b for a, b in zip(losses, ref)]
-    print("gpu", [round(x, 4) for x in losses])
-    print("ref", [round(x, 4) for x in ref])
-    print("rel", [f"{x:.2e}" for x in rel])
-    assert max(rel) <= 5e-3, rel
+    print(mathname, "gpu", [round(x, 4) for x in losses])
+    print(mathname, "ref", [round(x, 4) for x in ref])
+    print(mathname, "rel", [f"{x:.2e}" for x in rel])
+    assert max(rel) <= bar, rel
     assert llmk.device_status() == 0
     m.close()
 
 
-def test_small_model_gradients_vs_oracle(cuda_dev):
-    """One forward/backward of a 2-layer model: loss and every gradient tensor vs the oracle."""
+@pytest.mark.parametrize("mathname,tol", [("tf32", 1e-2), ("bf16", 5e-2)])
+def test_small_model_gradients_vs_oracle(cuda_dev, mathname, tol):
+    """One forward/backward of a 2-layer model: loss and every gradient tensor vs the oracle
+    (norm-wise relative error, the reference tests' isApprox metric)."""
     import llmk
+    math = llmk.MATH_TF32 if mathname == "tf32" else llmk.MATH_BF16
     cfg = O.config(max_seq_len=128, vocab_size=1000, padded_vocab_size=1024, num_layers=2, num_heads=2, channels=128)
     B, T = 2, 128
     params = O.init_params(cfg, 7)
@@ -61,12 +69,12 @@ def test_small_model_gradients_vs_oracle(cuda_dev):
     ref.zero_grad()
     ref.backward()
     g_ref = ref.grads()
-    m = _model(llmk, cfg, B, T)
+    m = _model(llmk, cfg, B, T, math)
     m.load_parameters(params)
     # lr = 0: the step leaves the parameters unchanged and exposes the gradients
     loss = m.train_step(inp, tgt, 0.0, t=1)
     g = m.read_gradients()
-    assert abs(loss - loss_ref) / loss_ref < 1e-2, (loss, loss_ref)
+    assert abs(loss - loss_ref) / loss_ref < 1e-3, (loss, loss_ref)
     sizes = O.param_sizes(cfg)
     names = ["wte", "wpe", "ln1w", "ln1b", "qkvw", "qkvb", "attprojw", "attprojb", "ln2w", "ln2b", "fcw", "fcb",
              "fcprojw", "fcprojb", "lnfw", "lnfb"]
@@ -75,6 +83,6 @@ def test_small_model_gradients_vs_oracle(cuda_dev):
         a, b = g[off:off + n].astype(np.float64), g_ref[off:off + n].astype(np.float64)
         off += n
         nrm = np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30)
-        assert nrm < 5e-2, f"{name}: norm-rel err {nrm:.3e}"
+        assert nrm < tol, f"{name}: norm-rel err {nrm:.3e}"
     assert np.array_equal(m.read_parameters(), params)
     m.close()
