@@ -118,6 +118,24 @@ size_t llmk_colsum_workspace(int M, int N);
 int llmk_colsum(float* dbias, const void* x, llmk_dtype x_dtype, int M, int N, int accumulate, void* workspace,
                 size_t workspace_bytes, void* stream);
 
+/* llmk_colsum for callers that cannot allocate device memory when they call
+ * it: code that runs inside another framework's memory pool or under a fixed
+ * memory budget where cudaMalloc after start-up is not allowed, or that must
+ * not stall its stream (cudaMalloc can synchronise the device). It takes no
+ * workspace: its partial sums live in a fixed array inside the library (1 MiB,
+ * held by every GPU that loads the library until the process exits), so it
+ * calls no cudaMalloc / cudaFree and allocates nothing. Limit: the partial
+ * sums of one call (about 2 x SMs / ceil(N / 256) rows of N floats) must fit
+ * in 262144 floats; larger M x N is rejected with LLMK_ERR_UNSUPPORTED (use
+ * llmk_colsum). The first call on a device looks up the array's device
+ * address with that device current; make that first call before any stream
+ * capture. All calls share the array: calls that can overlap on the GPU
+ * (different streams, or different host threads on one device) race and must
+ * be serialised by the caller. Results equal llmk_colsum's.
+ * No counterpart in the reference: its column sum takes no scratch
+ * (gpt2/cuda/matmul.cu:26-187). */
+int llmk_colsum_noalloc(float* dbias, const void* x, llmk_dtype x_dtype, int M, int N, int accumulate, void* stream);
+
 /* ------------------------------------------------------------ attention */
 /* Causal multi-head attention, head size 64, bf16 in/out, fp32 softmax and
  * accumulation. qkv: (B, T, C3) bf16, Q|K|V blocks of C = C3/3 columns, head

@@ -6,6 +6,8 @@
 // The reference runs the weight gradient as B batched GEMMs writing the same
 // output (matmul.cu:430-435); here it is one GEMM with K = B*T.
 #include <algorithm>
+#include <mutex>
+#include <string>
 
 #include "ptx.cuh"
 #include "runtime.h"
@@ -95,6 +97,15 @@ size_t colsum_workspace(int M, int N) {
   return static_cast<size_t>(colsum_chunks(M, N)) * N * sizeof(float);
 }
 
+// Scratch of llmk_colsum_noalloc: a fixed device array that every GPU loading
+// this library holds until the process exits (1 MiB). Host code must not pass
+// `g_colsum_noalloc_scratch` itself to a kernel (on the host it names a
+// host-side stand-in); it passes the device address fetched once per device.
+constexpr int kColsumNoAllocFloats = 1 << 18;
+static __device__ __align__(256) float g_colsum_noalloc_scratch[kColsumNoAllocFloats];
+static float* g_colsum_noalloc_ptr[64] = {};
+static std::mutex g_colsum_noalloc_mu;
+
 }  // namespace llmk
 
 using namespace llmk;
@@ -110,6 +121,39 @@ int llmk_colsum(float* dbias, const void* x, llmk_dtype x_dtype, int M, int N, i
   if (!workspace || workspace_bytes < colsum_workspace(M, N))
     return fail(LLMK_ERR_WORKSPACE, "colsum: workspace too small");
   return colsum_launch(dbias, x, x_dtype == LLMK_BF16, M, N, accumulate, static_cast<float*>(workspace),
+                       static_cast<cudaStream_t>(stream));
+}
+
+// Column sum for callers that may not allocate device memory (see llmk.h).
+// The first call on a device resolves the device address of the file-scope
+// scratch array with that device current; later calls reuse it.
+int llmk_colsum_noalloc(float* dbias, const void* x, llmk_dtype x_dtype, int M, int N, int accumulate, void* stream) {
+  if (!dbias || !x || M <= 0 || N <= 0) return fail(LLMK_ERR_INVALID_ARG, "colsum_noalloc: bad arguments");
+  if (N % 8 || !aligned16(x))
+    return fail(LLMK_ERR_UNSUPPORTED, "colsum_noalloc: N % 8 == 0 and 16-byte alignment required");
+  const size_t need = static_cast<size_t>(colsum_chunks(M, N)) * N;
+  if (need > static_cast<size_t>(kColsumNoAllocFloats))
+    return fail(LLMK_ERR_UNSUPPORTED,
+                "colsum_noalloc: M x N needs " + std::to_string(need) + " scratch floats, more than the fixed " +
+                    std::to_string(kColsumNoAllocFloats) + " (use llmk_colsum with a caller workspace)");
+  int dev = 0;
+  LLMK_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return fail(LLMK_ERR_UNSUPPORTED, "colsum_noalloc: device index out of range");
+  float* scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_colsum_noalloc_mu);
+    if (!g_colsum_noalloc_ptr[dev]) {
+      void* p = nullptr;
+      cudaError_t e = cudaGetSymbolAddress(&p, g_colsum_noalloc_scratch);
+      if (e != cudaSuccess || p == nullptr)
+        return fail(LLMK_ERR_CUDA, std::string("colsum_noalloc: cudaGetSymbolAddress: ") + cudaGetErrorString(e));
+      g_colsum_noalloc_ptr[dev] = static_cast<float*>(p);
+    }
+    scratch = g_colsum_noalloc_ptr[dev];
+  }
+  // Pass 1 overwrites every partial that pass 2 reads, so nothing in the
+  // shared scratch has to start at zero.
+  return colsum_launch(dbias, x, x_dtype == LLMK_BF16, M, N, accumulate, scratch,
                        static_cast<cudaStream_t>(stream));
 }
 

@@ -57,6 +57,7 @@ SIGNATURES: dict[str, tuple] = {
     "llmk_matmul_backward": (i32, [vp, i32, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, vp, sz, vp]),
     "llmk_colsum_workspace": (sz, [i32, i32]),
     "llmk_colsum": (i32, [vp, vp, i32, i32, i32, i32, vp, sz, vp]),
+    "llmk_colsum_noalloc": (i32, [vp, vp, i32, i32, i32, i32, vp]),
     "llmk_attention_forward": (i32, [vp, vp, vp, i32, i32, i32, i32, vp]),
     "llmk_attention_backward_workspace": (sz, [i32, i32, i32, i32]),
     "llmk_attention_backward": (i32, [vp, vp, vp, vp, vp, i32, i32, i32, i32, vp, sz, vp]),
