@@ -166,16 +166,18 @@ int llmk_layernorm_forward(void* out, llmk_dtype out_dtype, float* mean, float* 
 
 /* dinp (+)= LN backward (LLMK_ACCUM_DINP selects +=); dgamma, dbeta (+)=
  * (LLMK_ACCUM_DPARAM selects +=, as the reference). dinp_bf16 (optional)
- * receives a bf16 copy of the final dinp. dout fp32 or bf16.
- * workspace >= llmk_layernorm_backward_workspace(N, C) (per-block partials,
- * reduced in a fixed order: deterministic).
+ * receives a bf16 copy of the final dinp; dinp_colsum (optional, [C]) the
+ * column sums of the final dinp (overwritten) — the bias gradient of a linear
+ * layer whose output gradient is dinp, fused here instead of a separate pass.
+ * dout fp32 or bf16. workspace >= llmk_layernorm_backward_workspace(N, C)
+ * (per-block partials, reduced in a fixed order: deterministic).
  * Replaces gpt2cuda::BatchLayerNormBackward, gpt2/cuda/layernorm.cu:351-353. */
 #define LLMK_ACCUM_DPARAM 8
 size_t llmk_layernorm_backward_workspace(int N, int C);
-int llmk_layernorm_backward(float* dinp, void* dinp_bf16, float* dgamma, float* dbeta, const void* dout,
-                            llmk_dtype dout_dtype, const float* inp, const float* gamma, const float* mean,
-                            const float* rstd, int N, int C, int flags, void* workspace, size_t workspace_bytes,
-                            void* stream);
+int llmk_layernorm_backward(float* dinp, void* dinp_bf16, float* dgamma, float* dbeta, float* dinp_colsum,
+                            const void* dout, llmk_dtype dout_dtype, const float* inp, const float* gamma,
+                            const float* mean, const float* rstd, int N, int C, int flags, void* workspace,
+                            size_t workspace_bytes, void* stream);
 
 /* --------------------------------------------------- elementwise helpers */
 /* GELU (tanh form, gpt2/gelu.h:7-8) forward / backward over n elements
@@ -198,9 +200,11 @@ int llmk_encoder_forward(float* out, const int* tokens, const float* wte, const 
                          void* stream);
 /* dwte[tokens[b,t],:] += dout[b,t,:]; dwpe[t,:] += sum_b dout[b,t,:]. Summed
  * in position order (deterministic; the reference scatters with float
- * atomicAdd, encoder.cu:17-25). workspace >= llmk_encoder_backward_workspace(B,T). */
+ * atomicAdd, encoder.cu:17-25): positions are sorted by token in one CTA when
+ * B*T <= 32768 and V < 2^17, and linked by a scan otherwise. V = rows of dwte.
+ * workspace >= llmk_encoder_backward_workspace(B,T). */
 size_t llmk_encoder_backward_workspace(int B, int T);
-int llmk_encoder_backward(float* dwte, float* dwpe, const float* dout, const int* tokens, int B, int T, int C,
+int llmk_encoder_backward(float* dwte, float* dwpe, const float* dout, const int* tokens, int B, int T, int C, int V,
                           void* workspace, size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------ softmax + cross-entropy */

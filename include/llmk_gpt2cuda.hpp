@@ -140,7 +140,7 @@ void BatchLayerNormBackward(Vec& d_inputs, Vec& d_gamma, Vec& d_beta, const Vec&
                             const Vec& gamma, const Vec& means, const Vec& rstds, int B, int T, int C,
                             cudaStream_t stream) {
   const size_t ws = llmk_layernorm_backward_workspace(B * T, C);
-  llmk_detail::check(llmk_layernorm_backward(d_inputs.data(), nullptr, d_gamma.data(), d_beta.data(),
+  llmk_detail::check(llmk_layernorm_backward(d_inputs.data(), nullptr, d_gamma.data(), d_beta.data(), nullptr,
                                              d_outputs.data(), LLMK_F32, inputs.data(), gamma.data(), means.data(),
                                              rstds.data(), B * T, C, LLMK_ACCUM_DINP | LLMK_ACCUM_DPARAM,
                                              llmk_detail::scratch(ws), ws, stream),
@@ -189,10 +189,9 @@ void BatchEncoderForward(VecF& outputs, const VecI& inputs, const VecF& wte, con
 template <class VecF, class VecI>
 void BatchEncoderBackward(VecF& d_wte, VecF& d_wpe, const VecF& d_outputs, const VecI& inputs, int B, int T, int C,
                           int Vp, int MaxT, cudaStream_t stream) {
-  (void)Vp;
   (void)MaxT;
   const size_t ws = llmk_encoder_backward_workspace(B, T);
-  llmk_detail::check(llmk_encoder_backward(d_wte.data(), d_wpe.data(), d_outputs.data(), inputs.data(), B, T, C,
+  llmk_detail::check(llmk_encoder_backward(d_wte.data(), d_wpe.data(), d_outputs.data(), inputs.data(), B, T, C, Vp,
                                            llmk_detail::scratch(ws), ws, stream),
                      "BatchEncoderBackward");
 }

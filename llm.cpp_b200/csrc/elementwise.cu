@@ -58,8 +58,10 @@ __device__ __forceinline__ float warp_max(float v) {
 
 // ------------------------------------------------------------ LayerNorm
 // One warp per row; two-pass mean / variance as the reference CPU path
-// (gpt2/layernorm.cpp:16-23). The row is re-read from L1 for each pass.
-template <typename OutT>
+// (gpt2/layernorm.cpp:16-23). kV > 0: C == 128 * kV and the row stays in
+// registers between the passes (one global read); kV == 0: any C % 4 == 0,
+// the row is re-read from L1 for each pass.
+template <typename OutT, int kV>
 __global__ void __launch_bounds__(256) layernorm_fwd_kernel(OutT* __restrict__ out, float* __restrict__ mean,
                                                             float* __restrict__ rstd, const float* __restrict__ inp,
                                                             const float* __restrict__ gamma,
@@ -68,24 +70,50 @@ __global__ void __launch_bounds__(256) layernorm_fwd_kernel(OutT* __restrict__ o
   const int lane = threadIdx.x & 31;
   if (row >= N) return;
   const float* x = inp + static_cast<long long>(row) * C;
-  float s = 0.f;
-  for (int c = lane * 4; c < C; c += 128) {
-    float4 v = ld4(x + c);
-    s += (v.x + v.y) + (v.z + v.w);
-  }
-  const float m = warp_sum(s) / C;
-  float q = 0.f;
-  for (int c = lane * 4; c < C; c += 128) {
-    float4 v = ld4(x + c);
-    float a = v.x - m, b = v.y - m, d = v.z - m, e = v.w - m;
-    q += (a * a + b * b) + (d * d + e * e);
-  }
-  const float r = rsqrtf(warp_sum(q) / C + 1e-5f);
   OutT* y = out + static_cast<long long>(row) * C;
-  for (int c = lane * 4; c < C; c += 128) {
-    float4 v = ld4(x + c), g = ld4(gamma + c), b = ld4(beta + c);
-    st4(y + c, make_float4((v.x - m) * r * g.x + b.x, (v.y - m) * r * g.y + b.y, (v.z - m) * r * g.z + b.z,
-                           (v.w - m) * r * g.w + b.w));
+  float m, r;
+  if constexpr (kV > 0) {
+    float4 v[kV];
+    float s = 0.f;
+#pragma unroll
+    for (int k = 0; k < kV; ++k) {
+      v[k] = ld4(x + lane * 4 + k * 128);
+      s += (v[k].x + v[k].y) + (v[k].z + v[k].w);
+    }
+    m = warp_sum(s) / C;
+    float q = 0.f;
+#pragma unroll
+    for (int k = 0; k < kV; ++k) {
+      float a = v[k].x - m, b = v[k].y - m, d = v[k].z - m, e = v[k].w - m;
+      q += (a * a + b * b) + (d * d + e * e);
+    }
+    r = rsqrtf(warp_sum(q) / C + 1e-5f);
+#pragma unroll
+    for (int k = 0; k < kV; ++k) {
+      const int c = lane * 4 + k * 128;
+      float4 g = ld4(gamma + c), b = ld4(beta + c);
+      st4(y + c, make_float4((v[k].x - m) * r * g.x + b.x, (v[k].y - m) * r * g.y + b.y,
+                             (v[k].z - m) * r * g.z + b.z, (v[k].w - m) * r * g.w + b.w));
+    }
+  } else {
+    float s = 0.f;
+    for (int c = lane * 4; c < C; c += 128) {
+      float4 v = ld4(x + c);
+      s += (v.x + v.y) + (v.z + v.w);
+    }
+    m = warp_sum(s) / C;
+    float q = 0.f;
+    for (int c = lane * 4; c < C; c += 128) {
+      float4 v = ld4(x + c);
+      float a = v.x - m, b = v.y - m, d = v.z - m, e = v.w - m;
+      q += (a * a + b * b) + (d * d + e * e);
+    }
+    r = rsqrtf(warp_sum(q) / C + 1e-5f);
+    for (int c = lane * 4; c < C; c += 128) {
+      float4 v = ld4(x + c), g = ld4(gamma + c), b = ld4(beta + c);
+      st4(y + c, make_float4((v.x - m) * r * g.x + b.x, (v.y - m) * r * g.y + b.y, (v.z - m) * r * g.z + b.z,
+                             (v.w - m) * r * g.w + b.w));
+    }
   }
   if (lane == 0) {
     if (mean) mean[row] = m;
@@ -94,10 +122,11 @@ __global__ void __launch_bounds__(256) layernorm_fwd_kernel(OutT* __restrict__ o
 }
 
 // dx = rstd * (g*dy - mean(g*dy) - xhat * mean(g*dy*xhat)) (gpt2/layernorm.cpp:60-69);
-// dinp (+)= dx; optional bf16 copy of the new dinp. Each warp accumulates
-// dgamma/dbeta of its rows into its own smem slice; the block then reduces
-// the slices in warp order into partial[block][2][C].
-template <typename DoutT>
+// dinp (+)= dx; optional bf16 copy of the new dinp. Each warp accumulates, for
+// the rows it handles, dgamma (dy*xhat), dbeta (dy) and the column sums of the
+// final dinp into its own smem slice [3][C]; the block then reduces the
+// slices in warp order into partial[block][3][C]. kV as in the forward.
+template <typename DoutT, int kV>
 __global__ void __launch_bounds__(256) layernorm_bwd_kernel(float* __restrict__ dinp, __nv_bfloat16* __restrict__ dinp_bf16,
                                                             float* __restrict__ partial, const DoutT* __restrict__ dout,
                                                             const float* __restrict__ inp,
@@ -105,69 +134,120 @@ __global__ void __launch_bounds__(256) layernorm_bwd_kernel(float* __restrict__ 
                                                             const float* __restrict__ mean,
                                                             const float* __restrict__ rstd, int N, int C,
                                                             int rows_per_block, int accumulate) {
-  extern __shared__ float sm[];  // [warps][2][C]
+  extern __shared__ float sm[];  // [warps][3][C]
   const int warps = blockDim.x / 32;
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  float* dg = sm + static_cast<size_t>(w) * 2 * C;
+  float* dg = sm + static_cast<size_t>(w) * 3 * C;
   float* db = dg + C;
-  for (int c = lane; c < C; c += 32) {
-    dg[c] = 0.f;
-    db[c] = 0.f;
-  }
+  float* ds = db + C;
+  for (int c = lane; c < 3 * C; c += 32) dg[c] = 0.f;
   __syncwarp();
   const int r0 = blockIdx.x * rows_per_block;
   const int r1 = min(N, r0 + rows_per_block);
   for (int row = r0 + w; row < r1; row += warps) {
     const DoutT* dy = dout + static_cast<long long>(row) * C;
     const float* x = inp + static_cast<long long>(row) * C;
+    float* dx = dinp + static_cast<long long>(row) * C;
     const float m = mean[row], r = rstd[row];
     float s1 = 0.f, s2 = 0.f;
-    for (int c = lane * 4; c < C; c += 128) {
-      float4 d = ld4(dy + c), v = ld4(x + c), g = ld4(gamma + c);
-      float4 xh = make_float4((v.x - m) * r, (v.y - m) * r, (v.z - m) * r, (v.w - m) * r);
-      float4 gd = make_float4(g.x * d.x, g.y * d.y, g.z * d.z, g.w * d.w);
-      s1 += (gd.x + gd.y) + (gd.z + gd.w);
-      s2 += (gd.x * xh.x + gd.y * xh.y) + (gd.z * xh.z + gd.w * xh.w);
-      float4 a = ld4(dg + c), b = ld4(db + c);
-      st4(dg + c, make_float4(a.x + d.x * xh.x, a.y + d.y * xh.y, a.z + d.z * xh.z, a.w + d.w * xh.w));
-      st4(db + c, make_float4(b.x + d.x, b.y + d.y, b.z + d.z, b.w + d.w));
-    }
-    s1 = warp_sum(s1) / C;
-    s2 = warp_sum(s2) / C;
-    float* dx = dinp + static_cast<long long>(row) * C;
-    for (int c = lane * 4; c < C; c += 128) {
-      float4 d = ld4(dy + c), v = ld4(x + c), g = ld4(gamma + c);
-      float4 o;
-      o.x = r * ((g.x * d.x - (v.x - m) * r * s2) - s1);
-      o.y = r * ((g.y * d.y - (v.y - m) * r * s2) - s1);
-      o.z = r * ((g.z * d.z - (v.z - m) * r * s2) - s1);
-      o.w = r * ((g.w * d.w - (v.w - m) * r * s2) - s1);
-      if (accumulate) {
-        float4 p = ld4(dx + c);
-        o.x += p.x; o.y += p.y; o.z += p.z; o.w += p.w;
+    if constexpr (kV > 0) {
+      float4 d[kV], xh[kV];
+#pragma unroll
+      for (int k = 0; k < kV; ++k) {
+        const int c = lane * 4 + k * 128;
+        d[k] = ld4(dy + c);
+        float4 v = ld4(x + c), g = ld4(gamma + c);
+        xh[k] = make_float4((v.x - m) * r, (v.y - m) * r, (v.z - m) * r, (v.w - m) * r);
+        float4 gd = make_float4(g.x * d[k].x, g.y * d[k].y, g.z * d[k].z, g.w * d[k].w);
+        s1 += (gd.x + gd.y) + (gd.z + gd.w);
+        s2 += (gd.x * xh[k].x + gd.y * xh[k].y) + (gd.z * xh[k].z + gd.w * xh[k].w);
       }
-      st4(dx + c, o);
-      if (dinp_bf16) st4(dinp_bf16 + static_cast<long long>(row) * C + c, o);
+      s1 = warp_sum(s1) / C;
+      s2 = warp_sum(s2) / C;
+#pragma unroll
+      for (int k = 0; k < kV; ++k) {
+        const int c = lane * 4 + k * 128;
+        float4 g = ld4(gamma + c);
+        float4 o;
+        o.x = r * ((g.x * d[k].x - xh[k].x * s2) - s1);
+        o.y = r * ((g.y * d[k].y - xh[k].y * s2) - s1);
+        o.z = r * ((g.z * d[k].z - xh[k].z * s2) - s1);
+        o.w = r * ((g.w * d[k].w - xh[k].w * s2) - s1);
+        if (accumulate) {
+          float4 p = ld4(dx + c);
+          o.x += p.x; o.y += p.y; o.z += p.z; o.w += p.w;
+        }
+        st4(dx + c, o);
+        if (dinp_bf16) st4(dinp_bf16 + static_cast<long long>(row) * C + c, o);
+        float4 a = ld4(dg + c), b = ld4(db + c), e = ld4(ds + c);
+        st4(dg + c, make_float4(a.x + d[k].x * xh[k].x, a.y + d[k].y * xh[k].y, a.z + d[k].z * xh[k].z,
+                                a.w + d[k].w * xh[k].w));
+        st4(db + c, make_float4(b.x + d[k].x, b.y + d[k].y, b.z + d[k].z, b.w + d[k].w));
+        st4(ds + c, make_float4(e.x + o.x, e.y + o.y, e.z + o.z, e.w + o.w));
+      }
+    } else {
+      for (int c = lane * 4; c < C; c += 128) {
+        float4 d = ld4(dy + c), v = ld4(x + c), g = ld4(gamma + c);
+        float4 xh = make_float4((v.x - m) * r, (v.y - m) * r, (v.z - m) * r, (v.w - m) * r);
+        float4 gd = make_float4(g.x * d.x, g.y * d.y, g.z * d.z, g.w * d.w);
+        s1 += (gd.x + gd.y) + (gd.z + gd.w);
+        s2 += (gd.x * xh.x + gd.y * xh.y) + (gd.z * xh.z + gd.w * xh.w);
+        float4 a = ld4(dg + c), b = ld4(db + c);
+        st4(dg + c, make_float4(a.x + d.x * xh.x, a.y + d.y * xh.y, a.z + d.z * xh.z, a.w + d.w * xh.w));
+        st4(db + c, make_float4(b.x + d.x, b.y + d.y, b.z + d.z, b.w + d.w));
+      }
+      s1 = warp_sum(s1) / C;
+      s2 = warp_sum(s2) / C;
+      for (int c = lane * 4; c < C; c += 128) {
+        float4 d = ld4(dy + c), v = ld4(x + c), g = ld4(gamma + c);
+        float4 o;
+        o.x = r * ((g.x * d.x - (v.x - m) * r * s2) - s1);
+        o.y = r * ((g.y * d.y - (v.y - m) * r * s2) - s1);
+        o.z = r * ((g.z * d.z - (v.z - m) * r * s2) - s1);
+        o.w = r * ((g.w * d.w - (v.w - m) * r * s2) - s1);
+        if (accumulate) {
+          float4 p = ld4(dx + c);
+          o.x += p.x; o.y += p.y; o.z += p.z; o.w += p.w;
+        }
+        st4(dx + c, o);
+        if (dinp_bf16) st4(dinp_bf16 + static_cast<long long>(row) * C + c, o);
+        float4 e = ld4(ds + c);
+        st4(ds + c, make_float4(e.x + o.x, e.y + o.y, e.z + o.z, e.w + o.w));
+      }
     }
   }
   __syncthreads();
-  float* out = partial + static_cast<size_t>(blockIdx.x) * 2 * C;
-  for (int c = threadIdx.x; c < 2 * C; c += blockDim.x) {
+  float* out = partial + static_cast<size_t>(blockIdx.x) * 3 * C;
+  for (int c = threadIdx.x; c < 3 * C; c += blockDim.x) {
     float s = 0.f;
-    for (int k = 0; k < warps; ++k) s += sm[static_cast<size_t>(k) * 2 * C + c];
+    for (int k = 0; k < warps; ++k) s += sm[static_cast<size_t>(k) * 3 * C + c];
     out[c] = s;
   }
 }
 
-// dgamma[c] (+)= sum_b partial[b][0][c]; dbeta likewise from [b][1][c].
-__global__ void layernorm_bwd_reduce(float* __restrict__ dgamma, float* __restrict__ dbeta,
+// dst[c] (+)= sum over blocks of partial[b][c] for the 3C columns
+// (dgamma | dbeta | dinp column sums), in block order: 32 columns x 8 block
+// lanes per CTA, lanes combined in a fixed order.
+__global__ void layernorm_bwd_reduce(float* __restrict__ dgamma, float* __restrict__ dbeta, float* __restrict__ dsum,
                                      const float* __restrict__ partial, int blocks, int C, int accumulate) {
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= 2 * C) return;
+  __shared__ float red[8][33];
+  const int c = blockIdx.x * 32 + threadIdx.x;
   float s = 0.f;
-  for (int b = 0; b < blocks; ++b) s += partial[static_cast<size_t>(b) * 2 * C + c];
-  float* dst = c < C ? dgamma + c : dbeta + (c - C);
-  *dst = accumulate ? *dst + s : s;
+  if (c < 3 * C)
+    for (int b = threadIdx.y; b < blocks; b += 8) s += partial[static_cast<size_t>(b) * 3 * C + c];
+  red[threadIdx.y][threadIdx.x] = s;
+  __syncthreads();
+  if (threadIdx.y != 0 || c >= 3 * C) return;
+  float t = 0.f;
+#pragma unroll
+  for (int y = 0; y < 8; ++y) t += red[y][threadIdx.x];
+  if (c < C) {
+    dgamma[c] = accumulate ? dgamma[c] + t : t;
+  } else if (c < 2 * C) {
+    dbeta[c - C] = accumulate ? dbeta[c - C] + t : t;
+  } else if (dsum) {
+    dsum[c - 2 * C] = t;
+  }
 }
 
 // ------------------------------------------------------------ GELU / residual
@@ -272,6 +352,55 @@ __global__ void encoder_bwd_wte_kernel(float* __restrict__ dwte, const float* __
     st4(dst, make_float4(o.x + s.x, o.y + s.y, o.z + s.z, o.w + s.w));
   }
 }
+// Sorts the keys (token << 15 | position) of BT <= 32768 positions with a
+// bitonic network in one CTA's shared memory (n = next power of two >= BT,
+// padded with 0xFFFFFFFF). Equal tokens end up adjacent, positions ascending.
+constexpr int kSortMaxBT = 32768;
+__global__ void __launch_bounds__(1024) encoder_sort_kernel(unsigned int* __restrict__ sorted,
+                                                            const int* __restrict__ tokens, int BT, int n) {
+  extern __shared__ unsigned int key[];
+  for (int i = threadIdx.x; i < n; i += blockDim.x)
+    key[i] = i < BT ? (static_cast<unsigned int>(tokens[i]) << 15) | static_cast<unsigned int>(i) : 0xFFFFFFFFu;
+  __syncthreads();
+  for (int k = 2; k <= n; k <<= 1) {
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const int ixj = i ^ j;
+        if (ixj > i) {
+          const unsigned int a = key[i], b = key[ixj];
+          const bool ascending = (i & k) == 0;
+          if ((a > b) == ascending) {
+            key[i] = b;
+            key[ixj] = a;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+  for (int i = threadIdx.x; i < BT; i += blockDim.x) sorted[i] = key[i];
+}
+// dwte[tok,:] += sum of dout rows of the positions holding tok, in position
+// order: the first sorted key of each run of equal tokens sums its run.
+__global__ void encoder_bwd_wte_sorted_kernel(float* __restrict__ dwte, const float* __restrict__ dout,
+                                              const unsigned int* __restrict__ sorted, int BT, int C) {
+  const int c4 = C / 4;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < static_cast<long long>(BT) * c4;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int idx = static_cast<int>(i / c4), c = static_cast<int>(i - static_cast<long long>(idx) * c4) * 4;
+    const unsigned int tok = sorted[idx] >> 15;
+    if (idx > 0 && (sorted[idx - 1] >> 15) == tok) continue;
+    float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int j = idx; j < BT && (sorted[j] >> 15) == tok; ++j) {
+      float4 d = ld4(dout + static_cast<long long>(sorted[j] & 0x7FFFu) * C + c);
+      s.x += d.x; s.y += d.y; s.z += d.z; s.w += d.w;
+    }
+    float* dst = dwte + static_cast<long long>(tok) * C + c;
+    float4 o = ld4(dst);
+    st4(dst, make_float4(o.x + s.x, o.y + s.y, o.z + s.z, o.w + s.w));
+  }
+}
+
 // Builds first_of / next_same on the device: for each position, the next
 // later position holding the same token (or -1), and whether no earlier
 // position holds it. O(BT * window) scan per position, bounded by BT.
@@ -434,18 +563,34 @@ static bool a16(const void* p) { return p == nullptr || aligned16(p); }
 
 extern "C" {
 
+}  // extern "C"
+
+template <typename OutT>
+static void ln_fwd_dispatch(OutT* out, float* mean, float* rstd, const float* inp, const float* gamma,
+                            const float* beta, int N, int C, cudaStream_t s) {
+  const int grid = (N + 7) / 8;
+  switch (C % 128 ? 0 : C / 128) {
+    case 4: layernorm_fwd_kernel<OutT, 4><<<grid, 256, 0, s>>>(out, mean, rstd, inp, gamma, beta, N, C); break;
+    case 6: layernorm_fwd_kernel<OutT, 6><<<grid, 256, 0, s>>>(out, mean, rstd, inp, gamma, beta, N, C); break;
+    case 8: layernorm_fwd_kernel<OutT, 8><<<grid, 256, 0, s>>>(out, mean, rstd, inp, gamma, beta, N, C); break;
+    case 10: layernorm_fwd_kernel<OutT, 10><<<grid, 256, 0, s>>>(out, mean, rstd, inp, gamma, beta, N, C); break;
+    case 12: layernorm_fwd_kernel<OutT, 12><<<grid, 256, 0, s>>>(out, mean, rstd, inp, gamma, beta, N, C); break;
+    default: layernorm_fwd_kernel<OutT, 0><<<grid, 256, 0, s>>>(out, mean, rstd, inp, gamma, beta, N, C); break;
+  }
+}
+
+extern "C" {
+
 int llmk_layernorm_forward(void* out, llmk_dtype out_dtype, float* mean, float* rstd, const float* inp,
                            const float* gamma, const float* beta, int N, int C, void* stream) {
   if (!out || !inp || !gamma || !beta || N <= 0 || C <= 0) return fail(LLMK_ERR_INVALID_ARG, "layernorm_forward");
   if (C % 4 || !a16(out) || !a16(inp) || !a16(gamma) || !a16(beta))
     return fail(LLMK_ERR_UNSUPPORTED, "layernorm_forward: C % 4 == 0 and 16-byte alignment required");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const int grid = (N + 7) / 8;
   if (out_dtype == LLMK_BF16)
-    layernorm_fwd_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(static_cast<__nv_bfloat16*>(out), mean, rstd, inp,
-                                                             gamma, beta, N, C);
+    ln_fwd_dispatch(static_cast<__nv_bfloat16*>(out), mean, rstd, inp, gamma, beta, N, C, s);
   else
-    layernorm_fwd_kernel<float><<<grid, 256, 0, s>>>(static_cast<float*>(out), mean, rstd, inp, gamma, beta, N, C);
+    ln_fwd_dispatch(static_cast<float*>(out), mean, rstd, inp, gamma, beta, N, C, s);
   count_launch();
   LLMK_CUDA(cudaGetLastError());
   return LLMK_OK;
@@ -453,40 +598,62 @@ int llmk_layernorm_forward(void* out, llmk_dtype out_dtype, float* mean, float* 
 
 size_t llmk_layernorm_backward_workspace(int N, int C) {
   if (N <= 0 || C <= 0) return 0;
-  return static_cast<size_t>(ln_bwd_blocks(N)) * 2 * C * sizeof(float);
+  return static_cast<size_t>(ln_bwd_blocks(N)) * 3 * C * sizeof(float);
 }
 
-int llmk_layernorm_backward(float* dinp, void* dinp_bf16, float* dgamma, float* dbeta, const void* dout,
-                            llmk_dtype dout_dtype, const float* inp, const float* gamma, const float* mean,
-                            const float* rstd, int N, int C, int flags, void* workspace, size_t workspace_bytes,
-                            void* stream) {
+}  // extern "C"
+
+template <typename DoutT, int kV>
+static int ln_bwd_launch(int blocks, size_t smem, cudaStream_t s, float* dinp, __nv_bfloat16* dinp_bf16, float* part,
+                         const DoutT* dout, const float* inp, const float* gamma, const float* mean, const float* rstd,
+                         int N, int C, int rows_per_block, int acc_in) {
+  auto k = layernorm_bwd_kernel<DoutT, kV>;
+  LLMK_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+  k<<<blocks, 256, smem, s>>>(dinp, dinp_bf16, part, dout, inp, gamma, mean, rstd, N, C, rows_per_block, acc_in);
+  return LLMK_OK;
+}
+
+template <typename DoutT>
+static int ln_bwd_dispatch(int blocks, size_t smem, cudaStream_t s, float* dinp, __nv_bfloat16* dinp_bf16,
+                           float* part, const DoutT* dout, const float* inp, const float* gamma, const float* mean,
+                           const float* rstd, int N, int C, int rows_per_block, int acc_in) {
+  switch (C % 128 ? 0 : C / 128) {
+    case 4: return ln_bwd_launch<DoutT, 4>(blocks, smem, s, dinp, dinp_bf16, part, dout, inp, gamma, mean, rstd, N, C, rows_per_block, acc_in);
+    case 6: return ln_bwd_launch<DoutT, 6>(blocks, smem, s, dinp, dinp_bf16, part, dout, inp, gamma, mean, rstd, N, C, rows_per_block, acc_in);
+    case 8: return ln_bwd_launch<DoutT, 8>(blocks, smem, s, dinp, dinp_bf16, part, dout, inp, gamma, mean, rstd, N, C, rows_per_block, acc_in);
+    case 10: return ln_bwd_launch<DoutT, 10>(blocks, smem, s, dinp, dinp_bf16, part, dout, inp, gamma, mean, rstd, N, C, rows_per_block, acc_in);
+    default: return ln_bwd_launch<DoutT, 0>(blocks, smem, s, dinp, dinp_bf16, part, dout, inp, gamma, mean, rstd, N, C, rows_per_block, acc_in);
+  }
+}
+
+extern "C" {
+
+int llmk_layernorm_backward(float* dinp, void* dinp_bf16, float* dgamma, float* dbeta, float* dinp_colsum,
+                            const void* dout, llmk_dtype dout_dtype, const float* inp, const float* gamma,
+                            const float* mean, const float* rstd, int N, int C, int flags, void* workspace,
+                            size_t workspace_bytes, void* stream) {
   if (!dinp || !dgamma || !dbeta || !dout || !inp || !gamma || !mean || !rstd || N <= 0 || C <= 0)
     return fail(LLMK_ERR_INVALID_ARG, "layernorm_backward");
   if (C % 4 || !a16(dinp) || !a16(dinp_bf16) || !a16(dout) || !a16(inp) || !a16(gamma))
     return fail(LLMK_ERR_UNSUPPORTED, "layernorm_backward: C % 4 == 0 and 16-byte alignment required");
   const int blocks = ln_bwd_blocks(N);
-  if (!workspace || workspace_bytes < static_cast<size_t>(blocks) * 2 * C * sizeof(float))
+  if (!workspace || workspace_bytes < static_cast<size_t>(blocks) * 3 * C * sizeof(float))
     return fail(LLMK_ERR_WORKSPACE, "layernorm_backward: workspace too small");
-  const size_t smem = static_cast<size_t>(8) * 2 * C * sizeof(float);
-  if (smem > 200 * 1024) return fail(LLMK_ERR_UNSUPPORTED, "layernorm_backward: C too large");
+  const size_t smem = static_cast<size_t>(8) * 3 * C * sizeof(float);
+  if (smem > 220 * 1024) return fail(LLMK_ERR_UNSUPPORTED, "layernorm_backward: C too large");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int rows_per_block = (N + blocks - 1) / blocks;
   float* part = static_cast<float*>(workspace);
   const int acc_in = (flags & LLMK_ACCUM_DINP) ? 1 : 0;
-  if (dout_dtype == LLMK_BF16) {
-    auto k = layernorm_bwd_kernel<__nv_bfloat16>;
-    LLMK_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
-    k<<<blocks, 256, smem, s>>>(dinp, static_cast<__nv_bfloat16*>(dinp_bf16), part,
-                                static_cast<const __nv_bfloat16*>(dout), inp, gamma, mean, rstd, N, C, rows_per_block,
-                                acc_in);
-  } else {
-    auto k = layernorm_bwd_kernel<float>;
-    LLMK_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
-    k<<<blocks, 256, smem, s>>>(dinp, static_cast<__nv_bfloat16*>(dinp_bf16), part, static_cast<const float*>(dout),
-                                inp, gamma, mean, rstd, N, C, rows_per_block, acc_in);
-  }
-  layernorm_bwd_reduce<<<(2 * C + 255) / 256, 256, 0, s>>>(dgamma, dbeta, part, blocks, C,
-                                                          (flags & LLMK_ACCUM_DPARAM) ? 1 : 0);
+  if (dout_dtype == LLMK_BF16)
+    LLMK_TRY(ln_bwd_dispatch(blocks, smem, s, dinp, static_cast<__nv_bfloat16*>(dinp_bf16), part,
+                             static_cast<const __nv_bfloat16*>(dout), inp, gamma, mean, rstd, N, C, rows_per_block,
+                             acc_in));
+  else
+    LLMK_TRY(ln_bwd_dispatch(blocks, smem, s, dinp, static_cast<__nv_bfloat16*>(dinp_bf16), part,
+                             static_cast<const float*>(dout), inp, gamma, mean, rstd, N, C, rows_per_block, acc_in));
+  layernorm_bwd_reduce<<<(3 * C + 31) / 32, dim3(32, 8), 0, s>>>(dgamma, dbeta, dinp_colsum, part, blocks, C,
+                                                                 (flags & LLMK_ACCUM_DPARAM) ? 1 : 0);
   count_launch(2);
   LLMK_CUDA(cudaGetLastError());
   return LLMK_OK;
@@ -588,21 +755,34 @@ int llmk_encoder_forward(float* out, const int* tokens, const float* wte, const 
 
 size_t llmk_encoder_backward_workspace(int B, int T) { return static_cast<size_t>(2) * B * T * sizeof(int); }
 
-int llmk_encoder_backward(float* dwte, float* dwpe, const float* dout, const int* tokens, int B, int T, int C,
+int llmk_encoder_backward(float* dwte, float* dwpe, const float* dout, const int* tokens, int B, int T, int C, int V,
                           void* workspace, size_t workspace_bytes, void* stream) {
-  if (!dwte || !dwpe || !dout || !tokens || B <= 0 || T <= 0 || C <= 0)
+  if (!dwte || !dwpe || !dout || !tokens || B <= 0 || T <= 0 || C <= 0 || V <= 0)
     return fail(LLMK_ERR_INVALID_ARG, "encoder_backward");
   if (C % 4 || !a16(dwte) || !a16(dwpe) || !a16(dout)) return fail(LLMK_ERR_UNSUPPORTED, "encoder_backward: C % 4");
   if (!workspace || workspace_bytes < llmk_encoder_backward_workspace(B, T))
     return fail(LLMK_ERR_WORKSPACE, "encoder_backward: workspace too small");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int BT = B * T;
-  int* first_of = static_cast<int*>(workspace);
-  int* next_same = first_of + BT;
   encoder_bwd_wpe_kernel<<<grid_for(static_cast<long long>(T) * C, 256), 256, 0, s>>>(dwpe, dout, B, T, C);
-  encoder_links_kernel<<<(BT + 255) / 256, 256, 0, s>>>(first_of, next_same, tokens, BT);
-  encoder_bwd_wte_kernel<<<grid_for(static_cast<long long>(BT) * C / 4, 256), 256, 0, s>>>(dwte, dout, tokens,
-                                                                                          first_of, next_same, BT, C);
+  if (BT <= kSortMaxBT && V < (1 << 17)) {
+    // sort (token, position) keys once, then one pass over runs of equal tokens
+    int n = 1;
+    while (n < BT) n <<= 1;
+    const size_t smem = static_cast<size_t>(n) * sizeof(unsigned int);
+    LLMK_CUDA(cudaFuncSetAttribute(encoder_sort_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   static_cast<int>(smem)));
+    unsigned int* sorted = static_cast<unsigned int*>(workspace);
+    encoder_sort_kernel<<<1, 1024, smem, s>>>(sorted, tokens, BT, n);
+    encoder_bwd_wte_sorted_kernel<<<grid_for(static_cast<long long>(BT) * C / 4, 256), 256, 0, s>>>(dwte, dout, sorted,
+                                                                                                   BT, C);
+  } else {
+    int* first_of = static_cast<int*>(workspace);
+    int* next_same = first_of + BT;
+    encoder_links_kernel<<<(BT + 255) / 256, 256, 0, s>>>(first_of, next_same, tokens, BT);
+    encoder_bwd_wte_kernel<<<grid_for(static_cast<long long>(BT) * C / 4, 256), 256, 0, s>>>(dwte, dout, tokens,
+                                                                                            first_of, next_same, BT, C);
+  }
   count_launch(3);
   LLMK_CUDA(cudaGetLastError());
   return LLMK_OK;

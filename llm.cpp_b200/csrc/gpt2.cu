@@ -113,7 +113,7 @@ struct llmk_gpt2 {
   ncclComm_t comm = nullptr;
   int rank = 0, world = 1;
   std::vector<cudaEvent_t> layer_done;
-  cudaEvent_t embed_done = nullptr, comm_done = nullptr;
+  cudaEvent_t embed_done = nullptr, comm_done = nullptr, h2d_done = nullptr;
   unsigned long long steps = 0;
 };
 
@@ -205,6 +205,7 @@ void free_all(llmk_gpt2* g) {
   for (auto e : g->layer_done) cudaEventDestroy(e);
   if (g->embed_done) cudaEventDestroy(g->embed_done);
   if (g->comm_done) cudaEventDestroy(g->comm_done);
+  if (g->h2d_done) cudaEventDestroy(g->h2d_done);
   if (g->comm) ncclCommDestroy(g->comm);
   if (g->comm_stream) cudaStreamDestroy(g->comm_stream);
   if (g->own_stream && g->stream) cudaStreamDestroy(g->stream);
@@ -271,6 +272,7 @@ int alloc_all(llmk_gpt2* g) {
   for (auto& e : g->layer_done) LLMK_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
   LLMK_CUDA(cudaEventCreateWithFlags(&g->embed_done, cudaEventDisableTiming));
   LLMK_CUDA(cudaEventCreateWithFlags(&g->comm_done, cudaEventDisableTiming));
+  LLMK_CUDA(cudaEventCreateWithFlags(&g->h2d_done, cudaEventDisableTiming));
   return LLMK_OK;
 }
 
@@ -365,7 +367,10 @@ int llmk_gpt2_load_parameters(llmk_gpt2* g, const float* host_params, size_t n) 
   LLMK_TRY(ensure_device(g));
   std::vector<float> tmp(n);
   permute_params(g, host_params, tmp.data(), 0);
-  LLMK_CUDA(cudaMemcpy(g->params, tmp.data(), n * sizeof(float), cudaMemcpyHostToDevice));
+  // On the model's stream: a plain cudaMemcpy from pageable memory runs on the
+  // legacy stream and may return before its DMA lands, which a kernel on the
+  // model's non-blocking stream would not wait for.
+  LLMK_CUDA(cudaMemcpyAsync(g->params, tmp.data(), n * sizeof(float), cudaMemcpyHostToDevice, g->stream));
   if (g->params_bf16)
     LLMK_TRY(llmk_cast(g->params_bf16, LLMK_BF16, g->params, LLMK_F32, static_cast<long long>(n), g->stream));
   LLMK_CUDA(cudaMemsetAsync(g->m, 0, n * sizeof(float), g->stream));
@@ -481,17 +486,19 @@ int llmk_gpt2_backward(llmk_gpt2* g) {
   LLMK_TRY(llmk_gemm(g->dln, LLMK_F32, C, g->logits, 0, Vp, W(g->off_wte), 1, C, mm, BT, C, Vp, nullptr, nullptr, 0, s));
   LLMK_TRY(llmk_gemm(G + g->off_wte, LLMK_F32, C, g->logits, 1, Vp, g->lnf, 1, C, mm, Vp, C, BT, nullptr, ws, wsb, s));
   const float* xL = L > 0 ? g->acts[L - 1].res3 : g->encoded;
-  LLMK_TRY(llmk_layernorm_backward(g->dres, dres_mirror, G + g->off_lnfw, G + g->off_lnfb, g->dln, LLMK_F32, xL,
-                                   P + g->off_lnfw, g->lnf_mean, g->lnf_rstd, BT, C, 0, ws, wsb, s));
+  // the column sums of the new dres are the last layer's fcproj bias gradient
+  LLMK_TRY(llmk_layernorm_backward(g->dres, dres_mirror, G + g->off_lnfw, G + g->off_lnfb,
+                                   L > 0 ? G + g->lp[L - 1].fcprojb : nullptr, g->dln, LLMK_F32, xL, P + g->off_lnfw,
+                                   g->lnf_mean, g->lnf_rstd, BT, C, 0, ws, wsb, s));
   for (int l = L - 1; l >= 0; --l) {
     // Layer::Backward (gpt2/cuda/layer.cu:180-266); dres = d(layer output)
     const LayerParams& p = g->lp[l];
     LayerActs& a = g->acts[l];
     const float* x = l > 0 ? g->acts[l - 1].res3 : g->encoded;
-    // fcproj: dW = dres^T fch_gelu, db = colsum(dres), dfch = (dres Wfcproj) * gelu'(fch_pre)
+    // fcproj: dW = dres^T fch_gelu, dfch = (dres Wfcproj) * gelu'(fch_pre); its bias
+    // gradient colsum(dres) came out of the LayerNorm backward that produced dres
     LLMK_TRY(llmk_gemm(G + p.fcprojw, LLMK_F32, 4 * C, dres_op, 1, C, a.fch_gelu, 1, 4 * C, mm, C, 4 * C, BT, nullptr,
                        ws, wsb, s));
-    LLMK_TRY(llmk_colsum(G + p.fcprojb, g->dres, LLMK_F32, BT, C, 0, ws, wsb, s));
     llmk_epilogue eg = epi(nullptr, nullptr, 0, a.fch_pre, 4 * C, LLMK_EPI_GELU_BWD | aux_f32);
     LLMK_TRY(llmk_gemm(g->dfch, adt, 4 * C, dres_op, 0, C, W(p.fcprojw), 1, 4 * C, mm, BT, 4 * C, C, &eg, nullptr, 0,
                        s));
@@ -499,12 +506,12 @@ int llmk_gpt2_backward(llmk_gpt2* g) {
     LLMK_TRY(llmk_gemm(G + p.fcw, LLMK_F32, C, g->dfch, 1, 4 * C, a.ln2, 1, C, mm, 4 * C, C, BT, nullptr, ws, wsb, s));
     LLMK_TRY(llmk_colsum(G + p.fcb, g->dfch, adt, BT, 4 * C, 0, ws, wsb, s));
     LLMK_TRY(llmk_gemm(g->dln, LLMK_F32, C, g->dfch, 0, 4 * C, W(p.fcw), 1, C, mm, BT, C, 4 * C, nullptr, nullptr, 0, s));
-    // ln2: dres += LN2 backward (dres becomes d(res2))
-    LLMK_TRY(llmk_layernorm_backward(g->dres, dres_mirror, G + p.ln2w, G + p.ln2b, g->dln, LLMK_F32, a.res2,
-                                     P + p.ln2w, a.ln2_mean, a.ln2_rstd, BT, C, LLMK_ACCUM_DINP, ws, wsb, s));
-    // attproj: dW = dres^T atty, db = colsum(dres), datty = dres Wproj
+    // ln2: dres += LN2 backward (dres becomes d(res2)); its column sums are the
+    // attproj bias gradient
+    LLMK_TRY(llmk_layernorm_backward(g->dres, dres_mirror, G + p.ln2w, G + p.ln2b, G + p.attprojb, g->dln, LLMK_F32,
+                                     a.res2, P + p.ln2w, a.ln2_mean, a.ln2_rstd, BT, C, LLMK_ACCUM_DINP, ws, wsb, s));
+    // attproj: dW = dres^T atty, datty = dres Wproj
     LLMK_TRY(llmk_gemm(G + p.attprojw, LLMK_F32, C, dres_op, 1, C, a.atty, 1, C, mm, C, C, BT, nullptr, ws, wsb, s));
-    LLMK_TRY(llmk_colsum(G + p.attprojb, g->dres, LLMK_F32, BT, C, 0, ws, wsb, s));
     LLMK_TRY(llmk_gemm(g->datty, adt, C, dres_op, 0, C, W(p.attprojw), 1, C, mm, BT, C, C, nullptr, nullptr, 0, s));
     // attention
     if (bf) {
@@ -518,14 +525,16 @@ int llmk_gpt2_backward(llmk_gpt2* g) {
     LLMK_TRY(llmk_gemm(G + p.qkvw, LLMK_F32, C, g->dqkv, 1, 3 * C, a.ln1, 1, C, mm, 3 * C, C, BT, nullptr, ws, wsb, s));
     LLMK_TRY(llmk_colsum(G + p.qkvb, g->dqkv, adt, BT, 3 * C, 0, ws, wsb, s));
     LLMK_TRY(llmk_gemm(g->dln, LLMK_F32, C, g->dqkv, 0, 3 * C, W(p.qkvw), 1, C, mm, BT, C, 3 * C, nullptr, nullptr, 0, s));
-    // ln1: dres += LN1 backward (dres becomes d(layer input))
-    LLMK_TRY(llmk_layernorm_backward(g->dres, dres_mirror, G + p.ln1w, G + p.ln1b, g->dln, LLMK_F32, x, P + p.ln1w,
-                                     a.ln1_mean, a.ln1_rstd, BT, C, LLMK_ACCUM_DINP, ws, wsb, s));
+    // ln1: dres += LN1 backward (dres becomes d(layer input)); its column sums are
+    // the previous layer's fcproj bias gradient
+    LLMK_TRY(llmk_layernorm_backward(g->dres, dres_mirror, G + p.ln1w, G + p.ln1b, l > 0 ? G + g->lp[l - 1].fcprojb : nullptr,
+                                     g->dln, LLMK_F32, x, P + p.ln1w, a.ln1_mean, a.ln1_rstd, BT, C, LLMK_ACCUM_DINP, ws,
+                                     wsb, s));
     // this layer's gradients are final: reduce them while the layers below run
     LLMK_TRY(allreduce_bucket(g, g->layer_done[l], p.begin, p.end));
   }
   // encoder backward (gpt2cuda.cu:413): dwte += scatter, dwpe += sum over batch
-  LLMK_TRY(llmk_encoder_backward(G + g->off_wte, G + g->off_wpe, g->dres, g->inputs, B, T, C, ws, wsb, s));
+  LLMK_TRY(llmk_encoder_backward(G + g->off_wte, G + g->off_wpe, g->dres, g->inputs, B, T, C, Vp, ws, wsb, s));
   // wte/wpe bucket, then lnf bucket
   LLMK_TRY(allreduce_bucket(g, g->embed_done, g->off_wte, g->off_wpe + g->tsize[llmk::WPE]));
   if (g->world > 1) {
@@ -552,12 +561,16 @@ int llmk_gpt2_update(llmk_gpt2* g, float lr, float beta1, float beta2, float eps
 int llmk_gpt2_set_train_data(llmk_gpt2* g, const int* host_inputs, const int* host_targets) {
   if (!g || !host_inputs) return fail(LLMK_ERR_INVALID_ARG, "gpt2_set_train_data");
   const size_t BT = static_cast<size_t>(g->B) * g->T;
+  // the pinned staging buffers are reused: the previous step's copies out of
+  // them must have finished before they are overwritten
+  LLMK_CUDA(cudaEventSynchronize(g->h2d_done));
   std::memcpy(g->h_inputs, host_inputs, BT * sizeof(int));
   LLMK_CUDA(cudaMemcpyAsync(g->inputs, g->h_inputs, BT * sizeof(int), cudaMemcpyHostToDevice, g->stream));
   if (host_targets) {
     std::memcpy(g->h_targets, host_targets, BT * sizeof(int));
     LLMK_CUDA(cudaMemcpyAsync(g->targets, g->h_targets, BT * sizeof(int), cudaMemcpyHostToDevice, g->stream));
   }
+  LLMK_CUDA(cudaEventRecord(g->h2d_done, g->stream));
   return LLMK_OK;
 }
 

@@ -63,7 +63,7 @@ SIGNATURES: dict[str, tuple] = {
     "llmk_attention_backward": (i32, [vp, vp, vp, vp, vp, i32, i32, i32, i32, vp, sz, vp]),
     "llmk_layernorm_forward": (i32, [vp, i32, vp, vp, vp, vp, vp, i32, i32, vp]),
     "llmk_layernorm_backward_workspace": (sz, [i32, i32]),
-    "llmk_layernorm_backward": (i32, [vp, vp, vp, vp, vp, i32, vp, vp, vp, vp, i32, i32, i32, vp, sz, vp]),
+    "llmk_layernorm_backward": (i32, [vp, vp, vp, vp, vp, vp, i32, vp, vp, vp, vp, i32, i32, i32, vp, sz, vp]),
     "llmk_gelu_forward": (i32, [vp, vp, i32, i64, vp]),
     "llmk_gelu_backward": (i32, [vp, vp, vp, i32, i64, i32, vp]),
     "llmk_residual_forward": (i32, [vp, vp, vp, i32, i64, vp]),
@@ -71,7 +71,7 @@ SIGNATURES: dict[str, tuple] = {
     "llmk_cast": (i32, [vp, i32, vp, i32, i64, vp]),
     "llmk_encoder_forward": (i32, [vp, vp, vp, vp, i32, i32, i32, vp]),
     "llmk_encoder_backward_workspace": (sz, [i32, i32]),
-    "llmk_encoder_backward": (i32, [vp, vp, vp, vp, i32, i32, i32, vp, sz, vp]),
+    "llmk_encoder_backward": (i32, [vp, vp, vp, vp, i32, i32, i32, i32, vp, sz, vp]),
     "llmk_softmax_crossentropy": (i32, [vp, vp, vp, i32, vp, i32, i32, i32, f32, vp]),
     "llmk_mean": (i32, [vp, vp, i32, vp]),
     "llmk_adamw": (i32, [vp, vp, vp, vp, vp, i64, f32, f32, f32, f32, f32, i32, f32, vp]),

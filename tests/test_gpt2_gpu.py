@@ -74,7 +74,7 @@ def test_small_model_gradients_vs_oracle(cuda_dev, mathname, tol):
     # lr = 0: the step leaves the parameters unchanged and exposes the gradients
     loss = m.train_step(inp, tgt, 0.0, t=1)
     g = m.read_gradients()
-    assert abs(loss - loss_ref) / loss_ref < 1e-3, (loss, loss_ref)
+    assert abs(loss - loss_ref) / loss_ref < (1e-3 if mathname == "tf32" else 1e-2), (loss, loss_ref)
     sizes = O.param_sizes(cfg)
     names = ["wte", "wpe", "ln1w", "ln1b", "qkvw", "qkvb", "attprojw", "attprojb", "ln2w", "ln2b", "fcw", "fcb",
              "fcprojw", "fcprojb", "lnfw", "lnfb"]
@@ -85,4 +85,29 @@ def test_small_model_gradients_vs_oracle(cuda_dev, mathname, tol):
         nrm = np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30)
         assert nrm < tol, f"{name}: norm-rel err {nrm:.3e}"
     assert np.array_equal(m.read_parameters(), params)
+    m.close()
+
+
+@pytest.mark.parametrize("mathname", ["bf16", "tf32"])
+def test_repeated_steps_agree(cuda_dev, mathname):
+    """The same step (lr = 0) repeated five times gives the same gradients: a
+    race between kernels, streams or CTAs shows up as run-to-run spread (the
+    only unordered sum is the attention dQ reduction, ~1e-7 relative)."""
+    import llmk
+    math = llmk.MATH_TF32 if mathname == "tf32" else llmk.MATH_BF16
+    cfg = O.config(max_seq_len=128, vocab_size=1000, padded_vocab_size=1024, num_layers=2, num_heads=2, channels=128)
+    B, T = 2, 128
+    params = O.init_params(cfg, 11)
+    toks = O.tokens(B * T + 1, cfg.vocab_size, 11)
+    m = _model(llmk, cfg, B, T, math)
+    m.load_parameters(params)
+    first = None
+    for _ in range(5):
+        m.train_step(toks[:-1], toks[1:], 0.0, t=1)
+        g = m.read_gradients().astype(np.float64)
+        if first is None:
+            first = g
+        else:
+            err = np.abs(g - first).max() / np.abs(first).max()
+            assert err < 1e-5, err
     m.close()

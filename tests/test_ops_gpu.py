@@ -103,9 +103,10 @@ def test_layernorm_vs_oracle(cuda_dev):
     ws_b = llmk.lib().llmk_layernorm_backward_workspace(N, C)
     ws = torch.empty(ws_b // 4 + 64, device=cuda_dev)
     dyd = T(dy, cuda_dev)
+    dsum = torch.full((C,), float("nan"), device=cuda_dev)
     llmk.call("llmk_layernorm_backward", dinp.data_ptr(), dinp_b.data_ptr(), dg.data_ptr(), db.data_ptr(),
-              dyd.data_ptr(), llmk.F32, xd.data_ptr(), gd.data_ptr(), mean.data_ptr(), rstd.data_ptr(), N, C,
-              llmk.ACCUM_DINP | llmk.ACCUM_DPARAM, ws.data_ptr(), ws_b, s)
+              dsum.data_ptr(), dyd.data_ptr(), llmk.F32, xd.data_ptr(), gd.data_ptr(), mean.data_ptr(),
+              rstd.data_ptr(), N, C, llmk.ACCUM_DINP | llmk.ACCUM_DPARAM, ws.data_ptr(), ws_b, s)
     dxo = np.zeros_like(x)
     dgo = np.ones(C, np.float32)
     dbo = np.ones(C, np.float32)
@@ -115,7 +116,44 @@ def test_layernorm_vs_oracle(cuda_dev):
     assert max_rel_err(dinp_b.float().cpu(), torch.from_numpy(dxo + d0)) < 1e-2
     assert max_rel_err(dg.cpu(), torch.from_numpy(dgo)) < 1e-4
     assert max_rel_err(db.cpu(), torch.from_numpy(dbo)) < 1e-4
+    # fused column sums of the final dinp (the next linear layer's bias gradient)
+    assert max_rel_err(dsum.cpu(), torch.from_numpy((dxo + d0).astype(np.float64).sum(0))) < 1e-4
     assert llmk.device_status() == 0
+
+
+@pytest.mark.parametrize("C", [768, 1280, 200])
+def test_layernorm_widths(cuda_dev, C):
+    """Register-resident (C = 768, 1280) and generic (C = 200) LayerNorm paths vs the oracle."""
+    import torch
+    import llmk
+    N = 257
+    x = O.normal((N, C), 71, std=1.5)
+    g = O.normal((C,), 72)
+    be = O.normal((C,), 73)
+    dy = O.normal((N, C), 74)
+    s = llmk.stream_ptr()
+    xd, gd, bd, dyd = T(x, cuda_dev), T(g, cuda_dev), T(be, cuda_dev), T(dy, cuda_dev)
+    y = torch.empty(N, C, device=cuda_dev)
+    mean = torch.empty(N, device=cuda_dev)
+    rstd = torch.empty(N, device=cuda_dev)
+    llmk.call("llmk_layernorm_forward", y.data_ptr(), llmk.F32, mean.data_ptr(), rstd.data_ptr(), xd.data_ptr(),
+              gd.data_ptr(), bd.data_ptr(), N, C, s)
+    dinp = torch.empty(N, C, device=cuda_dev)
+    dg = torch.empty(C, device=cuda_dev)
+    db = torch.empty(C, device=cuda_dev)
+    ws_b = llmk.lib().llmk_layernorm_backward_workspace(N, C)
+    ws = torch.empty(ws_b // 4 + 64, device=cuda_dev)
+    llmk.call("llmk_layernorm_backward", dinp.data_ptr(), None, dg.data_ptr(), db.data_ptr(), None, dyd.data_ptr(),
+              llmk.F32, xd.data_ptr(), gd.data_ptr(), mean.data_ptr(), rstd.data_ptr(), N, C, 0, ws.data_ptr(), ws_b,
+              s)
+    yo, mo, ro = np.zeros_like(x), np.zeros(N, np.float32), np.zeros(N, np.float32)
+    O.orc().orc_layernorm_forward(yo, mo.ctypes.data, ro.ctypes.data, x, g, be, N, C)
+    dxo, dgo, dbo = np.zeros_like(x), np.zeros(C, np.float32), np.zeros(C, np.float32)
+    O.orc().orc_layernorm_backward(dxo, dgo, dbo, dy, x, g, mo, ro, N, C)
+    torch.cuda.synchronize()
+    assert max_rel_err(y, yo) < 1e-5
+    assert max_rel_err(dinp, dxo) < 1e-4
+    assert max_rel_err(dg, dgo) < 1e-4 and max_rel_err(db, dbo) < 1e-4
 
 
 def test_gelu_residual_vs_oracle(cuda_dev):
@@ -167,12 +205,34 @@ def test_encoder_vs_oracle(cuda_dev):
     ws = torch.empty(ws_b // 4 + 16, device=cuda_dev)
     doutd = T(dout, cuda_dev)
     llmk.call("llmk_encoder_backward", dwte.data_ptr(), dwpe.data_ptr(), doutd.data_ptr(), tokd.data_ptr(), B, Tt, C,
-              ws.data_ptr(), ws_b, s)
+              V, ws.data_ptr(), ws_b, s)
     a, b = np.zeros((V, C), np.float32), np.zeros((Tt, C), np.float32)
     O.orc().orc_encoder_backward(a, b, dout, tok, B, Tt, C)
     torch.cuda.synchronize()
     assert max_rel_err(dwte.cpu(), torch.from_numpy(a)) < 1e-5
     assert max_rel_err(dwpe.cpu(), torch.from_numpy(b)) < 1e-5
+
+
+@pytest.mark.parametrize("B,Tt,V", [(16, 1024, 50257), (33, 1024, 3000)])
+def test_encoder_backward_sizes(cuda_dev, B, Tt, V):
+    """B*T = 16384 exercises the one-CTA sort path, B*T = 33792 the scan fallback."""
+    import torch
+    import llmk
+    C = 128
+    tok = O.tokens(B * Tt, V, 35)
+    dout = O.normal((B * Tt, C), 36)
+    tokd, doutd = T(tok, cuda_dev), T(dout, cuda_dev)
+    dwte = torch.zeros(V, C, device=cuda_dev)
+    dwpe = torch.zeros(Tt, C, device=cuda_dev)
+    ws_b = llmk.lib().llmk_encoder_backward_workspace(B, Tt)
+    ws = torch.empty(ws_b // 4 + 16, device=cuda_dev)
+    llmk.call("llmk_encoder_backward", dwte.data_ptr(), dwpe.data_ptr(), doutd.data_ptr(), tokd.data_ptr(), B, Tt, C,
+              V, ws.data_ptr(), ws_b, llmk.stream_ptr())
+    a, b = np.zeros((V, C), np.float32), np.zeros((Tt, C), np.float32)
+    O.orc().orc_encoder_backward(a, b, dout, tok, B, Tt, C)
+    torch.cuda.synchronize()
+    assert max_rel_err(dwte, a) < 1e-5
+    assert max_rel_err(dwpe, b) < 1e-5
 
 
 @pytest.mark.parametrize("dtname", ["f32", "bf16"])
