@@ -92,13 +92,10 @@ void BatchMatmulNTBackward(Vec& d_inputs, Vec& d_weight, Vec& d_bias, const Vec&
 template <class Vec>
 void BatchCausalAttentionForward(Vec& outputs, Vec& logsumexp, const Vec& inputs, int B, int T, int C3, int NH,
                                  cudaStream_t stream) {
-  const long long n_in = 1LL * B * T * C3, n_out = 1LL * B * T * (C3 / 3);
+  const long long n_in = 1LL * B * T * C3;
   void* qkv = llmk_detail::scratch(n_in * 2, 1);
-  void* out = llmk_detail::scratch(n_out * 2, 2);
   llmk_detail::check(llmk_cast(qkv, LLMK_BF16, inputs.data(), LLMK_F32, n_in, stream), "BatchCausalAttentionForward");
-  llmk_detail::check(llmk_attention_forward(out, logsumexp.data(), qkv, B, T, C3, NH, stream),
-                     "BatchCausalAttentionForward");
-  llmk_detail::check(llmk_cast(outputs.data(), LLMK_F32, out, LLMK_BF16, n_out, stream),
+  llmk_detail::check(llmk_attention_forward(outputs.data(), LLMK_F32, logsumexp.data(), qkv, B, T, C3, NH, stream),
                      "BatchCausalAttentionForward");
 }
 
@@ -109,21 +106,17 @@ void BatchCausalAttentionBackward(Vec& d_inputs, Vec& att_D, const Vec& d_output
                                   const Vec& inputs, const Vec& logsumexp, int B, int T, int C3, int NH,
                                   cudaStream_t stream) {
   (void)att_D;
-  const long long n_in = 1LL * B * T * C3, n_out = 1LL * B * T * (C3 / 3);
+  const long long n_in = 1LL * B * T * C3;
   const size_t ws = llmk_attention_backward_workspace(B, T, C3, NH);
-  char* base = static_cast<char*>(llmk_detail::scratch(ws + (2 * n_in + 2 * n_out) * 2 + n_in * 4 + 1024, 3));
+  char* base = static_cast<char*>(llmk_detail::scratch(ws + n_in * 6 + 1024, 3));
   void* qkv = base;
-  void* dq = base + n_in * 2;
-  void* out = base + n_in * 4;
-  void* dout = base + n_in * 4 + n_out * 2;
-  float* dq32 = reinterpret_cast<float*>(base + n_in * 4 + n_out * 4);
-  void* work = base + n_in * 8 + n_out * 4;
+  float* dq32 = reinterpret_cast<float*>(base + n_in * 2);
+  void* work = base + n_in * 6;
   const char* w = "BatchCausalAttentionBackward";
   llmk_detail::check(llmk_cast(qkv, LLMK_BF16, inputs.data(), LLMK_F32, n_in, stream), w);
-  llmk_detail::check(llmk_cast(out, LLMK_BF16, outputs.data(), LLMK_F32, n_out, stream), w);
-  llmk_detail::check(llmk_cast(dout, LLMK_BF16, d_outputs.data(), LLMK_F32, n_out, stream), w);
-  llmk_detail::check(llmk_attention_backward(dq, dout, out, qkv, logsumexp.data(), B, T, C3, NH, work, ws, stream), w);
-  llmk_detail::check(llmk_cast(dq32, LLMK_F32, dq, LLMK_BF16, n_in, stream), w);
+  llmk_detail::check(llmk_attention_backward(dq32, d_outputs.data(), outputs.data(), LLMK_F32, qkv, logsumexp.data(), B,
+                                             T, C3, NH, work, ws, stream),
+                     w);
   llmk_detail::check(llmk_residual_forward(d_inputs.data(), d_inputs.data(), dq32, LLMK_F32, n_in, stream), w);
 }
 

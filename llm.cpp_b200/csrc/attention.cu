@@ -67,7 +67,7 @@ struct FwdSmem {
 };
 
 __global__ void __launch_bounds__(192, 1)
-    attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, __nv_bfloat16* __restrict__ out,
+    attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, void* __restrict__ out_ptr, int out_f32,
                     float* __restrict__ lse, int B, int T, int NH, int C, unsigned int* status) {
   using S = FwdSmem;
   extern __shared__ uint8_t smem_raw[];
@@ -256,15 +256,23 @@ __global__ void __launch_bounds__(192, 1)
       const int t = q0 + r;
       if (t < T) {
         const float inv = 1.0f / l;
-        __nv_bfloat16* dst = out + (static_cast<long long>(b) * T + t) * C + h * HD;
+        const long long off = (static_cast<long long>(b) * T + t) * C + h * HD;
+        if (out_f32) {
+          float4* dst = reinterpret_cast<float4*>(static_cast<float*>(out_ptr) + off);
 #pragma unroll
-        for (int ch = 0; ch < HD / 8; ++ch) {
-          uint4 u;
-          u.x = pack_bf16x2(o[ch * 8 + 0] * inv, o[ch * 8 + 1] * inv);
-          u.y = pack_bf16x2(o[ch * 8 + 2] * inv, o[ch * 8 + 3] * inv);
-          u.z = pack_bf16x2(o[ch * 8 + 4] * inv, o[ch * 8 + 5] * inv);
-          u.w = pack_bf16x2(o[ch * 8 + 6] * inv, o[ch * 8 + 7] * inv);
-          reinterpret_cast<uint4*>(dst)[ch] = u;
+          for (int ch = 0; ch < HD / 4; ++ch)
+            dst[ch] = make_float4(o[ch * 4] * inv, o[ch * 4 + 1] * inv, o[ch * 4 + 2] * inv, o[ch * 4 + 3] * inv);
+        } else {
+          __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(out_ptr) + off;
+#pragma unroll
+          for (int ch = 0; ch < HD / 8; ++ch) {
+            uint4 u;
+            u.x = pack_bf16x2(o[ch * 8 + 0] * inv, o[ch * 8 + 1] * inv);
+            u.y = pack_bf16x2(o[ch * 8 + 2] * inv, o[ch * 8 + 3] * inv);
+            u.z = pack_bf16x2(o[ch * 8 + 4] * inv, o[ch * 8 + 5] * inv);
+            u.w = pack_bf16x2(o[ch * 8 + 6] * inv, o[ch * 8 + 7] * inv);
+            reinterpret_cast<uint4*>(dst)[ch] = u;
+          }
         }
         // natural-log LSE: (m2 + log2 l) * ln 2
         lse[(static_cast<long long>(b) * NH + h) * T + t] = (m + __log2f(l)) * 0.6931471805599453f;
@@ -280,27 +288,50 @@ __global__ void __launch_bounds__(192, 1)
 }
 
 // ----------------------------------------------------------------- backward
+__device__ __forceinline__ void load8f(const __nv_bfloat16* p, float* v) {
+  uint4 a = *reinterpret_cast<const uint4*>(p);
+  const __nv_bfloat162* x = reinterpret_cast<const __nv_bfloat162*>(&a);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 u = __bfloat1622float2(x[i]);
+    v[2 * i] = u.x;
+    v[2 * i + 1] = u.y;
+  }
+}
+__device__ __forceinline__ void load8f(const float* p, float* v) {
+  float4 a = reinterpret_cast<const float4*>(p)[0], b = reinterpret_cast<const float4*>(p)[1];
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
 // D[b,h,t] = sum_i dO[b,t,h*64+i] * O[b,t,h*64+i]; zeroes dq_acc for the row.
+// With fp32 dO / O (IoT = float) it also writes the bf16 copy of dO the MMA
+// reads (dout16).
+template <typename IoT>
 __global__ void attn_bwd_pre_kernel(float* __restrict__ D, float* __restrict__ dq_acc,
-                                    const __nv_bfloat16* __restrict__ dout, const __nv_bfloat16* __restrict__ o,
-                                    int B, int T, int NH, int C) {
+                                    __nv_bfloat16* __restrict__ dout16, const IoT* __restrict__ dout,
+                                    const IoT* __restrict__ o, int B, int T, int NH, int C) {
   const long long idx = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;  // (b, t, h)
   if (idx >= static_cast<long long>(B) * T * NH) return;
   const int h = static_cast<int>(idx % NH);
   const long long bt = idx / NH;
   const int b = static_cast<int>(bt / T), t = static_cast<int>(bt % T);
-  const uint4* pd = reinterpret_cast<const uint4*>(dout + bt * C + h * HD);
-  const uint4* po = reinterpret_cast<const uint4*>(o + bt * C + h * HD);
+  const IoT* pd = dout + bt * C + h * HD;
+  const IoT* po = o + bt * C + h * HD;
   float s = 0.f;
 #pragma unroll
   for (int k = 0; k < HD / 8; ++k) {
-    uint4 a = pd[k], c = po[k];
-    const __nv_bfloat162* x = reinterpret_cast<const __nv_bfloat162*>(&a);
-    const __nv_bfloat162* y = reinterpret_cast<const __nv_bfloat162*>(&c);
+    float x[8], y[8];
+    load8f(pd + 8 * k, x);
+    load8f(po + 8 * k, y);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      float2 u = __bfloat1622float2(x[i]), v = __bfloat1622float2(y[i]);
-      s += u.x * v.x + u.y * v.y;
+    for (int i = 0; i < 8; ++i) s += x[i] * y[i];
+    if constexpr (sizeof(IoT) == 4) {
+      uint4 u;
+      u.x = pack_bf16x2(x[0], x[1]);
+      u.y = pack_bf16x2(x[2], x[3]);
+      u.z = pack_bf16x2(x[4], x[5]);
+      u.w = pack_bf16x2(x[6], x[7]);
+      *reinterpret_cast<uint4*>(dout16 + bt * C + h * HD + 8 * k) = u;
     }
   }
   D[(static_cast<long long>(b) * NH + h) * T + t] = s;
@@ -309,8 +340,9 @@ __global__ void attn_bwd_pre_kernel(float* __restrict__ D, float* __restrict__ d
   for (int k = 0; k < HD / 4; ++k) z[k] = make_float4(0.f, 0.f, 0.f, 0.f);
 }
 
-// dqkv[:, :, 0:C] = bf16(dq_acc * scale)
-__global__ void attn_bwd_post_kernel(__nv_bfloat16* __restrict__ dqkv, const float* __restrict__ dq_acc, int BT, int C,
+// dqkv[:, :, 0:C] = dq_acc * scale (bf16 or fp32)
+template <typename IoT>
+__global__ void attn_bwd_post_kernel(IoT* __restrict__ dqkv, const float* __restrict__ dq_acc, int BT, int C,
                                      float scale) {
   const long long n8 = static_cast<long long>(BT) * C / 8;
   for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n8;
@@ -320,12 +352,18 @@ __global__ void attn_bwd_post_kernel(__nv_bfloat16* __restrict__ dqkv, const flo
     const int c = static_cast<int>(e - bt * C);
     const float4* p = reinterpret_cast<const float4*>(dq_acc + e);
     float4 a = p[0], bb = p[1];
-    uint4 u;
-    u.x = pack_bf16x2(a.x * scale, a.y * scale);
-    u.y = pack_bf16x2(a.z * scale, a.w * scale);
-    u.z = pack_bf16x2(bb.x * scale, bb.y * scale);
-    u.w = pack_bf16x2(bb.z * scale, bb.w * scale);
-    *reinterpret_cast<uint4*>(dqkv + bt * 3 * C + c) = u;
+    if constexpr (sizeof(IoT) == 4) {
+      float4* d = reinterpret_cast<float4*>(dqkv + bt * 3 * C + c);
+      d[0] = make_float4(a.x * scale, a.y * scale, a.z * scale, a.w * scale);
+      d[1] = make_float4(bb.x * scale, bb.y * scale, bb.z * scale, bb.w * scale);
+    } else {
+      uint4 u;
+      u.x = pack_bf16x2(a.x * scale, a.y * scale);
+      u.y = pack_bf16x2(a.z * scale, a.w * scale);
+      u.z = pack_bf16x2(bb.x * scale, bb.y * scale);
+      u.w = pack_bf16x2(bb.z * scale, bb.w * scale);
+      *reinterpret_cast<uint4*>(dqkv + bt * 3 * C + c) = u;
+    }
   }
 }
 
@@ -348,7 +386,7 @@ __device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, 
 
 __global__ void __launch_bounds__(192, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_do,
-                    __nv_bfloat16* __restrict__ dqkv, float* __restrict__ dq_acc, const float* __restrict__ lse,
+                    void* __restrict__ dqkv_ptr, int io_f32, float* __restrict__ dq_acc, const float* __restrict__ lse,
                     const float* __restrict__ Dvec, int B, int T, int NH, int C, unsigned int* status) {
   using S = BwdSmem;
   extern __shared__ uint8_t smem_raw[];
@@ -581,8 +619,8 @@ __global__ void __launch_bounds__(192, 1)
         // (.sync.aligned): every lane loads, only lanes of keys < T store.
         const int tk = k0 + r;
         const bool key_ok = tk < T;
-        __nv_bfloat16* dk = dqkv + (static_cast<long long>(b) * T + (key_ok ? tk : 0)) * 3 * C + C + h * HD;
-        __nv_bfloat16* dvp = dk + C;
+        // element offset of this key's dK slice; dV is C further
+        const long long dk_off = (static_cast<long long>(b) * T + (key_ok ? tk : 0)) * 3 * C + C + h * HD;
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
 #pragma unroll
@@ -591,15 +629,24 @@ __global__ void __launch_bounds__(192, 1)
             tmem_ld_32x32b_x32(tmem + lane_base + (which == 0 ? 320 : 256) + half * 32, v);
             tmem_ld_wait();
             if (key_ok) {
-              __nv_bfloat16* dst = (which == 0 ? dk : dvp) + half * 32;
+              const long long off = dk_off + (which == 0 ? 0 : C) + half * 32;
+              if (io_f32) {
+                float4* dst = reinterpret_cast<float4*>(static_cast<float*>(dqkv_ptr) + off);
 #pragma unroll
-              for (int ch = 0; ch < 4; ++ch) {
-                uint4 u;
-                u.x = pack_bf16x2(__uint_as_float(v[ch * 8 + 0]) * sc, __uint_as_float(v[ch * 8 + 1]) * sc);
-                u.y = pack_bf16x2(__uint_as_float(v[ch * 8 + 2]) * sc, __uint_as_float(v[ch * 8 + 3]) * sc);
-                u.z = pack_bf16x2(__uint_as_float(v[ch * 8 + 4]) * sc, __uint_as_float(v[ch * 8 + 5]) * sc);
-                u.w = pack_bf16x2(__uint_as_float(v[ch * 8 + 6]) * sc, __uint_as_float(v[ch * 8 + 7]) * sc);
-                reinterpret_cast<uint4*>(dst)[ch] = u;
+                for (int ch = 0; ch < 8; ++ch)
+                  dst[ch] = make_float4(__uint_as_float(v[ch * 4]) * sc, __uint_as_float(v[ch * 4 + 1]) * sc,
+                                        __uint_as_float(v[ch * 4 + 2]) * sc, __uint_as_float(v[ch * 4 + 3]) * sc);
+              } else {
+                __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(dqkv_ptr) + off;
+#pragma unroll
+                for (int ch = 0; ch < 4; ++ch) {
+                  uint4 u;
+                  u.x = pack_bf16x2(__uint_as_float(v[ch * 8 + 0]) * sc, __uint_as_float(v[ch * 8 + 1]) * sc);
+                  u.y = pack_bf16x2(__uint_as_float(v[ch * 8 + 2]) * sc, __uint_as_float(v[ch * 8 + 3]) * sc);
+                  u.z = pack_bf16x2(__uint_as_float(v[ch * 8 + 4]) * sc, __uint_as_float(v[ch * 8 + 5]) * sc);
+                  u.w = pack_bf16x2(__uint_as_float(v[ch * 8 + 6]) * sc, __uint_as_float(v[ch * 8 + 7]) * sc);
+                  reinterpret_cast<uint4*>(dst)[ch] = u;
+                }
               }
             }
           }
@@ -641,9 +688,11 @@ using namespace llmk;
 
 extern "C" {
 
-int llmk_attention_forward(void* out, float* lse, const void* qkv, int B, int T, int C3, int NH, void* stream) {
+int llmk_attention_forward(void* out, llmk_dtype out_dtype, float* lse, const void* qkv, int B, int T, int C3, int NH,
+                           void* stream) {
   if (!out || !lse || !qkv) return fail(LLMK_ERR_INVALID_ARG, "attention_forward: null pointer");
   LLMK_TRY(check_shapes(B, T, C3, NH));
+  if (out_dtype != LLMK_BF16 && out_dtype != LLMK_F32) return fail(LLMK_ERR_UNSUPPORTED, "attention_forward: out dtype");
   if (!aligned16(out) || !aligned16(qkv)) return fail(LLMK_ERR_UNSUPPORTED, "attention_forward: alignment");
   const int C = C3 / 3;
   CUtensorMap tm;
@@ -652,47 +701,66 @@ int llmk_attention_forward(void* out, float* lse, const void* qkv, int B, int T,
   LLMK_TRY(set_smem(reinterpret_cast<const void*>(attn_fwd_kernel), FwdSmem::BYTES));
   const int nq = (T + TILE - 1) / TILE;
   attn_fwd_kernel<<<nq * B * NH, 192, FwdSmem::BYTES, static_cast<cudaStream_t>(stream)>>>(
-      tm, static_cast<__nv_bfloat16*>(out), lse, B, T, NH, C, device_status_ptr());
+      tm, out, out_dtype == LLMK_F32 ? 1 : 0, lse, B, T, NH, C, device_status_ptr());
   count_launch();
   LLMK_CUDA(cudaGetLastError());
   return LLMK_OK;
 }
 
-size_t llmk_attention_backward_workspace(int B, int T, int C3, int NH) {
-  if (B <= 0 || T <= 0 || C3 <= 0 || NH <= 0) return 0;
-  const size_t d = static_cast<size_t>(B) * NH * T * sizeof(float);
-  const size_t dq = static_cast<size_t>(B) * T * (C3 / 3) * sizeof(float);
-  return ((d + 255) / 256) * 256 + dq;
+static size_t attn_ws_parts(int B, int T, int C, int NH, size_t* dq_off, size_t* do16_off) {
+  const size_t d = ((static_cast<size_t>(B) * NH * T * sizeof(float) + 255) / 256) * 256;
+  const size_t dq = ((static_cast<size_t>(B) * T * C * sizeof(float) + 255) / 256) * 256;
+  const size_t do16 = static_cast<size_t>(B) * T * C * sizeof(__nv_bfloat16);
+  if (dq_off) *dq_off = d;
+  if (do16_off) *do16_off = d + dq;
+  return d + dq + do16;
 }
 
-int llmk_attention_backward(void* dqkv, const void* dout, const void* out, const void* qkv, const float* lse, int B,
-                            int T, int C3, int NH, void* workspace, size_t workspace_bytes, void* stream) {
+size_t llmk_attention_backward_workspace(int B, int T, int C3, int NH) {
+  if (B <= 0 || T <= 0 || C3 <= 0 || NH <= 0) return 0;
+  return attn_ws_parts(B, T, C3 / 3, NH, nullptr, nullptr);
+}
+
+int llmk_attention_backward(void* dqkv, const void* dout, const void* out, llmk_dtype io_dtype, const void* qkv,
+                            const float* lse, int B, int T, int C3, int NH, void* workspace, size_t workspace_bytes,
+                            void* stream) {
   if (!dqkv || !dout || !out || !qkv || !lse) return fail(LLMK_ERR_INVALID_ARG, "attention_backward: null pointer");
   LLMK_TRY(check_shapes(B, T, C3, NH));
+  if (io_dtype != LLMK_BF16 && io_dtype != LLMK_F32) return fail(LLMK_ERR_UNSUPPORTED, "attention_backward: io dtype");
   if (!aligned16(dqkv) || !aligned16(dout) || !aligned16(out) || !aligned16(qkv))
     return fail(LLMK_ERR_UNSUPPORTED, "attention_backward: alignment");
   if (!workspace || workspace_bytes < llmk_attention_backward_workspace(B, T, C3, NH) || !aligned16(workspace))
     return fail(LLMK_ERR_WORKSPACE, "attention_backward: workspace too small");
   const int C = C3 / 3;
+  const bool f32 = io_dtype == LLMK_F32;
+  size_t dq_off, do16_off;
+  attn_ws_parts(B, T, C, NH, &dq_off, &do16_off);
   float* Dv = static_cast<float*>(workspace);
-  float* dq = reinterpret_cast<float*>(static_cast<char*>(workspace) +
-                                       ((static_cast<size_t>(B) * NH * T * sizeof(float) + 255) / 256) * 256);
+  float* dq = reinterpret_cast<float*>(static_cast<char*>(workspace) + dq_off);
+  __nv_bfloat16* do16 = reinterpret_cast<__nv_bfloat16*>(static_cast<char*>(workspace) + do16_off);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const long long rows = static_cast<long long>(B) * T * NH;
-  attn_bwd_pre_kernel<<<static_cast<int>((rows + 127) / 128), 128, 0, s>>>(
-      Dv, dq, static_cast<const __nv_bfloat16*>(dout), static_cast<const __nv_bfloat16*>(out), B, T, NH, C);
+  if (f32)
+    attn_bwd_pre_kernel<float><<<static_cast<int>((rows + 127) / 128), 128, 0, s>>>(
+        Dv, dq, do16, static_cast<const float*>(dout), static_cast<const float*>(out), B, T, NH, C);
+  else
+    attn_bwd_pre_kernel<__nv_bfloat16><<<static_cast<int>((rows + 127) / 128), 128, 0, s>>>(
+        Dv, dq, nullptr, static_cast<const __nv_bfloat16*>(dout), static_cast<const __nv_bfloat16*>(out), B, T, NH, C);
+  // the MMAs read dO as bf16: the caller's buffer, or the copy the pre-pass made
+  const void* dout_mma = f32 ? static_cast<const void*>(do16) : dout;
   CUtensorMap tq, td;
   LLMK_TRY(make_tmap_3d(&tq, qkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, C3, T, B, static_cast<uint64_t>(C3) * 2,
                         static_cast<uint64_t>(T) * C3 * 2, HD, TILE, 1));
-  LLMK_TRY(make_tmap_3d(&td, dout, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, C, T, B, static_cast<uint64_t>(C) * 2,
+  LLMK_TRY(make_tmap_3d(&td, dout_mma, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, C, T, B, static_cast<uint64_t>(C) * 2,
                         static_cast<uint64_t>(T) * C * 2, HD, TILE, 1));
   LLMK_TRY(set_smem(reinterpret_cast<const void*>(attn_bwd_kernel), BwdSmem::BYTES));
   const int nk = (T + TILE - 1) / TILE;
-  attn_bwd_kernel<<<nk * B * NH, 192, BwdSmem::BYTES, s>>>(tq, td, static_cast<__nv_bfloat16*>(dqkv), dq, lse, Dv, B,
-                                                            T, NH, C, device_status_ptr());
+  attn_bwd_kernel<<<nk * B * NH, 192, BwdSmem::BYTES, s>>>(tq, td, dqkv, f32 ? 1 : 0, dq, lse, Dv, B, T, NH, C,
+                                                            device_status_ptr());
   const long long n8 = static_cast<long long>(B) * T * C / 8;
-  attn_bwd_post_kernel<<<static_cast<int>(std::min<long long>((n8 + 255) / 256, 148LL * 16)), 256, 0, s>>>(
-      static_cast<__nv_bfloat16*>(dqkv), dq, B * T, C, 0.125f);
+  const int pg = static_cast<int>(std::min<long long>((n8 + 255) / 256, 148LL * 16));
+  if (f32) attn_bwd_post_kernel<float><<<pg, 256, 0, s>>>(static_cast<float*>(dqkv), dq, B * T, C, 0.125f);
+  else attn_bwd_post_kernel<__nv_bfloat16><<<pg, 256, 0, s>>>(static_cast<__nv_bfloat16*>(dqkv), dq, B * T, C, 0.125f);
   count_launch(3);
   LLMK_CUDA(cudaGetLastError());
   return LLMK_OK;

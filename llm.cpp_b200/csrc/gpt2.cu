@@ -75,8 +75,8 @@ struct LayerActs {
   float *ln1_mean, *ln1_rstd, *ln2_mean, *ln2_rstd, *lse, *res2, *res3;
   // GEMM operands in the activation dtype (bf16, or fp32 in tf32 mode)
   void *ln1, *qkv, *atty, *ln2, *fch_pre, *fch_gelu;
-  // tf32 mode only: bf16 copies of the attention operands
-  __nv_bfloat16 *qkv16, *atty16;
+  // tf32 mode only: bf16 copy of q, k, v for the attention MMAs
+  __nv_bfloat16* qkv16;
 };
 
 struct llmk_gpt2 {
@@ -102,7 +102,6 @@ struct llmk_gpt2 {
   float *dres = nullptr, *dln = nullptr;
   __nv_bfloat16* dres_bf16 = nullptr;  // bf16 mode: GEMM copy of dres
   void *datty = nullptr, *dqkv = nullptr, *dfch = nullptr;
-  __nv_bfloat16 *datty16 = nullptr, *dqkv16 = nullptr;  // tf32 mode: attention-side copies
   void* workspace = nullptr;
   size_t workspace_bytes = 0;
   int *inputs = nullptr, *targets = nullptr;
@@ -193,11 +192,10 @@ void free_all(llmk_gpt2* g) {
   f(g->params); f(g->grads); f(g->m); f(g->v); f(g->params_bf16); f(g->encoded);
   for (auto& a : g->acts) {
     f(a.ln1_mean); f(a.ln1_rstd); f(a.ln2_mean); f(a.ln2_rstd); f(a.lse); f(a.res2); f(a.res3);
-    f(a.ln1); f(a.qkv); f(a.atty); f(a.ln2); f(a.fch_pre); f(a.fch_gelu); f(a.qkv16); f(a.atty16);
+    f(a.ln1); f(a.qkv); f(a.atty); f(a.ln2); f(a.fch_pre); f(a.fch_gelu); f(a.qkv16);
   }
   f(g->lnf_mean); f(g->lnf_rstd); f(g->losses); f(g->loss); f(g->lnf); f(g->logits);
   f(g->dres); f(g->dln); f(g->dres_bf16); f(g->datty); f(g->dqkv); f(g->dfch); f(g->workspace);
-  f(g->datty16); f(g->dqkv16);
   f(g->inputs); f(g->targets);
   if (g->h_inputs) cudaFreeHost(g->h_inputs);
   if (g->h_targets) cudaFreeHost(g->h_targets);
@@ -235,13 +233,10 @@ int alloc_all(llmk_gpt2* g) {
     LLMK_TRY(dalloc(&a.ln2_mean, BT)); LLMK_TRY(dalloc(&a.ln2_rstd, BT));
     LLMK_TRY(dalloc(&a.lse, B * NH * T));
     LLMK_TRY(dalloc(&a.res2, BT * C)); LLMK_TRY(dalloc(&a.res3, BT * C));
-    a.qkv16 = a.atty16 = nullptr;
+    a.qkv16 = nullptr;
     LLMK_TRY(aalloc(&a.ln1, BT * C)); LLMK_TRY(aalloc(&a.qkv, BT * 3 * C)); LLMK_TRY(aalloc(&a.atty, BT * C));
     LLMK_TRY(aalloc(&a.ln2, BT * C)); LLMK_TRY(aalloc(&a.fch_pre, BT * 4 * C)); LLMK_TRY(aalloc(&a.fch_gelu, BT * 4 * C));
-    if (!bf) {
-      LLMK_TRY(dalloc(&a.qkv16, BT * 3 * C));
-      LLMK_TRY(dalloc(&a.atty16, BT * C));
-    }
+    if (!bf) LLMK_TRY(dalloc(&a.qkv16, BT * 3 * C));
   }
   LLMK_TRY(dalloc(&g->lnf_mean, BT)); LLMK_TRY(dalloc(&g->lnf_rstd, BT));
   LLMK_TRY(dalloc(&g->losses, BT)); LLMK_TRY(dalloc(&g->loss, 1));
@@ -249,10 +244,6 @@ int alloc_all(llmk_gpt2* g) {
   LLMK_TRY(dalloc(&g->dres, BT * C)); LLMK_TRY(dalloc(&g->dln, BT * C));
   if (bf) LLMK_TRY(dalloc(&g->dres_bf16, BT * C));
   LLMK_TRY(aalloc(&g->datty, BT * C)); LLMK_TRY(aalloc(&g->dqkv, BT * 3 * C)); LLMK_TRY(aalloc(&g->dfch, BT * 4 * C));
-  if (!bf) {
-    LLMK_TRY(dalloc(&g->datty16, BT * C));
-    LLMK_TRY(dalloc(&g->dqkv16, BT * 3 * C));
-  }
   LLMK_TRY(dalloc(&g->inputs, BT)); LLMK_TRY(dalloc(&g->targets, BT));
   LLMK_CUDA(cudaMallocHost(reinterpret_cast<void**>(&g->h_inputs), BT * sizeof(int)));
   LLMK_CUDA(cudaMallocHost(reinterpret_cast<void**>(&g->h_targets), BT * sizeof(int)));
@@ -422,12 +413,12 @@ int llmk_gpt2_forward(llmk_gpt2* g, const int* d_inputs, const int* d_targets) {
     llmk_epilogue e1 = epi(P + p.qkvb);
     LLMK_TRY(llmk_gemm(a.qkv, adt, 3 * C, a.ln1, 0, C, W(p.qkvw), 0, C, mm, BT, 3 * C, C, &e1, nullptr, 0, s));
     if (bf) {
-      LLMK_TRY(llmk_attention_forward(a.atty, a.lse, a.qkv, B, T, 3 * C, NH, s));
+      LLMK_TRY(llmk_attention_forward(a.atty, LLMK_BF16, a.lse, a.qkv, B, T, 3 * C, NH, s));
     } else {
-      // the attention kernels are bf16: round the fp32 operands once, widen the output
+      // the attention MMAs take bf16 operands: round q, k, v once; the output
+      // leaves the kernel in fp32
       LLMK_TRY(llmk_cast(a.qkv16, LLMK_BF16, a.qkv, LLMK_F32, static_cast<long long>(BT) * 3 * C, s));
-      LLMK_TRY(llmk_attention_forward(a.atty16, a.lse, a.qkv16, B, T, 3 * C, NH, s));
-      LLMK_TRY(llmk_cast(a.atty, LLMK_F32, a.atty16, LLMK_BF16, static_cast<long long>(BT) * C, s));
+      LLMK_TRY(llmk_attention_forward(a.atty, LLMK_F32, a.lse, a.qkv16, B, T, 3 * C, NH, s));
     }
     llmk_epilogue e2 = epi(P + p.attprojb, x, C);  // residual add fused
     LLMK_TRY(llmk_gemm(a.res2, LLMK_F32, C, a.atty, 0, C, W(p.attprojw), 0, C, mm, BT, C, C, &e2, nullptr, 0, s));
@@ -514,13 +505,9 @@ int llmk_gpt2_backward(llmk_gpt2* g) {
     LLMK_TRY(llmk_gemm(G + p.attprojw, LLMK_F32, C, dres_op, 1, C, a.atty, 1, C, mm, C, C, BT, nullptr, ws, wsb, s));
     LLMK_TRY(llmk_gemm(g->datty, adt, C, dres_op, 0, C, W(p.attprojw), 1, C, mm, BT, C, C, nullptr, nullptr, 0, s));
     // attention
-    if (bf) {
-      LLMK_TRY(llmk_attention_backward(g->dqkv, g->datty, a.atty, a.qkv, a.lse, B, T, 3 * C, NH, ws, wsb, s));
-    } else {
-      LLMK_TRY(llmk_cast(g->datty16, LLMK_BF16, g->datty, LLMK_F32, static_cast<long long>(BT) * C, s));
-      LLMK_TRY(llmk_attention_backward(g->dqkv16, g->datty16, a.atty16, a.qkv16, a.lse, B, T, 3 * C, NH, ws, wsb, s));
-      LLMK_TRY(llmk_cast(g->dqkv, LLMK_F32, g->dqkv16, LLMK_BF16, static_cast<long long>(BT) * 3 * C, s));
-    }
+    // (tf32 mode: fp32 dO, O and dqkv; q, k, v from the bf16 copy the forward made)
+    LLMK_TRY(llmk_attention_backward(g->dqkv, g->datty, a.atty, adt, bf ? a.qkv : a.qkv16, a.lse, B, T, 3 * C, NH, ws,
+                                     wsb, s));
     // qkv: dW = dqkv^T ln1, db = colsum(dqkv), dln1 = dqkv Wqkv
     LLMK_TRY(llmk_gemm(G + p.qkvw, LLMK_F32, C, g->dqkv, 1, 3 * C, a.ln1, 1, C, mm, 3 * C, C, BT, nullptr, ws, wsb, s));
     LLMK_TRY(llmk_colsum(G + p.qkvb, g->dqkv, adt, BT, 3 * C, 0, ws, wsb, s));

@@ -58,9 +58,9 @@ SIGNATURES: dict[str, tuple] = {
     "llmk_colsum_workspace": (sz, [i32, i32]),
     "llmk_colsum": (i32, [vp, vp, i32, i32, i32, i32, vp, sz, vp]),
     "llmk_colsum_noalloc": (i32, [vp, vp, i32, i32, i32, i32, vp]),
-    "llmk_attention_forward": (i32, [vp, vp, vp, i32, i32, i32, i32, vp]),
+    "llmk_attention_forward": (i32, [vp, i32, vp, vp, i32, i32, i32, i32, vp]),
     "llmk_attention_backward_workspace": (sz, [i32, i32, i32, i32]),
-    "llmk_attention_backward": (i32, [vp, vp, vp, vp, vp, i32, i32, i32, i32, vp, sz, vp]),
+    "llmk_attention_backward": (i32, [vp, vp, vp, i32, vp, vp, i32, i32, i32, i32, vp, sz, vp]),
     "llmk_layernorm_forward": (i32, [vp, i32, vp, vp, vp, vp, vp, i32, i32, vp]),
     "llmk_layernorm_backward_workspace": (sz, [i32, i32]),
     "llmk_layernorm_backward": (i32, [vp, vp, vp, vp, vp, vp, i32, vp, vp, vp, vp, i32, i32, i32, vp, sz, vp]),

@@ -49,8 +49,8 @@ def main() -> None:
         out = torch.empty(Bb, T, C, device=dev, dtype=torch.bfloat16)
         lse = torch.empty(Bb, NH, T, device=dev)
         s = llmk.stream_ptr()
-        run = lambda: llmk.call("llmk_attention_forward", out.data_ptr(), lse.data_ptr(), qkv.data_ptr(), Bb, T,
-                                3 * C, NH, s)
+        run = lambda: llmk.call("llmk_attention_forward", out.data_ptr(), llmk.BF16, lse.data_ptr(), qkv.data_ptr(),
+                                Bb, T, 3 * C, NH, s)
         flop = 4.0 * Bb * NH * 64 * T * (T + 1) / 2
     else:
         Bb, T = (a.dims + [16, 1024][len(a.dims):])[:2]

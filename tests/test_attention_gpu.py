@@ -18,31 +18,34 @@ def _bf16_round(x):
     return torch.from_numpy(x).bfloat16().float().numpy()
 
 
-def _run_gpu(qkv_np, dout_np, B, T, C, NH, dev):
+def _run_gpu(qkv_np, dout_np, B, T, C, NH, dev, io="bf16"):
+    """One forward + backward through the C ABI. io: dtype of O, dO and dqkv."""
     import torch
     import llmk
+    tdt, code = (torch.bfloat16, llmk.BF16) if io == "bf16" else (torch.float32, llmk.F32)
     qkv = torch.from_numpy(qkv_np).to(dev).bfloat16().contiguous()
-    dout = torch.from_numpy(dout_np).to(dev).bfloat16().contiguous()
-    out = torch.full((B, T, C), float("nan"), device=dev, dtype=torch.bfloat16)
+    dout = torch.from_numpy(dout_np).to(dev).to(tdt).contiguous()
+    out = torch.full((B, T, C), float("nan"), device=dev, dtype=tdt)
     lse = torch.full((B, NH, T), float("nan"), device=dev)
     s = llmk.stream_ptr()
-    llmk.call("llmk_attention_forward", out.data_ptr(), lse.data_ptr(), qkv.data_ptr(), B, T, 3 * C, NH, s)
+    llmk.call("llmk_attention_forward", out.data_ptr(), code, lse.data_ptr(), qkv.data_ptr(), B, T, 3 * C, NH, s)
     ws_b = llmk.lib().llmk_attention_backward_workspace(B, T, 3 * C, NH)
     ws = torch.empty(ws_b // 4 + 64, device=dev)
-    dqkv = torch.full((B, T, 3 * C), float("nan"), device=dev, dtype=torch.bfloat16)
-    llmk.call("llmk_attention_backward", dqkv.data_ptr(), dout.data_ptr(), out.data_ptr(), qkv.data_ptr(),
+    dqkv = torch.full((B, T, 3 * C), float("nan"), device=dev, dtype=tdt)
+    llmk.call("llmk_attention_backward", dqkv.data_ptr(), dout.data_ptr(), out.data_ptr(), code, qkv.data_ptr(),
               lse.data_ptr(), B, T, 3 * C, NH, ws.data_ptr(), ws_b, s)
     torch.cuda.synchronize()
     assert llmk.device_status() == 0
     return out.float().cpu().numpy(), lse.cpu().numpy(), dqkv.float().cpu().numpy()
 
 
+@pytest.mark.parametrize("io", ["bf16", "f32"])
 @pytest.mark.parametrize("B,T,NH", [(1, 128, 1), (2, 256, 2), (1, 200, 3), (2, 64, 2), (1, 384, 2), (1, 1, 1)])
-def test_attention_vs_oracle(cuda_dev, B, T, NH):
+def test_attention_vs_oracle(cuda_dev, B, T, NH, io):
     C = 64 * NH
     qkv = _bf16_round(O.normal((B, T, 3 * C), 100 + T))
     dout = _bf16_round(O.normal((B, T, C), 200 + T))
-    out_g, lse_g, dqkv_g = _run_gpu(qkv, dout, B, T, C, NH, cuda_dev)
+    out_g, lse_g, dqkv_g = _run_gpu(qkv, dout, B, T, C, NH, cuda_dev, io)
     out_o = np.zeros((B, T, C), np.float32)
     att = np.zeros((B, NH, T, T), np.float32)
     lse_o = np.zeros((B, NH, T), np.float32)
@@ -93,6 +96,20 @@ def test_attention_rejects_head_size(cuda_dev):
     out = torch.zeros(1, 128, 96, device=cuda_dev, dtype=torch.bfloat16)
     lse = torch.zeros(1, 3, 128, device=cuda_dev)
     with pytest.raises(llmk.LlmkError) as e:
-        llmk.call("llmk_attention_forward", out.data_ptr(), lse.data_ptr(), qkv.data_ptr(), 1, 128, 288, 3,
+        llmk.call("llmk_attention_forward", out.data_ptr(), llmk.BF16, lse.data_ptr(), qkv.data_ptr(), 1, 128, 288, 3,
                   llmk.stream_ptr())
     assert e.value.code == 2
+
+
+def test_attention_f32_output_is_unrounded(cuda_dev):
+    """fp32 output mode returns the fp32 accumulator: it rounds to the bf16 output
+    of the bf16 mode (same kernel, same q, k, v) and is not itself bf16-valued."""
+    B, T, NH = 2, 256, 2
+    C = 64 * NH
+    qkv = _bf16_round(O.normal((B, T, 3 * C), 31))
+    dout = _bf16_round(O.normal((B, T, C), 32))
+    o16, l16, _ = _run_gpu(qkv, dout, B, T, C, NH, cuda_dev, "bf16")
+    o32, l32, _ = _run_gpu(qkv, dout, B, T, C, NH, cuda_dev, "f32")
+    assert np.array_equal(l16, l32)
+    assert np.array_equal(_bf16_round(o32), o16)
+    assert not np.array_equal(o32, o16)
