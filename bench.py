@@ -14,7 +14,10 @@ value: tokens/s of the whole job with tokens already resident in HBM,
 timed with CUDA events on the trainer's stream over exactly K steps between
 barriers, max over ranks. e2e: the same through llmk_gpt2_train_step from
 pinned host tokens to a host loss every step. roofline: the tcgen05 GEMM
-kernel over the step's GEMM shapes, timed alone with CUDA events.
+kernel over every GEMM of the step, timed live in the step (K further steps
+with CUDA events around each library call of the trainer); kernels: the same
+per kernel class with its share of the step and its fraction of the measured
+tensor or HBM peak; gemm_alone_*: each GEMM shape timed alone.
 cpu_baseline: the reference's own CPU training step (oracle/_ref, the
 llm.cpp sources built by oracle/Makefile) on a bounded sample, rank 0 only.
 """
@@ -42,6 +45,9 @@ METRIC = "GPT-2 124M train tokens/sec (B=16/GPU, T=1024)"
 # step at T=1024 would take tens of minutes; T=256 steps take a few seconds
 # each and overstate, not understate, the reference's throughput at T=1024.
 REF_SAMPLE = dict(B=1, T=256)
+# DRAM bytes (read + write) per gemm_tc_kernel launch of one training step,
+# from an ncu capture of the step's launches (profiles/); None until captured.
+GEMM_TRAFFIC_PER_LAUNCH = None
 
 
 def seeded_init_params(seed: int):
@@ -285,6 +291,20 @@ def main() -> None:
     launches = llmk.lib().llmk_launch_count() - n0
     ms = e0.elapsed_time(e1) / args.steps
     clocks = sampler.stop()
+    # per-kernel-class device time inside the training step: the same K steps
+    # again, with CUDA events on the trainer stream around every library call
+    # (kept out of the timed region above; the events add a little device time)
+    model.set_timing(True)
+    ei0, ei1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ei0.record(stream)
+    for _ in range(args.steps):
+        model.step_device(d_in, d_tg, LR, t)
+        t += 1
+    ei1.record(stream)
+    ei1.synchronize()
+    timed_ms = ei0.elapsed_time(ei1) / args.steps
+    classes = model.timing_report()
+    model.set_timing(False)
     # e2e: host tokens in, host loss out, every step
     barrier()
     w0 = time.perf_counter()
@@ -312,7 +332,21 @@ def main() -> None:
     if rank == 0:
         peaks = measured_peaks()
         roof = gemm_roofline(llmk, torch, BT)
-        achieved = roof["achieved_tflops"]
+        kernels = {}
+        for name, c in classes.items():
+            if c["calls"] == 0:
+                continue
+            tensor = c["unit"] == "flop"
+            rate = c["work"] / (c["ms"] * 1e-3) / (1e12 if tensor else 1e9) if c["ms"] > 0 else 0.0
+            peak = peaks["bf16_tflops"] if tensor else peaks["hbm_gbs"]
+            kernels[name] = {"ms_per_step": round(c["ms"] / args.steps, 4),
+                             "share": round(c["ms"] / args.steps / timed_ms, 4),
+                             "launches_per_step": c["launches"] // args.steps,
+                             "achieved": round(rate, 1), "unit": "TFLOP/s" if tensor else "GB/s",
+                             "frac": round(rate / peak, 4)}
+        g = classes["gemm"]
+        gemm_launches = max(g["launches"], 1)
+        achieved = g["work"] / (g["ms"] * 1e-3) / 1e12
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
@@ -324,12 +358,18 @@ def main() -> None:
                     "d2h_bytes_per_step": 4},
             "gpu_launches": int(launches),
             "loss": last_loss,
-            "roofline": {"kernel": "gemm_tc_kernel (all GEMM shapes of one step, timed alone)", "bound": "tensor",
-                         "achieved": round(achieved, 1), "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
-                         "frac": round(achieved / peaks["bf16_tflops"], 4), "traffic": None,
-                         "peak_source": peaks["source"] + " (bf16 burst)"},
-            "gemm_tflops": roof["per_gemm"],
-            "step_gemm_ms": round(roof["step_gemm_ms"], 3),
+            "roofline": {"kernel": "gemm_tc_kernel (every GEMM of the step, timed live in the step)",
+                         "bound": "tensor", "achieved": round(achieved, 1), "peak": peaks["bf16_tflops"],
+                         "unit": "TFLOP/s", "frac": round(achieved / peaks["bf16_tflops"], 4),
+                         "traffic": GEMM_TRAFFIC_PER_LAUNCH,
+                         "flop_per_launch": g["work"] / gemm_launches,
+                         "launch_ms": g["ms"] / gemm_launches,
+                         "peak_source": peaks["source"] + " bf16 burst (the step runs at max SM clock)"},
+            "kernels": kernels,
+            "instrumented_ms_per_step": round(timed_ms, 3),
+            "gemm_alone_tflops": roof["per_gemm"],
+            "gemm_alone_step_ms": round(roof["step_gemm_ms"], 3),
+            "gemm_alone_tflops_avg": round(roof["achieved_tflops"], 1),
             "clocks": clocks,
         }
         if not args.no_cpu_baseline:

@@ -100,6 +100,29 @@ int llmk_gpt2_broadcast_parameters(llmk_gpt2* model, int root);
  * communicator and returns LLMK_ERR_NCCL / LLMK_ERR_DEVICE_TIMEOUT. */
 int llmk_gpt2_synchronize(llmk_gpt2* model, int timeout_ms);
 
+/* ------------------------------------------------------- step timing */
+/* Per-kernel-class device time of the training step. The reference has no
+ * counterpart (its trainers time whole steps only, gpt2/traincuda.cpp). While
+ * timing is on, every library call llmk_gpt2_forward / _backward / _update
+ * makes is bracketed by two CUDA events on the model stream (a few
+ * microseconds of device time per call); llmk_gpt2_set_timing also clears the
+ * records. The report synchronises the model stream and sums, per class, the
+ * calls, the kernel launches they made, their device time and their
+ * algorithmic work: FLOPs (unit 0) for gemm / attention_fwd /
+ * attention_bwd, HBM bytes with each operand read once and each result
+ * written once (unit 1) for the bandwidth-bound classes. */
+typedef struct llmk_kernel_stat {
+  char name[24];
+  long long calls;
+  long long launches;
+  double ms;
+  double work;
+  int unit;
+} llmk_kernel_stat;
+int llmk_gpt2_set_timing(llmk_gpt2* model, int enable);
+/* Writes min(max, *count) records; *count = number of classes. */
+int llmk_gpt2_timing_report(llmk_gpt2* model, llmk_kernel_stat* out, int max, int* count);
+
 #ifdef __cplusplus
 }
 #endif

@@ -9,12 +9,21 @@
 // instruction descriptor's transpose bits absorb it, so no operand is ever
 // transposed in memory.
 //
-// CTA = 6 warps: warp 0 issues TMA loads into a kStages-deep ring of 128B-
-// swizzled smem stages, warp 1 owns TMEM and issues tcgen05.mma (one thread),
-// warps 2..5 drain the double-buffered TMEM accumulator (tcgen05.ld) through
-// the fused epilogue (bias, residual add, GELU, GELU-backward, accumulate)
-// while the next tile's mainloop runs. Split-K writes fp32 partial tiles to a
-// caller workspace, reduced deterministically by gemm_splitk_reduce.
+// CTA pairs (kPair): a cluster of two CTAs on two SMs computes a 256 x BN
+// tile with cta_group::2 MMAs issued by the leader CTA. Each CTA stages its
+// own 128 rows of A and half of the BN rows of B, so per SM the operand
+// traffic per MMA FLOP is a third lower than with one CTA per tile; each CTA's
+// TMEM holds its 128 x BN slice of the accumulator. Without kPair one CTA
+// computes a 128 x BN tile alone (small M).
+//
+// CTA = 10 warps: warp 0 issues TMA loads into a kStages-deep ring of 128B-
+// swizzled smem stages, warp 1 owns TMEM and (in the leader) issues
+// tcgen05.mma from one thread, warps 2..9 drain the double-buffered TMEM
+// accumulator (two warps per 32-lane TMEM quarter, one per column half)
+// through the fused epilogue (bias, residual add, GELU, GELU-backward,
+// accumulate) while the next tile's mainloop runs. Split-K writes fp32
+// partial tiles to a caller workspace, reduced deterministically by
+// gemm_splitk_reduce.
 #include <algorithm>
 #include <cstdio>
 
@@ -37,15 +46,16 @@ struct EpiParams {
   float* partial;  // split-K: fp32 [splits][M][N] workspace (raw accumulators)
 };
 
-template <bool kTF32, bool kAMN, bool kBMN, int kBN>
+template <bool kTF32, bool kAMN, bool kBMN, int kBN, bool kPair>
 struct Cfg {
   static constexpr int kElem = kTF32 ? 4 : 2;
-  static constexpr int BM = 128;
+  static constexpr int BM = 128;                   // accumulator rows per CTA
+  static constexpr int kMmaM = kPair ? 256 : 128;  // rows per tile (per MMA)
+  static constexpr int BNC = kPair ? kBN / 2 : kBN;  // B rows this CTA stages
   static constexpr int BK = 128 / kElem;           // K per stage (one 128-byte swizzle row)
   static constexpr int kAtomMN = 128 / kElem;      // M/N elements per 128-byte atom (MN-major)
-  static constexpr int kStages = (kBN == 256) ? 4 : 6;
   static constexpr int A_BYTES = BM * 128;
-  static constexpr int B_BYTES = kBN * 128;
+  static constexpr int B_BYTES = BNC * 128;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int kRowsPerMma = 32 / kElem;   // K of one MMA (16 bf16, 8 tf32)
   static constexpr int kKSteps = BK / kRowsPerMma; // 4
@@ -54,20 +64,30 @@ struct Cfg {
   // groups, 512 B apart); bf16 the plain 128B swizzle (8-row groups, 1024 B).
   static constexpr uint32_t kMNLayout = kTF32 ? kLayoutSW128Base32 : kLayoutSW128;
   static constexpr uint32_t kMNSbo = kTF32 ? 512 : 1024;
-  static constexpr int kThreads = 192;
-  // Epilogue staging for TMA stores: 4 warps x 2 buffers x [32 rows x 128 B].
+  static constexpr int kEpiWarps = 8;
+  static constexpr int kThreads = 64 + 32 * kEpiWarps;
+  // Epilogue staging for TMA stores: 8 warps x 2 buffers x [32 rows x 128 B].
+  static constexpr int STAGING_BYTES = kEpiWarps * 2 * 4096;
+  // as many operand stages as fit beside the staging buffers (227 KB per CTA)
+  static constexpr int kStagesFit = (232448 - 1024 - 256 - STAGING_BYTES) / STAGE_BYTES;
+  static constexpr int kStages = kStagesFit > 8 ? 8 : kStagesFit;
   static constexpr int STAGING_OFF = kStages * STAGE_BYTES;
-  static constexpr int STAGING_BYTES = 4 * 2 * 4096;
   static constexpr int BAR_OFF = STAGING_OFF + STAGING_BYTES;
   static constexpr size_t SMEM = size_t(BAR_OFF) + 256 + 1024;
   static_assert(kBN == 128 || kBN == 256, "BN");
+  static_assert(kStages >= 3, "stages");
+  static_assert(!kBMN || BNC % kAtomMN == 0, "B atoms");
 };
 
-__device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& m_blk, int& n_blk, int& split) {
+// Tile order: groups of G m-blocks; inside a group m runs fastest, so the
+// CTAs in flight share B panels, and the group's G A panels stay in L2 while
+// the group walks every n-block. G = num_m (one group) reads B from DRAM once
+// and sweeps A from L2: the host picks it when B is the operand that does not
+// fit in L2 beside the output stream (the tied lm_head forward).
+__device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int G, int& m_blk, int& n_blk, int& split) {
   const int per_split = num_m * num_n;
   split = t / per_split;
   t -= split * per_split;
-  constexpr int G = 8;  // m-blocks per raster group: consecutive tiles share B panels in L2
   const int per_group = G * num_n;
   const int g = t / per_group;
   const int r = t - g * per_group;
@@ -126,12 +146,12 @@ __device__ __forceinline__ void epi_ops8(const EpiParams& ep, long long gm, int 
       else store8_bf16(ep.aux + gm * ep.ldaux + gn, v);
     }
 #pragma unroll
-    for (int j = 0; j < 8; ++j) v[j] = gelu_tanh(v[j]);
+    for (int j = 0; j < 8; ++j) v[j] = ep.d_bf16 ? gelu_tanh_fast(v[j]) : gelu_tanh(v[j]);
   } else if (ep.flags & LLMK_EPI_GELU_BWD) {
     if (ep.flags & LLMK_EPI_AUX_F32) load8(reinterpret_cast<const float*>(ep.aux) + gm * ep.ldaux + gn, t);
     else load8_bf16(ep.aux + gm * ep.ldaux + gn, t);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) v[j] *= gelu_tanh_grad(t[j]);
+    for (int j = 0; j < 8; ++j) v[j] *= ep.d_bf16 ? gelu_tanh_grad_fast(t[j]) : gelu_tanh_grad(t[j]);
   }
   if (ep.flags & LLMK_EPI_ACCUMULATE) {
     if (ep.d_bf16) load8_bf16(static_cast<const __nv_bfloat16*>(ep.D) + gm * ep.ldd + gn, t);
@@ -187,12 +207,81 @@ __device__ __forceinline__ void epi_apply8(const EpiParams& ep, long long gm, in
   }
 }
 
-template <bool kTF32, bool kAMN, bool kBMN, int kBN>
-__global__ void __launch_bounds__(192, 1)
+// Drains columns [c_begin, c_end) of one warp's 32 accumulator rows (TMEM
+// lanes from `tsrc`) through the fused epilogue in chunks of 4 KB: 64 bf16 or
+// 32 fp32 columns.
+// Each chunk is written 128B-swizzled into one of the warp's two staging
+// buffers and stored by one lane with a TMA store; the buffers alternate, so
+// a chunk's smem writes only wait for the store issued two chunks earlier.
+// Rows / columns past M / N are clipped by the tensor map.
+template <bool kBF16>
+__device__ __forceinline__ void epilogue_cols(const EpiParams& ep, const CUtensorMap* tmD, uint32_t tsrc, int row0,
+                                              int n0, int c_begin, int c_end, int sp, int M, int N, int lane,
+                                              uint8_t* stg, uint32_t& nstore) {
+  constexpr int CW = kBF16 ? 64 : 32;  // columns per chunk
+  const long long gm = row0 + lane;
+  const bool row_ok = gm < M && !ep.partial;
+  const int r7 = lane & 7;
+#pragma unroll 1
+  for (int c0 = c_begin; c0 < c_end; c0 += CW) {
+    const int gn0 = n0 + c0;
+    if (gn0 >= N) break;
+    float v[CW];
+    {
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(tsrc + c0, r);
+      if constexpr (kBF16) {
+        uint32_t r2[32];
+        tmem_ld_32x32b_x32(tsrc + c0 + 32, r2);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[32 + j] = __uint_as_float(r2[j]);
+      } else {
+        tmem_ld_wait();
+      }
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+    }
+    if (row_ok) {
+#pragma unroll
+      for (int k = 0; k < CW / 8; ++k)
+        if (gn0 + k * 8 < N) epi_ops8(ep, gm, gn0 + k * 8, v + k * 8);
+    }
+    uint8_t* buf = stg + (nstore & 1u) * 4096;
+    // the store that last read this buffer (two chunks ago) must be done reading
+    if (lane == 0) bulk_wait_read1();
+    __syncwarp();
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      uint4 u;
+      if constexpr (kBF16) {
+        u.x = pack_bf16x2(v[k * 8 + 0], v[k * 8 + 1]);
+        u.y = pack_bf16x2(v[k * 8 + 2], v[k * 8 + 3]);
+        u.z = pack_bf16x2(v[k * 8 + 4], v[k * 8 + 5]);
+        u.w = pack_bf16x2(v[k * 8 + 6], v[k * 8 + 7]);
+      } else {
+        u = make_uint4(__float_as_uint(v[k * 4]), __float_as_uint(v[k * 4 + 1]), __float_as_uint(v[k * 4 + 2]),
+                       __float_as_uint(v[k * 4 + 3]));
+      }
+      *reinterpret_cast<uint4*>(buf + lane * 128 + ((k ^ r7) << 4)) = u;
+    }
+    fence_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      if (ep.partial) tma_store_3d(tmD, buf, gn0, row0, sp);
+      else tma_store_2d(tmD, buf, gn0, row0);
+      bulk_commit();
+    }
+    ++nstore;
+  }
+}
+
+template <bool kTF32, bool kAMN, bool kBMN, int kBN, bool kPair>
+__global__ void __launch_bounds__(Cfg<kTF32, kAMN, kBMN, kBN, kPair>::kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmD, EpiParams ep, int M, int N, int K, int splits,
-                   unsigned int* status) {
-  using C = Cfg<kTF32, kAMN, kBMN, kBN>;
+                   int group_m, unsigned int* status) {
+  using C = Cfg<kTF32, kAMN, kBMN, kBN, kPair>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
@@ -205,6 +294,8 @@ __global__ void __launch_bounds__(192, 1)
 
   const int warp = warp_id();
   const int lane = lane_id();
+  const uint32_t rank = kPair ? cluster_ctarank() : 0u;
+  const bool leader = rank == 0;
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::kStages; ++s) {
       mbar_init(full + s, 1);
@@ -212,7 +303,8 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(accf + a, 1);
-      mbar_init(acce + a, 128);
+      // one arrival per epilogue warp, of both CTAs of a pair (on the leader's barrier)
+      mbar_init(acce + a, kPair ? 2 * C::kEpiWarps : C::kEpiWarps);
     }
     mbar_init(done, 1);
     *abort_flag = 0;
@@ -223,49 +315,81 @@ __global__ void __launch_bounds__(192, 1)
     tma_prefetch_desc(&tmB);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, C::kTmemCols);
-    tmem_relinquish();
+    if (kPair) {
+      tmem_alloc_pair(tmem_slot, C::kTmemCols);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, C::kTmemCols);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  __syncwarp();
+  // the peer's barriers are initialised before any remote arrive / complete_tx
+  if (kPair) cluster_sync();
+  else __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  const int num_m = (M + C::BM - 1) / C::BM;
+  const int num_m = (M + C::kMmaM - 1) / C::kMmaM;
   const int num_n = (N + kBN - 1) / kBN;
   const int num_tiles = num_m * num_n * splits;
   const int num_kb = (K + C::BK - 1) / C::BK;
   const int kb_per = (num_kb + splits - 1) / splits;
+  const int unit = kPair ? static_cast<int>(blockIdx.x) >> 1 : static_cast<int>(blockIdx.x);
+  const int units = kPair ? static_cast<int>(gridDim.x) >> 1 : static_cast<int>(gridDim.x);
 
   if (warp == 0) {
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      for (int tile = unit; tile < num_tiles; tile += units) {
         int mb, nb, sp;
-        tile_coords(tile, num_m, num_n, mb, nb, sp);
-        const int m0 = mb * C::BM, n0 = nb * kBN;
+        tile_coords(tile, num_m, num_n, group_m, mb, nb, sp);
+        const int m0 = mb * C::kMmaM + static_cast<int>(rank) * C::BM;
+        const int nc0 = nb * kBN + static_cast<int>(rank) * C::BNC;
         const int kb0 = sp * kb_per, kb1 = min(num_kb, kb0 + kb_per);
         bool ok = true;
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(empty + stage, phase ^ 1u, status, abort_flag)) { ok = false; break; }
           uint8_t* sA = smem + stage * C::STAGE_BYTES;
           uint8_t* sB = sA + C::A_BYTES;
-          mbar_arrive_expect_tx(full + stage, C::STAGE_BYTES);
           const int k0 = kb * C::BK;
-          if (!kAMN) {
-            tma_load_2d(sA, &tmA, full + stage, k0, m0);
-          } else {
+          if (kPair) {
+            // both CTAs' loads complete on the leader's full barrier, which
+            // expects the bytes of the pair
+            const uint32_t fb = mapa_shared(smem_u32(full + stage), 0);
+            if (leader) mbar_arrive_expect_tx(full + stage, 2 * C::STAGE_BYTES);
+            if (!kAMN) {
+              tma_load_2d_pair(sA, &tmA, fb, k0, m0);
+            } else {
 #pragma unroll
-            for (int j = 0; j < C::BM / C::kAtomMN; ++j)
-              tma_load_2d(sA + j * C::BK * 128, &tmA, full + stage, m0 + j * C::kAtomMN, k0);
-          }
-          if (!kBMN) {
-            tma_load_2d(sB, &tmB, full + stage, k0, n0);
-          } else {
+              for (int j = 0; j < C::BM / C::kAtomMN; ++j)
+                tma_load_2d_pair(sA + j * C::BK * 128, &tmA, fb, m0 + j * C::kAtomMN, k0);
+            }
+            if (!kBMN) {
+              tma_load_2d_pair(sB, &tmB, fb, k0, nc0);
+            } else {
 #pragma unroll
-            for (int j = 0; j < kBN / C::kAtomMN; ++j)
-              tma_load_2d(sB + j * C::BK * 128, &tmB, full + stage, n0 + j * C::kAtomMN, k0);
+              for (int j = 0; j < C::BNC / C::kAtomMN; ++j)
+                tma_load_2d_pair(sB + j * C::BK * 128, &tmB, fb, nc0 + j * C::kAtomMN, k0);
+            }
+          } else {
+            mbar_arrive_expect_tx(full + stage, C::STAGE_BYTES);
+            if (!kAMN) {
+              tma_load_2d(sA, &tmA, full + stage, k0, m0);
+            } else {
+#pragma unroll
+              for (int j = 0; j < C::BM / C::kAtomMN; ++j)
+                tma_load_2d(sA + j * C::BK * 128, &tmA, full + stage, m0 + j * C::kAtomMN, k0);
+            }
+            if (!kBMN) {
+              tma_load_2d(sB, &tmB, full + stage, k0, nc0);
+            } else {
+#pragma unroll
+              for (int j = 0; j < C::BNC / C::kAtomMN; ++j)
+                tma_load_2d(sB + j * C::BK * 128, &tmB, full + stage, nc0 + j * C::kAtomMN, k0);
+            }
           }
           if (++stage == C::kStages) { stage = 0; phase ^= 1u; }
         }
@@ -273,15 +397,15 @@ __global__ void __launch_bounds__(192, 1)
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      const uint32_t idesc = idesc_f32acc(128, kBN, kTF32 ? kFmtTF32 : kFmtBF16, kAMN, kBMN);
+    if (lane == 0 && leader) {
+      const uint32_t idesc = idesc_f32acc(C::kMmaM, kBN, kTF32 ? kFmtTF32 : kFmtBF16, kAMN, kBMN);
       int stage = 0;
       uint32_t phase = 0;
       int local = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
+      for (int tile = unit; tile < num_tiles && ok; tile += units, ++local) {
         int mb, nb, sp;
-        tile_coords(tile, num_m, num_n, mb, nb, sp);
+        tile_coords(tile, num_m, num_n, group_m, mb, nb, sp);
         const int kb0 = sp * kb_per, kb1 = min(num_kb, kb0 + kb_per);
         const int acc = local & 1;
         const uint32_t aphase = (local >> 1) & 1;
@@ -301,109 +425,72 @@ __global__ void __launch_bounds__(192, 1)
             if (!kBMN) bdesc = sdesc_sw128(sB + ks * 32, 16, 1024);
             else bdesc = sdesc_sw128(sB + ks * C::kRowsPerMma * 128, C::BK * 128, C::kMNSbo, C::kMNLayout);
             const uint32_t accum = (kb > kb0 || ks > 0) ? 1u : 0u;
-            if (kTF32) mma_tf32_ss(d_tmem, adesc, bdesc, idesc, accum);
-            else mma_f16_ss(d_tmem, adesc, bdesc, idesc, accum);
+            if (kPair) {
+              if (kTF32) mma_tf32_ss_pair(d_tmem, adesc, bdesc, idesc, accum);
+              else mma_f16_ss_pair(d_tmem, adesc, bdesc, idesc, accum);
+            } else {
+              if (kTF32) mma_tf32_ss(d_tmem, adesc, bdesc, idesc, accum);
+              else mma_f16_ss(d_tmem, adesc, bdesc, idesc, accum);
+            }
           }
-          mma_commit(empty + stage);
+          // the stage is free in both CTAs once these MMAs have read it
+          if (kPair) mma_commit_pair(empty + stage, 3);
+          else mma_commit(empty + stage);
           if (++stage == C::kStages) { stage = 0; phase ^= 1u; }
         }
         if (!ok) break;
-        mma_commit(accf + acc);
+        if (kPair) mma_commit_pair(accf + acc, 3);
+        else mma_commit(accf + acc);
       }
       // All MMAs issued by this thread complete before TMEM is released.
-      mma_commit(done);
+      if (kPair) mma_commit_pair(done, 1);
+      else mma_commit(done);
       mbar_wait(done, 0, status, nullptr);
     }
     __syncwarp();
   } else {
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int ew = warp - 2;               // epilogue warp 0..7
+    const int q = warp & 3;                // TMEM lane quarter this warp may access
+    const int half = ew >> 2;              // column half of the tile
+    uint8_t* stg = smem + C::STAGING_OFF + ew * 8192;  // two 4 KB buffers, used alternately
+    uint32_t nstore = 0;                               // store groups this warp committed
+    const uint32_t acce_leader0 = kPair ? mapa_shared(smem_u32(acce), 0) : smem_u32(acce);
     int local = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+    for (int tile = unit; tile < num_tiles; tile += units, ++local) {
       int mb, nb, sp;
-      tile_coords(tile, num_m, num_n, mb, nb, sp);
-      const int m0 = mb * C::BM, n0 = nb * kBN;
+      tile_coords(tile, num_m, num_n, group_m, mb, nb, sp);
+      const int m0 = mb * C::kMmaM + static_cast<int>(rank) * C::BM;
+      const int n0 = nb * kBN;
       const int acc = local & 1;
       const uint32_t aphase = (local >> 1) & 1;
       bool ok = mbar_wait(accf + acc, aphase, status, abort_flag);
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
-      const long long gm = m0 + q * 32 + lane;
-      const bool row_ok = gm < M;
-      // 64-column groups: two TMEM loads, epilogue ops in registers, then the
-      // row is written 128B-swizzled into this warp's staging buffer and one
-      // lane issues a TMA store of the warp's [32 x 32] fp32 or [32 x 64] bf16
-      // block (rows / columns past M / N are clipped by the tensor map).
-      uint8_t* stg = smem + C::STAGING_OFF + (q * 2) * 4096;
-      const bool bf16_out = ep.d_bf16 && !ep.partial;
-#pragma unroll 1
-      for (int g = 0; g < kBN / 64; ++g) {
-        const int gn0 = n0 + g * 64;
-        if (gn0 >= N) break;
-        float v[64];
-        {
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * kBN + g * 64, r);
-          tmem_ld_wait();
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-          tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * kBN + g * 64 + 32, r);
-          tmem_ld_wait();
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[32 + j] = __uint_as_float(r[j]);
-        }
-        if (row_ok && !ep.partial) {
-#pragma unroll
-          for (int k = 0; k < 8; ++k)
-            if (gn0 + k * 8 < N) epi_ops8(ep, gm, gn0 + k * 8, v + k * 8);
-        }
-        // the previous group's stores must have read the staging buffers
-        if (lane == 0) bulk_wait_read0();
-        __syncwarp();
-        const int r7 = lane & 7;
-        if (bf16_out) {
-#pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            uint4 u;
-            u.x = pack_bf16x2(v[k * 8 + 0], v[k * 8 + 1]);
-            u.y = pack_bf16x2(v[k * 8 + 2], v[k * 8 + 3]);
-            u.z = pack_bf16x2(v[k * 8 + 4], v[k * 8 + 5]);
-            u.w = pack_bf16x2(v[k * 8 + 6], v[k * 8 + 7]);
-            *reinterpret_cast<uint4*>(stg + lane * 128 + ((k ^ r7) << 4)) = u;
-          }
-        } else {
-#pragma unroll
-          for (int h = 0; h < 2; ++h)
-#pragma unroll
-            for (int k = 0; k < 8; ++k)
-              *reinterpret_cast<float4*>(stg + h * 4096 + lane * 128 + ((k ^ r7) << 4)) =
-                  make_float4(v[h * 32 + k * 4], v[h * 32 + k * 4 + 1], v[h * 32 + k * 4 + 2], v[h * 32 + k * 4 + 3]);
-        }
-        fence_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          const int y = m0 + q * 32;
-          if (bf16_out) {
-            tma_store_2d(&tmD, stg, gn0, y);
-          } else if (ep.partial) {
-            tma_store_3d(&tmD, stg, gn0, y, sp);
-            if (gn0 + 32 < N) tma_store_3d(&tmD, stg + 4096, gn0 + 32, y, sp);
-          } else {
-            tma_store_2d(&tmD, stg, gn0, y);
-            if (gn0 + 32 < N) tma_store_2d(&tmD, stg + 4096, gn0 + 32, y);
-          }
-          bulk_commit();
-        }
-      }
+      const uint32_t tsrc = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * kBN;
+      const int cb = half * (kBN / 2), ce = cb + kBN / 2;
+      if (ep.d_bf16 && !ep.partial)
+        epilogue_cols<true>(ep, &tmD, tsrc, m0 + q * 32, n0, cb, ce, sp, M, N, lane, stg, nstore);
+      else
+        epilogue_cols<false>(ep, &tmD, tsrc, m0 + q * 32, n0, cb, ce, sp, M, N, lane, stg, nstore);
       tc_fence_before();
-      mbar_arrive(acce + acc);
+      __syncwarp();
+      if (lane == 0) {
+        if (kPair) mbar_arrive_cluster(acce_leader0 + acc * 8);
+        else mbar_arrive(acce + acc);
+      }
     }
   }
   if (warp >= 2 && lane == 0) bulk_wait0();  // stores complete before the CTA retires
   tc_fence_before();
-  __syncthreads();
+  __syncwarp();
+  // the leader's MMAs into the peer's TMEM, and the peer's remote arrivals on
+  // the leader's barriers, are done before either CTA frees TMEM or exits
+  if (kPair) cluster_sync();
+  else __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, C::kTmemCols);
+    if (kPair) tmem_dealloc_pair(tmem_base, C::kTmemCols);
+    else tmem_dealloc(tmem_base, C::kTmemCols);
   }
 }
 
@@ -426,11 +513,48 @@ __global__ void gemm_splitk_reduce(EpiParams ep, int M, int N, int splits) {
   }
 }
 
-template <bool kTF32, bool kAMN, bool kBMN, int kBN>
+// Persistent grid: one CTA (or CTA pair) per SM that can hold one, at most
+// one per tile. Pairs need two SMs of one GPC, so their count comes from the
+// occupancy calculator (cached per kernel and device).
+template <typename Kern>
+int persistent_units(Kern kern, bool pair, size_t smem, int threads, int* units) {
+  static int cache[2][64] = {};
+  int dev = 0;
+  LLMK_CUDA(cudaGetDevice(&dev));
+  if (dev >= 64) dev = 63;
+  int& c = cache[pair ? 1 : 0][dev];
+  if (c == 0) {
+    if (!pair) {
+      c = num_sms();
+    } else {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(2 * num_sms());
+      cfg.blockDim = dim3(threads);
+      cfg.dynamicSmemBytes = smem;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = 2;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      int clusters = 0;
+      if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) != cudaSuccess || clusters <= 0) {
+        cudaGetLastError();
+        clusters = num_sms() / 2;
+      }
+      c = std::min(clusters, num_sms() / 2);
+    }
+  }
+  *units = c;
+  return LLMK_OK;
+}
+
+template <bool kTF32, bool kAMN, bool kBMN, int kBN, bool kPair>
 int launch_gemm(const void* A, long long lda, const void* B, long long ldb, int M, int N, int K, EpiParams ep,
                 int splits, cudaStream_t stream) {
-  using C = Cfg<kTF32, kAMN, kBMN, kBN>;
-  auto kern = gemm_tc_kernel<kTF32, kAMN, kBMN, kBN>;
+  using C = Cfg<kTF32, kAMN, kBMN, kBN, kPair>;
+  auto kern = gemm_tc_kernel<kTF32, kAMN, kBMN, kBN, kPair>;
   static bool attr_done[64] = {};
   int dev = 0;
   LLMK_CUDA(cudaGetDevice(&dev));
@@ -443,7 +567,7 @@ int launch_gemm(const void* A, long long lda, const void* B, long long ldb, int 
   const CUtensorMapSwizzle mn_swz = kTF32 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B;
   if (!kAMN) LLMK_TRY(make_tmap_2d(&ta, A, dt, K, M, lda * C::kElem, C::BK, C::BM));
   else LLMK_TRY(make_tmap_2d(&ta, A, dt, M, K, lda * C::kElem, C::kAtomMN, C::BK, mn_swz));
-  if (!kBMN) LLMK_TRY(make_tmap_2d(&tb, B, dt, K, N, ldb * C::kElem, C::BK, kBN));
+  if (!kBMN) LLMK_TRY(make_tmap_2d(&tb, B, dt, K, N, ldb * C::kElem, C::BK, C::BNC));
   else LLMK_TRY(make_tmap_2d(&tb, B, dt, N, K, ldb * C::kElem, C::kAtomMN, C::BK, mn_swz));
   CUtensorMap td;
   if (ep.partial) {
@@ -454,41 +578,83 @@ int launch_gemm(const void* A, long long lda, const void* B, long long ldb, int 
   } else {
     LLMK_TRY(make_tmap_2d(&td, ep.D, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, N, M, ep.ldd * 4, 32, 32));
   }
-  const int num_tiles = ((M + C::BM - 1) / C::BM) * ((N + kBN - 1) / kBN) * splits;
-  const int grid = std::min(num_tiles, num_sms());
+  const int num_m = (M + C::kMmaM - 1) / C::kMmaM;
+  const int num_tiles = num_m * ((N + kBN - 1) / kBN) * splits;
+  // raster group (tile rows): one group over all of M when B is large (> 32 MB,
+  // so it would be re-read from DRAM once per group) and A fits in L2 (<= 32 MB)
+  const double a_bytes = static_cast<double>(M) * K * C::kElem, b_bytes = static_cast<double>(N) * K * C::kElem;
+  const int group_m = (b_bytes > 32e6 && a_bytes <= 32e6) ? num_m : std::min(8, num_m);
+  int units = 0;
+  LLMK_TRY(persistent_units(kern, kPair, C::SMEM, C::kThreads, &units));
+  units = std::min(units, num_tiles);
   unsigned int* st = device_status_ptr();
-  kern<<<grid, C::kThreads, C::SMEM, static_cast<cudaStream_t>(stream)>>>(ta, tb, td, ep, M, N, K, splits, st);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (kPair) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * units);
+    cfg.blockDim = dim3(C::kThreads);
+    cfg.dynamicSmemBytes = C::SMEM;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    LLMK_CUDA(cudaLaunchKernelEx(&cfg, kern, ta, tb, td, ep, M, N, K, splits, group_m, st));
+  } else {
+    kern<<<units, C::kThreads, C::SMEM, s>>>(ta, tb, td, ep, M, N, K, splits, group_m, st);
+  }
   count_launch();
   LLMK_CUDA(cudaGetLastError());
   return LLMK_OK;
 }
 
-template <bool kTF32, int kBN>
+template <bool kTF32, int kBN, bool kPair>
 int dispatch_major(int a_trans, int b_trans, const void* A, long long lda, const void* B, long long ldb, int M,
                    int N, int K, const EpiParams& ep, int splits, cudaStream_t s) {
-  if (!a_trans && !b_trans) return launch_gemm<kTF32, false, false, kBN>(A, lda, B, ldb, M, N, K, ep, splits, s);
-  if (!a_trans && b_trans) return launch_gemm<kTF32, false, true, kBN>(A, lda, B, ldb, M, N, K, ep, splits, s);
-  if (a_trans && b_trans) return launch_gemm<kTF32, true, true, kBN>(A, lda, B, ldb, M, N, K, ep, splits, s);
-  return launch_gemm<kTF32, true, false, kBN>(A, lda, B, ldb, M, N, K, ep, splits, s);
+  if (!a_trans && !b_trans) return launch_gemm<kTF32, false, false, kBN, kPair>(A, lda, B, ldb, M, N, K, ep, splits, s);
+  if (!a_trans && b_trans) return launch_gemm<kTF32, false, true, kBN, kPair>(A, lda, B, ldb, M, N, K, ep, splits, s);
+  if (a_trans && b_trans) return launch_gemm<kTF32, true, true, kBN, kPair>(A, lda, B, ldb, M, N, K, ep, splits, s);
+  return launch_gemm<kTF32, true, false, kBN, kPair>(A, lda, B, ldb, M, N, K, ep, splits, s);
+}
+
+// kind: 0 = single CTA, BN 128; 1 = CTA pair, BN 128; 2 = CTA pair, BN 256
+template <bool kTF32>
+int dispatch_kind(int kind, int a_trans, int b_trans, const void* A, long long lda, const void* B, long long ldb,
+                  int M, int N, int K, const EpiParams& ep, int splits, cudaStream_t s) {
+  if (kind == 2) return dispatch_major<kTF32, 256, true>(a_trans, b_trans, A, lda, B, ldb, M, N, K, ep, splits, s);
+  if (kind == 1) return dispatch_major<kTF32, 128, true>(a_trans, b_trans, A, lda, B, ldb, M, N, K, ep, splits, s);
+  return dispatch_major<kTF32, 128, false>(a_trans, b_trans, A, lda, B, ldb, M, N, K, ep, splits, s);
 }
 
 }  // namespace
 
-// Chooses BN and the split-K factor. Split-K only when the output tile grid
-// leaves most SMs idle and K is long (the dweight GEMMs: M,N = layer width,
-// K = B*T tokens).
-static void plan_gemm(int M, int N, int K, int elem, int* bn, int* splits) {
+// Chooses the kernel kind (CTA pair with BN 256 or 128 for M >= 256, else a
+// single CTA with BN 128) and the split-K factor. Split-K only when the tile
+// grid leaves most SMs idle and K is long (the dweight GEMMs: M,N = layer
+// width, K = B*T tokens).
+static void plan_gemm(int M, int N, int K, int elem, int* kind, int* splits) {
   const int sms = num_sms();
-  const int num_m = (M + 127) / 128;
-  const int t256 = num_m * ((N + 255) / 256), t128 = num_m * ((N + 127) / 128);
-  const long long w256 = (t256 + sms - 1) / sms, w128 = (t128 + sms - 1) / sms;
-  // A 128-wide tile costs ~half a 256-wide one plus a smem-bandwidth penalty.
-  *bn = (w256 * 256 * 10 <= w128 * 128 * 11) ? 256 : 128;
-  const int tiles = (*bn == 256) ? t256 : t128;
+  int tiles, units;
+  if (M >= 256) {
+    units = sms / 2;
+    const int num_m = (M + 255) / 256;
+    const int t256 = num_m * ((N + 255) / 256), t128 = num_m * ((N + 127) / 128);
+    const long long w256 = (t256 + units - 1) / units, w128 = (t128 + units - 1) / units;
+    // a 128-wide tile costs about half a 256-wide one plus a fixed overhead
+    *kind = (w256 * 256 * 10 <= w128 * 128 * 11) ? 2 : 1;
+    tiles = (*kind == 2) ? t256 : t128;
+  } else {
+    units = sms;
+    *kind = 0;
+    tiles = ((M + 127) / 128) * ((N + 127) / 128);
+  }
   const int bk = 128 / elem;
   const int num_kb = (K + bk - 1) / bk;
   int s = 1;
-  while (tiles * s < sms && num_kb / (s * 2) >= 8) s *= 2;
+  while (tiles * s < units && num_kb / (s * 2) >= 8) s *= 2;
   // Every split must own at least one K block (an empty split would publish
   // a stale accumulator).
   while (s > 1 && ((num_kb + s - 1) / s) * (s - 1) >= num_kb) s /= 2;
@@ -526,17 +692,14 @@ static int gemm_impl(void* D, llmk_dtype d_dtype, long long ldd, const void* A, 
       return fail(LLMK_ERR_UNSUPPORTED, "gemm: epilogue operands need 16-byte alignment");
     if ((ep.flags & LLMK_EPI_GELU_BWD) && !ep.aux) return fail(LLMK_ERR_INVALID_ARG, "gemm: GELU_BWD needs aux");
   }
-  int bn, splits;
-  plan_gemm(M, N, K, elem, &bn, &splits);
+  int kind, splits;
+  plan_gemm(M, N, K, elem, &kind, &splits);
   const size_t need = static_cast<size_t>(splits) * M * N * sizeof(float);
   if (splits > 1 && (!workspace || workspace_bytes < need || !aligned16(workspace))) splits = 1;
   if (splits > 1) ep.partial = static_cast<float*>(workspace);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  int rc;
-  if (elem == 4) rc = bn == 256 ? dispatch_major<true, 256>(a_trans, b_trans, A, lda, B, ldb, M, N, K, ep, splits, s)
-                                : dispatch_major<true, 128>(a_trans, b_trans, A, lda, B, ldb, M, N, K, ep, splits, s);
-  else rc = bn == 256 ? dispatch_major<false, 256>(a_trans, b_trans, A, lda, B, ldb, M, N, K, ep, splits, s)
-                      : dispatch_major<false, 128>(a_trans, b_trans, A, lda, B, ldb, M, N, K, ep, splits, s);
+  const int rc = elem == 4 ? dispatch_kind<true>(kind, a_trans, b_trans, A, lda, B, ldb, M, N, K, ep, splits, s)
+                           : dispatch_kind<false>(kind, a_trans, b_trans, A, lda, B, ldb, M, N, K, ep, splits, s);
   if (rc != LLMK_OK || splits == 1) return rc;
   const long long groups = static_cast<long long>(M) * (N / 8);
   const int grid = static_cast<int>(std::min<long long>((groups + 255) / 256, num_sms() * 8LL));
@@ -550,8 +713,8 @@ extern "C" {
 
 size_t llmk_gemm_workspace(int M, int N, int K, llmk_math math) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
-  int bn, splits;
-  plan_gemm(M, N, K, math == LLMK_MATH_TF32 ? 4 : 2, &bn, &splits);
+  int kind, splits;
+  plan_gemm(M, N, K, math == LLMK_MATH_TF32 ? 4 : 2, &kind, &splits);
   return splits > 1 ? static_cast<size_t>(splits) * M * N * sizeof(float) : 0;
 }
 

@@ -114,11 +114,69 @@ struct llmk_gpt2 {
   std::vector<cudaEvent_t> layer_done;
   cudaEvent_t embed_done = nullptr, comm_done = nullptr, h2d_done = nullptr;
   unsigned long long steps = 0;
+  // per-kernel-class timing (llmk_gpt2_set_timing): event pairs on `stream`
+  struct Mark {
+    int cls;
+    double work;
+    int e0, e1;
+    unsigned long long launches;
+  };
+  bool timing = false;
+  std::vector<cudaEvent_t> tev;
+  size_t tev_used = 0;
+  std::vector<Mark> marks;
 };
 
 namespace {
 
 int ensure_device(llmk_gpt2* g) { return llmk::cuda_check(cudaSetDevice(g->device), "cudaSetDevice"); }
+
+// ------------------------------------------------------- step timing
+// Kernel classes of one training step; work is algorithmic FLOPs for the
+// tensor-core classes and algorithmic HBM bytes (each operand read once,
+// each result written once) for the bandwidth classes.
+enum KClass { KC_GEMM = 0, KC_ATTN_FWD, KC_ATTN_BWD, KC_LN_FWD, KC_LN_BWD, KC_XENT, KC_COLSUM, KC_ADAMW, KC_ENCODER,
+              KC_CAST, KC_OTHER, KC_COUNT };
+const char* const kClassName[KC_COUNT] = {"gemm", "attention_fwd", "attention_bwd", "layernorm_fwd", "layernorm_bwd",
+                                          "softmax_xent", "colsum", "adamw", "encoder", "cast", "other"};
+const int kClassUnit[KC_COUNT] = {0, 0, 0, 1, 1, 1, 1, 1, 1, 1, 1};  // 0 flop, 1 byte
+
+int timing_event(llmk_gpt2* g) {
+  if (g->tev_used == g->tev.size()) {
+    cudaEvent_t e;
+    if (cudaEventCreate(&e) != cudaSuccess) return -1;
+    g->tev.push_back(e);
+  }
+  return static_cast<int>(g->tev_used++);
+}
+
+// Brackets the launches of one library call with two events on the model
+// stream while timing is on; a no-op otherwise.
+struct TimedScope {
+  llmk_gpt2* g;
+  int idx = -1;
+  TimedScope(llmk_gpt2* model, int cls, double work) : g(model) {
+    if (!g->timing) return;
+    const int e0 = timing_event(g);
+    if (e0 < 0 || cudaEventRecord(g->tev[e0], g->stream) != cudaSuccess) return;
+    idx = static_cast<int>(g->marks.size());
+    g->marks.push_back({cls, work, e0, -1, llmk_launch_count()});
+  }
+  ~TimedScope() {
+    if (idx < 0) return;
+    const int e1 = timing_event(g);
+    if (e1 < 0 || cudaEventRecord(g->tev[e1], g->stream) != cudaSuccess) {
+      g->marks.resize(idx);
+      return;
+    }
+    g->marks[idx].e1 = e1;
+    g->marks[idx].launches = llmk_launch_count() - g->marks[idx].launches;
+  }
+  TimedScope(const TimedScope&) = delete;
+  TimedScope& operator=(const TimedScope&) = delete;
+};
+
+double causal_pairs(int T) { return 0.5 * static_cast<double>(T) * (T + 1); }
 
 int nccl_check(ncclResult_t r, const char* what) {
   if (r == ncclSuccess) return LLMK_OK;
@@ -204,6 +262,7 @@ void free_all(llmk_gpt2* g) {
   if (g->embed_done) cudaEventDestroy(g->embed_done);
   if (g->comm_done) cudaEventDestroy(g->comm_done);
   if (g->h2d_done) cudaEventDestroy(g->h2d_done);
+  for (auto e : g->tev) cudaEventDestroy(e);
   if (g->comm) ncclCommDestroy(g->comm);
   if (g->comm_stream) cudaStreamDestroy(g->comm_stream);
   if (g->own_stream && g->stream) cudaStreamDestroy(g->stream);
@@ -384,6 +443,36 @@ static int read_flat(llmk_gpt2* g, const float* dev, float* host_out, size_t n) 
 int llmk_gpt2_read_parameters(llmk_gpt2* g, float* host_out, size_t n) { return read_flat(g, g ? g->params : nullptr, host_out, n); }
 int llmk_gpt2_read_gradients(llmk_gpt2* g, float* host_out, size_t n) { return read_flat(g, g ? g->grads : nullptr, host_out, n); }
 
+// Timed wrappers of the library calls the step makes (work = algorithmic
+// FLOPs or HBM bytes of the call, for the per-class step report).
+namespace {
+struct StepOps {
+  llmk_gpt2* g;
+  cudaStream_t s;
+  llmk_math mm;
+  double ae;  // activation element size
+  int gemm(void* D, llmk_dtype dt, long long ldd, const void* A, int at, long long lda, const void* Bm, int bt,
+           long long ldb, int M, int N, int K, const llmk_epilogue* e, void* w, size_t wb) const {
+    TimedScope ts(g, KC_GEMM, 2.0 * M * N * K);
+    return llmk_gemm(D, dt, ldd, A, at, lda, Bm, bt, ldb, mm, M, N, K, e, w, wb, s);
+  }
+  int ln_fwd(void* out, llmk_dtype dt, float* mean, float* rstd, const float* x, const float* w, const float* b,
+             int N, int C) const {
+    TimedScope ts(g, KC_LN_FWD, static_cast<double>(N) * C * (4.0 + ae) + 8.0 * N + 8.0 * C);
+    return llmk_layernorm_forward(out, dt, mean, rstd, x, w, b, N, C, s);
+  }
+  int ln_bwd(float* dinp, void* mirror, float* dw, float* db, float* colsum, const float* dout, const float* x,
+             const float* w, const float* mean, const float* rstd, int N, int C, int flags, void* ws,
+             size_t wsb) const {
+    const double dres = (flags & LLMK_ACCUM_DINP) ? 8.0 : 4.0;
+    TimedScope ts(g, KC_LN_BWD,
+                  static_cast<double>(N) * C * (4.0 + 4.0 + dres + (mirror ? 2.0 : 0.0)) + 8.0 * N + 16.0 * C);
+    return llmk_layernorm_backward(dinp, mirror, dw, db, colsum, dout, LLMK_F32, x, w, mean, rstd, N, C, flags, ws,
+                                   wsb, s);
+  }
+};
+}  // namespace
+
 int llmk_gpt2_forward(llmk_gpt2* g, const int* d_inputs, const int* d_targets) {
   if (!g || !d_inputs) return fail(LLMK_ERR_INVALID_ARG, "gpt2_forward: null argument");
   const int B = g->B, T = g->T, C = g->cfg.channels, NH = g->cfg.num_heads, L = g->cfg.num_layers;
@@ -393,6 +482,8 @@ int llmk_gpt2_forward(llmk_gpt2* g, const int* d_inputs, const int* d_targets) {
   const llmk_math mm = g->math;
   const llmk_dtype adt = g->adt;
   const bool bf = mm == LLMK_MATH_BF16;
+  const StepOps op{g, s, mm, static_cast<double>(g->ae)};
+  const double bt_c = static_cast<double>(BT) * C;
   // GEMM weights: the bf16 mirror in bf16 mode, the fp32 master in tf32 mode
   auto W = [&](size_t off) -> const void* {
     return bf ? static_cast<const void*>(g->params_bf16 + off) : static_cast<const void*>(P + off);
@@ -403,42 +494,55 @@ int llmk_gpt2_forward(llmk_gpt2* g, const int* d_inputs, const int* d_targets) {
   if (d_targets && d_targets != g->targets)
     LLMK_CUDA(cudaMemcpyAsync(g->targets, d_targets, BT * sizeof(int), cudaMemcpyDeviceToDevice, s));
   // encoder (gpt2cuda.cu:313)
-  LLMK_TRY(llmk_encoder_forward(g->encoded, g->inputs, P + g->off_wte, P + g->off_wpe, B, T, C, s));
+  {
+    TimedScope ts(g, KC_ENCODER, bt_c * 12.0 + 4.0 * BT);
+    LLMK_TRY(llmk_encoder_forward(g->encoded, g->inputs, P + g->off_wte, P + g->off_wpe, B, T, C, s));
+  }
   const float* x = g->encoded;
+  const double attn_flop = 4.0 * B * NH * (C / NH) * causal_pairs(T);
   for (int l = 0; l < L; ++l) {
     // Layer::Forward (gpt2/cuda/layer.cu:151-177)
     const LayerParams& p = g->lp[l];
     LayerActs& a = g->acts[l];
-    LLMK_TRY(llmk_layernorm_forward(a.ln1, adt, a.ln1_mean, a.ln1_rstd, x, P + p.ln1w, P + p.ln1b, BT, C, s));
+    LLMK_TRY(op.ln_fwd(a.ln1, adt, a.ln1_mean, a.ln1_rstd, x, P + p.ln1w, P + p.ln1b, BT, C));
     llmk_epilogue e1 = epi(P + p.qkvb);
-    LLMK_TRY(llmk_gemm(a.qkv, adt, 3 * C, a.ln1, 0, C, W(p.qkvw), 0, C, mm, BT, 3 * C, C, &e1, nullptr, 0, s));
+    LLMK_TRY(op.gemm(a.qkv, adt, 3 * C, a.ln1, 0, C, W(p.qkvw), 0, C, BT, 3 * C, C, &e1, nullptr, 0));
     if (bf) {
+      TimedScope ts(g, KC_ATTN_FWD, attn_flop);
       LLMK_TRY(llmk_attention_forward(a.atty, LLMK_BF16, a.lse, a.qkv, B, T, 3 * C, NH, s));
     } else {
       // the attention MMAs take bf16 operands: round q, k, v once; the output
       // leaves the kernel in fp32
-      LLMK_TRY(llmk_cast(a.qkv16, LLMK_BF16, a.qkv, LLMK_F32, static_cast<long long>(BT) * 3 * C, s));
+      {
+        TimedScope ts(g, KC_CAST, bt_c * 3.0 * 6.0);
+        LLMK_TRY(llmk_cast(a.qkv16, LLMK_BF16, a.qkv, LLMK_F32, static_cast<long long>(BT) * 3 * C, s));
+      }
+      TimedScope ts(g, KC_ATTN_FWD, attn_flop);
       LLMK_TRY(llmk_attention_forward(a.atty, LLMK_F32, a.lse, a.qkv16, B, T, 3 * C, NH, s));
     }
     llmk_epilogue e2 = epi(P + p.attprojb, x, C);  // residual add fused
-    LLMK_TRY(llmk_gemm(a.res2, LLMK_F32, C, a.atty, 0, C, W(p.attprojw), 0, C, mm, BT, C, C, &e2, nullptr, 0, s));
-    LLMK_TRY(llmk_layernorm_forward(a.ln2, adt, a.ln2_mean, a.ln2_rstd, a.res2, P + p.ln2w, P + p.ln2b, BT, C, s));
+    LLMK_TRY(op.gemm(a.res2, LLMK_F32, C, a.atty, 0, C, W(p.attprojw), 0, C, BT, C, C, &e2, nullptr, 0));
+    LLMK_TRY(op.ln_fwd(a.ln2, adt, a.ln2_mean, a.ln2_rstd, a.res2, P + p.ln2w, P + p.ln2b, BT, C));
     // GELU fused, pre-activation kept for the backward
     llmk_epilogue e3 = epi(P + p.fcb, nullptr, 0, a.fch_pre, 4 * C, LLMK_EPI_GELU | aux_f32);
-    LLMK_TRY(llmk_gemm(a.fch_gelu, adt, 4 * C, a.ln2, 0, C, W(p.fcw), 0, C, mm, BT, 4 * C, C, &e3, nullptr, 0, s));
+    LLMK_TRY(op.gemm(a.fch_gelu, adt, 4 * C, a.ln2, 0, C, W(p.fcw), 0, C, BT, 4 * C, C, &e3, nullptr, 0));
     llmk_epilogue e4 = epi(P + p.fcprojb, a.res2, C);
-    LLMK_TRY(llmk_gemm(a.res3, LLMK_F32, C, a.fch_gelu, 0, 4 * C, W(p.fcprojw), 0, 4 * C, mm, BT, C, 4 * C, &e4,
-                       nullptr, 0, s));
+    LLMK_TRY(op.gemm(a.res3, LLMK_F32, C, a.fch_gelu, 0, 4 * C, W(p.fcprojw), 0, 4 * C, BT, C, 4 * C, &e4, nullptr,
+                     0));
     x = a.res3;
   }
-  LLMK_TRY(llmk_layernorm_forward(g->lnf, adt, g->lnf_mean, g->lnf_rstd, x, P + g->off_lnfw, P + g->off_lnfb, BT, C, s));
+  LLMK_TRY(op.ln_fwd(g->lnf, adt, g->lnf_mean, g->lnf_rstd, x, P + g->off_lnfw, P + g->off_lnfb, BT, C));
   // tied lm_head (gpt2cuda.cu:323): logits[BT, Vp] = lnf * wte^T, no bias
-  LLMK_TRY(llmk_gemm(g->logits, adt, Vp, g->lnf, 0, C, W(g->off_wte), 0, C, mm, BT, Vp, C, nullptr, nullptr, 0, s));
+  LLMK_TRY(op.gemm(g->logits, adt, Vp, g->lnf, 0, C, W(g->off_wte), 0, C, BT, Vp, C, nullptr, nullptr, 0));
   if (g->have_targets) {
     // softmax + cross-entropy + its backward in one pass; dlogits overwrite the
     // logits in place with scale 1/(B*T) (gpt2cuda.cu:398)
-    LLMK_TRY(llmk_softmax_crossentropy(g->losses, g->logits, g->logits, adt, g->targets, BT, V, Vp,
-                                       1.0f / static_cast<float>(BT), s));
+    {
+      TimedScope ts(g, KC_XENT, 2.0 * BT * static_cast<double>(Vp) * g->ae + 8.0 * BT);
+      LLMK_TRY(llmk_softmax_crossentropy(g->losses, g->logits, g->logits, adt, g->targets, BT, V, Vp,
+                                         1.0f / static_cast<float>(BT), s));
+    }
+    TimedScope ts(g, KC_OTHER, 4.0 * BT);
     LLMK_TRY(llmk_mean(g->loss, g->losses, BT, s));
   }
   return LLMK_OK;
@@ -472,15 +576,20 @@ int llmk_gpt2_backward(llmk_gpt2* g) {
   float* G = g->grads;
   void* ws = g->workspace;
   const size_t wsb = g->workspace_bytes;
-  LLMK_TRY(llmk_gpt2_zero_grad(g));
+  const StepOps op{g, s, mm, static_cast<double>(g->ae)};
+  const double bt_c = static_cast<double>(BT) * C;
+  const double attn_flop = 10.0 * B * NH * (C / NH) * causal_pairs(T);
+  {
+    TimedScope ts(g, KC_OTHER, static_cast<double>(g->tsize[llmk::WPE]) * 4.0);
+    LLMK_TRY(llmk_gpt2_zero_grad(g));
+  }
   // lm_head backward (gpt2cuda.cu:402): dlnf = dlogits * wte; dwte = dlogits^T * lnf
-  LLMK_TRY(llmk_gemm(g->dln, LLMK_F32, C, g->logits, 0, Vp, W(g->off_wte), 1, C, mm, BT, C, Vp, nullptr, nullptr, 0, s));
-  LLMK_TRY(llmk_gemm(G + g->off_wte, LLMK_F32, C, g->logits, 1, Vp, g->lnf, 1, C, mm, Vp, C, BT, nullptr, ws, wsb, s));
+  LLMK_TRY(op.gemm(g->dln, LLMK_F32, C, g->logits, 0, Vp, W(g->off_wte), 1, C, BT, C, Vp, nullptr, nullptr, 0));
+  LLMK_TRY(op.gemm(G + g->off_wte, LLMK_F32, C, g->logits, 1, Vp, g->lnf, 1, C, Vp, C, BT, nullptr, ws, wsb));
   const float* xL = L > 0 ? g->acts[L - 1].res3 : g->encoded;
   // the column sums of the new dres are the last layer's fcproj bias gradient
-  LLMK_TRY(llmk_layernorm_backward(g->dres, dres_mirror, G + g->off_lnfw, G + g->off_lnfb,
-                                   L > 0 ? G + g->lp[L - 1].fcprojb : nullptr, g->dln, LLMK_F32, xL, P + g->off_lnfw,
-                                   g->lnf_mean, g->lnf_rstd, BT, C, 0, ws, wsb, s));
+  LLMK_TRY(op.ln_bwd(g->dres, dres_mirror, G + g->off_lnfw, G + g->off_lnfb, L > 0 ? G + g->lp[L - 1].fcprojb : nullptr,
+                     g->dln, xL, P + g->off_lnfw, g->lnf_mean, g->lnf_rstd, BT, C, 0, ws, wsb));
   for (int l = L - 1; l >= 0; --l) {
     // Layer::Backward (gpt2/cuda/layer.cu:180-266); dres = d(layer output)
     const LayerParams& p = g->lp[l];
@@ -488,40 +597,50 @@ int llmk_gpt2_backward(llmk_gpt2* g) {
     const float* x = l > 0 ? g->acts[l - 1].res3 : g->encoded;
     // fcproj: dW = dres^T fch_gelu, dfch = (dres Wfcproj) * gelu'(fch_pre); its bias
     // gradient colsum(dres) came out of the LayerNorm backward that produced dres
-    LLMK_TRY(llmk_gemm(G + p.fcprojw, LLMK_F32, 4 * C, dres_op, 1, C, a.fch_gelu, 1, 4 * C, mm, C, 4 * C, BT, nullptr,
-                       ws, wsb, s));
+    LLMK_TRY(op.gemm(G + p.fcprojw, LLMK_F32, 4 * C, dres_op, 1, C, a.fch_gelu, 1, 4 * C, C, 4 * C, BT, nullptr, ws,
+                     wsb));
     llmk_epilogue eg = epi(nullptr, nullptr, 0, a.fch_pre, 4 * C, LLMK_EPI_GELU_BWD | aux_f32);
-    LLMK_TRY(llmk_gemm(g->dfch, adt, 4 * C, dres_op, 0, C, W(p.fcprojw), 1, 4 * C, mm, BT, 4 * C, C, &eg, nullptr, 0,
-                       s));
+    LLMK_TRY(op.gemm(g->dfch, adt, 4 * C, dres_op, 0, C, W(p.fcprojw), 1, 4 * C, BT, 4 * C, C, &eg, nullptr, 0));
     // fc: dW = dfch^T ln2, db = colsum(dfch), dln2 = dfch Wfc
-    LLMK_TRY(llmk_gemm(G + p.fcw, LLMK_F32, C, g->dfch, 1, 4 * C, a.ln2, 1, C, mm, 4 * C, C, BT, nullptr, ws, wsb, s));
-    LLMK_TRY(llmk_colsum(G + p.fcb, g->dfch, adt, BT, 4 * C, 0, ws, wsb, s));
-    LLMK_TRY(llmk_gemm(g->dln, LLMK_F32, C, g->dfch, 0, 4 * C, W(p.fcw), 1, C, mm, BT, C, 4 * C, nullptr, nullptr, 0, s));
+    LLMK_TRY(op.gemm(G + p.fcw, LLMK_F32, C, g->dfch, 1, 4 * C, a.ln2, 1, C, 4 * C, C, BT, nullptr, ws, wsb));
+    {
+      TimedScope ts(g, KC_COLSUM, bt_c * 4.0 * g->ae + 16.0 * C);
+      LLMK_TRY(llmk_colsum(G + p.fcb, g->dfch, adt, BT, 4 * C, 0, ws, wsb, s));
+    }
+    LLMK_TRY(op.gemm(g->dln, LLMK_F32, C, g->dfch, 0, 4 * C, W(p.fcw), 1, C, BT, C, 4 * C, nullptr, nullptr, 0));
     // ln2: dres += LN2 backward (dres becomes d(res2)); its column sums are the
     // attproj bias gradient
-    LLMK_TRY(llmk_layernorm_backward(g->dres, dres_mirror, G + p.ln2w, G + p.ln2b, G + p.attprojb, g->dln, LLMK_F32,
-                                     a.res2, P + p.ln2w, a.ln2_mean, a.ln2_rstd, BT, C, LLMK_ACCUM_DINP, ws, wsb, s));
+    LLMK_TRY(op.ln_bwd(g->dres, dres_mirror, G + p.ln2w, G + p.ln2b, G + p.attprojb, g->dln, a.res2, P + p.ln2w,
+                       a.ln2_mean, a.ln2_rstd, BT, C, LLMK_ACCUM_DINP, ws, wsb));
     // attproj: dW = dres^T atty, datty = dres Wproj
-    LLMK_TRY(llmk_gemm(G + p.attprojw, LLMK_F32, C, dres_op, 1, C, a.atty, 1, C, mm, C, C, BT, nullptr, ws, wsb, s));
-    LLMK_TRY(llmk_gemm(g->datty, adt, C, dres_op, 0, C, W(p.attprojw), 1, C, mm, BT, C, C, nullptr, nullptr, 0, s));
+    LLMK_TRY(op.gemm(G + p.attprojw, LLMK_F32, C, dres_op, 1, C, a.atty, 1, C, C, C, BT, nullptr, ws, wsb));
+    LLMK_TRY(op.gemm(g->datty, adt, C, dres_op, 0, C, W(p.attprojw), 1, C, BT, C, C, nullptr, nullptr, 0));
     // attention
     // (tf32 mode: fp32 dO, O and dqkv; q, k, v from the bf16 copy the forward made)
-    LLMK_TRY(llmk_attention_backward(g->dqkv, g->datty, a.atty, adt, bf ? a.qkv : a.qkv16, a.lse, B, T, 3 * C, NH, ws,
-                                     wsb, s));
+    {
+      TimedScope ts(g, KC_ATTN_BWD, attn_flop);
+      LLMK_TRY(llmk_attention_backward(g->dqkv, g->datty, a.atty, adt, bf ? a.qkv : a.qkv16, a.lse, B, T, 3 * C, NH,
+                                       ws, wsb, s));
+    }
     // qkv: dW = dqkv^T ln1, db = colsum(dqkv), dln1 = dqkv Wqkv
-    LLMK_TRY(llmk_gemm(G + p.qkvw, LLMK_F32, C, g->dqkv, 1, 3 * C, a.ln1, 1, C, mm, 3 * C, C, BT, nullptr, ws, wsb, s));
-    LLMK_TRY(llmk_colsum(G + p.qkvb, g->dqkv, adt, BT, 3 * C, 0, ws, wsb, s));
-    LLMK_TRY(llmk_gemm(g->dln, LLMK_F32, C, g->dqkv, 0, 3 * C, W(p.qkvw), 1, C, mm, BT, C, 3 * C, nullptr, nullptr, 0, s));
+    LLMK_TRY(op.gemm(G + p.qkvw, LLMK_F32, C, g->dqkv, 1, 3 * C, a.ln1, 1, C, 3 * C, C, BT, nullptr, ws, wsb));
+    {
+      TimedScope ts(g, KC_COLSUM, bt_c * 3.0 * g->ae + 12.0 * C);
+      LLMK_TRY(llmk_colsum(G + p.qkvb, g->dqkv, adt, BT, 3 * C, 0, ws, wsb, s));
+    }
+    LLMK_TRY(op.gemm(g->dln, LLMK_F32, C, g->dqkv, 0, 3 * C, W(p.qkvw), 1, C, BT, C, 3 * C, nullptr, nullptr, 0));
     // ln1: dres += LN1 backward (dres becomes d(layer input)); its column sums are
     // the previous layer's fcproj bias gradient
-    LLMK_TRY(llmk_layernorm_backward(g->dres, dres_mirror, G + p.ln1w, G + p.ln1b, l > 0 ? G + g->lp[l - 1].fcprojb : nullptr,
-                                     g->dln, LLMK_F32, x, P + p.ln1w, a.ln1_mean, a.ln1_rstd, BT, C, LLMK_ACCUM_DINP, ws,
-                                     wsb, s));
+    LLMK_TRY(op.ln_bwd(g->dres, dres_mirror, G + p.ln1w, G + p.ln1b, l > 0 ? G + g->lp[l - 1].fcprojb : nullptr, g->dln,
+                       x, P + p.ln1w, a.ln1_mean, a.ln1_rstd, BT, C, LLMK_ACCUM_DINP, ws, wsb));
     // this layer's gradients are final: reduce them while the layers below run
     LLMK_TRY(allreduce_bucket(g, g->layer_done[l], p.begin, p.end));
   }
   // encoder backward (gpt2cuda.cu:413): dwte += scatter, dwpe += sum over batch
-  LLMK_TRY(llmk_encoder_backward(G + g->off_wte, G + g->off_wpe, g->dres, g->inputs, B, T, C, Vp, ws, wsb, s));
+  {
+    TimedScope ts(g, KC_ENCODER, bt_c * 12.0 + 8.0 * static_cast<double>(T) * C + 4.0 * BT);
+    LLMK_TRY(llmk_encoder_backward(G + g->off_wte, G + g->off_wpe, g->dres, g->inputs, B, T, C, Vp, ws, wsb, s));
+  }
   // wte/wpe bucket, then lnf bucket
   LLMK_TRY(allreduce_bucket(g, g->embed_done, g->off_wte, g->off_wpe + g->tsize[llmk::WPE]));
   if (g->world > 1) {
@@ -539,6 +658,8 @@ int llmk_gpt2_update(llmk_gpt2* g, float lr, float beta1, float beta2, float eps
   // one multi-tensor launch over the flat buffer (the reference launches one
   // AdamW per tensor, gpt2cuda.cu:434-441); gradients are averaged over ranks
   const float scale = 1.0f / static_cast<float>(g->world);
+  // p, g, m, v read; p, m, v written; plus the bf16 mirror in bf16 mode
+  TimedScope ts(g, KC_ADAMW, static_cast<double>(g->nparams) * (28.0 + (g->params_bf16 ? 2.0 : 0.0)));
   LLMK_TRY(llmk_adamw(g->params, g->params_bf16, g->grads, g->m, g->v, static_cast<long long>(g->nparams), lr, beta1,
                       beta2, eps, weight_decay, t, scale, g->stream));
   ++g->steps;
@@ -669,6 +790,40 @@ int llmk_gpt2_broadcast_parameters(llmk_gpt2* g, int root) {
   if (g->params_bf16)
     LLMK_TRY(llmk_cast(g->params_bf16, LLMK_BF16, g->params, LLMK_F32, static_cast<long long>(g->nparams), g->stream));
   LLMK_CUDA(cudaStreamSynchronize(g->stream));
+  return LLMK_OK;
+}
+
+int llmk_gpt2_set_timing(llmk_gpt2* g, int enable) {
+  if (!g) return fail(LLMK_ERR_INVALID_ARG, "gpt2_set_timing");
+  g->timing = enable != 0;
+  g->marks.clear();
+  g->tev_used = 0;
+  return LLMK_OK;
+}
+
+int llmk_gpt2_timing_report(llmk_gpt2* g, llmk_kernel_stat* out, int max, int* count) {
+  if (!g || (!out && max > 0)) return fail(LLMK_ERR_INVALID_ARG, "gpt2_timing_report");
+  LLMK_TRY(ensure_device(g));
+  LLMK_CUDA(cudaStreamSynchronize(g->stream));
+  llmk_kernel_stat acc[KC_COUNT];
+  std::memset(acc, 0, sizeof(acc));
+  for (int c = 0; c < KC_COUNT; ++c) {
+    std::strncpy(acc[c].name, kClassName[c], sizeof(acc[c].name) - 1);
+    acc[c].unit = kClassUnit[c];
+  }
+  for (const auto& m : g->marks) {
+    if (m.e1 < 0) continue;
+    float ms = 0.f;
+    LLMK_CUDA(cudaEventElapsedTime(&ms, g->tev[m.e0], g->tev[m.e1]));
+    llmk_kernel_stat& a = acc[m.cls];
+    a.calls += 1;
+    a.launches += static_cast<long long>(m.launches);
+    a.ms += ms;
+    a.work += m.work;
+  }
+  const int n = std::min<int>(max, KC_COUNT);
+  for (int c = 0; c < n; ++c) out[c] = acc[c];
+  if (count) *count = KC_COUNT;
   return LLMK_OK;
 }
 

@@ -35,6 +35,11 @@ class Epilogue(C.Structure):
                 ("ldaux", C.c_longlong), ("flags", C.c_int)]
 
 
+class KernelStat(C.Structure):
+    _fields_ = [("name", C.c_char * 24), ("calls", C.c_longlong), ("launches", C.c_longlong), ("ms", C.c_double),
+                ("work", C.c_double), ("unit", C.c_int)]
+
+
 class GPT2Config(C.Structure):
     _fields_ = [("max_seq_len", C.c_int), ("vocab_size", C.c_int), ("padded_vocab_size", C.c_int),
                 ("num_layers", C.c_int), ("num_heads", C.c_int), ("channels", C.c_int)]
@@ -100,6 +105,8 @@ SIGNATURES: dict[str, tuple] = {
     "llmk_gpt2_enable_dp": (i32, [vp, vp, sz, i32, i32]),
     "llmk_gpt2_broadcast_parameters": (i32, [vp, i32]),
     "llmk_gpt2_synchronize": (i32, [vp, i32]),
+    "llmk_gpt2_set_timing": (i32, [vp, i32]),
+    "llmk_gpt2_timing_report": (i32, [vp, C.POINTER(KernelStat), i32, C.POINTER(i32)]),
 }
 
 _lib = None
@@ -253,6 +260,20 @@ class GPT2:
 
     def synchronize(self, timeout_ms=0):
         call("llmk_gpt2_synchronize", self.h, timeout_ms)
+
+    def set_timing(self, enable: bool):
+        """Per-kernel-class event timing of later steps (clears old records)."""
+        call("llmk_gpt2_set_timing", self.h, 1 if enable else 0)
+
+    def timing_report(self) -> dict:
+        """{class: {calls, launches, ms, work, unit}} summed over the timed steps;
+        unit is "flop" or "byte" (algorithmic work of the class)."""
+        out = (KernelStat * 32)()
+        n = C.c_int(0)
+        call("llmk_gpt2_timing_report", self.h, out, 32, C.byref(n))
+        return {out[i].name.decode(): {"calls": out[i].calls, "launches": out[i].launches, "ms": out[i].ms,
+                                       "work": out[i].work, "unit": "flop" if out[i].unit == 0 else "byte"}
+                for i in range(min(n.value, 32))}
 
     def close(self):
         if getattr(self, "h", None):

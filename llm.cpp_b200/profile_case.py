@@ -2,6 +2,7 @@
 
     python llm.cpp_b200/profile_case.py gemm    [M N K] [--trans A B] [--reps R]
     python llm.cpp_b200/profile_case.py attn    [B T NH] [--reps R]
+    python llm.cpp_b200/profile_case.py attnbwd [B T NH] [--reps R]
     python llm.cpp_b200/profile_case.py step    [B T]    [--reps R]
 
 Each case allocates its inputs once, runs one warm-up launch and R timed
@@ -21,7 +22,7 @@ sys.path.insert(0, HERE)
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["gemm", "attn", "step"])
+    ap.add_argument("case", choices=["gemm", "attn", "attnbwd", "step"])
     ap.add_argument("dims", nargs="*", type=int)
     ap.add_argument("--trans", nargs=2, type=int, default=[0, 0])
     ap.add_argument("--reps", type=int, default=3)
@@ -52,6 +53,23 @@ def main() -> None:
         run = lambda: llmk.call("llmk_attention_forward", out.data_ptr(), llmk.BF16, lse.data_ptr(), qkv.data_ptr(),
                                 Bb, T, 3 * C, NH, s)
         flop = 4.0 * Bb * NH * 64 * T * (T + 1) / 2
+    elif a.case == "attnbwd":
+        Bb, T, NH = (a.dims + [8, 1024, 12][len(a.dims):])[:3]
+        C = 64 * NH
+        s = llmk.stream_ptr()
+        qkv = torch.randn(Bb, T, 3 * C, device=dev).bfloat16()
+        out = torch.empty(Bb, T, C, device=dev, dtype=torch.bfloat16)
+        dout = torch.randn(Bb, T, C, device=dev).bfloat16()
+        dqkv = torch.empty(Bb, T, 3 * C, device=dev, dtype=torch.bfloat16)
+        lse = torch.empty(Bb, NH, T, device=dev)
+        wsb = llmk.lib().llmk_attention_backward_workspace(Bb, T, 3 * C, NH)
+        ws = torch.empty(wsb // 4 + 64, device=dev)
+        llmk.call("llmk_attention_forward", out.data_ptr(), llmk.BF16, lse.data_ptr(), qkv.data_ptr(), Bb, T, 3 * C,
+                  NH, s)
+        run = lambda: llmk.call("llmk_attention_backward", dqkv.data_ptr(), dout.data_ptr(), out.data_ptr(), llmk.BF16,
+                                qkv.data_ptr(), lse.data_ptr(), Bb, T, 3 * C, NH, ws.data_ptr(), wsb, s)
+        # S = QK^T, dP = dO V^T, dV += P^T dO, dK += dS^T Q, dQ += dS K over the causal half
+        flop = 10.0 * Bb * NH * 64 * T * (T + 1) / 2
     else:
         Bb, T = (a.dims + [16, 1024][len(a.dims):])[:2]
         m = llmk.GPT2(Bb, T)

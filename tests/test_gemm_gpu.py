@@ -30,7 +30,10 @@ def _operands(torch, M, N, K, a_trans, b_trans, math, dev, seed):
 
 @pytest.mark.parametrize("form", FORMS)
 @pytest.mark.parametrize("mathname", ["bf16", "tf32"])
-@pytest.mark.parametrize("shape", [(128, 256, 64), (256, 128, 128), (384, 768, 192), (200, 136, 72)])
+# M < 256: single-CTA tiles; M >= 256: CTA-pair tiles of 256 rows, including a
+# ragged last pair (640, 1000) and N / K that are not tile multiples
+@pytest.mark.parametrize("shape", [(128, 256, 64), (256, 128, 128), (384, 768, 192), (200, 136, 72),
+                                   (640, 392, 200), (1000, 520, 136)])
 def test_gemm_forms(cuda_dev, form, mathname, shape):
     import torch
     import llmk
@@ -68,11 +71,13 @@ def test_gemm_layer_shapes(cuda_dev, mathname):
     assert llmk.device_status() == 0
 
 
-def test_gemm_epilogues(cuda_dev):
-    """bias, residual, GELU (+ pre-activation store), GELU-backward, accumulate, bf16 output."""
+@pytest.mark.parametrize("M", [192, 512])
+def test_gemm_epilogues(cuda_dev, M):
+    """bias, residual, GELU (+ pre-activation store), GELU-backward, accumulate, bf16 output
+    (M = 192: single-CTA tiles, 512: CTA pairs)."""
     import torch
     import llmk
-    M, N, K = 256, 512, 128
+    N, K = 512, 128
     A, B, ref = _operands(torch, M, N, K, 0, 0, llmk.MATH_BF16, cuda_dev, seed=5)
     ref = ref.float()
     bias = torch.randn(N, device=cuda_dev)

@@ -111,3 +111,36 @@ def test_repeated_steps_agree(cuda_dev, mathname):
             err = np.abs(g - first).max() / np.abs(first).max()
             assert err < 1e-5, err
     m.close()
+
+
+def test_step_timing_report(cuda_dev):
+    """Per-kernel-class step timing: every GEMM of the step is counted once per
+    step with its 2*M*N*K FLOPs, and timing does not change the step's result."""
+    import llmk
+    cfg = O.config(max_seq_len=128, vocab_size=1000, padded_vocab_size=1024, num_layers=2, num_heads=2, channels=128)
+    B, T = 2, 128
+    params = O.init_params(cfg, 12)
+    toks = O.tokens(B * T + 1, cfg.vocab_size, 12)
+    m = _model(llmk, cfg, B, T, llmk.MATH_BF16)
+    m.load_parameters(params)
+    m.train_step(toks[:-1], toks[1:], 0.0, t=1)
+    g0 = m.read_gradients()
+    m.set_timing(True)
+    for _ in range(2):
+        m.train_step(toks[:-1], toks[1:], 0.0, t=1)
+    rep = m.timing_report()
+    m.set_timing(False)
+    assert np.array_equal(m.read_gradients(), g0)
+    L, C, Vp, BT = cfg.num_layers, cfg.channels, cfg.padded_vocab_size, B * T
+    per_layer = 2 * BT * C * (3 * C + C + 4 * C + 4 * C)  # forward MACs x 2 of qkv, attproj, fc, fcproj
+    flop = 3 * (L * per_layer + 2 * BT * Vp * C)  # forward, dinp, dweight
+    gm = rep["gemm"]
+    assert gm["calls"] == 2 * (3 * 4 * L + 3) and gm["unit"] == "flop"
+    assert abs(gm["work"] - 2 * flop) <= 1e-9 * flop
+    assert gm["ms"] > 0 and gm["launches"] >= gm["calls"]
+    for name in ("attention_fwd", "attention_bwd", "layernorm_fwd", "layernorm_bwd", "adamw", "softmax_xent"):
+        assert rep[name]["calls"] > 0 and rep[name]["ms"] > 0, name
+    assert rep["attention_fwd"]["calls"] == 2 * L
+    m.set_timing(True)
+    assert m.timing_report()["gemm"]["calls"] == 0
+    m.close()
