@@ -17,5 +17,8 @@
 
 /* Bits of the per-device status word written by kernels. */
 #define LLMK_DEV_TIMEOUT 1u
+/* a kernel found its dynamic shared memory less aligned than it declared
+ * (it returned without doing any work) */
+#define LLMK_DEV_SMEM_ALIGN 2u
 
 #endif /* LLMK_STATUS_H_ */

@@ -10,19 +10,22 @@
 // {3C, T, B} with a {64, 128, 1} box serves Q, K, V, dO and O tiles: rows past
 // T of a batch read as zeros.
 //
-// Forward: one CTA per (128-query tile, head, batch), heaviest tiles first.
-// warp 0 = TMA, warp 1 = tcgen05 issuer (S = Q K^T into TMEM, O_part = P V),
-// warps 2..5 = softmax (thread = query row): exp2 online softmax, P -> smem
-// (bf16, 128B-swizzled K-major), O accumulated in registers from O_part.
-// S and O_part are double-buffered in TMEM so the MMAs of tile j+1 overlap the
-// softmax of tile j.
+// Forward: persistent, one CTA per SM walking (128-query tile, head, batch)
+// items heaviest first; warp 0 = TMA, warp 1 = tcgen05 issuer (S = Q K^T
+// into TMEM, O_part = P V), warps 2..5 = softmax (thread = query row): exp2
+// online softmax, P -> smem (bf16, 128B-swizzled K-major), O accumulated in
+// registers from O_part. S, P and O_part are double-buffered and Q is
+// double-buffered across items, so the MMAs of tile j+1 (or of the next
+// item) overlap the softmax of tile j.
 //
 // Backward: one CTA per (128-key tile, head, batch) walking query tiles from
-// the diagonal down. S^T = K Q^T and dP^T = V dO^T land in TMEM; softmax warps
-// (thread = key row) form P^T and dS^T = P^T (dP^T - D) in smem; then
-// dV += P^T dO and dK += dS^T Q accumulate in TMEM and dQ_i = dS K is added
-// to an fp32 workspace with vector reductions. D = rowsum(dO * O) and the
-// final dQ scaling run as small pre/post kernels.
+// the diagonal down. S^T = K Q^T and dP^T = V dO^T land in TMEM; 16 softmax
+// warps (4 per TMEM lane quarter, 32 query columns each) form P^T and
+// dS^T = P^T (dP^T - D) in smem (double-buffered); then dV += P^T dO and
+// dK += dS^T Q accumulate in TMEM, dQ_i = dS K lands in one of two TMEM
+// buffers and is added to an fp32 workspace with vector reductions while the
+// next query tile runs. D = rowsum(dO * O) and the final dQ scaling run as
+// small pre/post kernels.
 #include <algorithm>
 
 #include "ptx.cuh"
@@ -59,12 +62,28 @@ __device__ __forceinline__ void st_tile_chunk(uint8_t* tile, int r, int chunk, c
 // ------------------------------------------------------------------ forward
 struct FwdSmem {
   static constexpr int kStages = 2;
-  static constexpr int Q_OFF = 0;
-  static constexpr int KV_OFF = TILE_BYTES;                          // stages x (K, V)
+  static constexpr int Q_OFF = 0;                                    // 2 x Q (double-buffered across items)
+  static constexpr int KV_OFF = 2 * TILE_BYTES;                      // stages x (K, V)
   static constexpr int P_OFF = KV_OFF + kStages * 2 * TILE_BYTES;    // 2 x [128 x 128] bf16
   static constexpr int BAR_OFF = P_OFF + 2 * 2 * TILE_BYTES;
   static constexpr size_t BYTES = BAR_OFF + 256 + 1024;
 };
+
+// Work item w (0 .. nq*B*NH-1) of the attention kernels: query
+// (forward) or key (backward) tile `tile` of head bh. Items are ordered by
+// decreasing work, and CTA c walks items c, c + gridDim.x, ... .
+struct AttnItem {
+  int tile, b, h, bh;
+};
+__device__ __forceinline__ AttnItem fwd_item(int w, int nq, int B, int NH) {
+  const int bh_count = B * NH;
+  AttnItem it;
+  it.tile = nq - 1 - w / bh_count;  // most key tiles first
+  it.bh = w % bh_count;
+  it.b = it.bh / NH;
+  it.h = it.bh % NH;
+  return it;
+}
 
 __global__ void __launch_bounds__(192, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, void* __restrict__ out_ptr, int out_f32,
@@ -76,8 +95,9 @@ __global__ void __launch_bounds__(192, 1)
   uint8_t* sKV = smem + S::KV_OFF;
   uint8_t* sP = smem + S::P_OFF;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::BAR_OFF);
-  uint64_t* q_full = bars;
-  uint64_t* kv_full = bars + 1;                  // [2]
+  uint64_t* q_full = bars;                       // [2]
+  uint64_t* q_empty = q_full + 2;                // [2]
+  uint64_t* kv_full = q_empty + 2;               // [2]
   uint64_t* kv_empty = kv_full + S::kStages;     // [2]
   uint64_t* s_full = kv_empty + S::kStages;      // [2]
   uint64_t* p_full = s_full + 2;                 // [2]
@@ -87,24 +107,19 @@ __global__ void __launch_bounds__(192, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int nq = (T + TILE - 1) / TILE;
-  const int bh_count = B * NH;
-  const int qt = nq - 1 - static_cast<int>(blockIdx.x) / bh_count;  // heaviest first
-  const int bh = static_cast<int>(blockIdx.x) % bh_count;
-  const int b = bh / NH, h = bh % NH;
-  const int q0 = qt * TILE;
-  const int n_kv = qt + 1;
-
+  const int n_items = nq * B * NH;
   const int warp = warp_id(), lane = lane_id();
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
-    for (int s = 0; s < S::kStages; ++s) {
-      mbar_init(kv_full + s, 1);
-      mbar_init(kv_empty + s, 1);
-    }
     for (int i = 0; i < 2; ++i) {
+      mbar_init(q_full + i, 1);
+      mbar_init(q_empty + i, 1);
       mbar_init(s_full + i, 1);
       mbar_init(p_full + i, 128);
       mbar_init(o_full + i, 1);
+    }
+    for (int s = 0; s < S::kStages; ++s) {
+      mbar_init(kv_full + s, 1);
+      mbar_init(kv_empty + s, 1);
     }
     mbar_init(done, 1);
     *abort_flag = 0;
@@ -119,21 +134,31 @@ __global__ void __launch_bounds__(192, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   // TMEM columns: S[0] 0..127, S[1] 128..255, O_part[0] 256..319, O_part[1] 320..383
+  // Buffers and barrier phases follow two running counters shared by all roles:
+  // the item count n (Q buffer n&1) and the key-tile step count g over all
+  // items (S / P / O_part buffer g&1, KV stage g%kStages).
 
   if (warp == 0) {
     if (lane == 0) {
       tma_prefetch_desc(&tm_qkv);
-      mbar_arrive_expect_tx(q_full, TILE_BYTES);
-      tma_load_3d(sQ, &tm_qkv, q_full, h * HD, q0, b);
       int stage = 0;
       uint32_t phase = 0;
-      for (int j = 0; j < n_kv; ++j) {
-        if (!mbar_wait(kv_empty + stage, phase ^ 1u, status, abort_flag, 1)) break;
-        uint8_t* sK = sKV + stage * 2 * TILE_BYTES;
-        mbar_arrive_expect_tx(kv_full + stage, 2 * TILE_BYTES);
-        tma_load_3d(sK, &tm_qkv, kv_full + stage, C + h * HD, j * TILE, b);
-        tma_load_3d(sK + TILE_BYTES, &tm_qkv, kv_full + stage, 2 * C + h * HD, j * TILE, b);
-        if (++stage == S::kStages) { stage = 0; phase ^= 1u; }
+      bool ok = true;
+      int n = 0;
+      for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x, ++n) {
+        const AttnItem it = fwd_item(w, nq, B, NH);
+        const int qb = n & 1;
+        if (!mbar_wait(q_empty + qb, ((n >> 1) & 1) ^ 1u, status, abort_flag, 1)) break;
+        mbar_arrive_expect_tx(q_full + qb, TILE_BYTES);
+        tma_load_3d(sQ + qb * TILE_BYTES, &tm_qkv, q_full + qb, it.h * HD, it.tile * TILE, it.b);
+        for (int j = 0; j <= it.tile; ++j) {
+          if (!mbar_wait(kv_empty + stage, phase ^ 1u, status, abort_flag, 1)) { ok = false; break; }
+          uint8_t* sK = sKV + stage * 2 * TILE_BYTES;
+          mbar_arrive_expect_tx(kv_full + stage, 2 * TILE_BYTES);
+          tma_load_3d(sK, &tm_qkv, kv_full + stage, C + it.h * HD, j * TILE, it.b);
+          tma_load_3d(sK + TILE_BYTES, &tm_qkv, kv_full + stage, 2 * C + it.h * HD, j * TILE, it.b);
+          if (++stage == S::kStages) { stage = 0; phase ^= 1u; }
+        }
       }
     }
   } else if (warp == 1) {
@@ -142,48 +167,64 @@ __global__ void __launch_bounds__(192, 1)
       const uint32_t idesc_s = idesc_f32acc(128, 128, kFmtBF16, false, false);
       // O_part = P V: M=128 queries, N=64 hd, K=128 keys; V is [keys][hd] = N-major.
       const uint32_t idesc_o = idesc_f32acc(128, HD, kFmtBF16, false, true);
-      const uint32_t q_addr = smem_u32(sQ);
-      bool ok = mbar_wait(q_full, 0, status, abort_flag, 2);
-      auto issue_s = [&](int j, int st) {
-        const uint32_t k_addr = smem_u32(sKV + st * 2 * TILE_BYTES);
-        const uint32_t d = tmem + (j & 1) * 128;
+      // The key-tile steps of all this CTA's items form one sequence; S of
+      // step g+1 is issued before O_part of step g so the tensor core works
+      // while the softmax warps turn S(g) into P(g).
+      struct Step {
+        int w, j, n;  // item, key tile within it, item count
+      };
+      auto next_step = [&](Step st) -> Step {
+        const AttnItem it = fwd_item(st.w, nq, B, NH);
+        if (st.j < it.tile) return {st.w, st.j + 1, st.n};
+        return {st.w + static_cast<int>(gridDim.x), 0, st.n + 1};
+      };
+      bool ok = true;
+      int kst = 0;        // KV stage of the step whose S was issued last
+      uint32_t kph = 0;
+      Step cur{static_cast<int>(blockIdx.x), 0, 0};
+      auto issue_s = [&](const Step& st, uint32_t g) -> bool {
+        // Q of a new item
+        if (st.j == 0) {
+          if (!mbar_wait(q_full + (st.n & 1), (st.n >> 1) & 1, status, abort_flag, 2)) return false;
+        }
+        if (!mbar_wait(kv_full + kst, kph, status, abort_flag, 3)) return false;
+        tc_fence_after();
+        const uint32_t q_addr = smem_u32(sQ + (st.n & 1) * TILE_BYTES);
+        const uint32_t k_addr = smem_u32(sKV + kst * 2 * TILE_BYTES);
+        const uint32_t d = tmem + (g & 1) * 128;
 #pragma unroll
         for (int ks = 0; ks < HD / 16; ++ks)
           mma_f16_ss(d, sdesc_sw128(q_addr + ks * 32, 16, 1024), sdesc_sw128(k_addr + ks * 32, 16, 1024), idesc_s,
                      ks > 0);
-        mma_commit(s_full + (j & 1));
+        mma_commit(s_full + (g & 1));
+        // the item's last S: its Q buffer is free once these MMAs are done
+        if (st.j == fwd_item(st.w, nq, B, NH).tile) mma_commit(q_empty + (st.n & 1));
+        return true;
       };
-      int stage = 0;
-      uint32_t phase = 0;
-      if (ok) ok = mbar_wait(kv_full + 0, 0, status, abort_flag, 3);
-      if (ok) {
-        tc_fence_after();
-        issue_s(0, 0);
-      }
-      for (int j = 0; j < n_kv && ok; ++j) {
-        const int st = stage;
-        const int nst = (stage + 1 == S::kStages) ? 0 : stage + 1;
-        const uint32_t nph = (stage + 1 == S::kStages) ? (phase ^ 1u) : phase;
-        if (j + 1 < n_kv) {
-          if (!mbar_wait(kv_full + nst, nph, status, abort_flag, 3)) { ok = false; break; }
-          tc_fence_after();
-          issue_s(j + 1, nst);
+      uint32_t g = 0;
+      if (cur.w < n_items) ok = issue_s(cur, 0);
+      while (cur.w < n_items && ok) {
+        const int st = kst;
+        const Step nxt = next_step(cur);
+        if (++kst == S::kStages) { kst = 0; kph ^= 1u; }
+        if (nxt.w < n_items) {
+          if (!issue_s(nxt, g + 1)) { ok = false; break; }
         }
-        if (!mbar_wait(p_full + (j & 1), (j >> 1) & 1, status, abort_flag, 4)) { ok = false; break; }
+        if (!mbar_wait(p_full + (g & 1), (g >> 1) & 1, status, abort_flag, 4)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t p_addr = smem_u32(sP + (j & 1) * 2 * TILE_BYTES);
+        const uint32_t p_addr = smem_u32(sP + (g & 1) * 2 * TILE_BYTES);
         const uint32_t v_addr = smem_u32(sKV + st * 2 * TILE_BYTES + TILE_BYTES);
-        const uint32_t d = tmem + 256 + (j & 1) * HD;
+        const uint32_t d = tmem + 256 + (g & 1) * HD;
 #pragma unroll
         for (int ks = 0; ks < TILE / 16; ++ks) {
           const uint64_t a = sdesc_sw128(p_addr + (ks >> 2) * TILE_BYTES + (ks & 3) * 32, 16, 1024);
           const uint64_t bd = sdesc_sw128(v_addr + ks * 2048, TILE_BYTES, 1024);
           mma_f16_ss(d, a, bd, idesc_o, ks > 0);
         }
-        mma_commit(o_full + (j & 1));
+        mma_commit(o_full + (g & 1));
         mma_commit(kv_empty + st);
-        stage = nst;
-        phase = nph;
+        cur = nxt;
+        ++g;
       }
       mma_commit(done);
       mbar_wait(done, 0, status, nullptr, 5);
@@ -194,69 +235,94 @@ __global__ void __launch_bounds__(192, 1)
     const int r = q * 32 + lane;  // query row within the tile (= TMEM lane)
     const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
     const float sl2 = 0.125f * 1.4426950408889634f;  // softmax scale * log2(e)
-    float m = -INFINITY, l = 0.f, alpha_prev = 0.f;
-    float o[HD];
-#pragma unroll
-    for (int i = 0; i < HD; ++i) o[i] = 0.f;
     bool ok = true;
-    auto consume_o = [&](int jj, float alpha) -> bool {
-      bool w = mbar_wait(o_full + (jj & 1), (jj >> 1) & 1, status, abort_flag, 7);
-      if (!__all_sync(0xffffffffu, w)) return false;
-      tc_fence_after();
-      uint32_t v[32];
+    uint32_t g = 0;
+    for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x) {
+      const AttnItem it = fwd_item(w, nq, B, NH);
+      const int qt = it.tile, n_kv = qt + 1;
+      float m = -INFINITY, l = 0.f, alpha_prev = 0.f;
+      float o[HD];
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        tmem_ld_32x32b_x32(tmem + lane_base + 256 + (jj & 1) * HD + half * 32, v);
+      for (int i = 0; i < HD; ++i) o[i] = 0.f;
+      auto consume_o = [&](uint32_t gg, float alpha) -> bool {
+        bool wt = mbar_wait(o_full + (gg & 1), (gg >> 1) & 1, status, abort_flag, 7);
+        if (!__all_sync(0xffffffffu, wt)) return false;
+        tc_fence_after();
+        uint32_t v[32], v2[32];
+        tmem_ld_32x32b_x32(tmem + lane_base + 256 + (gg & 1) * HD, v);
+        tmem_ld_32x32b_x32(tmem + lane_base + 256 + (gg & 1) * HD + 32, v2);
         tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) o[half * 32 + i] = o[half * 32 + i] * alpha + __uint_as_float(v[i]);
+        for (int i = 0; i < 32; ++i) {
+          o[i] = fmaf(o[i], alpha, __uint_as_float(v[i]));
+          o[32 + i] = fmaf(o[32 + i], alpha, __uint_as_float(v2[i]));
+        }
+        return true;
+      };
+      for (int j = 0; j < n_kv; ++j, ++g) {
+        bool wt = mbar_wait(s_full + (g & 1), (g >> 1) & 1, status, abort_flag, 6);
+        if (!__all_sync(0xffffffffu, wt)) { ok = false; break; }
+        tc_fence_after();
+        float sc[TILE];
+#pragma unroll
+        for (int c = 0; c < 4; c += 2) {
+          uint32_t v[32], v2[32];
+          tmem_ld_32x32b_x32(tmem + lane_base + (g & 1) * 128 + c * 32, v);
+          tmem_ld_32x32b_x32(tmem + lane_base + (g & 1) * 128 + c * 32 + 32, v2);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            sc[c * 32 + i] = __uint_as_float(v[i]) * sl2;
+            sc[c * 32 + 32 + i] = __uint_as_float(v2[i]) * sl2;
+          }
+        }
+        if (j == qt) {  // diagonal tile: key index > query index is masked
+#pragma unroll
+          for (int i = 0; i < TILE; ++i)
+            if (i > r) sc[i] = -INFINITY;
+        }
+        // row max as a tree (short dependency chains)
+        float mx8[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) mx8[k] = sc[k];
+#pragma unroll
+        for (int i = 8; i < TILE; i += 8)
+#pragma unroll
+          for (int k = 0; k < 8; ++k) mx8[k] = fmaxf(mx8[k], sc[i + k]);
+        const float mx = fmaxf(m, fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                                        fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]))));
+        const float alpha = ex2(m - mx);  // 0 on the first tile (m = -inf)
+        float rs8[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) rs8[k] = 0.f;
+        uint8_t* pt = sP + (g & 1) * 2 * TILE_BYTES;
+#pragma unroll
+        for (int ch = 0; ch < TILE / 8; ++ch) {
+          float pv[8];
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            pv[k] = ex2(sc[ch * 8 + k] - mx);
+            rs8[k] += pv[k];
+          }
+          st_tile_chunk(pt, r, ch, pv);
+        }
+        const float rs = ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
+        l = l * alpha + rs;
+        m = mx;
+        fence_async_smem();
+        tc_fence_before();
+        mbar_arrive(p_full + (g & 1));
+        if (j > 0 && !consume_o(g - 1, alpha_prev)) { ok = false; break; }
+        alpha_prev = alpha;
       }
-      return true;
-    };
-    for (int j = 0; j < n_kv; ++j) {
-      bool w = mbar_wait(s_full + (j & 1), (j >> 1) & 1, status, abort_flag, 6);
-      if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
-      tc_fence_after();
-      float s[TILE];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(tmem + lane_base + (j & 1) * 128 + c * 32, v);
-        tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(v[i]) * sl2;
+      if (!ok || !consume_o(g - 1, alpha_prev)) {
+        ok = false;
+        break;
       }
-      if (j == qt) {  // diagonal tile: key index > query index is masked
-#pragma unroll
-        for (int i = 0; i < TILE; ++i)
-          if (i > r) s[i] = -INFINITY;
-      }
-      float mx = m;
-#pragma unroll
-      for (int i = 0; i < TILE; ++i) mx = fmaxf(mx, s[i]);
-      const float alpha = ex2(m - mx);  // 0 on the first tile (m = -inf)
-      float rs = 0.f;
-#pragma unroll
-      for (int i = 0; i < TILE; ++i) {
-        s[i] = ex2(s[i] - mx);
-        rs += s[i];
-      }
-      l = l * alpha + rs;
-      m = mx;
-      uint8_t* pt = sP + (j & 1) * 2 * TILE_BYTES;
-#pragma unroll
-      for (int ch = 0; ch < TILE / 8; ++ch) st_tile_chunk(pt, r, ch, s + ch * 8);
-      fence_async_smem();
-      tc_fence_before();
-      mbar_arrive(p_full + (j & 1));
-      if (j > 0 && !consume_o(j - 1, alpha_prev)) { ok = false; break; }
-      alpha_prev = alpha;
-    }
-    if (ok && consume_o(n_kv - 1, alpha_prev)) {
-      const int t = q0 + r;
+      const int t = qt * TILE + r;
       if (t < T) {
         const float inv = 1.0f / l;
-        const long long off = (static_cast<long long>(b) * T + t) * C + h * HD;
+        const long long off = (static_cast<long long>(it.b) * T + t) * C + it.h * HD;
         if (out_f32) {
           float4* dst = reinterpret_cast<float4*>(static_cast<float*>(out_ptr) + off);
 #pragma unroll
@@ -275,7 +341,7 @@ __global__ void __launch_bounds__(192, 1)
           }
         }
         // natural-log LSE: (m2 + log2 l) * ln 2
-        lse[(static_cast<long long>(b) * NH + h) * T + t] = (m + __log2f(l)) * 0.6931471805599453f;
+        lse[static_cast<long long>(it.bh) * T + t] = (m + __log2f(l)) * 0.6931471805599453f;
       }
     }
     tc_fence_before();
@@ -367,69 +433,144 @@ __global__ void attn_bwd_post_kernel(IoT* __restrict__ dqkv, const float* __rest
   }
 }
 
+// The backward's buffers fill the 227 KB a CTA may use, leaving no room for a
+// runtime alignment pad: the dynamic shared memory is declared 1024-byte
+// aligned (the 128B-swizzle atom) and the kernel checks that it is.
 struct BwdSmem {
   static constexpr int kStages = 2;
   static constexpr int K_OFF = 0;
   static constexpr int V_OFF = TILE_BYTES;
-  static constexpr int QD_OFF = 2 * TILE_BYTES;                       // stages x (Q_i, dO_i)
-  static constexpr int P_OFF = QD_OFF + kStages * 2 * TILE_BYTES;      // P^T [128 keys x 128 q]
-  static constexpr int DS_OFF = P_OFF + 2 * TILE_BYTES;                // dS^T [128 keys x 128 q]
-  static constexpr int LD_OFF = DS_OFF + 2 * TILE_BYTES;               // stages x (LSE2[128], D[128]) fp32
+  static constexpr int QD_OFF = 2 * TILE_BYTES;                    // stages x (Q_i, dO_i)
+  static constexpr int PD_OFF = QD_OFF + kStages * 2 * TILE_BYTES;  // 2 x (P^T, dS^T) [128 keys x 128 q]
+  static constexpr int PD_BYTES = 4 * TILE_BYTES;
+  static constexpr int LD_OFF = PD_OFF + 2 * PD_BYTES;             // stages x (LSE2[128], D[128]) fp32
   static constexpr int BAR_OFF = LD_OFF + kStages * 2 * TILE * 4;
-  static constexpr size_t BYTES = BAR_OFF + 256 + 1024;
+  static constexpr size_t BYTES = BAR_OFF + 256;
+  static_assert(BYTES <= 232448, "backward smem");
 };
+
+// Backward CTA = 2 + kBwdSoftmaxWarps warps: warp 0 TMA, warp 1 tcgen05
+// issuer, the rest softmax-gradient warps. Warp w reads TMEM lanes
+// 32*(w%4).. (key rows of S^T / dP^T / dK / dV, query rows of dQ) and owns
+// column group (w-2)/4 of every tile it touches: kBwdSoftmaxWarps/4 warps
+// share each lane quarter and split its columns.
+//
+// A CTA walks key-tile items c, c + gridDim.x, ... (most query tiles first);
+// the launch uses one CTA per item. The query-tile steps g of a CTA's items
+// form one sequence. P^T / dS^T
+// (smem) and dQ (TMEM) are double-buffered by step parity, so the softmax
+// warps turn S^T / dP^T of step g into P^T / dS^T while the gradient MMAs of
+// step g-1 run, and then add dQ of step g-1 to the fp32 accumulator with
+// vector reductions straight from registers.
+#ifndef LLMK_BWD_SOFTMAX_WARPS
+#define LLMK_BWD_SOFTMAX_WARPS 16
+#endif
+constexpr int kBwdSoftmaxWarps = LLMK_BWD_SOFTMAX_WARPS;  // 8 or 16
+constexpr int kBwdThreads = 64 + 32 * kBwdSoftmaxWarps;
+constexpr int kBwdCols = 4 * TILE / kBwdSoftmaxWarps;     // S^T columns per warp (64 or 32)
+constexpr int kBwdGradCols = HD * 4 / kBwdSoftmaxWarps;   // dQ / dK / dV columns per warp (32 or 16)
+static_assert(kBwdSoftmaxWarps == 8 || kBwdSoftmaxWarps == 16, "softmax warps");
+
+__device__ __forceinline__ AttnItem bwd_item(int w, int B, int NH) {
+  const int bh_count = B * NH;
+  AttnItem it;
+  it.tile = w / bh_count;  // key tile kt: query tiles kt..nk-1, so kt = 0 first
+  it.bh = w % bh_count;
+  it.b = it.bh / NH;
+  it.h = it.bh % NH;
+  return it;
+}
 
 __device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, float d) {
   asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d)
                : "memory");
 }
 
-__global__ void __launch_bounds__(192, 1)
+// P^T = exp2(S^T * scale*log2e - LSE2) and dS^T = P^T (dP^T - D) for one
+// thread's key row `key` and kCols query columns tq0.., written as 16-byte
+// chunks chunk0.. of row r of the swizzled P^T / dS^T tiles. ld: the tile's
+// LSE2 / D of those columns (smem, read as broadcast vectors). kMask: the
+// diagonal tile (query < key masked) or a tile reaching past T (padded
+// queries masked).
+template <bool kMask, int kCols>
+__device__ __forceinline__ void bwd_p_ds(const uint32_t* sv, const uint32_t* dv, const float* ld_l2,
+                                         const float* ld_d, int tq0, int key, int T, uint8_t* p_tile,
+                                         uint8_t* ds_tile, int r, int chunk0) {
+  const float sl2 = 0.125f * 1.4426950408889634f;
+#pragma unroll
+  for (int c = 0; c < kCols / 8; ++c) {
+    float l2[8], dd[8];
+    *reinterpret_cast<float4*>(l2) = reinterpret_cast<const float4*>(ld_l2 + c * 8)[0];
+    *reinterpret_cast<float4*>(l2 + 4) = reinterpret_cast<const float4*>(ld_l2 + c * 8)[1];
+    *reinterpret_cast<float4*>(dd) = reinterpret_cast<const float4*>(ld_d + c * 8)[0];
+    *reinterpret_cast<float4*>(dd + 4) = reinterpret_cast<const float4*>(ld_d + c * 8)[1];
+    float p[8], ds[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int tq = tq0 + c * 8 + k;
+      float pv = ex2(fmaf(__uint_as_float(sv[c * 8 + k]), sl2, -l2[k]));
+      if (kMask && (tq < key || tq >= T)) pv = 0.f;  // causal (query before key) and padded queries
+      p[k] = pv;
+      ds[k] = pv * (__uint_as_float(dv[c * 8 + k]) - dd[k]);
+    }
+    st_tile_chunk(p_tile, r, chunk0 + c, p);
+    st_tile_chunk(ds_tile, r, chunk0 + c, ds);
+  }
+}
+
+__global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_do,
-                    void* __restrict__ dqkv_ptr, int io_f32, float* __restrict__ dq_acc, const float* __restrict__ lse,
-                    const float* __restrict__ Dvec, int B, int T, int NH, int C, unsigned int* status) {
+                    void* __restrict__ dqkv_ptr, int io_f32, float* __restrict__ dq_acc,
+                    const float* __restrict__ lse, const float* __restrict__ Dvec, int B, int T, int NH, int C,
+                    unsigned int* status) {
   using S = BwdSmem;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  extern __shared__ __align__(1024) uint8_t smem_bwd[];
+  if ((smem_u32(smem_bwd) & 1023u) != 0) {  // uniform: every thread returns before any barrier
+    if (threadIdx.x == 0) atomicOr(status, LLMK_DEV_SMEM_ALIGN);
+    return;
+  }
+  uint8_t* smem = smem_bwd;
   uint8_t* sK = smem + S::K_OFF;
   uint8_t* sV = smem + S::V_OFF;
   uint8_t* sQD = smem + S::QD_OFF;
-  uint8_t* sP = smem + S::P_OFF;
-  uint8_t* sDS = smem + S::DS_OFF;
+  uint8_t* sPD = smem + S::PD_OFF;  // buffer b: P^T at b*PD_BYTES, dS^T 2 tiles further
   float* sLD = reinterpret_cast<float*>(smem + S::LD_OFF);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::BAR_OFF);
-  uint64_t* kv_full = bars;                       // K, V loaded
-  uint64_t* qd_full = bars + 1;                   // [2] Q_i, dO_i (+ LSE/D by the TMA warp's lanes)
+  uint64_t* kv_full = bars;                       // K, V of an item loaded
+  uint64_t* kv_empty = bars + 1;                  // an item's last gradient MMAs done (K, V free)
+  uint64_t* qd_full = bars + 2;                   // [2] Q_i, dO_i
   uint64_t* qd_empty = qd_full + S::kStages;      // [2]
   uint64_t* sdp_full = qd_empty + S::kStages;     // S^T and dP^T in TMEM
-  uint64_t* ps_full = sdp_full + 1;               // P^T, dS^T in smem (128 arrivals)
-  uint64_t* grad_done = ps_full + 1;              // dV, dK, dQ MMAs of this tile done
-  uint64_t* dq_free = grad_done + 1;              // dQ TMEM read (128 arrivals)
-  uint64_t* ld_full = dq_free + 1;                // [2] LSE/D staged (32 arrivals)
+  uint64_t* sdp_free = sdp_full + 1;              // S^T / dP^T read into registers (one arrival per warp)
+  uint64_t* ps_full = sdp_free + 1;               // [2] P^T, dS^T of step parity b in smem
+  uint64_t* grad_done = ps_full + 2;              // [2] gradient MMAs of step parity b done
+  uint64_t* dq_free = grad_done + 2;              // [2] dQ TMEM buffer b read
+  uint64_t* dkv_free = dq_free + 2;               // an item's dK / dV TMEM read
+  uint64_t* ld_full = dkv_free + 1;               // [2] LSE2 / D of a ring stage staged
   uint64_t* done = ld_full + S::kStages;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int nk = (T + TILE - 1) / TILE;
-  const int bh_count = B * NH;
-  const int kt = static_cast<int>(blockIdx.x) / bh_count;  // lightest last: kt=0 has the most q tiles
-  const int bh = static_cast<int>(blockIdx.x) % bh_count;
-  const int b = bh / NH, h = bh % NH;
-  const int k0 = kt * TILE;
-  const int nqi = nk - kt;  // query tiles kt..nk-1
+  const int n_items = nk * B * NH;
   const int warp = warp_id(), lane = lane_id();
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
+    mbar_init(kv_empty, 1);
     for (int s = 0; s < S::kStages; ++s) {
       mbar_init(qd_full + s, 1);
       mbar_init(qd_empty + s, 1);
-      mbar_init(ld_full + s, 32);
+      mbar_init(ld_full + s, 1);
     }
     mbar_init(sdp_full, 1);
-    mbar_init(ps_full, 128);
-    mbar_init(grad_done, 1);
-    mbar_init(dq_free, 128);
+    mbar_init(sdp_free, kBwdSoftmaxWarps);
+    for (int b2 = 0; b2 < 2; ++b2) {
+      mbar_init(ps_full + b2, kBwdSoftmaxWarps);
+      mbar_init(grad_done + b2, 1);
+      mbar_init(dq_free + b2, kBwdSoftmaxWarps);
+    }
+    mbar_init(dkv_free, kBwdSoftmaxWarps);
     mbar_init(done, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -442,39 +583,56 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  // TMEM columns: S^T 0..127, dP^T 128..255, dV 256..319, dK 320..383, dQ 384..447
+  // TMEM columns: S^T 0..127, dP^T 128..255, dV 256..319, dK 320..383,
+  // dQ[0] 384..447, dQ[1] 448..511
 
   if (warp == 0) {
-    // lane 0 issues TMA; all 32 lanes stage LSE (log2 units) and D for each q tile.
+    // lane 0 issues the TMA loads; all 32 lanes stage LSE (log2 units) and D
+    // of each query tile next to its Q / dO ring stage (0 past T)
     if (lane == 0) {
       tma_prefetch_desc(&tm_qkv);
       tma_prefetch_desc(&tm_do);
-      mbar_arrive_expect_tx(kv_full, 2 * TILE_BYTES);
-      tma_load_3d(sK, &tm_qkv, kv_full, C + h * HD, k0, b);
-      tma_load_3d(sV, &tm_qkv, kv_full, 2 * C + h * HD, k0, b);
     }
     int stage = 0;
     uint32_t phase = 0;
-    const float* lse_bh = lse + static_cast<long long>(bh) * T;
-    const float* d_bh = Dvec + static_cast<long long>(bh) * T;
-    for (int i = 0; i < nqi; ++i) {
-      const int q0 = (kt + i) * TILE;
-      bool w = mbar_wait(qd_empty + stage, phase ^ 1u, status, abort_flag, 8);
-      if (!__all_sync(0xffffffffu, w)) break;
-      if (lane == 0) {
-        uint8_t* sq = sQD + stage * 2 * TILE_BYTES;
-        mbar_arrive_expect_tx(qd_full + stage, 2 * TILE_BYTES);
-        tma_load_3d(sq, &tm_qkv, qd_full + stage, h * HD, q0, b);
-        tma_load_3d(sq + TILE_BYTES, &tm_do, qd_full + stage, h * HD, q0, b);
+    bool ok = true;
+    int n = 0;
+    for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x, ++n) {
+      const AttnItem it = bwd_item(w, B, NH);
+      const int kt = it.tile, nqi = nk - kt;
+      const float* lse_bh = lse + static_cast<long long>(it.bh) * T;
+      const float* d_bh = Dvec + static_cast<long long>(it.bh) * T;
+      for (int i = 0; i < nqi; ++i) {
+        const int q0 = (kt + i) * TILE;
+        bool wt = mbar_wait(qd_empty + stage, phase ^ 1u, status, abort_flag, 8);
+        if (!__all_sync(0xffffffffu, wt)) { ok = false; break; }
+        if (lane == 0) {
+          uint8_t* sq = sQD + stage * 2 * TILE_BYTES;
+          mbar_arrive_expect_tx(qd_full + stage, 2 * TILE_BYTES);
+          tma_load_3d(sq, &tm_qkv, qd_full + stage, it.h * HD, q0, it.b);
+          tma_load_3d(sq + TILE_BYTES, &tm_do, qd_full + stage, it.h * HD, q0, it.b);
+        }
+        float* ld = sLD + stage * 2 * TILE;
+        for (int k = lane; k < TILE; k += 32) {
+          const int t = q0 + k;
+          ld[k] = t < T ? lse_bh[t] * 1.4426950408889634f : 0.f;
+          ld[TILE + k] = t < T ? d_bh[t] : 0.f;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(ld_full + stage);
+        if (++stage == S::kStages) { stage = 0; phase ^= 1u; }
+        if (i == 0) {
+          // K, V of this item once the previous item's gradient MMAs are done
+          // (after its first Q / dO tile, which only needs a free ring stage)
+          wt = mbar_wait(kv_empty, (n & 1) ^ 1u, status, abort_flag, 19);
+          if (!__all_sync(0xffffffffu, wt)) { ok = false; break; }
+          if (lane == 0) {
+            mbar_arrive_expect_tx(kv_full, 2 * TILE_BYTES);
+            tma_load_3d(sK, &tm_qkv, kv_full, C + it.h * HD, kt * TILE, it.b);
+            tma_load_3d(sV, &tm_qkv, kv_full, 2 * C + it.h * HD, kt * TILE, it.b);
+          }
+        }
       }
-      float* ld = sLD + stage * 2 * TILE;
-      for (int k = lane; k < TILE; k += 32) {
-        const int t = q0 + k;
-        ld[k] = t < T ? lse_bh[t] * 1.4426950408889634f : 0.f;
-        ld[TILE + k] = t < T ? d_bh[t] : 0.f;
-      }
-      mbar_arrive(ld_full + stage);
-      if (++stage == S::kStages) { stage = 0; phase ^= 1u; }
     }
   } else if (warp == 1) {
     if (lane == 0) {
@@ -486,16 +644,8 @@ __global__ void __launch_bounds__(192, 1)
       // B = K stored [keys][hd] = N-major.
       const uint32_t idesc_q = idesc_f32acc(128, HD, kFmtBF16, true, true);
       const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV);
-      const uint32_t p_addr = smem_u32(sP), ds_addr = smem_u32(sDS);
-      bool ok = mbar_wait(kv_full, 0, status, abort_flag, 9);
-      int stage = 0;
-      uint32_t phase = 0;
-      for (int i = 0; i < nqi && ok; ++i) {
-        if (!mbar_wait(qd_full + stage, phase, status, abort_flag, 10)) { ok = false; break; }
-        // S^T / dP^T TMEM is free once the softmax warps published the previous P^T/dS^T.
-        if (i > 0 && !mbar_wait(ps_full, (i - 1) & 1, status, abort_flag, 11)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t q_addr = smem_u32(sQD + stage * 2 * TILE_BYTES);
+      auto issue_sdp = [&](int st) {
+        const uint32_t q_addr = smem_u32(sQD + st * 2 * TILE_BYTES);
         const uint32_t do_addr = q_addr + TILE_BYTES;
 #pragma unroll
         for (int ks = 0; ks < HD / 16; ++ks)
@@ -506,27 +656,64 @@ __global__ void __launch_bounds__(192, 1)
           mma_f16_ss(tmem + 128, sdesc_sw128(v_addr + ks * 32, 16, 1024), sdesc_sw128(do_addr + ks * 32, 16, 1024),
                      idesc_s, ks > 0);
         mma_commit(sdp_full);
-        // P^T and dS^T of this tile written to smem
-        if (!mbar_wait(ps_full, i & 1, status, abort_flag, 12)) { ok = false; break; }
-        // dQ TMEM free (previous tile's dQ read by the epilogue warps)
-        if (i > 0 && !mbar_wait(dq_free, (i - 1) & 1, status, abort_flag, 13)) { ok = false; break; }
-        tc_fence_after();
+      };
+      bool ok = true;
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t g = 0;
+      bool issued = false;  // S^T / dP^T of step g already issued
+      int n = 0;
+      for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x, ++n) {
+        const int nqi = nk - bwd_item(w, B, NH).tile;
+        for (int j = 0; j < nqi; ++j, ++g) {
+          const int nst = stage + 1 == S::kStages ? 0 : stage + 1;
+          const uint32_t nph = stage + 1 == S::kStages ? phase ^ 1u : phase;
+          const uint32_t pb = g & 1;
+          if (!issued) {
+            // first step of an item: its K, V, and the S^T / dP^T TMEM of the previous step
+            if ((j == 0 && !mbar_wait(kv_full, n & 1, status, abort_flag, 9)) ||
+                !mbar_wait(qd_full + stage, phase, status, abort_flag, 10) ||
+                (g > 0 && !mbar_wait(sdp_free, (g - 1) & 1, status, abort_flag, 11))) { ok = false; break; }
+            tc_fence_after();
+            issue_sdp(stage);
+          }
+          issued = false;
+          if (j + 1 < nqi) {
+            // next step of this item as soon as the softmax warps hold this one in registers
+            if (!mbar_wait(sdp_free, g & 1, status, abort_flag, 11) ||
+                !mbar_wait(qd_full + nst, nph, status, abort_flag, 10)) { ok = false; break; }
+            tc_fence_after();
+            issue_sdp(nst);
+            issued = true;
+          }
+          // P^T / dS^T of this step in smem; dQ buffer pb read (step g-2); at an
+          // item's first step, the previous item's dK / dV read
+          if (!mbar_wait(ps_full + pb, (g >> 1) & 1, status, abort_flag, 12) ||
+              (g >= 2 && !mbar_wait(dq_free + pb, ((g >> 1) & 1) ^ 1u, status, abort_flag, 13)) ||
+              (j == 0 && !mbar_wait(dkv_free, (n & 1) ^ 1u, status, abort_flag, 14))) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t q_addr = smem_u32(sQD + stage * 2 * TILE_BYTES);
+          const uint32_t do_addr = q_addr + TILE_BYTES;
+          const uint32_t p_addr = smem_u32(sPD + pb * S::PD_BYTES), ds_addr = p_addr + 2 * TILE_BYTES;
 #pragma unroll
-        for (int ks = 0; ks < TILE / 16; ++ks) {
-          const uint32_t koff = (ks >> 2) * TILE_BYTES + (ks & 3) * 32;  // K (= q) offset in a [128 x 128] K-major tile
-          mma_f16_ss(tmem + 256, sdesc_sw128(p_addr + koff, 16, 1024),
-                     sdesc_sw128(do_addr + ks * 2048, TILE_BYTES, 1024), idesc_kv, (i > 0 || ks > 0));
-          mma_f16_ss(tmem + 320, sdesc_sw128(ds_addr + koff, 16, 1024),
-                     sdesc_sw128(q_addr + ks * 2048, TILE_BYTES, 1024), idesc_kv, (i > 0 || ks > 0));
+          for (int ks = 0; ks < TILE / 16; ++ks) {
+            const uint32_t koff = (ks >> 2) * TILE_BYTES + (ks & 3) * 32;  // K (= q) offset in a [128 x 128] K-major tile
+            mma_f16_ss(tmem + 256, sdesc_sw128(p_addr + koff, 16, 1024),
+                       sdesc_sw128(do_addr + ks * 2048, TILE_BYTES, 1024), idesc_kv, (j > 0 || ks > 0));
+            mma_f16_ss(tmem + 320, sdesc_sw128(ds_addr + koff, 16, 1024),
+                       sdesc_sw128(q_addr + ks * 2048, TILE_BYTES, 1024), idesc_kv, (j > 0 || ks > 0));
+          }
+          // dQ = dS K: A = dS^T as M-major (q atoms 16 KB apart, key groups 1 KB apart), K-step = 16 keys.
+#pragma unroll
+          for (int ks = 0; ks < TILE / 16; ++ks)
+            mma_f16_ss(tmem + 384 + pb * HD, sdesc_sw128(ds_addr + ks * 2048, TILE_BYTES, 1024),
+                       sdesc_sw128(k_addr + ks * 2048, TILE_BYTES, 1024), idesc_q, ks > 0);
+          mma_commit(grad_done + pb);
+          mma_commit(qd_empty + stage);
+          if (j + 1 == nqi) mma_commit(kv_empty);
+          stage = nst;
+          phase = nph;
         }
-        // dQ = dS K: A = dS^T as M-major (q atoms 16 KB apart, key groups 1 KB apart), K-step = 16 keys.
-#pragma unroll
-        for (int ks = 0; ks < TILE / 16; ++ks)
-          mma_f16_ss(tmem + 384, sdesc_sw128(ds_addr + ks * 2048, TILE_BYTES, 1024),
-                     sdesc_sw128(k_addr + ks * 2048, TILE_BYTES, 1024), idesc_q, ks > 0);
-        mma_commit(grad_done);
-        mma_commit(qd_empty + stage);
-        if (++stage == S::kStages) { stage = 0; phase ^= 1u; }
       }
       mma_commit(done);
       mbar_wait(done, 0, status, nullptr, 5);
@@ -534,125 +721,138 @@ __global__ void __launch_bounds__(192, 1)
     __syncwarp();
   } else {
     const int q = warp & 3;
-    const int r = q * 32 + lane;  // key row within the tile for S^T/dP^T/dK/dV; query row for dQ
+    const int cq = (warp - 2) >> 2;  // column quarter
+    const int r = q * 32 + lane;     // key row within the tile for S^T/dP^T/dK/dV; query row for dQ
     const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
-    const float sl2 = 0.125f * 1.4426950408889634f;
-    int stage = 0;
-    uint32_t phase = 0;
-    bool ok = true;
-    for (int i = 0; i < nqi; ++i) {
-      const int qt = kt + i;
-      bool w = mbar_wait(ld_full + stage, phase, status, abort_flag, 15) &&
-               mbar_wait(sdp_full, i & 1, status, abort_flag, 16);
-      // previous tile's dV/dK/dQ MMAs read P^T/dS^T: wait before overwriting them
-      if (i > 0) w = w && mbar_wait(grad_done, (i - 1) & 1, status, abort_flag, 17);
-      if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
-      tc_fence_after();
-      if (i > 0) {
-        // dQ of the previous q tile: TMEM lane = query row
-        const int tq = (qt - 1) * TILE + r;
-        uint32_t v[32];
+    // dQ of step gg (TMEM buffer gg&1, lane = query row, columns cq*16..+16)
+    // added to the fp32 accumulator with vector reductions
+    auto flush_dq = [&](uint32_t gg, int b, int h, int qt) {
+      uint32_t v[kBwdGradCols];
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          tmem_ld_32x32b_x32(tmem + lane_base + 384 + half * 32, v);
-          tmem_ld_wait();
-          if (tq < T) {
-            float* dst = dq_acc + (static_cast<long long>(b) * T + tq) * C + h * HD + half * 32;
+      for (int c16 = 0; c16 < kBwdGradCols; c16 += 16)
+        tmem_ld_32x32b_x16(tmem + lane_base + 384 + (gg & 1) * HD + cq * kBwdGradCols + c16,
+                           *reinterpret_cast<uint32_t(*)[16]>(v + c16));
+      tmem_ld_wait();
+      const int tq = qt * TILE + r;
+      if (tq < T) {
+        float* dst = dq_acc + (static_cast<long long>(b) * T + tq) * C + h * HD + cq * kBwdGradCols;
 #pragma unroll
-            for (int k = 0; k < 8; ++k)
-              red_add_v4(dst + 4 * k, __uint_as_float(v[4 * k]), __uint_as_float(v[4 * k + 1]),
-                         __uint_as_float(v[4 * k + 2]), __uint_as_float(v[4 * k + 3]));
-          }
-        }
-        tc_fence_before();
-        mbar_arrive(dq_free);
+        for (int k = 0; k < kBwdGradCols / 4; ++k)
+          red_add_v4(dst + 4 * k, __uint_as_float(v[4 * k]), __uint_as_float(v[4 * k + 1]),
+                     __uint_as_float(v[4 * k + 2]), __uint_as_float(v[4 * k + 3]));
       }
-      const float* ld = sLD + stage * 2 * TILE;
-      const int key = k0 + r;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t sv[32], dv[32];
-        tmem_ld_32x32b_x32(tmem + lane_base + c * 32, sv);
-        tmem_ld_32x32b_x32(tmem + lane_base + 128 + c * 32, dv);
+    };
+    // dK (scaled) and dV of key tile kt, columns cq*16..+16: TMEM lane = key row.
+    // tcgen05.ld is warp-collective (.sync.aligned): every lane loads, only
+    // lanes of keys < T store.
+    auto drain_dkv = [&](int b, int h, int kt) {
+      const int tk = kt * TILE + r;
+      const bool key_ok = tk < T;
+      // element offset of this key's dK slice; dV is C further
+      const long long dk_off =
+          (static_cast<long long>(b) * T + (key_ok ? tk : 0)) * 3 * C + C + h * HD + cq * kBwdGradCols;
+#pragma unroll
+      for (int part = 0; part < 2 * kBwdGradCols / 16; ++part) {  // dK (cols 320.., scaled), then dV (cols 256..)
+        const int which = part / (kBwdGradCols / 16), c16 = (part % (kBwdGradCols / 16)) * 16;
+        uint32_t x[16];
+        tmem_ld_32x32b_x16(tmem + lane_base + (which == 0 ? 320 : 256) + cq * kBwdGradCols + c16, x);
         tmem_ld_wait();
-        float p[32], ds[32];
+        if (key_ok) {
+          const float sc = which == 0 ? 0.125f : 1.0f;
+          const long long off = dk_off + (which == 0 ? 0 : C) + c16;
+          if (io_f32) {
+            float4* dst = reinterpret_cast<float4*>(static_cast<float*>(dqkv_ptr) + off);
 #pragma unroll
-        for (int k = 0; k < 32; ++k) {
-          const int qi = c * 32 + k;
-          const int tq = qt * TILE + qi;
-          float pv = ex2(__uint_as_float(sv[k]) * sl2 - ld[qi]);
-          if (tq < key || tq >= T) pv = 0.f;  // causal (query before key) and padded queries
-          p[k] = pv;
-          ds[k] = pv * (__uint_as_float(dv[k]) - ld[TILE + qi]);
-        }
+            for (int ch = 0; ch < 4; ++ch)
+              dst[ch] = make_float4(__uint_as_float(x[ch * 4]) * sc, __uint_as_float(x[ch * 4 + 1]) * sc,
+                                    __uint_as_float(x[ch * 4 + 2]) * sc, __uint_as_float(x[ch * 4 + 3]) * sc);
+          } else {
+            __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(dqkv_ptr) + off;
 #pragma unroll
-        for (int ch = 0; ch < 4; ++ch) {
-          st_tile_chunk(sP, r, c * 4 + ch, p + ch * 8);
-          st_tile_chunk(sDS, r, c * 4 + ch, ds + ch * 8);
-        }
-      }
-      fence_async_smem();
-      tc_fence_before();
-      mbar_arrive(ps_full);
-      if (++stage == S::kStages) { stage = 0; phase ^= 1u; }
-    }
-    if (ok) {
-      bool w = mbar_wait(grad_done, (nqi - 1) & 1, status, abort_flag, 18);
-      if (__all_sync(0xffffffffu, w)) {
-        tc_fence_after();
-        uint32_t v[32];
-        // last dQ
-        const int tq = (kt + nqi - 1) * TILE + r;
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          tmem_ld_32x32b_x32(tmem + lane_base + 384 + half * 32, v);
-          tmem_ld_wait();
-          if (tq < T) {
-            float* dst = dq_acc + (static_cast<long long>(b) * T + tq) * C + h * HD + half * 32;
-#pragma unroll
-            for (int k = 0; k < 8; ++k)
-              red_add_v4(dst + 4 * k, __uint_as_float(v[4 * k]), __uint_as_float(v[4 * k + 1]),
-                         __uint_as_float(v[4 * k + 2]), __uint_as_float(v[4 * k + 3]));
-          }
-        }
-        // dK (scaled) and dV: TMEM lane = key row. tcgen05.ld is warp-collective
-        // (.sync.aligned): every lane loads, only lanes of keys < T store.
-        const int tk = k0 + r;
-        const bool key_ok = tk < T;
-        // element offset of this key's dK slice; dV is C further
-        const long long dk_off = (static_cast<long long>(b) * T + (key_ok ? tk : 0)) * 3 * C + C + h * HD;
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {
-#pragma unroll
-          for (int which = 0; which < 2; ++which) {  // 0: dK (cols 320..383, scaled), 1: dV (cols 256..319)
-            const float sc = which == 0 ? 0.125f : 1.0f;
-            tmem_ld_32x32b_x32(tmem + lane_base + (which == 0 ? 320 : 256) + half * 32, v);
-            tmem_ld_wait();
-            if (key_ok) {
-              const long long off = dk_off + (which == 0 ? 0 : C) + half * 32;
-              if (io_f32) {
-                float4* dst = reinterpret_cast<float4*>(static_cast<float*>(dqkv_ptr) + off);
-#pragma unroll
-                for (int ch = 0; ch < 8; ++ch)
-                  dst[ch] = make_float4(__uint_as_float(v[ch * 4]) * sc, __uint_as_float(v[ch * 4 + 1]) * sc,
-                                        __uint_as_float(v[ch * 4 + 2]) * sc, __uint_as_float(v[ch * 4 + 3]) * sc);
-              } else {
-                __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(dqkv_ptr) + off;
-#pragma unroll
-                for (int ch = 0; ch < 4; ++ch) {
-                  uint4 u;
-                  u.x = pack_bf16x2(__uint_as_float(v[ch * 8 + 0]) * sc, __uint_as_float(v[ch * 8 + 1]) * sc);
-                  u.y = pack_bf16x2(__uint_as_float(v[ch * 8 + 2]) * sc, __uint_as_float(v[ch * 8 + 3]) * sc);
-                  u.z = pack_bf16x2(__uint_as_float(v[ch * 8 + 4]) * sc, __uint_as_float(v[ch * 8 + 5]) * sc);
-                  u.w = pack_bf16x2(__uint_as_float(v[ch * 8 + 6]) * sc, __uint_as_float(v[ch * 8 + 7]) * sc);
-                  reinterpret_cast<uint4*>(dst)[ch] = u;
-                }
-              }
+            for (int ch = 0; ch < 2; ++ch) {
+              uint4 u;
+              u.x = pack_bf16x2(__uint_as_float(x[ch * 8 + 0]) * sc, __uint_as_float(x[ch * 8 + 1]) * sc);
+              u.y = pack_bf16x2(__uint_as_float(x[ch * 8 + 2]) * sc, __uint_as_float(x[ch * 8 + 3]) * sc);
+              u.z = pack_bf16x2(__uint_as_float(x[ch * 8 + 4]) * sc, __uint_as_float(x[ch * 8 + 5]) * sc);
+              u.w = pack_bf16x2(__uint_as_float(x[ch * 8 + 6]) * sc, __uint_as_float(x[ch * 8 + 7]) * sc);
+              reinterpret_cast<uint4*>(dst)[ch] = u;
             }
           }
         }
       }
+    };
+    bool ok = true;
+    uint32_t g = 0;
+    int stage = 0;
+    uint32_t phase = 0;
+    bool have_prev = false, prev_last = false;
+    int pbb = 0, phh = 0, pqt = 0, pkt = 0;  // the previous step's batch, head, q tile and key tile
+    // the previous step's gradient MMAs are done: flush its dQ and, at an item
+    // boundary, drain its item's dK / dV
+    auto finish_prev = [&]() -> bool {
+      const uint32_t gp = g - 1;
+      bool gd = mbar_wait(grad_done + (gp & 1), (gp >> 1) & 1, status, abort_flag, 17);
+      if (!__all_sync(0xffffffffu, gd)) return false;
+      tc_fence_after();
+      flush_dq(gp, pbb, phh, pqt);
+      if (prev_last) drain_dkv(pbb, phh, pkt);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(dq_free + (gp & 1));
+        if (prev_last) mbar_arrive(dkv_free);
+      }
+      return true;
+    };
+    for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x) {
+      const AttnItem it = bwd_item(w, B, NH);
+      const int kt = it.tile, nqi = nk - kt, k0 = kt * TILE;
+      for (int j = 0; j < nqi; ++j, ++g) {
+        const int qt = kt + j;
+        const uint32_t pb = g & 1;
+        bool wt = mbar_wait(ld_full + stage, phase, status, abort_flag, 15) &&
+                  mbar_wait(sdp_full, g & 1, status, abort_flag, 16);
+        if (!__all_sync(0xffffffffu, wt)) { ok = false; break; }
+        tc_fence_after();
+        // this warp's 32 columns of S^T and dP^T into registers, then release the TMEM
+        uint32_t sv[kBwdCols], dv[kBwdCols];
+#pragma unroll
+        for (int h32 = 0; h32 < kBwdCols / 32; ++h32) {
+          tmem_ld_32x32b_x32(tmem + lane_base + cq * kBwdCols + h32 * 32,
+                             *reinterpret_cast<uint32_t(*)[32]>(sv + h32 * 32));
+          tmem_ld_32x32b_x32(tmem + lane_base + 128 + cq * kBwdCols + h32 * 32,
+                             *reinterpret_cast<uint32_t(*)[32]>(dv + h32 * 32));
+        }
+        tmem_ld_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(sdp_free);
+        // P^T / dS^T buffer pb was last read by the gradient MMAs of step g-2,
+        // which finished before this warp flushed that step's dQ
+        uint8_t* p_tile = sPD + pb * S::PD_BYTES;
+        const int tq0 = qt * TILE + cq * kBwdCols;
+        const float* ld = sLD + stage * 2 * TILE + cq * kBwdCols;
+        if (qt == kt || qt * TILE + TILE > T)
+          bwd_p_ds<true, kBwdCols>(sv, dv, ld, ld + TILE, tq0, k0 + r, T, p_tile, p_tile + 2 * TILE_BYTES, r,
+                                   cq * kBwdCols / 8);
+        else
+          bwd_p_ds<false, kBwdCols>(sv, dv, ld, ld + TILE, tq0, k0 + r, T, p_tile, p_tile + 2 * TILE_BYTES, r,
+                                    cq * kBwdCols / 8);
+        fence_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(ps_full + pb);
+        if (++stage == S::kStages) { stage = 0; phase ^= 1u; }
+        if (have_prev && !finish_prev()) { ok = false; break; }
+        have_prev = true;
+        prev_last = j + 1 == nqi;
+        pbb = it.b;
+        phh = it.h;
+        pqt = qt;
+        pkt = kt;
+      }
     }
+    if (ok && have_prev) finish_prev();
     tc_fence_before();
   }
   __syncthreads();
@@ -700,7 +900,8 @@ int llmk_attention_forward(void* out, llmk_dtype out_dtype, float* lse, const vo
                         static_cast<uint64_t>(T) * C3 * 2, HD, TILE, 1));
   LLMK_TRY(set_smem(reinterpret_cast<const void*>(attn_fwd_kernel), FwdSmem::BYTES));
   const int nq = (T + TILE - 1) / TILE;
-  attn_fwd_kernel<<<nq * B * NH, 192, FwdSmem::BYTES, static_cast<cudaStream_t>(stream)>>>(
+  const int grid = std::min(nq * B * NH, num_sms());  // persistent: one CTA per SM
+  attn_fwd_kernel<<<grid, 192, FwdSmem::BYTES, static_cast<cudaStream_t>(stream)>>>(
       tm, out, out_dtype == LLMK_F32 ? 1 : 0, lse, B, T, NH, C, device_status_ptr());
   count_launch();
   LLMK_CUDA(cudaGetLastError());
@@ -755,8 +956,11 @@ int llmk_attention_backward(void* dqkv, const void* dout, const void* out, llmk_
                         static_cast<uint64_t>(T) * C * 2, HD, TILE, 1));
   LLMK_TRY(set_smem(reinterpret_cast<const void*>(attn_bwd_kernel), BwdSmem::BYTES));
   const int nk = (T + TILE - 1) / TILE;
-  attn_bwd_kernel<<<nk * B * NH, 192, BwdSmem::BYTES, s>>>(tq, td, dqkv, f32 ? 1 : 0, dq, lse, Dv, B, T, NH, C,
-                                                            device_status_ptr());
+  // one CTA per key-tile item: the hardware scheduler balances the uneven
+  // items better than a static persistent assignment (measured)
+  const int grid = nk * B * NH;
+  attn_bwd_kernel<<<grid, kBwdThreads, BwdSmem::BYTES, s>>>(tq, td, dqkv, f32 ? 1 : 0, dq, lse, Dv, B, T, NH, C,
+                                                             device_status_ptr());
   const long long n8 = static_cast<long long>(B) * T * C / 8;
   const int pg = static_cast<int>(std::min<long long>((n8 + 255) / 256, 148LL * 16));
   if (f32) attn_bwd_post_kernel<float><<<pg, 256, 0, s>>>(static_cast<float*>(dqkv), dq, B * T, C, 0.125f);

@@ -127,7 +127,7 @@ __global__ void __launch_bounds__(256) layernorm_fwd_kernel(OutT* __restrict__ o
 // final dinp into its own smem slice [3][C]; the block then reduces the
 // slices in warp order into partial[block][3][C]. kV as in the forward.
 template <typename DoutT, int kV>
-__global__ void __launch_bounds__(256) layernorm_bwd_kernel(float* __restrict__ dinp, __nv_bfloat16* __restrict__ dinp_bf16,
+__global__ void __launch_bounds__(256, 2) layernorm_bwd_kernel(float* __restrict__ dinp, __nv_bfloat16* __restrict__ dinp_bf16,
                                                             float* __restrict__ partial, const DoutT* __restrict__ dout,
                                                             const float* __restrict__ inp,
                                                             const float* __restrict__ gamma,
@@ -151,12 +151,19 @@ __global__ void __launch_bounds__(256) layernorm_bwd_kernel(float* __restrict__ 
     const float m = mean[row], r = rstd[row];
     float s1 = 0.f, s2 = 0.f;
     if constexpr (kV > 0) {
-      float4 d[kV], xh[kV];
+      float4 d[kV], xh[kV], old[kV];
+      // every global read of the row issued together: one memory latency per row
 #pragma unroll
       for (int k = 0; k < kV; ++k) {
         const int c = lane * 4 + k * 128;
         d[k] = ld4(dy + c);
-        float4 v = ld4(x + c), g = ld4(gamma + c);
+        xh[k] = ld4(x + c);
+        if (accumulate) old[k] = ld4(dx + c);
+      }
+#pragma unroll
+      for (int k = 0; k < kV; ++k) {
+        const int c = lane * 4 + k * 128;
+        const float4 v = xh[k], g = ld4(gamma + c);
         xh[k] = make_float4((v.x - m) * r, (v.y - m) * r, (v.z - m) * r, (v.w - m) * r);
         float4 gd = make_float4(g.x * d[k].x, g.y * d[k].y, g.z * d[k].z, g.w * d[k].w);
         s1 += (gd.x + gd.y) + (gd.z + gd.w);
@@ -174,8 +181,7 @@ __global__ void __launch_bounds__(256) layernorm_bwd_kernel(float* __restrict__ 
         o.z = r * ((g.z * d[k].z - xh[k].z * s2) - s1);
         o.w = r * ((g.w * d[k].w - xh[k].w * s2) - s1);
         if (accumulate) {
-          float4 p = ld4(dx + c);
-          o.x += p.x; o.y += p.y; o.z += p.z; o.w += p.w;
+          o.x += old[k].x; o.y += old[k].y; o.z += old[k].z; o.w += old[k].w;
         }
         st4(dx + c, o);
         if (dinp_bf16) st4(dinp_bf16 + static_cast<long long>(row) * C + c, o);

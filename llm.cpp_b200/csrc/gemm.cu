@@ -632,29 +632,35 @@ int dispatch_kind(int kind, int a_trans, int b_trans, const void* A, long long l
 }  // namespace
 
 // Chooses the kernel kind (CTA pair with BN 256 or 128 for M >= 256, else a
-// single CTA with BN 128) and the split-K factor. Split-K only when the tile
-// grid leaves most SMs idle and K is long (the dweight GEMMs: M,N = layer
-// width, K = B*T tokens).
+// single CTA with BN 128) and the split-K factor.
+//  - K long (>= 64 K blocks: the weight gradients, M, N = layer widths,
+//    K = B*T tokens): 256-wide pair tiles, and split-K by the largest power
+//    of two that keeps the work units within one wave of CTA pairs. Measured
+//    on B200 for the GPT-2 124M weight gradients this beats 128-wide tiles
+//    and deeper splits by 1.5-1.9x.
+//  - otherwise the tile width with the fewer waves (128-wide tiles cost about
+//    half a 256-wide one plus a fixed overhead), split only when a short tile
+//    grid leaves most SMs idle.
 static void plan_gemm(int M, int N, int K, int elem, int* kind, int* splits) {
   const int sms = num_sms();
+  const int bk = 128 / elem;
+  const int num_kb = (K + bk - 1) / bk;
   int tiles, units;
   if (M >= 256) {
     units = sms / 2;
     const int num_m = (M + 255) / 256;
     const int t256 = num_m * ((N + 255) / 256), t128 = num_m * ((N + 127) / 128);
     const long long w256 = (t256 + units - 1) / units, w128 = (t128 + units - 1) / units;
-    // a 128-wide tile costs about half a 256-wide one plus a fixed overhead
-    *kind = (w256 * 256 * 10 <= w128 * 128 * 11) ? 2 : 1;
+    if (num_kb >= 64) *kind = 2;
+    else *kind = (w256 * 256 * 10 <= w128 * 128 * 11) ? 2 : 1;
     tiles = (*kind == 2) ? t256 : t128;
   } else {
     units = sms;
     *kind = 0;
     tiles = ((M + 127) / 128) * ((N + 127) / 128);
   }
-  const int bk = 128 / elem;
-  const int num_kb = (K + bk - 1) / bk;
   int s = 1;
-  while (tiles * s < units && num_kb / (s * 2) >= 8) s *= 2;
+  while (tiles * s * 2 <= units && num_kb / (s * 2) >= 8) s *= 2;
   // Every split must own at least one K block (an empty split would publish
   // a stale accumulator).
   while (s > 1 && ((num_kb + s - 1) / s) * (s - 1) >= num_kb) s /= 2;

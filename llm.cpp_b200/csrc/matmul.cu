@@ -28,24 +28,31 @@ __global__ void __launch_bounds__(256) colsum_partial_kernel(const void* __restr
   const int r0 = blockIdx.y * rows_per_chunk;
   const int r1 = min(M, r0 + rows_per_chunk);
   float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-  if (n0 < N) {
-    for (int r = r0 + ty; r < r1; r += kRowLanes) {
-      if (kBF16) {
-        uint4 u = *reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(x) + static_cast<long long>(r) * N + n0);
-        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+  auto add_row = [&](int r) {
+    if (kBF16) {
+      uint4 u = *reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(x) + static_cast<long long>(r) * N + n0);
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          float2 f = __bfloat1622float2(h[i]);
-          acc[2 * i] += f.x;
-          acc[2 * i + 1] += f.y;
-        }
-      } else {
-        const float4* p = reinterpret_cast<const float4*>(static_cast<const float*>(x) + static_cast<long long>(r) * N + n0);
-        float4 a = p[0], b = p[1];
-        acc[0] += a.x; acc[1] += a.y; acc[2] += a.z; acc[3] += a.w;
-        acc[4] += b.x; acc[5] += b.y; acc[6] += b.z; acc[7] += b.w;
+      for (int i = 0; i < 4; ++i) {
+        float2 f = __bfloat1622float2(h[i]);
+        acc[2 * i] += f.x;
+        acc[2 * i + 1] += f.y;
       }
+    } else {
+      const float4* p = reinterpret_cast<const float4*>(static_cast<const float*>(x) + static_cast<long long>(r) * N + n0);
+      float4 a = p[0], b = p[1];
+      acc[0] += a.x; acc[1] += a.y; acc[2] += a.z; acc[3] += a.w;
+      acc[4] += b.x; acc[5] += b.y; acc[6] += b.z; acc[7] += b.w;
     }
+  };
+  if (n0 < N) {
+    // four rows per iteration: their loads are independent and in flight together
+    int r = r0 + ty;
+    for (; r + 3 * kRowLanes < r1; r += 4 * kRowLanes) {
+#pragma unroll
+      for (int u = 0; u < 4; ++u) add_row(r + u * kRowLanes);
+    }
+    for (; r < r1; r += kRowLanes) add_row(r);
   }
 #pragma unroll
   for (int j = 0; j < 8; ++j) red[ty][tx * 8 + j] = acc[j];
@@ -71,16 +78,19 @@ __global__ void colsum_final_kernel(const float* __restrict__ partial, float* __
 
 int colsum_chunks(int M, int N) {
   const int col_blocks = (N + kColsPerBlock - 1) / kColsPerBlock;
-  int chunks = (2 * num_sms() + col_blocks - 1) / col_blocks;
+  // about 8 blocks (64 warps) per SM: enough loads in flight to stream HBM
+  int chunks = (8 * num_sms() + col_blocks - 1) / col_blocks;
   chunks = std::max(1, std::min(chunks, (M + 63) / 64));
   return chunks;
 }
 
 }  // namespace
 
+// max_chunks > 0 caps the row chunks (and so the partial buffer) below the
+// bandwidth-optimal count.
 int colsum_launch(float* out, const void* x, bool bf16, int M, int N, int accumulate, float* partial,
-                  cudaStream_t s) {
-  const int chunks = colsum_chunks(M, N);
+                  cudaStream_t s, int max_chunks = 0) {
+  const int chunks = max_chunks > 0 ? std::min(colsum_chunks(M, N), max_chunks) : colsum_chunks(M, N);
   const int rows_per_chunk = (M + chunks - 1) / chunks;
   dim3 grid((N + kColsPerBlock - 1) / kColsPerBlock, chunks);
   dim3 block(32, kRowLanes);
@@ -131,8 +141,10 @@ int llmk_colsum_noalloc(float* dbias, const void* x, llmk_dtype x_dtype, int M, 
   if (!dbias || !x || M <= 0 || N <= 0) return fail(LLMK_ERR_INVALID_ARG, "colsum_noalloc: bad arguments");
   if (N % 8 || !aligned16(x))
     return fail(LLMK_ERR_UNSUPPORTED, "colsum_noalloc: N % 8 == 0 and 16-byte alignment required");
-  const size_t need = static_cast<size_t>(colsum_chunks(M, N)) * N;
-  if (need > static_cast<size_t>(kColsumNoAllocFloats))
+  // as many row chunks as the fixed scratch holds (at least one)
+  const int max_chunks = static_cast<int>(std::min<size_t>(colsum_chunks(M, N), kColsumNoAllocFloats / N));
+  const size_t need = static_cast<size_t>(std::max(max_chunks, 1)) * N;
+  if (max_chunks < 1 || need > static_cast<size_t>(kColsumNoAllocFloats))
     return fail(LLMK_ERR_UNSUPPORTED,
                 "colsum_noalloc: M x N needs " + std::to_string(need) + " scratch floats, more than the fixed " +
                     std::to_string(kColsumNoAllocFloats) + " (use llmk_colsum with a caller workspace)");
@@ -154,7 +166,7 @@ int llmk_colsum_noalloc(float* dbias, const void* x, llmk_dtype x_dtype, int M, 
   // Pass 1 overwrites every partial that pass 2 reads, so nothing in the
   // shared scratch has to start at zero.
   return colsum_launch(dbias, x, x_dtype == LLMK_BF16, M, N, accumulate, scratch,
-                       static_cast<cudaStream_t>(stream));
+                       static_cast<cudaStream_t>(stream), max_chunks);
 }
 
 int llmk_matmul_forward(void* out, llmk_dtype out_dtype, const void* inp, const void* weight, const float* bias,

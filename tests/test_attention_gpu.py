@@ -40,7 +40,10 @@ def _run_gpu(qkv_np, dout_np, B, T, C, NH, dev, io="bf16"):
 
 
 @pytest.mark.parametrize("io", ["bf16", "f32"])
-@pytest.mark.parametrize("B,T,NH", [(1, 128, 1), (2, 256, 2), (1, 200, 3), (2, 64, 2), (1, 384, 2), (1, 1, 1)])
+# (4, 600, 12): 240 work items over at most 148 persistent CTAs, so CTAs walk
+# several items of different lengths with a ragged last tile
+@pytest.mark.parametrize("B,T,NH", [(1, 128, 1), (2, 256, 2), (1, 200, 3), (2, 64, 2), (1, 384, 2), (1, 1, 1),
+                                    (4, 600, 12)])
 def test_attention_vs_oracle(cuda_dev, B, T, NH, io):
     C = 64 * NH
     qkv = _bf16_round(O.normal((B, T, 3 * C), 100 + T))

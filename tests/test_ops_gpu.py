@@ -269,6 +269,32 @@ def test_softmax_crossentropy_vs_oracle(cuda_dev, dtname):
     assert torch.count_nonzero(dl[:, V:]).item() == 0
 
 
+@pytest.mark.parametrize("BT,V,Vp", [(400, 50257, 50304), (333, 1001, 1008)])
+def test_softmax_crossentropy_rows_in_place(cuda_dev, BT, V, Vp):
+    """bf16 rows streamed through shared memory: more rows than SMs (each CTA
+    walks several rows through both buffers) and dlogits written over logits."""
+    import torch
+    import llmk
+    logits = bf(O.normal((BT, Vp), 43, std=2.0))
+    logits[:, V:] = 0.0
+    tgt = O.tokens(BT, V, 44)
+    ld = T(logits, cuda_dev, torch.bfloat16)
+    losses = torch.empty(BT, device=cuda_dev)
+    llmk.call("llmk_softmax_crossentropy", losses.data_ptr(), ld.data_ptr(), ld.data_ptr(), llmk.BF16,
+              T(tgt, cuda_dev).data_ptr(), BT, V, Vp, 1.0 / BT, llmk.stream_ptr())
+    probs = np.zeros((BT, V), np.float32)
+    O.orc().orc_softmax(probs, logits, BT, V, Vp)
+    lo = np.zeros(BT, np.float32)
+    O.orc().orc_cross_entropy(lo.ctypes.data, probs, tgt, BT, V)
+    dlo = np.zeros((BT, Vp), np.float32)
+    O.orc().orc_cross_entropy_softmax_backward(dlo, probs, tgt, BT, V, Vp)
+    torch.cuda.synchronize()
+    assert llmk.device_status() == 0
+    assert max_rel_err(losses.cpu(), torch.from_numpy(lo)) < 1e-4
+    assert max_rel_err(ld.float().cpu(), torch.from_numpy(dlo)) < 1e-2
+    assert torch.count_nonzero(ld[:, V:]).item() == 0
+
+
 def test_adamw_vs_oracle(cuda_dev):
     import torch
     import llmk
