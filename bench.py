@@ -344,7 +344,8 @@ def main() -> None:
                              "launches_per_step": c["launches"] // args.steps,
                              "achieved": round(rate, 1), "unit": "TFLOP/s" if tensor else "GB/s",
                              "frac": round(rate / peak, 4)}
-        g = classes["gemm"]
+        gemm_cls = [c for n, c in classes.items() if n.startswith("gemm")]
+        g = {k: sum(c[k] for c in gemm_cls) for k in ("ms", "work", "launches", "calls")}
         gemm_launches = max(g["launches"], 1)
         achieved = g["work"] / (g["ms"] * 1e-3) / 1e12
         line = {
@@ -366,6 +367,7 @@ def main() -> None:
                          "launch_ms": g["ms"] / gemm_launches,
                          "peak_source": peaks["source"] + " bf16 burst (the step runs at max SM clock)"},
             "kernels": kernels,
+            "gemm_ms_per_step": round(g["ms"] / args.steps, 3),
             "instrumented_ms_per_step": round(timed_ms, 3),
             "gemm_alone_tflops": roof["per_gemm"],
             "gemm_alone_step_ms": round(roof["step_gemm_ms"], 3),

@@ -44,6 +44,7 @@ struct EpiParams {
   long long ldaux;
   int flags;
   float* partial;  // split-K: fp32 [splits][M][N] workspace (raw accumulators)
+  int aux_tma;     // GELU pre-activation leaves by TMA store (aux dtype == D dtype)
 };
 
 template <bool kTF32, bool kAMN, bool kBMN, int kBN, bool kPair>
@@ -126,9 +127,12 @@ __device__ __forceinline__ void store8_bf16(__nv_bfloat16* p, const float* v) {
 }
 
 // Epilogue operations on 8 consecutive columns [gn, gn+8) of row gm (all in
-// bounds) except the final store: bias, residual, GELU (+ pre-activation
-// store) / GELU-backward, accumulate onto the old D.
-__device__ __forceinline__ void epi_ops8(const EpiParams& ep, long long gm, int gn, float* v) {
+// bounds) except the final store, in two parts: epi_pre8 adds bias and
+// residual (giving the GELU pre-activation); epi_post8 stores the
+// pre-activation when asked (store_aux), applies GELU / GELU-backward and
+// accumulates onto the old D. A bf16 output takes the SFU tanh in the GELU
+// pair (its error is below the bf16 rounding).
+__device__ __forceinline__ void epi_pre8(const EpiParams& ep, long long gm, int gn, float* v) {
   float t[8];
   if (ep.bias) {
     load8(ep.bias + gn, t);
@@ -140,8 +144,11 @@ __device__ __forceinline__ void epi_ops8(const EpiParams& ep, long long gm, int 
 #pragma unroll
     for (int j = 0; j < 8; ++j) v[j] += t[j];
   }
+}
+__device__ __forceinline__ void epi_post8(const EpiParams& ep, long long gm, int gn, float* v, bool store_aux) {
+  float t[8];
   if (ep.flags & LLMK_EPI_GELU) {
-    if (ep.aux) {
+    if (ep.aux && store_aux) {
       if (ep.flags & LLMK_EPI_AUX_F32) store8(reinterpret_cast<float*>(ep.aux) + gm * ep.ldaux + gn, v);
       else store8_bf16(ep.aux + gm * ep.ldaux + gn, v);
     }
@@ -207,21 +214,42 @@ __device__ __forceinline__ void epi_apply8(const EpiParams& ep, long long gm, in
   }
 }
 
+// Writes the 8 values of column group k (8 columns) of this lane's row into a
+// 128B-swizzled [32 rows x 128 B] staging buffer: bf16 = one 16-byte chunk,
+// fp32 = two.
+template <bool kBF16>
+__device__ __forceinline__ void stage8(uint8_t* buf, int lane, int k, const float* v) {
+  const int r7 = lane & 7;
+  if constexpr (kBF16) {
+    uint4 u;
+    u.x = pack_bf16x2(v[0], v[1]);
+    u.y = pack_bf16x2(v[2], v[3]);
+    u.z = pack_bf16x2(v[4], v[5]);
+    u.w = pack_bf16x2(v[6], v[7]);
+    *reinterpret_cast<uint4*>(buf + lane * 128 + ((k ^ r7) << 4)) = u;
+  } else {
+    *reinterpret_cast<uint4*>(buf + lane * 128 + (((2 * k) ^ r7) << 4)) =
+        make_uint4(__float_as_uint(v[0]), __float_as_uint(v[1]), __float_as_uint(v[2]), __float_as_uint(v[3]));
+    *reinterpret_cast<uint4*>(buf + lane * 128 + (((2 * k + 1) ^ r7) << 4)) =
+        make_uint4(__float_as_uint(v[4]), __float_as_uint(v[5]), __float_as_uint(v[6]), __float_as_uint(v[7]));
+  }
+}
+
 // Drains columns [c_begin, c_end) of one warp's 32 accumulator rows (TMEM
 // lanes from `tsrc`) through the fused epilogue in chunks of 4 KB: 64 bf16 or
-// 32 fp32 columns.
-// Each chunk is written 128B-swizzled into one of the warp's two staging
-// buffers and stored by one lane with a TMA store; the buffers alternate, so
-// a chunk's smem writes only wait for the store issued two chunks earlier.
-// Rows / columns past M / N are clipped by the tensor map.
-template <bool kBF16>
-__device__ __forceinline__ void epilogue_cols(const EpiParams& ep, const CUtensorMap* tmD, uint32_t tsrc, int row0,
-                                              int n0, int c_begin, int c_end, int sp, int M, int N, int lane,
-                                              uint8_t* stg, uint32_t& nstore) {
+// 32 fp32 columns. Each chunk is written 128B-swizzled into one of the warp's
+// two staging buffers and stored by one lane with a TMA store; the buffers
+// alternate, so a chunk's smem writes only wait for the store issued two
+// chunks earlier. kAux: the GELU pre-activation is staged too (first buffer)
+// and leaves by a second TMA store (tmX), so each chunk uses both buffers.
+// Rows / columns past M / N are clipped by the tensor maps.
+template <bool kBF16, bool kAux>
+__device__ __forceinline__ void epilogue_cols(const EpiParams& ep, const CUtensorMap* tmD, const CUtensorMap* tmX,
+                                              uint32_t tsrc, int row0, int n0, int c_begin, int c_end, int sp, int M,
+                                              int N, int lane, uint8_t* stg, uint32_t& nstore) {
   constexpr int CW = kBF16 ? 64 : 32;  // columns per chunk
   const long long gm = row0 + lane;
   const bool row_ok = gm < M && !ep.partial;
-  const int r7 = lane & 7;
 #pragma unroll 1
   for (int c0 = c_begin; c0 < c_end; c0 += CW) {
     const int gn0 = n0 + c0;
@@ -242,34 +270,35 @@ __device__ __forceinline__ void epilogue_cols(const EpiParams& ep, const CUtenso
 #pragma unroll
       for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
     }
+    uint8_t* buf = kAux ? stg + 4096 : stg + (nstore & 1u) * 4096;
+    if constexpr (kAux) {
+      // both buffers: every earlier store must be done reading
+      if (lane == 0) bulk_wait_read0();
+      __syncwarp();
+    }
     if (row_ok) {
 #pragma unroll
-      for (int k = 0; k < CW / 8; ++k)
-        if (gn0 + k * 8 < N) epi_ops8(ep, gm, gn0 + k * 8, v + k * 8);
-    }
-    uint8_t* buf = stg + (nstore & 1u) * 4096;
-    // the store that last read this buffer (two chunks ago) must be done reading
-    if (lane == 0) bulk_wait_read1();
-    __syncwarp();
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      uint4 u;
-      if constexpr (kBF16) {
-        u.x = pack_bf16x2(v[k * 8 + 0], v[k * 8 + 1]);
-        u.y = pack_bf16x2(v[k * 8 + 2], v[k * 8 + 3]);
-        u.z = pack_bf16x2(v[k * 8 + 4], v[k * 8 + 5]);
-        u.w = pack_bf16x2(v[k * 8 + 6], v[k * 8 + 7]);
-      } else {
-        u = make_uint4(__float_as_uint(v[k * 4]), __float_as_uint(v[k * 4 + 1]), __float_as_uint(v[k * 4 + 2]),
-                       __float_as_uint(v[k * 4 + 3]));
+      for (int k = 0; k < CW / 8; ++k) {
+        if (gn0 + k * 8 < N) {
+          epi_pre8(ep, gm, gn0 + k * 8, v + k * 8);
+          if constexpr (kAux) stage8<kBF16>(stg, lane, k, v + k * 8);
+          epi_post8(ep, gm, gn0 + k * 8, v + k * 8, !kAux);
+        }
       }
-      *reinterpret_cast<uint4*>(buf + lane * 128 + ((k ^ r7) << 4)) = u;
     }
+    if constexpr (!kAux) {
+      // the store that last read this buffer (two chunks ago) must be done reading
+      if (lane == 0) bulk_wait_read1();
+      __syncwarp();
+    }
+#pragma unroll
+    for (int k = 0; k < CW / 8; ++k) stage8<kBF16>(buf, lane, k, v + k * 8);
     fence_async_smem();
     __syncwarp();
     if (lane == 0) {
       if (ep.partial) tma_store_3d(tmD, buf, gn0, row0, sp);
       else tma_store_2d(tmD, buf, gn0, row0);
+      if constexpr (kAux) tma_store_2d(tmX, stg, gn0, row0);
       bulk_commit();
     }
     ++nstore;
@@ -279,8 +308,8 @@ __device__ __forceinline__ void epilogue_cols(const EpiParams& ep, const CUtenso
 template <bool kTF32, bool kAMN, bool kBMN, int kBN, bool kPair>
 __global__ void __launch_bounds__(Cfg<kTF32, kAMN, kBMN, kBN, kPair>::kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const __grid_constant__ CUtensorMap tmD, EpiParams ep, int M, int N, int K, int splits,
-                   int group_m, unsigned int* status) {
+                   const __grid_constant__ CUtensorMap tmD, const __grid_constant__ CUtensorMap tmX, EpiParams ep,
+                   int M, int N, int K, int splits, int group_m, unsigned int* status) {
   using C = Cfg<kTF32, kAMN, kBMN, kBN, kPair>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -463,15 +492,40 @@ __global__ void __launch_bounds__(Cfg<kTF32, kAMN, kBMN, kBN, kPair>::kThreads, 
       const int n0 = nb * kBN;
       const int acc = local & 1;
       const uint32_t aphase = (local >> 1) & 1;
+      const int cb = half * (kBN / 2), ce = cb + kBN / 2;
+      {
+        // while the tile's MMAs run, pull this thread's row segment of the
+        // epilogue's global operands (residual, GELU pre-activation, old D)
+        // into L2, so the epilogue's loads do not wait on DRAM
+        const long long gm = m0 + q * 32 + lane;
+        const int c0 = n0 + cb;
+        if (gm < M && c0 < N && !ep.partial) {
+          const uint32_t ncol = static_cast<uint32_t>(min(kBN / 2, N - c0));
+          if (ep.residual) prefetch_l2_bulk(ep.residual + gm * ep.ldr + c0, ncol * 4);
+          if (ep.flags & LLMK_EPI_GELU_BWD) {
+            if (ep.flags & LLMK_EPI_AUX_F32)
+              prefetch_l2_bulk(reinterpret_cast<const float*>(ep.aux) + gm * ep.ldaux + c0, ncol * 4);
+            else
+              prefetch_l2_bulk(ep.aux + gm * ep.ldaux + c0, ncol * 2);
+          }
+          if (ep.flags & LLMK_EPI_ACCUMULATE) {
+            if (ep.d_bf16) prefetch_l2_bulk(static_cast<const __nv_bfloat16*>(ep.D) + gm * ep.ldd + c0, ncol * 2);
+            else prefetch_l2_bulk(static_cast<const float*>(ep.D) + gm * ep.ldd + c0, ncol * 4);
+          }
+        }
+      }
       bool ok = mbar_wait(accf + acc, aphase, status, abort_flag);
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
       const uint32_t tsrc = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * kBN;
-      const int cb = half * (kBN / 2), ce = cb + kBN / 2;
-      if (ep.d_bf16 && !ep.partial)
-        epilogue_cols<true>(ep, &tmD, tsrc, m0 + q * 32, n0, cb, ce, sp, M, N, lane, stg, nstore);
-      else
-        epilogue_cols<false>(ep, &tmD, tsrc, m0 + q * 32, n0, cb, ce, sp, M, N, lane, stg, nstore);
+      const int r0 = m0 + q * 32;
+      if (ep.d_bf16 && !ep.partial) {
+        if (ep.aux_tma) epilogue_cols<true, true>(ep, &tmD, &tmX, tsrc, r0, n0, cb, ce, sp, M, N, lane, stg, nstore);
+        else epilogue_cols<true, false>(ep, &tmD, &tmX, tsrc, r0, n0, cb, ce, sp, M, N, lane, stg, nstore);
+      } else {
+        if (ep.aux_tma) epilogue_cols<false, true>(ep, &tmD, &tmX, tsrc, r0, n0, cb, ce, sp, M, N, lane, stg, nstore);
+        else epilogue_cols<false, false>(ep, &tmD, &tmX, tsrc, r0, n0, cb, ce, sp, M, N, lane, stg, nstore);
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
@@ -578,6 +632,12 @@ int launch_gemm(const void* A, long long lda, const void* B, long long ldb, int 
   } else {
     LLMK_TRY(make_tmap_2d(&td, ep.D, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, N, M, ep.ldd * 4, 32, 32));
   }
+  // GELU pre-activation map (same chunk boxes as D); a copy of D's otherwise
+  CUtensorMap tx = td;
+  if (ep.aux_tma) {
+    if (ep.d_bf16) LLMK_TRY(make_tmap_2d(&tx, ep.aux, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, N, M, ep.ldaux * 2, 64, 32));
+    else LLMK_TRY(make_tmap_2d(&tx, ep.aux, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, N, M, ep.ldaux * 4, 32, 32));
+  }
   const int num_m = (M + C::kMmaM - 1) / C::kMmaM;
   const int num_tiles = num_m * ((N + kBN - 1) / kBN) * splits;
   // raster group (tile rows): one group over all of M when B is large (> 32 MB,
@@ -602,9 +662,9 @@ int launch_gemm(const void* A, long long lda, const void* B, long long ldb, int 
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    LLMK_CUDA(cudaLaunchKernelEx(&cfg, kern, ta, tb, td, ep, M, N, K, splits, group_m, st));
+    LLMK_CUDA(cudaLaunchKernelEx(&cfg, kern, ta, tb, td, tx, ep, M, N, K, splits, group_m, st));
   } else {
-    kern<<<units, C::kThreads, C::SMEM, s>>>(ta, tb, td, ep, M, N, K, splits, group_m, st);
+    kern<<<units, C::kThreads, C::SMEM, s>>>(ta, tb, td, tx, ep, M, N, K, splits, group_m, st);
   }
   count_launch();
   LLMK_CUDA(cudaGetLastError());
@@ -703,6 +763,10 @@ static int gemm_impl(void* D, llmk_dtype d_dtype, long long ldd, const void* A, 
   const size_t need = static_cast<size_t>(splits) * M * N * sizeof(float);
   if (splits > 1 && (!workspace || workspace_bytes < need || !aligned16(workspace))) splits = 1;
   if (splits > 1) ep.partial = static_cast<float*>(workspace);
+  // the pre-activation store rides the TMA path when it has D's element type
+  ep.aux_tma = (ep.flags & LLMK_EPI_GELU) && ep.aux && !ep.partial &&
+               ((ep.flags & LLMK_EPI_AUX_F32) != 0) == (ep.d_bf16 == 0) &&
+               (ep.ldaux * (ep.d_bf16 ? 2 : 4)) % 16 == 0;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int rc = elem == 4 ? dispatch_kind<true>(kind, a_trans, b_trans, A, lda, B, ldb, M, N, K, ep, splits, s)
                            : dispatch_kind<false>(kind, a_trans, b_trans, A, lda, B, ldb, M, N, K, ep, splits, s);

@@ -135,11 +135,15 @@ int ensure_device(llmk_gpt2* g) { return llmk::cuda_check(cudaSetDevice(g->devic
 // Kernel classes of one training step; work is algorithmic FLOPs for the
 // tensor-core classes and algorithmic HBM bytes (each operand read once,
 // each result written once) for the bandwidth classes.
-enum KClass { KC_GEMM = 0, KC_ATTN_FWD, KC_ATTN_BWD, KC_LN_FWD, KC_LN_BWD, KC_XENT, KC_COLSUM, KC_ADAMW, KC_ENCODER,
-              KC_CAST, KC_OTHER, KC_COUNT };
-const char* const kClassName[KC_COUNT] = {"gemm", "attention_fwd", "attention_bwd", "layernorm_fwd", "layernorm_bwd",
-                                          "softmax_xent", "colsum", "adamw", "encoder", "cast", "other"};
-const int kClassUnit[KC_COUNT] = {0, 0, 0, 1, 1, 1, 1, 1, 1, 1, 1};  // 0 flop, 1 byte
+// The GEMM classes split the tensor-core work by form: layer forward, layer
+// input gradient, layer weight gradient, and all three forms of the tied
+// lm_head.
+enum KClass { KC_GEMM_FWD = 0, KC_GEMM_DINP, KC_GEMM_DW, KC_GEMM_LMHEAD, KC_ATTN_FWD, KC_ATTN_BWD, KC_LN_FWD,
+              KC_LN_BWD, KC_XENT, KC_COLSUM, KC_ADAMW, KC_ENCODER, KC_CAST, KC_OTHER, KC_COUNT };
+const char* const kClassName[KC_COUNT] = {"gemm_fwd", "gemm_dinp", "gemm_dweight", "gemm_lm_head", "attention_fwd",
+                                          "attention_bwd", "layernorm_fwd", "layernorm_bwd", "softmax_xent", "colsum",
+                                          "adamw", "encoder", "cast", "other"};
+const int kClassUnit[KC_COUNT] = {0, 0, 0, 0, 0, 0, 1, 1, 1, 1, 1, 1, 1, 1};  // 0 flop, 1 byte
 
 int timing_event(llmk_gpt2* g) {
   if (g->tev_used == g->tev.size()) {
@@ -451,9 +455,9 @@ struct StepOps {
   cudaStream_t s;
   llmk_math mm;
   double ae;  // activation element size
-  int gemm(void* D, llmk_dtype dt, long long ldd, const void* A, int at, long long lda, const void* Bm, int bt,
-           long long ldb, int M, int N, int K, const llmk_epilogue* e, void* w, size_t wb) const {
-    TimedScope ts(g, KC_GEMM, 2.0 * M * N * K);
+  int gemm(int cls, void* D, llmk_dtype dt, long long ldd, const void* A, int at, long long lda, const void* Bm,
+           int bt, long long ldb, int M, int N, int K, const llmk_epilogue* e, void* w, size_t wb) const {
+    TimedScope ts(g, cls, 2.0 * M * N * K);
     return llmk_gemm(D, dt, ldd, A, at, lda, Bm, bt, ldb, mm, M, N, K, e, w, wb, s);
   }
   int ln_fwd(void* out, llmk_dtype dt, float* mean, float* rstd, const float* x, const float* w, const float* b,
@@ -506,7 +510,7 @@ int llmk_gpt2_forward(llmk_gpt2* g, const int* d_inputs, const int* d_targets) {
     LayerActs& a = g->acts[l];
     LLMK_TRY(op.ln_fwd(a.ln1, adt, a.ln1_mean, a.ln1_rstd, x, P + p.ln1w, P + p.ln1b, BT, C));
     llmk_epilogue e1 = epi(P + p.qkvb);
-    LLMK_TRY(op.gemm(a.qkv, adt, 3 * C, a.ln1, 0, C, W(p.qkvw), 0, C, BT, 3 * C, C, &e1, nullptr, 0));
+    LLMK_TRY(op.gemm(KC_GEMM_FWD, a.qkv, adt, 3 * C, a.ln1, 0, C, W(p.qkvw), 0, C, BT, 3 * C, C, &e1, nullptr, 0));
     if (bf) {
       TimedScope ts(g, KC_ATTN_FWD, attn_flop);
       LLMK_TRY(llmk_attention_forward(a.atty, LLMK_BF16, a.lse, a.qkv, B, T, 3 * C, NH, s));
@@ -521,19 +525,19 @@ int llmk_gpt2_forward(llmk_gpt2* g, const int* d_inputs, const int* d_targets) {
       LLMK_TRY(llmk_attention_forward(a.atty, LLMK_F32, a.lse, a.qkv16, B, T, 3 * C, NH, s));
     }
     llmk_epilogue e2 = epi(P + p.attprojb, x, C);  // residual add fused
-    LLMK_TRY(op.gemm(a.res2, LLMK_F32, C, a.atty, 0, C, W(p.attprojw), 0, C, BT, C, C, &e2, nullptr, 0));
+    LLMK_TRY(op.gemm(KC_GEMM_FWD, a.res2, LLMK_F32, C, a.atty, 0, C, W(p.attprojw), 0, C, BT, C, C, &e2, nullptr, 0));
     LLMK_TRY(op.ln_fwd(a.ln2, adt, a.ln2_mean, a.ln2_rstd, a.res2, P + p.ln2w, P + p.ln2b, BT, C));
     // GELU fused, pre-activation kept for the backward
     llmk_epilogue e3 = epi(P + p.fcb, nullptr, 0, a.fch_pre, 4 * C, LLMK_EPI_GELU | aux_f32);
-    LLMK_TRY(op.gemm(a.fch_gelu, adt, 4 * C, a.ln2, 0, C, W(p.fcw), 0, C, BT, 4 * C, C, &e3, nullptr, 0));
+    LLMK_TRY(op.gemm(KC_GEMM_FWD, a.fch_gelu, adt, 4 * C, a.ln2, 0, C, W(p.fcw), 0, C, BT, 4 * C, C, &e3, nullptr, 0));
     llmk_epilogue e4 = epi(P + p.fcprojb, a.res2, C);
-    LLMK_TRY(op.gemm(a.res3, LLMK_F32, C, a.fch_gelu, 0, 4 * C, W(p.fcprojw), 0, 4 * C, BT, C, 4 * C, &e4, nullptr,
+    LLMK_TRY(op.gemm(KC_GEMM_FWD, a.res3, LLMK_F32, C, a.fch_gelu, 0, 4 * C, W(p.fcprojw), 0, 4 * C, BT, C, 4 * C, &e4, nullptr,
                      0));
     x = a.res3;
   }
   LLMK_TRY(op.ln_fwd(g->lnf, adt, g->lnf_mean, g->lnf_rstd, x, P + g->off_lnfw, P + g->off_lnfb, BT, C));
   // tied lm_head (gpt2cuda.cu:323): logits[BT, Vp] = lnf * wte^T, no bias
-  LLMK_TRY(op.gemm(g->logits, adt, Vp, g->lnf, 0, C, W(g->off_wte), 0, C, BT, Vp, C, nullptr, nullptr, 0));
+  LLMK_TRY(op.gemm(KC_GEMM_LMHEAD, g->logits, adt, Vp, g->lnf, 0, C, W(g->off_wte), 0, C, BT, Vp, C, nullptr, nullptr, 0));
   if (g->have_targets) {
     // softmax + cross-entropy + its backward in one pass; dlogits overwrite the
     // logits in place with scale 1/(B*T) (gpt2cuda.cu:398)
@@ -584,8 +588,8 @@ int llmk_gpt2_backward(llmk_gpt2* g) {
     LLMK_TRY(llmk_gpt2_zero_grad(g));
   }
   // lm_head backward (gpt2cuda.cu:402): dlnf = dlogits * wte; dwte = dlogits^T * lnf
-  LLMK_TRY(op.gemm(g->dln, LLMK_F32, C, g->logits, 0, Vp, W(g->off_wte), 1, C, BT, C, Vp, nullptr, nullptr, 0));
-  LLMK_TRY(op.gemm(G + g->off_wte, LLMK_F32, C, g->logits, 1, Vp, g->lnf, 1, C, Vp, C, BT, nullptr, ws, wsb));
+  LLMK_TRY(op.gemm(KC_GEMM_LMHEAD, g->dln, LLMK_F32, C, g->logits, 0, Vp, W(g->off_wte), 1, C, BT, C, Vp, nullptr, nullptr, 0));
+  LLMK_TRY(op.gemm(KC_GEMM_LMHEAD, G + g->off_wte, LLMK_F32, C, g->logits, 1, Vp, g->lnf, 1, C, Vp, C, BT, nullptr, ws, wsb));
   const float* xL = L > 0 ? g->acts[L - 1].res3 : g->encoded;
   // the column sums of the new dres are the last layer's fcproj bias gradient
   LLMK_TRY(op.ln_bwd(g->dres, dres_mirror, G + g->off_lnfw, G + g->off_lnfb, L > 0 ? G + g->lp[L - 1].fcprojb : nullptr,
@@ -597,24 +601,24 @@ int llmk_gpt2_backward(llmk_gpt2* g) {
     const float* x = l > 0 ? g->acts[l - 1].res3 : g->encoded;
     // fcproj: dW = dres^T fch_gelu, dfch = (dres Wfcproj) * gelu'(fch_pre); its bias
     // gradient colsum(dres) came out of the LayerNorm backward that produced dres
-    LLMK_TRY(op.gemm(G + p.fcprojw, LLMK_F32, 4 * C, dres_op, 1, C, a.fch_gelu, 1, 4 * C, C, 4 * C, BT, nullptr, ws,
+    LLMK_TRY(op.gemm(KC_GEMM_DW, G + p.fcprojw, LLMK_F32, 4 * C, dres_op, 1, C, a.fch_gelu, 1, 4 * C, C, 4 * C, BT, nullptr, ws,
                      wsb));
     llmk_epilogue eg = epi(nullptr, nullptr, 0, a.fch_pre, 4 * C, LLMK_EPI_GELU_BWD | aux_f32);
-    LLMK_TRY(op.gemm(g->dfch, adt, 4 * C, dres_op, 0, C, W(p.fcprojw), 1, 4 * C, BT, 4 * C, C, &eg, nullptr, 0));
+    LLMK_TRY(op.gemm(KC_GEMM_DINP, g->dfch, adt, 4 * C, dres_op, 0, C, W(p.fcprojw), 1, 4 * C, BT, 4 * C, C, &eg, nullptr, 0));
     // fc: dW = dfch^T ln2, db = colsum(dfch), dln2 = dfch Wfc
-    LLMK_TRY(op.gemm(G + p.fcw, LLMK_F32, C, g->dfch, 1, 4 * C, a.ln2, 1, C, 4 * C, C, BT, nullptr, ws, wsb));
+    LLMK_TRY(op.gemm(KC_GEMM_DW, G + p.fcw, LLMK_F32, C, g->dfch, 1, 4 * C, a.ln2, 1, C, 4 * C, C, BT, nullptr, ws, wsb));
     {
       TimedScope ts(g, KC_COLSUM, bt_c * 4.0 * g->ae + 16.0 * C);
       LLMK_TRY(llmk_colsum(G + p.fcb, g->dfch, adt, BT, 4 * C, 0, ws, wsb, s));
     }
-    LLMK_TRY(op.gemm(g->dln, LLMK_F32, C, g->dfch, 0, 4 * C, W(p.fcw), 1, C, BT, C, 4 * C, nullptr, nullptr, 0));
+    LLMK_TRY(op.gemm(KC_GEMM_DINP, g->dln, LLMK_F32, C, g->dfch, 0, 4 * C, W(p.fcw), 1, C, BT, C, 4 * C, nullptr, nullptr, 0));
     // ln2: dres += LN2 backward (dres becomes d(res2)); its column sums are the
     // attproj bias gradient
     LLMK_TRY(op.ln_bwd(g->dres, dres_mirror, G + p.ln2w, G + p.ln2b, G + p.attprojb, g->dln, a.res2, P + p.ln2w,
                        a.ln2_mean, a.ln2_rstd, BT, C, LLMK_ACCUM_DINP, ws, wsb));
     // attproj: dW = dres^T atty, datty = dres Wproj
-    LLMK_TRY(op.gemm(G + p.attprojw, LLMK_F32, C, dres_op, 1, C, a.atty, 1, C, C, C, BT, nullptr, ws, wsb));
-    LLMK_TRY(op.gemm(g->datty, adt, C, dres_op, 0, C, W(p.attprojw), 1, C, BT, C, C, nullptr, nullptr, 0));
+    LLMK_TRY(op.gemm(KC_GEMM_DW, G + p.attprojw, LLMK_F32, C, dres_op, 1, C, a.atty, 1, C, C, C, BT, nullptr, ws, wsb));
+    LLMK_TRY(op.gemm(KC_GEMM_DINP, g->datty, adt, C, dres_op, 0, C, W(p.attprojw), 1, C, BT, C, C, nullptr, nullptr, 0));
     // attention
     // (tf32 mode: fp32 dO, O and dqkv; q, k, v from the bf16 copy the forward made)
     {
@@ -623,12 +627,12 @@ int llmk_gpt2_backward(llmk_gpt2* g) {
                                        ws, wsb, s));
     }
     // qkv: dW = dqkv^T ln1, db = colsum(dqkv), dln1 = dqkv Wqkv
-    LLMK_TRY(op.gemm(G + p.qkvw, LLMK_F32, C, g->dqkv, 1, 3 * C, a.ln1, 1, C, 3 * C, C, BT, nullptr, ws, wsb));
+    LLMK_TRY(op.gemm(KC_GEMM_DW, G + p.qkvw, LLMK_F32, C, g->dqkv, 1, 3 * C, a.ln1, 1, C, 3 * C, C, BT, nullptr, ws, wsb));
     {
       TimedScope ts(g, KC_COLSUM, bt_c * 3.0 * g->ae + 12.0 * C);
       LLMK_TRY(llmk_colsum(G + p.qkvb, g->dqkv, adt, BT, 3 * C, 0, ws, wsb, s));
     }
-    LLMK_TRY(op.gemm(g->dln, LLMK_F32, C, g->dqkv, 0, 3 * C, W(p.qkvw), 1, C, BT, C, 3 * C, nullptr, nullptr, 0));
+    LLMK_TRY(op.gemm(KC_GEMM_DINP, g->dln, LLMK_F32, C, g->dqkv, 0, 3 * C, W(p.qkvw), 1, C, BT, C, 3 * C, nullptr, nullptr, 0));
     // ln1: dres += LN1 backward (dres becomes d(layer input)); its column sums are
     // the previous layer's fcproj bias gradient
     LLMK_TRY(op.ln_bwd(g->dres, dres_mirror, G + p.ln1w, G + p.ln1b, l > 0 ? G + g->lp[l - 1].fcprojb : nullptr, g->dln,

@@ -98,6 +98,13 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
+// Asynchronous prefetch of [src, src + bytes) into L2 (16-byte aligned
+// address, bytes a multiple of 16); no completion to wait for.
+__device__ __forceinline__ void prefetch_l2_bulk(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(src)), "r"(bytes)
+               : "memory");
+}
+
 // TMA stores (shared -> global), tracked per issuing thread by bulk groups.
 // Rows / columns outside the tensor map's extent are not written.
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int x, int y) {

@@ -71,6 +71,26 @@ def test_gemm_layer_shapes(cuda_dev, mathname):
     assert llmk.device_status() == 0
 
 
+def test_gemm_weight_gradient_long_k(cuda_dev):
+    """Weight-gradient form with K = 8192 tokens: 256-wide CTA-pair tiles and
+    split-K sized to one wave (the planner's long-K path), bf16 and tf32."""
+    import torch
+    import llmk
+    for math, tol in ((llmk.MATH_BF16, 1e-4), (llmk.MATH_TF32, 2e-3)):
+        for M, N in ((768, 768), (2304, 768), (768, 3072)):
+            K = 8192
+            A, B, ref = _operands(torch, M, N, K, 1, 1, math, cuda_dev, seed=M + N)
+            ws_bytes = llmk.lib().llmk_gemm_workspace(M, N, K, math)
+            assert ws_bytes > 0  # split-K
+            ws = torch.empty(ws_bytes // 4, device=cuda_dev)
+            D = torch.full((M, N), float("nan"), device=cuda_dev)
+            llmk.gemm(D, A, B, a_trans=1, b_trans=1, math=math, M=M, N=N, K=K, workspace=ws)
+            torch.cuda.synchronize()
+            err = max_rel_err(D.cpu(), ref)
+            assert err < tol, (math, M, N, err)
+    assert llmk.device_status() == 0
+
+
 @pytest.mark.parametrize("M", [192, 512])
 def test_gemm_epilogues(cuda_dev, M):
     """bias, residual, GELU (+ pre-activation store), GELU-backward, accumulate, bf16 output
@@ -100,6 +120,12 @@ def test_gemm_epilogues(cuda_dev, M):
     assert max_rel_err(pre.float(), z) < 1e-2
     gelu = torch.nn.functional.gelu(z, approximate="tanh")
     assert max_rel_err(Dg.float(), gelu) < 1e-2
+    # fp32 output with a bf16 pre-activation (stored directly, not by TMA)
+    Df = torch.empty(M, N, device=cuda_dev)
+    pre2 = torch.empty(M, N, device=cuda_dev, dtype=torch.bfloat16)
+    llmk.gemm(Df, A, B, bias=bias, aux=pre2, flags=llmk.EPI_GELU)
+    assert max_rel_err(pre2.float(), z) < 1e-2
+    assert max_rel_err(Df, gelu) < 1e-4
     # GELU backward: D = (A B^T) * gelu'(pre)
     Db = torch.empty(M, N, device=cuda_dev, dtype=torch.bfloat16)
     llmk.gemm(Db, A, B, aux=pre, flags=llmk.EPI_GELU_BWD)

@@ -134,13 +134,15 @@ def test_step_timing_report(cuda_dev):
     L, C, Vp, BT = cfg.num_layers, cfg.channels, cfg.padded_vocab_size, B * T
     per_layer = 2 * BT * C * (3 * C + C + 4 * C + 4 * C)  # forward MACs x 2 of qkv, attproj, fc, fcproj
     flop = 3 * (L * per_layer + 2 * BT * Vp * C)  # forward, dinp, dweight
-    gm = rep["gemm"]
-    assert gm["calls"] == 2 * (3 * 4 * L + 3) and gm["unit"] == "flop"
-    assert abs(gm["work"] - 2 * flop) <= 1e-9 * flop
-    assert gm["ms"] > 0 and gm["launches"] >= gm["calls"]
+    for name, calls in (("gemm_fwd", 4 * L), ("gemm_dinp", 4 * L), ("gemm_dweight", 4 * L), ("gemm_lm_head", 3)):
+        assert rep[name]["calls"] == 2 * calls and rep[name]["unit"] == "flop", name
+        assert rep[name]["ms"] > 0 and rep[name]["launches"] >= rep[name]["calls"], name
+    gemm_work = sum(rep[n]["work"] for n in ("gemm_fwd", "gemm_dinp", "gemm_dweight", "gemm_lm_head"))
+    assert abs(gemm_work - 2 * flop) <= 1e-9 * flop
+    assert abs(rep["gemm_lm_head"]["work"] - 2 * 3 * 2 * BT * Vp * C) <= 1e-9 * flop
     for name in ("attention_fwd", "attention_bwd", "layernorm_fwd", "layernorm_bwd", "adamw", "softmax_xent"):
         assert rep[name]["calls"] > 0 and rep[name]["ms"] > 0, name
     assert rep["attention_fwd"]["calls"] == 2 * L
     m.set_timing(True)
-    assert m.timing_report()["gemm"]["calls"] == 0
+    assert m.timing_report()["gemm_fwd"]["calls"] == 0
     m.close()
