@@ -45,9 +45,11 @@ METRIC = "GPT-2 124M train tokens/sec (B=16/GPU, T=1024)"
 # step at T=1024 would take tens of minutes; T=256 steps take a few seconds
 # each and overstate, not understate, the reference's throughput at T=1024.
 REF_SAMPLE = dict(B=1, T=256)
-# DRAM bytes (read + write) per gemm_tc_kernel launch of one training step,
-# from an ncu capture of the step's launches (profiles/); None until captured.
-GEMM_TRAFFIC_PER_LAUNCH = None
+# DRAM bytes (read + write) per gemm_tc_kernel launch of one training step:
+# an ncu capture of every GEMM shape of the step at BT = 8192 gave 56.8 MB per
+# launch on average; all shapes scale with BT, so 113.5 MB at BT = 16384
+# (profiles/gemm_step_shapes_bt8192_dram.md).
+GEMM_TRAFFIC_PER_LAUNCH = 113.5e6
 
 
 def seeded_init_params(seed: int):

@@ -369,41 +369,49 @@ __device__ __forceinline__ void load8f(const float* p, float* v) {
   v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
 }
 
-// D[b,h,t] = sum_i dO[b,t,h*64+i] * O[b,t,h*64+i]; zeroes dq_acc for the row.
-// With fp32 dO / O (IoT = float) it also writes the bf16 copy of dO the MMA
-// reads (dout16).
+// D[b,h,t] = sum_i dO[b,t,h*64+i] * O[b,t,h*64+i] for every head of row
+// (b,t), and zeroes the row's dq_acc. One warp per row: lane l reads the
+// 16-byte chunks l, l+32, ... of dO and O (8 chunks per head, so each head's
+// sum is a reduction over 8 consecutive lanes). With fp32 dO / O (IoT =
+// float) it also writes the bf16 copy of dO the MMAs read (dout16).
 template <typename IoT>
-__global__ void attn_bwd_pre_kernel(float* __restrict__ D, float* __restrict__ dq_acc,
-                                    __nv_bfloat16* __restrict__ dout16, const IoT* __restrict__ dout,
-                                    const IoT* __restrict__ o, int B, int T, int NH, int C) {
-  const long long idx = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;  // (b, t, h)
-  if (idx >= static_cast<long long>(B) * T * NH) return;
-  const int h = static_cast<int>(idx % NH);
-  const long long bt = idx / NH;
+__global__ void __launch_bounds__(256) attn_bwd_pre_kernel(float* __restrict__ D, float* __restrict__ dq_acc,
+                                                           __nv_bfloat16* __restrict__ dout16,
+                                                           const IoT* __restrict__ dout, const IoT* __restrict__ o,
+                                                           int B, int T, int NH, int C) {
+  const long long bt = blockIdx.x * 8LL + (threadIdx.x >> 5);  // row (b, t)
+  const int lane = threadIdx.x & 31;
+  if (bt >= static_cast<long long>(B) * T) return;
   const int b = static_cast<int>(bt / T), t = static_cast<int>(bt % T);
-  const IoT* pd = dout + bt * C + h * HD;
-  const IoT* po = o + bt * C + h * HD;
-  float s = 0.f;
+  const IoT* pd = dout + bt * C;
+  const IoT* po = o + bt * C;
+  const int nchunk = C / 8;  // 8 per head
+  for (int c0 = 0; c0 < nchunk; c0 += 32) {
+    const int c = c0 + lane;
+    float s = 0.f;
+    if (c < nchunk) {
+      float x[8], y[8];
+      load8f(pd + 8 * c, x);
+      load8f(po + 8 * c, y);
 #pragma unroll
-  for (int k = 0; k < HD / 8; ++k) {
-    float x[8], y[8];
-    load8f(pd + 8 * k, x);
-    load8f(po + 8 * k, y);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) s += x[i] * y[i];
-    if constexpr (sizeof(IoT) == 4) {
-      uint4 u;
-      u.x = pack_bf16x2(x[0], x[1]);
-      u.y = pack_bf16x2(x[2], x[3]);
-      u.z = pack_bf16x2(x[4], x[5]);
-      u.w = pack_bf16x2(x[6], x[7]);
-      *reinterpret_cast<uint4*>(dout16 + bt * C + h * HD + 8 * k) = u;
+      for (int i = 0; i < 8; ++i) s += x[i] * y[i];
+      if constexpr (sizeof(IoT) == 4) {
+        uint4 u;
+        u.x = pack_bf16x2(x[0], x[1]);
+        u.y = pack_bf16x2(x[2], x[3]);
+        u.z = pack_bf16x2(x[4], x[5]);
+        u.w = pack_bf16x2(x[6], x[7]);
+        *reinterpret_cast<uint4*>(dout16 + bt * C + 8 * c) = u;
+      }
     }
+    // the 8 lanes of a head: fixed-order butterfly
+    s += __shfl_xor_sync(0xffffffffu, s, 1);
+    s += __shfl_xor_sync(0xffffffffu, s, 2);
+    s += __shfl_xor_sync(0xffffffffu, s, 4);
+    if (c < nchunk && (c & 7) == 0) D[(static_cast<long long>(b) * NH + c / 8) * T + t] = s;
   }
-  D[(static_cast<long long>(b) * NH + h) * T + t] = s;
-  float4* z = reinterpret_cast<float4*>(dq_acc + bt * C + h * HD);
-#pragma unroll
-  for (int k = 0; k < HD / 4; ++k) z[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+  float4* z = reinterpret_cast<float4*>(dq_acc + bt * C);
+  for (int k = lane; k < C / 4; k += 32) z[k] = make_float4(0.f, 0.f, 0.f, 0.f);
 }
 
 // dqkv[:, :, 0:C] = dq_acc * scale (bf16 or fp32)
@@ -940,12 +948,13 @@ int llmk_attention_backward(void* dqkv, const void* dout, const void* out, llmk_
   float* dq = reinterpret_cast<float*>(static_cast<char*>(workspace) + dq_off);
   __nv_bfloat16* do16 = reinterpret_cast<__nv_bfloat16*>(static_cast<char*>(workspace) + do16_off);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const long long rows = static_cast<long long>(B) * T * NH;
+  const long long rows = static_cast<long long>(B) * T;  // one warp per (b, t)
+  const int pre_grid = static_cast<int>((rows + 7) / 8);
   if (f32)
-    attn_bwd_pre_kernel<float><<<static_cast<int>((rows + 127) / 128), 128, 0, s>>>(
-        Dv, dq, do16, static_cast<const float*>(dout), static_cast<const float*>(out), B, T, NH, C);
+    attn_bwd_pre_kernel<float><<<pre_grid, 256, 0, s>>>(Dv, dq, do16, static_cast<const float*>(dout),
+                                                        static_cast<const float*>(out), B, T, NH, C);
   else
-    attn_bwd_pre_kernel<__nv_bfloat16><<<static_cast<int>((rows + 127) / 128), 128, 0, s>>>(
+    attn_bwd_pre_kernel<__nv_bfloat16><<<pre_grid, 256, 0, s>>>(
         Dv, dq, nullptr, static_cast<const __nv_bfloat16*>(dout), static_cast<const __nv_bfloat16*>(out), B, T, NH, C);
   // the MMAs read dO as bf16: the caller's buffer, or the copy the pre-pass made
   const void* dout_mma = f32 ? static_cast<const void*>(do16) : dout;

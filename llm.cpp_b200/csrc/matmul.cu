@@ -66,14 +66,23 @@ __global__ void __launch_bounds__(256) colsum_partial_kernel(const void* __restr
   if (n < N) partial[static_cast<long long>(blockIdx.y) * N + n] = s;
 }
 
-// Pass 2: out[n] (+)= sum over chunks, fixed order.
+// Pass 2: out[n] (+)= sum over chunks in a fixed order: block (32 columns x
+// 8 chunk lanes), lane y sums chunks y, y+8, ..., then the 8 lane sums are
+// added in order.
 __global__ void colsum_final_kernel(const float* __restrict__ partial, float* __restrict__ out, int N, int chunks,
                                     int accumulate) {
-  const int n = blockIdx.x * blockDim.x + threadIdx.x;
-  if (n >= N) return;
+  __shared__ float red[8][33];
+  const int n = blockIdx.x * 32 + threadIdx.x;
   float s = 0.f;
-  for (int c = 0; c < chunks; ++c) s += partial[static_cast<long long>(c) * N + n];
-  out[n] = accumulate ? out[n] + s : s;
+  if (n < N)
+    for (int c = threadIdx.y; c < chunks; c += 8) s += partial[static_cast<long long>(c) * N + n];
+  red[threadIdx.y][threadIdx.x] = s;
+  __syncthreads();
+  if (threadIdx.y != 0 || n >= N) return;
+  float t = 0.f;
+#pragma unroll
+  for (int y = 0; y < 8; ++y) t += red[y][threadIdx.x];
+  out[n] = accumulate ? out[n] + t : t;
 }
 
 int colsum_chunks(int M, int N) {
@@ -96,7 +105,7 @@ int colsum_launch(float* out, const void* x, bool bf16, int M, int N, int accumu
   dim3 block(32, kRowLanes);
   if (bf16) colsum_partial_kernel<true><<<grid, block, 0, s>>>(x, partial, M, N, rows_per_chunk);
   else colsum_partial_kernel<false><<<grid, block, 0, s>>>(x, partial, M, N, rows_per_chunk);
-  colsum_final_kernel<<<(N + 255) / 256, 256, 0, s>>>(partial, out, N, chunks, accumulate);
+  colsum_final_kernel<<<(N + 31) / 32, dim3(32, 8), 0, s>>>(partial, out, N, chunks, accumulate);
   count_launch(2);
   LLMK_CUDA(cudaGetLastError());
   return LLMK_OK;

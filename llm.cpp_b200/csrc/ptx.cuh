@@ -153,9 +153,11 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(d) : "r"(saddr), "r"(rank));
   return d;
 }
-// Arrive on an mbarrier of any CTA of the cluster (shared::cluster address).
+// Arrive on an mbarrier of any CTA of the cluster (shared::cluster address;
+// default .release.cta semantics: it publishes tcgen05 completion ordered by
+// tcgen05.fence::before_thread_sync, not generic memory writes).
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 // TMA tile load into this CTA's shared memory whose completion (bytes) is
 // counted on an mbarrier of either CTA of the pair (shared::cluster address):

@@ -4,6 +4,11 @@
     python llm.cpp_b200/profile_case.py attn    [B T NH] [--reps R]
     python llm.cpp_b200/profile_case.py attnbwd [B T NH] [--reps R]
     python llm.cpp_b200/profile_case.py step    [B T]    [--reps R]
+    python llm.cpp_b200/profile_case.py gemmset [BT]     [--reps R]
+
+gemmset runs each GEMM shape of one GPT-2 124M training step at BT tokens
+(fwd / dinp / dweight of QKV, attproj, FC, FCproj and the tied lm_head, in
+that order, bf16) once per rep, for per-shape ncu counters.
 
 Each case allocates its inputs once, runs one warm-up launch and R timed
 launches, prints the CUDA-event time per launch, and exits 0. Sizes default
@@ -22,7 +27,7 @@ sys.path.insert(0, HERE)
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["gemm", "attn", "attnbwd", "step"])
+    ap.add_argument("case", choices=["gemm", "attn", "attnbwd", "step", "gemmset"])
     ap.add_argument("dims", nargs="*", type=int)
     ap.add_argument("--trans", nargs=2, type=int, default=[0, 0])
     ap.add_argument("--reps", type=int, default=3)
@@ -70,6 +75,25 @@ def main() -> None:
                                 qkv.data_ptr(), lse.data_ptr(), Bb, T, 3 * C, NH, ws.data_ptr(), wsb, s)
         # S = QK^T, dP = dO V^T, dV += P^T dO, dK += dS^T Q, dQ += dS K over the causal half
         flop = 10.0 * Bb * NH * 64 * T * (T + 1) / 2
+    elif a.case == "gemmset":
+        BT = (a.dims + [16384])[0]
+        C, Vp = 768, 50304
+        shapes = []
+        for IC, OC in [(C, 3 * C), (C, C), (C, 4 * C), (4 * C, C)]:
+            shapes += [(BT, OC, IC, 0, 0), (BT, IC, OC, 0, 1), (OC, IC, BT, 1, 1)]
+        shapes += [(BT, Vp, C, 0, 0), (BT, C, Vp, 0, 1), (Vp, C, BT, 1, 1)]
+        bufs = []
+        for (M, N, K, at, bt) in shapes:
+            A = torch.randn((K, M) if at else (M, K), device=dev).bfloat16()
+            B = torch.randn((K, N) if bt else (N, K), device=dev).bfloat16()
+            D = torch.empty(M, N, device=dev, dtype=torch.float32 if at else torch.bfloat16)
+            wsb = llmk.lib().llmk_gemm_workspace(M, N, K, llmk.MATH_BF16)
+            bufs.append((A, B, D, torch.empty(max(wsb // 4, 1), device=dev), M, N, K, at, bt))
+
+        def run():
+            for (A, B, D, ws, M, N, K, at, bt) in bufs:
+                llmk.gemm(D, A, B, a_trans=at, b_trans=bt, M=M, N=N, K=K, workspace=ws)
+        flop = sum(2.0 * M * N * K for (_, _, _, _, M, N, K, _, _) in bufs)
     else:
         Bb, T = (a.dims + [16, 1024][len(a.dims):])[:2]
         m = llmk.GPT2(Bb, T)
