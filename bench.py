@@ -8,7 +8,8 @@ bf16 GEMMs and attention with fp32 master weights and AdamW (lr 3e-4,
 betas 0.9/0.999, eps 1e-8, wd 0), seeded initialisation, synthetic uniform
 tokens seeded per rank (1337 + rank). One step = forward + backward (with
 the per-layer NCCL gradient all-reduce when N > 1) + AdamW, all on the native
-trainer of libllmk.so (include/llmk_gpt2.h).
+trainer of libllmk.so (include/llmk_gpt2.h), replayed as one captured CUDA
+graph per step (llmk_gpt2_use_graph).
 
 value: tokens/s of the whole job with tokens already resident in HBM,
 timed with CUDA events on the trainer's stream over exactly K steps between
@@ -268,6 +269,8 @@ def main() -> None:
     inp_h, tgt_h = toks[:-1].copy(), toks[1:].copy()
     model.train_step(inp_h, tgt_h, 0.0, t=1, want_loss=False)  # tokens now resident in the model's buffers
     d_in, d_tg = model.buffers()
+    # every later step replays one captured CUDA graph of forward + backward + AdamW
+    model.use_graph(True)
     stream = torch.cuda.ExternalStream(model.stream)
 
     def barrier():

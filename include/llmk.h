@@ -235,6 +235,17 @@ int llmk_mean(float* out, const float* x, int n, void* stream);
 int llmk_adamw(float* params, void* params_bf16, const float* grads, float* m, float* v, long long n, float lr,
                float beta1, float beta2, float eps, float weight_decay, int t, float grad_scale, void* stream);
 
+/* AdamW reading its hyperparameters from device memory: hparams = 8 floats
+ * {lr, beta1, beta2, eps, weight_decay, 1/(1-beta1^t), 1/(1-beta2^t),
+ * grad_scale} (16-byte aligned), filled on the host by llmk_adamw_hparams.
+ * The reference has no counterpart (its AdamW takes host scalars,
+ * gpt2/cuda/adamw.cu:33-44); this form lets a captured CUDA graph replay the
+ * update with per-step values (llmk_gpt2_use_graph). */
+void llmk_adamw_hparams(float* out8, float lr, float beta1, float beta2, float eps, float weight_decay, int t,
+                        float grad_scale);
+int llmk_adamw_device_hparams(float* params, void* params_bf16, const float* grads, float* m, float* v, long long n,
+                              const float* hparams, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -100,6 +100,14 @@ int llmk_gpt2_broadcast_parameters(llmk_gpt2* model, int root);
  * communicator and returns LLMK_ERR_NCCL / LLMK_ERR_DEVICE_TIMEOUT. */
 int llmk_gpt2_synchronize(llmk_gpt2* model, int timeout_ms);
 
+/* CUDA-graph mode (enable != 0): llmk_gpt2_step_device (and so
+ * llmk_gpt2_train_step) captures forward + backward + AdamW once into a CUDA
+ * graph and then replays it, with the per-step AdamW values copied to device
+ * memory before each replay; a call with other device token buffers captures
+ * again. The reference launches every kernel each step
+ * (gpt2/cuda/gpt2cuda.cu:304-459). Steps run eagerly while step timing is on. */
+int llmk_gpt2_use_graph(llmk_gpt2* model, int enable);
+
 /* ------------------------------------------------------- step timing */
 /* Per-kernel-class device time of the training step. The reference has no
  * counterpart (its trainers time whole steps only, gpt2/traincuda.cpp). While

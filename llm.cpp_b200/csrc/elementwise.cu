@@ -528,10 +528,18 @@ __global__ void mean_kernel(float* __restrict__ out, const float* __restrict__ x
 // ------------------------------------------------------------ AdamW
 // p -= lr * (mhat / (sqrt(vhat) + eps) + wd * p) (gpt2/cuda/adamw.cu:18-30);
 // g is scaled by grad_scale on the fly (1/world for data-parallel averaging);
-// p_bf16 (optional) receives the updated parameters rounded to bf16.
+// p_bf16 (optional) receives the updated parameters rounded to bf16. The
+// hyperparameters come as kernel arguments, or (hp_dev != nullptr) from
+// device memory, so a captured CUDA graph replays with per-step values.
+struct AdamHP {
+  float lr, b1, b2, eps, wd, inv_c1, inv_c2, grad_scale;
+};
 __global__ void adamw_kernel(float* __restrict__ p, __nv_bfloat16* __restrict__ p_bf16, const float* __restrict__ g,
-                             float* __restrict__ m, float* __restrict__ v, long long n4, float lr, float b1, float b2,
-                             float eps, float wd, float inv_c1, float inv_c2, float grad_scale) {
+                             float* __restrict__ m, float* __restrict__ v, long long n4, AdamHP hp_arg,
+                             const AdamHP* __restrict__ hp_dev) {
+  const AdamHP hp = hp_dev ? *hp_dev : hp_arg;
+  const float lr = hp.lr, b1 = hp.b1, b2 = hp.b2, eps = hp.eps, wd = hp.wd, inv_c1 = hp.inv_c1, inv_c2 = hp.inv_c2,
+              grad_scale = hp.grad_scale;
   for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n4;
        i += static_cast<long long>(gridDim.x) * blockDim.x) {
     float4 pp = ld4(p + 4 * i), gg = ld4(g + 4 * i), mm = ld4(m + 4 * i), vv = ld4(v + 4 * i);
@@ -828,9 +836,35 @@ int llmk_adamw(float* params, void* params_bf16, const float* grads, float* m, f
   // bias corrections in double on the host, as gpt2/cuda/adamw.cu:38-40
   const float inv_c1 = static_cast<float>(1.0 / (1.0 - std::pow(static_cast<double>(beta1), t)));
   const float inv_c2 = static_cast<float>(1.0 / (1.0 - std::pow(static_cast<double>(beta2), t)));
+  const AdamHP hp{lr, beta1, beta2, eps, weight_decay, inv_c1, inv_c2, grad_scale};
   adamw_kernel<<<grid_for(n / 4, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      params, static_cast<__nv_bfloat16*>(params_bf16), grads, m, v, n / 4, lr, beta1, beta2, eps, weight_decay,
-      inv_c1, inv_c2, grad_scale);
+      params, static_cast<__nv_bfloat16*>(params_bf16), grads, m, v, n / 4, hp, nullptr);
+  count_launch();
+  LLMK_CUDA(cudaGetLastError());
+  return LLMK_OK;
+}
+
+void llmk_adamw_hparams(float* out8, float lr, float beta1, float beta2, float eps, float weight_decay, int t,
+                        float grad_scale) {
+  if (!out8) return;
+  out8[0] = lr;
+  out8[1] = beta1;
+  out8[2] = beta2;
+  out8[3] = eps;
+  out8[4] = weight_decay;
+  out8[5] = static_cast<float>(1.0 / (1.0 - std::pow(static_cast<double>(beta1), t > 0 ? t : 1)));
+  out8[6] = static_cast<float>(1.0 / (1.0 - std::pow(static_cast<double>(beta2), t > 0 ? t : 1)));
+  out8[7] = grad_scale;
+}
+
+int llmk_adamw_device_hparams(float* params, void* params_bf16, const float* grads, float* m, float* v, long long n,
+                              const float* hparams, void* stream) {
+  if (!params || !grads || !m || !v || n < 0 || !hparams) return fail(LLMK_ERR_INVALID_ARG, "adamw_device_hparams");
+  if (n % 4 || !a16(params) || !a16(params_bf16) || !a16(grads) || !a16(m) || !a16(v) || !a16(hparams))
+    return fail(LLMK_ERR_UNSUPPORTED, "adamw_device_hparams: n % 4 == 0 and 16-byte alignment required");
+  adamw_kernel<<<grid_for(n / 4, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      params, static_cast<__nv_bfloat16*>(params_bf16), grads, m, v, n / 4, AdamHP{},
+      reinterpret_cast<const AdamHP*>(hparams));
   count_launch();
   LLMK_CUDA(cudaGetLastError());
   return LLMK_OK;

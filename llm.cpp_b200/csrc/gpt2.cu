@@ -125,6 +125,12 @@ struct llmk_gpt2 {
   std::vector<cudaEvent_t> tev;
   size_t tev_used = 0;
   std::vector<Mark> marks;
+  // CUDA-graph mode (llmk_gpt2_use_graph)
+  bool use_graph = false;
+  cudaGraphExec_t graph_exec = nullptr;
+  const int *graph_in = nullptr, *graph_tg = nullptr;
+  unsigned long long graph_launches = 0;  // kernels one replay runs
+  float* hp_dev = nullptr;  // AdamW hyperparameters read by the captured update
 };
 
 namespace {
@@ -267,6 +273,8 @@ void free_all(llmk_gpt2* g) {
   if (g->comm_done) cudaEventDestroy(g->comm_done);
   if (g->h2d_done) cudaEventDestroy(g->h2d_done);
   for (auto e : g->tev) cudaEventDestroy(e);
+  if (g->graph_exec) cudaGraphExecDestroy(g->graph_exec);
+  f(g->hp_dev);
   if (g->comm) ncclCommDestroy(g->comm);
   if (g->comm_stream) cudaStreamDestroy(g->comm_stream);
   if (g->own_stream && g->stream) cudaStreamDestroy(g->stream);
@@ -308,6 +316,7 @@ int alloc_all(llmk_gpt2* g) {
   if (bf) LLMK_TRY(dalloc(&g->dres_bf16, BT * C));
   LLMK_TRY(aalloc(&g->datty, BT * C)); LLMK_TRY(aalloc(&g->dqkv, BT * 3 * C)); LLMK_TRY(aalloc(&g->dfch, BT * 4 * C));
   LLMK_TRY(dalloc(&g->inputs, BT)); LLMK_TRY(dalloc(&g->targets, BT));
+  LLMK_TRY(dalloc(&g->hp_dev, 8));
   LLMK_CUDA(cudaMallocHost(reinterpret_cast<void**>(&g->h_inputs), BT * sizeof(int)));
   LLMK_CUDA(cudaMallocHost(reinterpret_cast<void**>(&g->h_targets), BT * sizeof(int)));
   LLMK_CUDA(cudaMallocHost(reinterpret_cast<void**>(&g->h_loss), sizeof(float)));
@@ -657,6 +666,15 @@ int llmk_gpt2_backward(llmk_gpt2* g) {
   return LLMK_OK;
 }
 
+// AdamW over the flat buffer with its hyperparameters read from g->hp_dev
+// (the form a captured graph replays).
+static int update_device_hparams(llmk_gpt2* g) {
+  TimedScope ts(g, KC_ADAMW, static_cast<double>(g->nparams) * (28.0 + (g->params_bf16 ? 2.0 : 0.0)));
+  LLMK_TRY(llmk_adamw_device_hparams(g->params, g->params_bf16, g->grads, g->m, g->v,
+                                     static_cast<long long>(g->nparams), g->hp_dev, g->stream));
+  return LLMK_OK;
+}
+
 int llmk_gpt2_update(llmk_gpt2* g, float lr, float beta1, float beta2, float eps, float weight_decay, int t) {
   if (!g || t < 1) return fail(LLMK_ERR_INVALID_ARG, "gpt2_update");
   // one multi-tensor launch over the flat buffer (the reference launches one
@@ -702,9 +720,58 @@ int llmk_gpt2_device_loss(llmk_gpt2* g, const float** d_loss) {
 
 int llmk_gpt2_step_device(llmk_gpt2* g, const int* d_inputs, const int* d_targets, float lr, float beta1, float beta2,
                           float eps, float weight_decay, int t) {
-  LLMK_TRY(llmk_gpt2_forward(g, d_inputs, d_targets));
-  LLMK_TRY(llmk_gpt2_backward(g));
-  return llmk_gpt2_update(g, lr, beta1, beta2, eps, weight_decay, t);
+  if (!g || !d_inputs || !d_targets || t < 1) return fail(LLMK_ERR_INVALID_ARG, "gpt2_step_device");
+  if (!g->use_graph || g->timing) {
+    LLMK_TRY(llmk_gpt2_forward(g, d_inputs, d_targets));
+    LLMK_TRY(llmk_gpt2_backward(g));
+    return llmk_gpt2_update(g, lr, beta1, beta2, eps, weight_decay, t);
+  }
+  // this step's AdamW values, copied from pageable memory (staged before the
+  // call returns), ahead of the replay on the same stream
+  float hp[8];
+  llmk_adamw_hparams(hp, lr, beta1, beta2, eps, weight_decay, t, 1.0f / static_cast<float>(g->world));
+  LLMK_CUDA(cudaMemcpyAsync(g->hp_dev, hp, sizeof(hp), cudaMemcpyHostToDevice, g->stream));
+  if (!g->graph_exec || d_inputs != g->graph_in || d_targets != g->graph_tg) {
+    if (g->graph_exec) {
+      cudaGraphExecDestroy(g->graph_exec);
+      g->graph_exec = nullptr;
+    }
+    const unsigned long long n0 = llmk_launch_count();
+    LLMK_CUDA(cudaStreamBeginCapture(g->stream, cudaStreamCaptureModeThreadLocal));
+    int rc = llmk_gpt2_forward(g, d_inputs, d_targets);
+    if (rc == LLMK_OK) rc = llmk_gpt2_backward(g);
+    if (rc == LLMK_OK) rc = update_device_hparams(g);
+    cudaGraph_t graph = nullptr;
+    const cudaError_t ec = cudaStreamEndCapture(g->stream, &graph);  // always leave capture mode
+    if (rc != LLMK_OK) {
+      if (graph) cudaGraphDestroy(graph);
+      return rc;
+    }
+    LLMK_CUDA(ec);
+    const cudaError_t ei = cudaGraphInstantiate(&g->graph_exec, graph, 0);
+    cudaGraphDestroy(graph);
+    LLMK_CUDA(ei);
+    g->graph_in = d_inputs;
+    g->graph_tg = d_targets;
+    // the captured launches run at each replay, not at capture time
+    g->graph_launches = llmk_launch_count() - n0;
+    llmk::count_launch(0ull - g->graph_launches);
+  }
+  LLMK_CUDA(cudaGraphLaunch(g->graph_exec, g->stream));
+  llmk::count_launch(g->graph_launches);
+  ++g->steps;
+  return LLMK_OK;
+}
+
+int llmk_gpt2_use_graph(llmk_gpt2* g, int enable) {
+  if (!g) return fail(LLMK_ERR_INVALID_ARG, "gpt2_use_graph");
+  g->use_graph = enable != 0;
+  if (!g->use_graph && g->graph_exec) {
+    LLMK_CUDA(cudaStreamSynchronize(g->stream));
+    cudaGraphExecDestroy(g->graph_exec);
+    g->graph_exec = nullptr;
+  }
+  return LLMK_OK;
 }
 
 int llmk_gpt2_train_step(llmk_gpt2* g, const int* host_inputs, const int* host_targets, float lr, float beta1,

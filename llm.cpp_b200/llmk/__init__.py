@@ -80,6 +80,8 @@ SIGNATURES: dict[str, tuple] = {
     "llmk_softmax_crossentropy": (i32, [vp, vp, vp, i32, vp, i32, i32, i32, f32, vp]),
     "llmk_mean": (i32, [vp, vp, i32, vp]),
     "llmk_adamw": (i32, [vp, vp, vp, vp, vp, i64, f32, f32, f32, f32, f32, i32, f32, vp]),
+    "llmk_adamw_hparams": (None, [C.POINTER(f32), f32, f32, f32, f32, f32, i32, f32]),
+    "llmk_adamw_device_hparams": (i32, [vp, vp, vp, vp, vp, i64, vp, vp]),
     # model (include/llmk_gpt2.h)
     "llmk_gpt2_num_parameters": (sz, [C.POINTER(GPT2Config)]),
     "llmk_gpt2_parameter_count": (sz, [vp]),
@@ -106,6 +108,7 @@ SIGNATURES: dict[str, tuple] = {
     "llmk_gpt2_broadcast_parameters": (i32, [vp, i32]),
     "llmk_gpt2_synchronize": (i32, [vp, i32]),
     "llmk_gpt2_set_timing": (i32, [vp, i32]),
+    "llmk_gpt2_use_graph": (i32, [vp, i32]),
     "llmk_gpt2_timing_report": (i32, [vp, C.POINTER(KernelStat), i32, C.POINTER(i32)]),
 }
 
@@ -260,6 +263,10 @@ class GPT2:
 
     def synchronize(self, timeout_ms=0):
         call("llmk_gpt2_synchronize", self.h, timeout_ms)
+
+    def use_graph(self, enable: bool):
+        """Run step_device / train_step as replays of one captured CUDA graph."""
+        call("llmk_gpt2_use_graph", self.h, 1 if enable else 0)
 
     def set_timing(self, enable: bool):
         """Per-kernel-class event timing of later steps (clears old records)."""

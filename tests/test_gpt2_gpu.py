@@ -146,3 +146,30 @@ def test_step_timing_report(cuda_dev):
     m.set_timing(True)
     assert m.timing_report()["gemm_fwd"]["calls"] == 0
     m.close()
+
+
+@pytest.mark.parametrize("mathname", ["bf16", "tf32"])
+def test_graph_steps_match_eager(cuda_dev, mathname):
+    """CUDA-graph mode: captured steps (the AdamW step count and learning rate
+    changing per replay) give the eager steps' losses and parameters."""
+    import llmk
+    math = llmk.MATH_TF32 if mathname == "tf32" else llmk.MATH_BF16
+    cfg = O.config(max_seq_len=128, vocab_size=1000, padded_vocab_size=1024, num_layers=2, num_heads=2, channels=128)
+    B, T = 2, 128
+    params = O.init_params(cfg, 13)
+    toks = O.tokens(4 * B * T + 1, cfg.vocab_size, 13)
+    runs = []
+    for graph in (False, True):
+        m = _model(llmk, cfg, B, T, math)
+        m.load_parameters(params)
+        m.use_graph(graph)
+        losses = []
+        for step in range(4):
+            c = toks[step * B * T:(step + 1) * B * T + 1]
+            losses.append(m.train_step(c[:-1], c[1:], 1e-3 * (step + 1), t=step + 1))
+        runs.append((np.array(losses), m.read_parameters()))
+        m.close()
+    (l0, p0), (l1, p1) = runs
+    assert np.allclose(l0, l1, rtol=1e-5, atol=0), (l0, l1)
+    assert np.abs(p1 - p0).max() / np.abs(p0).max() < 1e-4
+    assert llmk.device_status() == 0

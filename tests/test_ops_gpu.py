@@ -306,11 +306,20 @@ def test_adamw_vs_oracle(cuda_dev):
     m = torch.zeros(n, device=cuda_dev)
     v = torch.zeros(n, device=cuda_dev)
     po, mo, vo = p0.copy(), np.zeros(n, np.float32), np.zeros(n, np.float32)
+    import ctypes
+    hp = torch.empty(8, device=cuda_dev)
     for t in range(1, 6):
         g = O.normal((n,), 60 + t)
         gd = T(g, cuda_dev)
-        llmk.call("llmk_adamw", p.data_ptr(), pb.data_ptr(), gd.data_ptr(), m.data_ptr(), v.data_ptr(), n, 3e-4, 0.9,
-                  0.999, 1e-8, 0.01, t, 1.0, s)
+        if t % 2:
+            llmk.call("llmk_adamw", p.data_ptr(), pb.data_ptr(), gd.data_ptr(), m.data_ptr(), v.data_ptr(), n, 3e-4,
+                      0.9, 0.999, 1e-8, 0.01, t, 1.0, s)
+        else:  # the same update with the hyperparameters read from device memory
+            h8 = (ctypes.c_float * 8)()
+            llmk.lib().llmk_adamw_hparams(h8, 3e-4, 0.9, 0.999, 1e-8, 0.01, t, 1.0)
+            hp.copy_(torch.tensor(list(h8), dtype=torch.float32))
+            llmk.call("llmk_adamw_device_hparams", p.data_ptr(), pb.data_ptr(), gd.data_ptr(), m.data_ptr(),
+                      v.data_ptr(), n, hp.data_ptr(), s)
         O.orc().orc_adamw(po, g, mo, vo, n, 3e-4, 0.9, 0.999, 1e-8, 0.01, t)
     torch.cuda.synchronize()
     assert max_rel_err(p.cpu(), torch.from_numpy(po)) < 1e-5
