@@ -110,6 +110,14 @@ SIGNATURES: dict[str, tuple] = {
     "llmk_gpt2_set_timing": (i32, [vp, i32]),
     "llmk_gpt2_use_graph": (i32, [vp, i32]),
     "llmk_gpt2_timing_report": (i32, [vp, C.POINTER(KernelStat), i32, C.POINTER(i32)]),
+    # include/llmk_data.h
+    "llmk_loader_create": (i32, [C.POINTER(vp), C.c_char_p, i32, i32, i32, i32, i32]),
+    "llmk_loader_destroy": (i32, [vp]),
+    "llmk_loader_next": (i32, [vp, vp, vp]),
+    "llmk_loader_reset": (i32, [vp]),
+    "llmk_loader_resume": (i32, [vp, sz, sz]),
+    "llmk_loader_position": (i32, [vp, C.POINTER(sz), C.POINTER(sz)]),
+    "llmk_loader_num_tokens": (i64, [vp]),
 }
 
 _lib = None
@@ -285,6 +293,49 @@ class GPT2:
     def close(self):
         if getattr(self, "h", None):
             lib().llmk_gpt2_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class DataLoader:
+    """Token-shard loader (include/llmk_data.h) with the reference
+    DataLoader's constructor arguments and batch order (utils/dataloader.h)."""
+
+    def __init__(self, path: str, B: int, T: int, rank: int = 0, world: int = 1, shuffle: bool = False):
+        import numpy as np
+        self.B, self.T = B, T
+        h = C.c_void_p()
+        call("llmk_loader_create", C.byref(h), os.fsencode(path), B, T, rank, world, 1 if shuffle else 0)
+        self.h = h
+        self.num_tokens = lib().llmk_loader_num_tokens(self.h)
+        self.inputs = np.empty((B, T), np.int32)
+        self.targets = np.empty((B, T), np.int32)
+
+    def next_batch(self):
+        """Fills and returns (inputs, targets), int32 arrays of shape (B, T)
+        owned by the loader (overwritten by the next call)."""
+        call("llmk_loader_next", self.h, self.inputs.ctypes.data, self.targets.ctypes.data)
+        return self.inputs, self.targets
+
+    def reset(self):
+        call("llmk_loader_reset", self.h)
+
+    def resume(self, shard_idx: int, sample_idx: int):
+        call("llmk_loader_resume", self.h, shard_idx, sample_idx)
+
+    def position(self) -> tuple[int, int]:
+        a, b = C.c_size_t(0), C.c_size_t(0)
+        call("llmk_loader_position", self.h, C.byref(a), C.byref(b))
+        return a.value, b.value
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().llmk_loader_destroy(self.h)
             self.h = None
 
     def __del__(self):

@@ -72,6 +72,12 @@ _REF_SIGS = {
     "ref_gelu_forward": (None, [fp, fp, i32, i32, i32]),
     "ref_gelu_backward": (None, [fp, fp, fp, i32, i32, i32]),
     "ref_gpt2_train": (i32, [C.c_char_p, i32, i32, ip, ip, i32, f32, fp, np.ctypeslib.ndpointer(dtype=np.float64)]),
+    "ref_loader_create": (vp, [C.c_char_p, i32, i32, i32, i32, i32]),
+    "ref_loader_destroy": (None, [vp]),
+    "ref_loader_next": (None, [vp, ip, ip]),
+    "ref_loader_reset": (None, [vp]),
+    "ref_loader_resume": (None, [vp, sz, sz]),
+    "ref_loader_num_tokens": (C.c_longlong, [vp]),
 }
 
 

@@ -2,8 +2,8 @@
 //
 // TEST INFRASTRUCTURE ONLY. oracle/Makefile compiles the reference sources
 // gpt2/{matmul,attention,layernorm,gelu,residual,softmax,cross_entropy,
-// encoder,adamw,global,layer,gpt2}.cpp where they lie (read-only) together
-// with this file into oracle/_ref/libref.so. Tests use it to pin the C
+// encoder,adamw,global,layer,gpt2}.cpp and utils/dataloader.cpp where they lie
+// (read-only) together with this file into oracle/_ref/libref.so. Tests use it to pin the C
 // restatement (oracle.c) and tests/golden/make_fixtures.py uses it to record
 // the reference's 20-step loss trajectory; bench.py's reference arm times
 // its training step. Buffers cross this boundary row-major; the reference's
@@ -13,6 +13,7 @@
 #include <vector>
 
 #include "attention.h"
+#include "dataloader.h"
 #include "gelu.h"
 #include "global.h"
 #include "gpt2.h"
@@ -134,5 +135,17 @@ int ref_gpt2_train(const char* checkpoint, int B, int T, const int* inputs, cons
   }
   return 0;
 }
+
+// DataLoader (utils/dataloader.cpp) behind opaque handles. The reference
+// exit()s on a bad shard, so callers pass only well-formed shard files.
+void* ref_loader_create(const char* path, int B, int T, int rank, int world, int shuffle) {
+  return new DataLoader(std::filesystem::path(path), (size_t)B, (size_t)T, (unsigned)rank, (unsigned)world,
+                        shuffle != 0);
+}
+void ref_loader_destroy(void* l) { delete static_cast<DataLoader*>(l); }
+void ref_loader_next(void* l, int* inputs, int* targets) { static_cast<DataLoader*>(l)->NextBatch(inputs, targets); }
+void ref_loader_reset(void* l) { static_cast<DataLoader*>(l)->Reset(); }
+void ref_loader_resume(void* l, size_t shard, size_t sample) { static_cast<DataLoader*>(l)->Resume(shard, sample); }
+long long ref_loader_num_tokens(void* l) { return (long long)static_cast<DataLoader*>(l)->num_tokens; }
 
 }  // extern "C"

@@ -3,6 +3,7 @@ in include/*.h is exported, argument validation fails cleanly, and the
 host-only planning helpers (workspace sizes, DP buckets, parameter layout)
 are consistent."""
 import ctypes as C
+import glob
 import os
 import re
 
@@ -16,8 +17,8 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 def declared_functions():
     names = []
-    for h in ("llmk.h", "llmk_gpt2.h"):
-        src = open(os.path.join(ROOT, "include", h)).read()
+    for h in sorted(glob.glob(os.path.join(ROOT, "include", "*.h"))):
+        src = open(h).read()
         src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
         names += re.findall(r"^\s*(?:const\s+)?[\w\s\*]+?\b(llmk_\w+)\s*\(", src, flags=re.M)
     return sorted(set(names))
@@ -78,6 +79,47 @@ def test_layer_major_permutation_roundtrip(llmk_lib):
     assert np.array_equal(back, src)
     assert not np.array_equal(lm, src)
     assert np.array_equal(np.sort(lm), src)
+
+
+def test_dataloader_adapter_matches_reference_api(llmk_lib, tmp_path):
+    """include/llmk_dataloader.hpp (the reference's DataLoader class over the
+    C ABI) compiles, links, and its NextBatch overloads return the batches the
+    shard holds; a bad shard throws std::invalid_argument."""
+    import shutil
+    import subprocess
+    import llmk
+    from oracle import dataloader as D
+    gxx = shutil.which("g++")
+    if gxx is None:
+        pytest.skip("g++ not available")
+    toks = np.arange(1, 2 * 3 * 16 + 2) % 50000
+    D.write_shard(str(tmp_path / "a.bin"), toks)
+    (tmp_path / "bad.bin").write_bytes(b"\0" * 1100)
+    src = tmp_path / "loader.cpp"
+    src.write_text(r'''
+#include <cstdio>
+#include "llmk_dataloader.hpp"
+int main(int argc, char** argv) {
+  DataLoader dl(argv[1], 2, 16, 0, 1, false);
+  std::vector<int> in(32), tg(32);
+  dl.NextBatch(in, tg);
+  int in2[32], tg2[32];
+  dl.NextBatch(in2, tg2);
+  std::printf("%zu %d %d %d %d\n", dl.num_tokens, in[0], tg[31], in2[0], tg2[31]);
+  try { std::vector<int> bad(3); dl.NextBatch(bad, tg); return 2; } catch (const std::invalid_argument&) {}
+  try { DataLoader b(argv[2], 2, 16, 0, 1, false); return 3; } catch (const std::invalid_argument&) {}
+  return 0;
+}
+''')
+    exe = tmp_path / "loader"
+    lib_dir = os.path.dirname(llmk.LIB_PATH)
+    r = subprocess.run([gxx, "-std=c++17", "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe),
+                        "-L", lib_dir, "-l:libllmk.so", f"-Wl,-rpath,{lib_dir}"], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    r = subprocess.run([str(exe), str(tmp_path / "a.bin"), str(tmp_path / "bad.bin")], capture_output=True,
+                       text=True, timeout=60)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert r.stdout.split() == [str(toks.size), "1", "33", "33", "65"]
 
 
 def test_adapter_compiles_and_links(llmk_lib, tmp_path):
