@@ -33,6 +33,8 @@ typedef struct llmk_gpt2 llmk_gpt2;
 /* Number of parameters of a configuration (padded vocabulary included). */
 size_t llmk_gpt2_num_parameters(const llmk_gpt2_config* cfg);
 size_t llmk_gpt2_parameter_count(const llmk_gpt2* model);
+/* The configuration the model was created with. */
+int llmk_gpt2_get_config(const llmk_gpt2* model, llmk_gpt2_config* cfg);
 
 /* Allocates a model for micro-batch B x T on the current device. math:
  * LLMK_MATH_BF16 (bf16 GEMM operands and activations, fp32 residual stream,
@@ -52,6 +54,46 @@ int llmk_gpt2_buffers(llmk_gpt2* model, int** d_inputs, int** d_targets);
 int llmk_gpt2_load_parameters(llmk_gpt2* model, const float* host_params, size_t n);
 int llmk_gpt2_read_parameters(llmk_gpt2* model, float* host_out, size_t n);
 int llmk_gpt2_read_gradients(llmk_gpt2* model, float* host_out, size_t n);
+/* AdamW first and second moments in llm.c order, host fp32 (new: the
+ * reference keeps them only in device memory, gpt2/cuda/gpt2cuda.h:137-140).
+ * Synchronous. */
+int llmk_gpt2_read_optimizer_state(llmk_gpt2* model, float* host_m, float* host_v, size_t n);
+int llmk_gpt2_load_optimizer_state(llmk_gpt2* model, const float* host_m, const float* host_v, size_t n);
+
+/* ------------------------------------------------ checkpoint files */
+/* llm.c v3 model file: 256 int32 header words ([0] = 20240326, [1] = 3,
+ * [2] max_seq_len, [3] vocab_size, [4] num_layers, [5] num_heads,
+ * [6] channels, [7] padded_vocab_size) followed by every parameter as fp32
+ * in llm.c order — the file the reference's GPT2 constructors read
+ * (gpt2/cuda/gpt2cuda.cu:33-166, gpt2/gpt2.cpp:112-230). Host only: reads
+ * the header into *cfg, and checks the file holds exactly that model's
+ * parameters. Bad magic / version / size -> LLMK_ERR_INVALID_ARG (the
+ * reference prints and exit()s). */
+int llmk_gpt2_checkpoint_config(const char* path, llmk_gpt2_config* cfg);
+/* Loads a model file into a model of the same configuration (parameters,
+ * bf16 copies; AdamW state reset). Synchronous. */
+int llmk_gpt2_load_checkpoint(llmk_gpt2* model, const char* path);
+/* Writes the model's parameters as a model file (new: the reference only
+ * reads them). Written to path + ".tmp" and renamed, so an interrupted save
+ * leaves the old file. Synchronous. */
+int llmk_gpt2_save_checkpoint(llmk_gpt2* model, const char* path);
+
+/* Training state (new; the reference has no resume path): the model file's
+ * header words and parameters, then the AdamW moments m and v (fp32, llm.c
+ * order), with header [0] = 20241202 (state magic), [1] = 1,
+ * [2..7] = the configuration as above, [8] = optimizer steps taken,
+ * [9] = world size that wrote it, [10..11] / [12..13] = data-loader shard and
+ * sample position (int64, low word first). Replicated data parallelism keeps
+ * the full state on every rank, so one rank saves and every rank loads. */
+typedef struct llmk_train_state {
+  int step;              /* AdamW steps done: the next update uses t = step + 1 */
+  int world;             /* ranks of the run that saved it (informational) */
+  long long shard_idx;   /* llmk_loader_position() of the next batch */
+  long long sample_idx;
+} llmk_train_state;
+int llmk_gpt2_save_state(llmk_gpt2* model, const char* path, const llmk_train_state* state);
+/* Restores parameters and AdamW moments and fills *state. Synchronous. */
+int llmk_gpt2_load_state(llmk_gpt2* model, const char* path, llmk_train_state* state);
 
 /* Copies B*T input (and target) tokens from host memory to the device,
  * through pinned staging. Replaces GPT2::SetTrainData (gpt2cuda.cu:350-367). */

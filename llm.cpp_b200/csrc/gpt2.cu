@@ -425,6 +425,12 @@ int llmk_gpt2_destroy(llmk_gpt2* g) {
 
 size_t llmk_gpt2_parameter_count(const llmk_gpt2* g) { return g ? g->nparams : 0; }
 
+int llmk_gpt2_get_config(const llmk_gpt2* g, llmk_gpt2_config* cfg) {
+  if (!g || !cfg) return fail(LLMK_ERR_INVALID_ARG, "gpt2_get_config: null argument");
+  *cfg = g->cfg;
+  return LLMK_OK;
+}
+
 int llmk_gpt2_load_parameters(llmk_gpt2* g, const float* host_params, size_t n) {
   if (!g || !host_params || n != g->nparams) return fail(LLMK_ERR_INVALID_ARG, "gpt2_load_parameters: size mismatch");
   LLMK_TRY(ensure_device(g));
@@ -455,6 +461,26 @@ static int read_flat(llmk_gpt2* g, const float* dev, float* host_out, size_t n) 
 
 int llmk_gpt2_read_parameters(llmk_gpt2* g, float* host_out, size_t n) { return read_flat(g, g ? g->params : nullptr, host_out, n); }
 int llmk_gpt2_read_gradients(llmk_gpt2* g, float* host_out, size_t n) { return read_flat(g, g ? g->grads : nullptr, host_out, n); }
+
+int llmk_gpt2_read_optimizer_state(llmk_gpt2* g, float* host_m, float* host_v, size_t n) {
+  LLMK_TRY(read_flat(g, g ? g->m : nullptr, host_m, n));
+  return read_flat(g, g->v, host_v, n);
+}
+
+int llmk_gpt2_load_optimizer_state(llmk_gpt2* g, const float* host_m, const float* host_v, size_t n) {
+  if (!g || !host_m || !host_v || n != g->nparams)
+    return fail(LLMK_ERR_INVALID_ARG, "gpt2_load_optimizer_state: size mismatch");
+  LLMK_TRY(ensure_device(g));
+  std::vector<float> tmp(n);
+  LLMK_CUDA(cudaStreamSynchronize(g->stream));
+  permute_params(g, host_m, tmp.data(), 0);
+  LLMK_CUDA(cudaMemcpyAsync(g->m, tmp.data(), n * sizeof(float), cudaMemcpyHostToDevice, g->stream));
+  LLMK_CUDA(cudaStreamSynchronize(g->stream));
+  permute_params(g, host_v, tmp.data(), 0);
+  LLMK_CUDA(cudaMemcpyAsync(g->v, tmp.data(), n * sizeof(float), cudaMemcpyHostToDevice, g->stream));
+  LLMK_CUDA(cudaStreamSynchronize(g->stream));
+  return LLMK_OK;
+}
 
 // Timed wrappers of the library calls the step makes (work = algorithmic
 // FLOPs or HBM bytes of the call, for the per-class step report).

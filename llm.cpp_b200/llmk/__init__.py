@@ -40,6 +40,10 @@ class KernelStat(C.Structure):
                 ("work", C.c_double), ("unit", C.c_int)]
 
 
+class TrainState(C.Structure):
+    _fields_ = [("step", C.c_int), ("world", C.c_int), ("shard_idx", C.c_longlong), ("sample_idx", C.c_longlong)]
+
+
 class GPT2Config(C.Structure):
     _fields_ = [("max_seq_len", C.c_int), ("vocab_size", C.c_int), ("padded_vocab_size", C.c_int),
                 ("num_layers", C.c_int), ("num_heads", C.c_int), ("channels", C.c_int)]
@@ -110,6 +114,14 @@ SIGNATURES: dict[str, tuple] = {
     "llmk_gpt2_set_timing": (i32, [vp, i32]),
     "llmk_gpt2_use_graph": (i32, [vp, i32]),
     "llmk_gpt2_timing_report": (i32, [vp, C.POINTER(KernelStat), i32, C.POINTER(i32)]),
+    "llmk_gpt2_get_config": (i32, [vp, C.POINTER(GPT2Config)]),
+    "llmk_gpt2_read_optimizer_state": (i32, [vp, vp, vp, sz]),
+    "llmk_gpt2_load_optimizer_state": (i32, [vp, vp, vp, sz]),
+    "llmk_gpt2_checkpoint_config": (i32, [C.c_char_p, C.POINTER(GPT2Config)]),
+    "llmk_gpt2_load_checkpoint": (i32, [vp, C.c_char_p]),
+    "llmk_gpt2_save_checkpoint": (i32, [vp, C.c_char_p]),
+    "llmk_gpt2_save_state": (i32, [vp, C.c_char_p, C.POINTER(TrainState)]),
+    "llmk_gpt2_load_state": (i32, [vp, C.c_char_p, C.POINTER(TrainState)]),
     # include/llmk_data.h
     "llmk_loader_create": (i32, [C.POINTER(vp), C.c_char_p, i32, i32, i32, i32, i32]),
     "llmk_loader_destroy": (i32, [vp]),
@@ -235,6 +247,45 @@ class GPT2:
         call("llmk_gpt2_read_gradients", self.h, out.ctypes.data, self.n)
         return out
 
+    @classmethod
+    def from_checkpoint(cls, path: str, B: int, T: int, math=MATH_BF16, stream=None) -> "GPT2":
+        """A model shaped by an llm.c v3 model file's header, with its
+        parameters loaded (the reference's GPT2(path, B, T) constructor)."""
+        c = checkpoint_config(path)
+        m = cls(B, T, c.max_seq_len, c.vocab_size, c.padded_vocab_size, c.num_layers, c.num_heads, c.channels,
+                math=math, stream=stream)
+        m.load_checkpoint(path)
+        return m
+
+    def load_checkpoint(self, path: str) -> None:
+        call("llmk_gpt2_load_checkpoint", self.h, os.fsencode(path))
+
+    def save_checkpoint(self, path: str) -> None:
+        call("llmk_gpt2_save_checkpoint", self.h, os.fsencode(path))
+
+    def save_state(self, path: str, step: int, loader_position=(0, 0), world: int = 1) -> None:
+        """Parameters + AdamW moments + step + data-loader position."""
+        st = TrainState(step, world, loader_position[0], loader_position[1])
+        call("llmk_gpt2_save_state", self.h, os.fsencode(path), C.byref(st))
+
+    def load_state(self, path: str) -> dict:
+        st = TrainState()
+        call("llmk_gpt2_load_state", self.h, os.fsencode(path), C.byref(st))
+        return {"step": st.step, "world": st.world, "loader_position": (st.shard_idx, st.sample_idx)}
+
+    def read_optimizer_state(self):
+        import numpy as np
+        m, v = np.empty(self.n, np.float32), np.empty(self.n, np.float32)
+        call("llmk_gpt2_read_optimizer_state", self.h, m.ctypes.data, v.ctypes.data, self.n)
+        return m, v
+
+    def load_optimizer_state(self, m, v) -> None:
+        import numpy as np
+        m = np.ascontiguousarray(m, dtype=np.float32)
+        v = np.ascontiguousarray(v, dtype=np.float32)
+        assert m.size == self.n and v.size == self.n
+        call("llmk_gpt2_load_optimizer_state", self.h, m.ctypes.data, v.ctypes.data, self.n)
+
     def train_step(self, inputs, targets, lr, t, b1=0.9, b2=0.999, eps=1e-8, wd=0.0, want_loss=True):
         """Host tokens in, host loss out (None when want_loss is False)."""
         import numpy as np
@@ -300,6 +351,14 @@ class GPT2:
             self.close()
         except Exception:
             pass
+
+
+def checkpoint_config(path: str) -> GPT2Config:
+    """Configuration in an llm.c v3 model file's header (host only; checks
+    magic, version and that the file holds exactly that many parameters)."""
+    c = GPT2Config()
+    call("llmk_gpt2_checkpoint_config", os.fsencode(path), C.byref(c))
+    return c
 
 
 class DataLoader:
