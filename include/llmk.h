@@ -222,6 +222,31 @@ int llmk_encoder_backward(float* dwte, float* dwpe, const float* dout, const int
  * gpt2/cuda/gpt2cuda.cu:325,342,398). */
 int llmk_softmax_crossentropy(float* losses, void* dlogits, const void* logits, llmk_dtype dtype, const int* targets,
                               int BT, int V, int Vp, float dscale, void* stream);
+/* ------------------------------- fused lm_head + softmax / cross-entropy */
+/* logits[BT, Vp] = inp[BT, C] * W[Vp, C]^T (+ bias) on the tensor cores
+ * (inp and W in the math mode's operand type: bf16, or fp32 for TF32), with
+ * the epilogue folding each row into per-64-column (max, sum exp) statistics
+ * in `workspace` (llmk_matmul_softmax_workspace bytes), then one pass per row.
+ * llmk_matmul_softmax_forward: probs = softmax over the first V columns of each
+ * row, 0 on [V, Vp); probs may alias logits. Replaces
+ * gpt2cuda::BatchMatmulNTSoftmaxForward (gpt2/cuda/matmul_softmax.cu:9-110,
+ * B*T rows flattened; the reference's weight is the same (Vp, C) row-major
+ * buffer). */
+size_t llmk_matmul_softmax_workspace(int BT, int Vp);
+int llmk_matmul_softmax_forward(void* probs, void* logits, llmk_dtype dtype, const void* inp, const void* W,
+                                const float* bias, int BT, int C, int Vp, int V, llmk_math math, void* workspace,
+                                size_t workspace_bytes, void* stream);
+/* The training step's lm_head + softmax + cross-entropy (+ its backward):
+ * losses[row] = logsumexp(logits[row, :V]) - logits[row, target] (NaN for a
+ * target outside [0, V)); with backward != 0 the logits buffer is then
+ * overwritten by dlogits = (softmax - onehot(target)) * dscale, 0 on
+ * [V, Vp). Replaces the reference step's lm_head matmul + Softmax +
+ * CrossEntropy + CrossEntropySoftmaxBackward (gpt2/cuda/gpt2cuda.cu:323-325,
+ * 398), in one GEMM and one pass over the logits. */
+int llmk_matmul_crossentropy_forward(float* losses, void* logits, llmk_dtype dtype, const void* inp, const void* W,
+                                     const float* bias, const int* targets, int BT, int C, int Vp, int V,
+                                     float dscale, int backward, llmk_math math, void* workspace,
+                                     size_t workspace_bytes, void* stream);
 /* *out = mean(x[0..n)) on the device, fixed reduction order. */
 int llmk_mean(float* out, const float* x, int n, void* stream);
 

@@ -45,6 +45,11 @@ struct EpiParams {
   int flags;
   float* partial;  // split-K: fp32 [splits][M][N] workspace (raw accumulators)
   int aux_tma;     // GELU pre-activation leaves by TMA store (aux dtype == D dtype)
+  // Row softmax statistics of D as stored (bf16-rounded for a bf16 D): for
+  // each row and each 64-column slot, (max, sum exp(x - max)) over the slot's
+  // columns below stats_cols, at stats[slot * M + row].
+  float2* stats;
+  int stats_cols;
 };
 
 template <bool kTF32, bool kAMN, bool kBMN, int kBN, bool kPair>
@@ -235,6 +240,45 @@ __device__ __forceinline__ void stage8(uint8_t* buf, int lane, int k, const floa
   }
 }
 
+
+// Folds columns [gn0, gn0 + CW) of this lane's row into the running softmax
+// statistics (m, s) and writes them out at the end of each 64-column slot.
+// For a bf16 D the values are first rounded as the store will round them, so
+// the statistics describe the stored logits exactly.
+template <bool kBF16, int CW>
+__device__ __forceinline__ void rowstats_chunk(const EpiParams& ep, long long gm, int gn0, int N, int M, float* v,
+                                               float& m, float& s) {
+  if constexpr (kBF16) {
+#pragma unroll
+    for (int j = 0; j < CW; j += 2) {
+      const uint32_t u = pack_bf16x2(v[j], v[j + 1]);
+      v[j] = __uint_as_float(u << 16);
+      v[j + 1] = __uint_as_float(u & 0xffff0000u);
+    }
+  }
+  // columns at or past stats_cols only in the chunk that holds the vocabulary end
+  const bool full = gn0 + CW <= ep.stats_cols;
+  float cm = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < CW; ++j)
+    if (full || gn0 + j < ep.stats_cols) cm = fmaxf(cm, v[j]);
+  if (cm > -INFINITY) {
+    const float mn = fmaxf(m, cm);
+    const float m2 = mn * kLog2e;
+    float acc = s * ex2_approx(m * kLog2e - m2);
+#pragma unroll
+    for (int j = 0; j < CW; ++j)
+      if (full || gn0 + j < ep.stats_cols) acc += ex2_approx(fmaf(v[j], kLog2e, -m2));
+    m = mn;
+    s = acc;
+  }
+  if (((gn0 + CW) & 63) == 0 || gn0 + CW >= N) {
+    if (gm < M) ep.stats[static_cast<long long>(gn0 >> 6) * M + gm] = make_float2(m, s);
+    m = -INFINITY;
+    s = 0.f;
+  }
+}
+
 // Drains columns [c_begin, c_end) of one warp's 32 accumulator rows (TMEM
 // lanes from `tsrc`) through the fused epilogue in chunks of 4 KB: 64 bf16 or
 // 32 fp32 columns. Each chunk is written 128B-swizzled into one of the warp's
@@ -242,14 +286,16 @@ __device__ __forceinline__ void stage8(uint8_t* buf, int lane, int k, const floa
 // alternate, so a chunk's smem writes only wait for the store issued two
 // chunks earlier. kAux: the GELU pre-activation is staged too (first buffer)
 // and leaves by a second TMA store (tmX), so each chunk uses both buffers.
-// Rows / columns past M / N are clipped by the tensor maps.
-template <bool kBF16, bool kAux>
+// Rows / columns past M / N are clipped by the tensor maps. kStats: row
+// softmax statistics as well (no other epilogue operation, no split-K).
+template <bool kBF16, bool kAux, bool kStats = false>
 __device__ __forceinline__ void epilogue_cols(const EpiParams& ep, const CUtensorMap* tmD, const CUtensorMap* tmX,
                                               uint32_t tsrc, int row0, int n0, int c_begin, int c_end, int sp, int M,
                                               int N, int lane, uint8_t* stg, uint32_t& nstore) {
   constexpr int CW = kBF16 ? 64 : 32;  // columns per chunk
   const long long gm = row0 + lane;
   const bool row_ok = gm < M && !ep.partial;
+  float st_m = -INFINITY, st_s = 0.f;
 #pragma unroll 1
   for (int c0 = c_begin; c0 < c_end; c0 += CW) {
     const int gn0 = n0 + c0;
@@ -276,7 +322,14 @@ __device__ __forceinline__ void epilogue_cols(const EpiParams& ep, const CUtenso
       if (lane == 0) bulk_wait_read0();
       __syncwarp();
     }
-    if (row_ok) {
+    if constexpr (kStats) {
+      if (ep.bias) {
+#pragma unroll
+        for (int k = 0; k < CW / 8; ++k)
+          if (gn0 + k * 8 < N) epi_pre8(ep, gm, gn0 + k * 8, v + k * 8);
+      }
+      rowstats_chunk<kBF16, CW>(ep, gm, gn0, N, M, v, st_m, st_s);
+    } else if (row_ok) {
 #pragma unroll
       for (int k = 0; k < CW / 8; ++k) {
         if (gn0 + k * 8 < N) {
@@ -305,7 +358,7 @@ __device__ __forceinline__ void epilogue_cols(const EpiParams& ep, const CUtenso
   }
 }
 
-template <bool kTF32, bool kAMN, bool kBMN, int kBN, bool kPair>
+template <bool kTF32, bool kAMN, bool kBMN, int kBN, bool kPair, bool kStats>
 __global__ void __launch_bounds__(Cfg<kTF32, kAMN, kBMN, kBN, kPair>::kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmD, const __grid_constant__ CUtensorMap tmX, EpiParams ep,
@@ -519,7 +572,10 @@ __global__ void __launch_bounds__(Cfg<kTF32, kAMN, kBMN, kBN, kPair>::kThreads, 
       tc_fence_after();
       const uint32_t tsrc = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * kBN;
       const int r0 = m0 + q * 32;
-      if (ep.d_bf16 && !ep.partial) {
+      if constexpr (kStats) {
+        if (ep.d_bf16) epilogue_cols<true, false, true>(ep, &tmD, &tmX, tsrc, r0, n0, cb, ce, sp, M, N, lane, stg, nstore);
+        else epilogue_cols<false, false, true>(ep, &tmD, &tmX, tsrc, r0, n0, cb, ce, sp, M, N, lane, stg, nstore);
+      } else if (ep.d_bf16 && !ep.partial) {
         if (ep.aux_tma) epilogue_cols<true, true>(ep, &tmD, &tmX, tsrc, r0, n0, cb, ce, sp, M, N, lane, stg, nstore);
         else epilogue_cols<true, false>(ep, &tmD, &tmX, tsrc, r0, n0, cb, ce, sp, M, N, lane, stg, nstore);
       } else {
@@ -604,11 +660,11 @@ int persistent_units(Kern kern, bool pair, size_t smem, int threads, int* units)
   return LLMK_OK;
 }
 
-template <bool kTF32, bool kAMN, bool kBMN, int kBN, bool kPair>
+template <bool kTF32, bool kAMN, bool kBMN, int kBN, bool kPair, bool kStats = false>
 int launch_gemm(const void* A, long long lda, const void* B, long long ldb, int M, int N, int K, EpiParams ep,
                 int splits, cudaStream_t stream) {
   using C = Cfg<kTF32, kAMN, kBMN, kBN, kPair>;
-  auto kern = gemm_tc_kernel<kTF32, kAMN, kBMN, kBN, kPair>;
+  auto kern = gemm_tc_kernel<kTF32, kAMN, kBMN, kBN, kPair, kStats>;
   static bool attr_done[64] = {};
   int dev = 0;
   LLMK_CUDA(cudaGetDevice(&dev));
@@ -674,6 +730,11 @@ int launch_gemm(const void* A, long long lda, const void* B, long long ldb, int 
 template <bool kTF32, int kBN, bool kPair>
 int dispatch_major(int a_trans, int b_trans, const void* A, long long lda, const void* B, long long ldb, int M,
                    int N, int K, const EpiParams& ep, int splits, cudaStream_t s) {
+  // row statistics: only the logits GEMM (both operands K-major) takes them
+  if (ep.stats) {
+    if (a_trans || b_trans) return fail(LLMK_ERR_UNSUPPORTED, "gemm: row statistics need K-major operands");
+    return launch_gemm<kTF32, false, false, kBN, kPair, true>(A, lda, B, ldb, M, N, K, ep, splits, s);
+  }
   if (!a_trans && !b_trans) return launch_gemm<kTF32, false, false, kBN, kPair>(A, lda, B, ldb, M, N, K, ep, splits, s);
   if (!a_trans && b_trans) return launch_gemm<kTF32, false, true, kBN, kPair>(A, lda, B, ldb, M, N, K, ep, splits, s);
   if (a_trans && b_trans) return launch_gemm<kTF32, true, true, kBN, kPair>(A, lda, B, ldb, M, N, K, ep, splits, s);
@@ -733,7 +794,8 @@ using namespace llmk;
 
 static int gemm_impl(void* D, llmk_dtype d_dtype, long long ldd, const void* A, int a_trans, long long lda,
                      const void* B, int b_trans, long long ldb, llmk_math math, int M, int N, int K,
-                     const llmk_epilogue* epi, void* workspace, size_t workspace_bytes, void* stream) {
+                     const llmk_epilogue* epi, void* workspace, size_t workspace_bytes, void* stream,
+                     float2* stats = nullptr, int stats_cols = 0) {
   if (!D || !A || !B) return fail(LLMK_ERR_INVALID_ARG, "gemm: null operand");
   if (M <= 0 || N <= 0 || K <= 0) return fail(LLMK_ERR_INVALID_ARG, "gemm: non-positive size");
   if (math != LLMK_MATH_BF16 && math != LLMK_MATH_TF32) return fail(LLMK_ERR_INVALID_ARG, "gemm: bad math mode");
@@ -762,6 +824,15 @@ static int gemm_impl(void* D, llmk_dtype d_dtype, long long ldd, const void* A, 
   plan_gemm(M, N, K, elem, &kind, &splits);
   const size_t need = static_cast<size_t>(splits) * M * N * sizeof(float);
   if (splits > 1 && (!workspace || workspace_bytes < need || !aligned16(workspace))) splits = 1;
+  if (stats) {
+    // statistics are taken from whole accumulators: no split-K, and only a
+    // bias may come before them
+    if (epi && (epi->residual || epi->aux || epi->flags))
+      return fail(LLMK_ERR_INVALID_ARG, "gemm: row statistics take a bias-only epilogue");
+    splits = 1;
+    ep.stats = stats;
+    ep.stats_cols = stats_cols;
+  }
   if (splits > 1) ep.partial = static_cast<float*>(workspace);
   // the pre-activation store rides the TMA path when it has D's element type
   ep.aux_tma = (ep.flags & LLMK_EPI_GELU) && ep.aux && !ep.partial &&
@@ -778,6 +849,20 @@ static int gemm_impl(void* D, llmk_dtype d_dtype, long long ldd, const void* A, 
   LLMK_CUDA(cudaGetLastError());
   return LLMK_OK;
 }
+
+namespace llmk {
+
+int gemm_rowstats(void* D, llmk_dtype d_dtype, long long ldd, const void* A, long long lda, const void* B,
+                  long long ldb, llmk_math math, int M, int N, int K, const float* bias, float2* stats,
+                  int stats_cols, cudaStream_t stream) {
+  if (!stats || !aligned16(stats) || stats_cols <= 0 || stats_cols > N)
+    return fail(LLMK_ERR_INVALID_ARG, "gemm_rowstats: statistics buffer / column count");
+  llmk_epilogue e{};
+  e.bias = bias;
+  return gemm_impl(D, d_dtype, ldd, A, 0, lda, B, 0, ldb, math, M, N, K, &e, nullptr, 0, stream, stats, stats_cols);
+}
+
+}  // namespace llmk
 
 extern "C" {
 

@@ -328,6 +328,7 @@ int alloc_all(llmk_gpt2* g) {
   ws = std::max(ws, llmk_gemm_workspace(iVp, iC, iBT, g->math));
   ws = std::max(ws, llmk_layernorm_backward_workspace(iBT, iC));
   ws = std::max(ws, llmk_attention_backward_workspace(g->B, g->T, 3 * iC, static_cast<int>(NH)));
+  ws = std::max(ws, llmk::rowstats_bytes(iBT, iVp));
   ws = std::max(ws, llmk_encoder_backward_workspace(g->B, g->T));
   g->workspace_bytes = ws;
   LLMK_CUDA(cudaMalloc(&g->workspace, std::max<size_t>(ws, 256)));
@@ -572,18 +573,27 @@ int llmk_gpt2_forward(llmk_gpt2* g, const int* d_inputs, const int* d_targets) {
   }
   LLMK_TRY(op.ln_fwd(g->lnf, adt, g->lnf_mean, g->lnf_rstd, x, P + g->off_lnfw, P + g->off_lnfb, BT, C));
   // tied lm_head (gpt2cuda.cu:323): logits[BT, Vp] = lnf * wte^T, no bias
-  LLMK_TRY(op.gemm(KC_GEMM_LMHEAD, g->logits, adt, Vp, g->lnf, 0, C, W(g->off_wte), 0, C, BT, Vp, C, nullptr, nullptr, 0));
-  if (g->have_targets) {
-    // softmax + cross-entropy + its backward in one pass; dlogits overwrite the
-    // logits in place with scale 1/(B*T) (gpt2cuda.cu:398)
-    {
-      TimedScope ts(g, KC_XENT, 2.0 * BT * static_cast<double>(Vp) * g->ae + 8.0 * BT);
-      LLMK_TRY(llmk_softmax_crossentropy(g->losses, g->logits, g->logits, adt, g->targets, BT, V, Vp,
-                                         1.0f / static_cast<float>(BT), s));
-    }
-    TimedScope ts(g, KC_OTHER, 4.0 * BT);
-    LLMK_TRY(llmk_mean(g->loss, g->losses, BT, s));
+  if (!g->have_targets) {
+    LLMK_TRY(op.gemm(KC_GEMM_LMHEAD, g->logits, adt, Vp, g->lnf, 0, C, W(g->off_wte), 0, C, BT, Vp, C, nullptr, nullptr, 0));
+    return LLMK_OK;
   }
+  // With targets, the lm_head GEMM's epilogue also reduces each row to
+  // per-slot softmax statistics (in the workspace, free during the forward),
+  // and one pass over the logits gives the losses and overwrites the logits
+  // with dlogits = (softmax - onehot) / (B*T) (gpt2cuda.cu:325,398).
+  auto* stats = static_cast<float2*>(g->workspace);
+  {
+    TimedScope ts(g, KC_GEMM_LMHEAD, 2.0 * BT * static_cast<double>(Vp) * C);
+    LLMK_TRY(llmk::gemm_rowstats(g->logits, adt, Vp, g->lnf, C, W(g->off_wte), C, g->math, BT, Vp, C, nullptr, stats,
+                                 V, s));
+  }
+  {
+    TimedScope ts(g, KC_XENT, 2.0 * BT * static_cast<double>(Vp) * g->ae + llmk::rowstats_bytes(BT, Vp) + 8.0 * BT);
+    LLMK_TRY(llmk::rowstats_finish(0, g->losses, g->logits, g->logits, adt, stats, g->targets, BT, V, Vp,
+                                   1.0f / static_cast<float>(BT), 1, s));
+  }
+  TimedScope ts(g, KC_OTHER, 4.0 * BT);
+  LLMK_TRY(llmk_mean(g->loss, g->losses, BT, s));
   return LLMK_OK;
 }
 

@@ -98,6 +98,16 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
+// Plain bulk copy global -> this CTA's shared memory (no tensor map),
+// completing on `bar` with `bytes` of transaction count. Both addresses
+// 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_load_1d(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
 // Asynchronous prefetch of [src, src + bytes) into L2 (16-byte aligned
 // address, bytes a multiple of 16); no completion to wait for.
 __device__ __forceinline__ void prefetch_l2_bulk(const void* src, uint32_t bytes) {
@@ -360,6 +370,15 @@ __device__ __forceinline__ float gelu_tanh_grad_fast(float x) {
   const float sech2 = 1.0f - th * th;
   return 0.5f * (1.0f + th) + 0.5f * x * sech2 * 0.7978845608f * (1.0f + 0.134145f * x2);
 }
+
+// 2^x by the SFU's approximate exp2 (flushes subnormal results to zero);
+// exp(x - m) = ex2_approx(x * log2(e) - m * log2(e)) is one FMA and one SFU op.
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+constexpr float kLog2e = 1.4426950408889634f;
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);

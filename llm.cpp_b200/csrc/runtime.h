@@ -38,6 +38,23 @@ int make_tmap_3d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, uin
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Row softmax statistics of a logits GEMM (gemm.cu): D[M, N] = A[M, K] *
+// B[N, K]^T (+ bias), both operands K-major, and for every row and 64-column
+// slot (max, sum exp(x - max)) over the slot's columns below stats_cols,
+// written to stats[slot * M + row] (ceil(N / 64) * M float2 values).
+int gemm_rowstats(void* D, llmk_dtype d_dtype, long long ldd, const void* A, long long lda, const void* B,
+                  long long ldb, llmk_math math, int M, int N, int K, const float* bias, float2* stats,
+                  int stats_cols, cudaStream_t stream);
+// One pass over logits[rows, ld] given their slot statistics (lmhead_xent.cu):
+// mode 0 = cross-entropy (losses; dlogits in place when `backward`), mode 1 =
+// softmax probabilities into `out`.
+int rowstats_finish(int mode, float* losses, void* out, const void* logits, llmk_dtype dtype, const float2* stats,
+                    const int* targets, int rows, int V, int ld, float dscale, int backward, cudaStream_t stream);
+// Workspace of the two: the slot planes, then one fp32 logsumexp per row.
+inline size_t rowstats_bytes(int rows, int ld) {
+  return static_cast<size_t>((ld + 63) / 64) * rows * 8 + (static_cast<size_t>(rows) * 4 + 15) / 16 * 16;
+}
+
 }  // namespace llmk
 
 #define LLMK_TRY(expr)            \

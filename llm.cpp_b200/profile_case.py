@@ -5,6 +5,11 @@
     python llm.cpp_b200/profile_case.py attnbwd [B T NH] [--reps R]
     python llm.cpp_b200/profile_case.py step    [B T]    [--reps R]
     python llm.cpp_b200/profile_case.py gemmset [BT]     [--reps R]
+    python llm.cpp_b200/profile_case.py lmxent  [BT]     [--variant fused|unfused|gemm] [--reps R]
+
+lmxent runs the GPT-2 124M lm_head + softmax + cross-entropy (+ dlogits in
+place) at BT tokens: fused (llmk_matmul_crossentropy_forward), unfused
+(llmk_gemm + llmk_softmax_crossentropy) or the logits GEMM alone.
 
 gemmset runs each GEMM shape of one GPT-2 124M training step at BT tokens
 (fwd / dinp / dweight of QKV, attproj, FC, FCproj and the tied lm_head, in
@@ -27,7 +32,8 @@ sys.path.insert(0, HERE)
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["gemm", "attn", "attnbwd", "step", "gemmset"])
+    ap.add_argument("case", choices=["gemm", "attn", "attnbwd", "step", "gemmset", "lmxent"])
+    ap.add_argument("--variant", choices=["fused", "unfused", "gemm"], default="fused")
     ap.add_argument("dims", nargs="*", type=int)
     ap.add_argument("--trans", nargs=2, type=int, default=[0, 0])
     ap.add_argument("--reps", type=int, default=3)
@@ -94,6 +100,29 @@ def main() -> None:
             for (A, B, D, ws, M, N, K, at, bt) in bufs:
                 llmk.gemm(D, A, B, a_trans=at, b_trans=bt, M=M, N=N, K=K, workspace=ws)
         flop = sum(2.0 * M * N * K for (_, _, _, _, M, N, K, _, _) in bufs)
+    elif a.case == "lmxent":
+        BT = (a.dims + [16384])[0]
+        C, V, Vp = 768, 50257, 50304
+        s = llmk.stream_ptr()
+        x = torch.randn(BT, C, device=dev).bfloat16()
+        W = (torch.randn(Vp, C, device=dev) * 0.05).bfloat16()
+        tg = torch.randint(0, V, (BT,), device=dev, dtype=torch.int32)
+        logits = torch.empty(BT, Vp, device=dev, dtype=torch.bfloat16)
+        losses = torch.empty(BT, device=dev)
+        wsb = llmk.lib().llmk_matmul_softmax_workspace(BT, Vp)
+        ws = torch.empty(wsb // 4 + 4, device=dev)
+        if a.variant == "fused":
+            run = lambda: llmk.call("llmk_matmul_crossentropy_forward", losses.data_ptr(), logits.data_ptr(),
+                                    llmk.BF16, x.data_ptr(), W.data_ptr(), None, tg.data_ptr(), BT, C, Vp, V,
+                                    1.0 / BT, 1, llmk.MATH_BF16, ws.data_ptr(), wsb, s)
+        elif a.variant == "unfused":
+            def run():
+                llmk.gemm(logits, x, W)
+                llmk.call("llmk_softmax_crossentropy", losses.data_ptr(), logits.data_ptr(), logits.data_ptr(),
+                          llmk.BF16, tg.data_ptr(), BT, V, Vp, 1.0 / BT, s)
+        else:
+            run = lambda: llmk.gemm(logits, x, W)
+        flop = 2.0 * BT * Vp * C
     else:
         Bb, T = (a.dims + [16, 1024][len(a.dims):])[:2]
         m = llmk.GPT2(Bb, T)
@@ -124,7 +153,8 @@ def main() -> None:
     e1.synchronize()
     ms = e0.elapsed_time(e1) / a.reps
     extra = f", {flop / ms / 1e9:.1f} TFLOP/s" if flop else ""
-    print(f"{a.case} {a.dims}: {ms:.4f} ms per launch{extra}; device status {llmk.device_status()}")
+    tag = f"{a.case}/{a.variant}" if a.case == "lmxent" else a.case
+    print(f"{tag} {a.dims}: {ms:.4f} ms per launch{extra}; device status {llmk.device_status()}")
 
 
 if __name__ == "__main__":

@@ -46,6 +46,15 @@ def test_argument_validation_without_gpu(llmk_lib):
     # D (fp32 per row and head) | fp32 dQ accumulator | bf16 copy of dO
     assert L.llmk_attention_backward_workspace(8, 1024, 2304, 12) == 8 * 12 * 1024 * 4 + 8 * 1024 * 768 * (4 + 2)
     assert L.llmk_layernorm_backward_workspace(16384, 768) > 0
+    # fused lm_head: one (max, sum) pair per row and 64-column slot, then the row lse
+    assert L.llmk_matmul_softmax_workspace(8192, 50304) == 8192 * 786 * 8 + 8192 * 4  # + one lse per row
+    assert L.llmk_matmul_crossentropy_forward(None, None, llmk.BF16, None, None, None, None, 8, 64, 512, 500, 1.0, 1,
+                                              llmk.MATH_BF16, None, 0, None) == 1
+    fake = 1 << 20  # never dereferenced: the missing workspace is refused first
+    assert L.llmk_matmul_crossentropy_forward(fake, fake, llmk.BF16, fake, fake, None, fake, 8, 64, 512, 500, 1.0, 1,
+                                              llmk.MATH_BF16, None, 0, None) == 5
+    assert L.llmk_matmul_softmax_forward(fake, fake, llmk.BF16, fake, fake, None, 8, 64, 510, 500, llmk.MATH_BF16,
+                                         fake, 1 << 20, None) == 2  # Vp % 8
 
 
 def test_dp_buckets_partition_parameters(llmk_lib):
