@@ -123,19 +123,20 @@ __global__ void __launch_bounds__(256) rowstats_lse_kernel(float* __restrict__ l
 // Stream: a persistent pass over the logits in units of 16 KB row segments
 // (unit u = row u / units_per_row, segment u % units_per_row). Warp 0 lane 0
 // streams this CTA's units into a ring of shared-memory stages with bulk
-// copies (up to kStages * 16 KB in flight per SM: enough to cover HBM latency
-// with one CTA per SM); the consumer warps turn each stage into output values
+// copies (two CTAs per SM, up to 2 * kStages * 16 KB in flight per SM: enough
+// to cover HBM latency); the consumer warps turn each stage into output values
 // and store them with 16-byte stores. kMode 0: out (which may be the logits
 // buffer) = (softmax - onehot) * dscale, 0 on [V, ld); kMode 1: out =
 // softmax, 0 on [V, ld). Every wait is bounded (device status on timeout).
 constexpr int kStageBytes = 16384;
-constexpr int kStages = 10;
+constexpr int kStages = 6;
+constexpr int kStreamCtasPerSm = 2;
 constexpr int kConsumerWarps = 16;
 constexpr int kStreamThreads = 32 * (kConsumerWarps + 1);
 constexpr size_t kStreamSmem = size_t(kStages) * kStageBytes + 2 * kStages * 8 + 16;
 
 template <typename T, int kMode>
-__global__ void __launch_bounds__(kStreamThreads, 1)
+__global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm)
     rowstats_stream_kernel(T* out, const T* logits, const float* __restrict__ lse, const int* __restrict__ targets,
                            int rows, int V, int ld, float dscale, unsigned int* status) {
   constexpr int CH = kStageBytes / static_cast<int>(sizeof(T));  // elements per unit
@@ -234,7 +235,7 @@ int rowstats_finish_t(float* losses, void* out, const void* logits, const float2
   }
   const long long units = static_cast<long long>(rows) * ((ld + kStageBytes / static_cast<int>(sizeof(T)) - 1) /
                                                           (kStageBytes / static_cast<int>(sizeof(T))));
-  const int grid = static_cast<int>(std::min<long long>(units, num_sms()));
+  const int grid = static_cast<int>(std::min<long long>(units, kStreamCtasPerSm * num_sms()));
   kern<<<grid, kStreamThreads, kStreamSmem, s>>>(static_cast<T*>(out), x, lse, targets, rows, V, ld, dscale,
                                                  device_status_ptr());
   count_launch();
