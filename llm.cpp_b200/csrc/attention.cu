@@ -38,12 +38,6 @@ constexpr int HD = 64;          // head size
 constexpr int TILE = 128;       // query / key tile
 constexpr int TILE_BYTES = TILE * HD * 2;  // 16 KB: one [128 x 64] bf16 tile, 128B rows
 
-__device__ __forceinline__ float ex2(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-
 // Byte offset of 16-byte chunk `c` (0..7) of row `r` inside a 1024B-aligned
 // 128B-swizzled atom column (TMA SWIZZLE_128B / UMMA SWIZZLE_128B pattern).
 __device__ __forceinline__ uint32_t sw128(int r, int c) { return r * 128 + ((c ^ (r & 7)) << 4); }
@@ -61,11 +55,12 @@ __device__ __forceinline__ void st_tile_chunk(uint8_t* tile, int r, int chunk, c
 
 // ------------------------------------------------------------------ forward
 struct FwdSmem {
-  static constexpr int kStages = 2;
+  static constexpr int kStages = 3;
   static constexpr int Q_OFF = 0;                                    // 2 x Q (double-buffered across items)
   static constexpr int KV_OFF = 2 * TILE_BYTES;                      // stages x (K, V)
   static constexpr int P_OFF = KV_OFF + kStages * 2 * TILE_BYTES;    // 2 x [128 x 128] bf16
-  static constexpr int BAR_OFF = P_OFF + 2 * 2 * TILE_BYTES;
+  static constexpr int RED_OFF = P_OFF + 2 * 2 * TILE_BYTES;        // row max / sum exchange, 3 KB
+  static constexpr int BAR_OFF = RED_OFF + 3 * 2 * TILE * 4;
   static constexpr size_t BYTES = BAR_OFF + 256 + 1024;
 };
 
@@ -85,7 +80,7 @@ __device__ __forceinline__ AttnItem fwd_item(int w, int nq, int B, int NH) {
   return it;
 }
 
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(320, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, void* __restrict__ out_ptr, int out_f32,
                     float* __restrict__ lse, int B, int T, int NH, int C, unsigned int* status) {
   using S = FwdSmem;
@@ -114,7 +109,7 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(q_full + i, 1);
       mbar_init(q_empty + i, 1);
       mbar_init(s_full + i, 1);
-      mbar_init(p_full + i, 128);
+      mbar_init(p_full + i, 256);
       mbar_init(o_full + i, 1);
     }
     for (int s = 0; s < S::kStages; ++s) {
@@ -133,7 +128,7 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  // TMEM columns: S[0] 0..127, S[1] 128..255, O_part[0] 256..319, O_part[1] 320..383
+  // TMEM columns: S[0] 0..127, S[1] 128..255, O 256..319
   // Buffers and barrier phases follow two running counters shared by all roles:
   // the item count n (Q buffer n&1) and the key-tile step count g over all
   // items (S / P / O_part buffer g&1, KV stage g%kStages).
@@ -214,12 +209,13 @@ __global__ void __launch_bounds__(192, 1)
         tc_fence_after();
         const uint32_t p_addr = smem_u32(sP + (g & 1) * 2 * TILE_BYTES);
         const uint32_t v_addr = smem_u32(sKV + st * 2 * TILE_BYTES + TILE_BYTES);
-        const uint32_t d = tmem + 256 + (g & 1) * HD;
+        // O accumulates in TMEM across the item's key tiles
+        const uint32_t d = tmem + 256;
 #pragma unroll
         for (int ks = 0; ks < TILE / 16; ++ks) {
           const uint64_t a = sdesc_sw128(p_addr + (ks >> 2) * TILE_BYTES + (ks & 3) * 32, 16, 1024);
           const uint64_t bd = sdesc_sw128(v_addr + ks * 2048, TILE_BYTES, 1024);
-          mma_f16_ss(d, a, bd, idesc_o, ks > 0);
+          mma_f16_ss(d, a, bd, idesc_o, (ks > 0 || cur.j > 0) ? 1u : 0u);
         }
         mma_commit(o_full + (g & 1));
         mma_commit(kv_empty + st);
@@ -231,118 +227,137 @@ __global__ void __launch_bounds__(192, 1)
     }
     __syncwarp();
   } else {
+    // Softmax warps 2..9: warp w may read TMEM lane quarter q = w % 4 (query
+    // rows 32q..32q+31) and owns key-column half h = (w-2)/4 of every S tile
+    // (and output columns 32h..32h+31 of O). The two warps of a quarter meet
+    // at named barrier 1+q to combine their row maxima (double-buffered by
+    // step parity) and, at the end of an item, their row sums.
     const int q = warp & 3;
+    const int h = (warp - 2) >> 2;
     const int r = q * 32 + lane;  // query row within the tile (= TMEM lane)
     const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
+    float* red_max = reinterpret_cast<float*>(smem + S::RED_OFF);  // [2 parity][2 halves][128 rows]
+    float* red_sum = red_max + 2 * 2 * TILE;                        // [2 halves][128 rows]
     const float sl2 = 0.125f * 1.4426950408889634f;  // softmax scale * log2(e)
+    // O (fp32, TMEM columns 256..319) accumulates P V over the item's key
+    // tiles. Exponents use a running reference m (log2 domain) that moves only
+    // when a tile's row maximum exceeds it by more than kRescale: then the
+    // warp waits for the previous P V, rescales its O columns and l in place.
+    // Otherwise P stays below 2^kRescale, well inside bf16 / fp32 range.
+    constexpr float kRescale = 8.f;
+    const uint32_t o_cols = tmem + lane_base + 256 + h * 32;
     bool ok = true;
     uint32_t g = 0;
     for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x) {
       const AttnItem it = fwd_item(w, nq, B, NH);
       const int qt = it.tile, n_kv = qt + 1;
-      float m = -INFINITY, l = 0.f, alpha_prev = 0.f;
-      float o[HD];
-#pragma unroll
-      for (int i = 0; i < HD; ++i) o[i] = 0.f;
-      auto consume_o = [&](uint32_t gg, float alpha) -> bool {
-        bool wt = mbar_wait(o_full + (gg & 1), (gg >> 1) & 1, status, abort_flag, 7);
-        if (!__all_sync(0xffffffffu, wt)) return false;
-        tc_fence_after();
-        uint32_t v[32], v2[32];
-        tmem_ld_32x32b_x32(tmem + lane_base + 256 + (gg & 1) * HD, v);
-        tmem_ld_32x32b_x32(tmem + lane_base + 256 + (gg & 1) * HD + 32, v2);
-        tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          o[i] = fmaf(o[i], alpha, __uint_as_float(v[i]));
-          o[32 + i] = fmaf(o[32 + i], alpha, __uint_as_float(v2[i]));
-        }
-        return true;
-      };
+      float m = -INFINITY, l = 0.f;
       for (int j = 0; j < n_kv; ++j, ++g) {
         bool wt = mbar_wait(s_full + (g & 1), (g >> 1) & 1, status, abort_flag, 6);
         if (!__all_sync(0xffffffffu, wt)) { ok = false; break; }
         tc_fence_after();
-        float sc[TILE];
-#pragma unroll
-        for (int c = 0; c < 4; c += 2) {
-          uint32_t v[32], v2[32];
-          tmem_ld_32x32b_x32(tmem + lane_base + (g & 1) * 128 + c * 32, v);
-          tmem_ld_32x32b_x32(tmem + lane_base + (g & 1) * 128 + c * 32 + 32, v2);
+        uint32_t sv[TILE / 2];  // raw scores of this half row
+        {
+          uint32_t* v = sv;
+          tmem_ld_32x32b_x32(tmem + lane_base + (g & 1) * 128 + h * 64, *reinterpret_cast<uint32_t(*)[32]>(v));
+          tmem_ld_32x32b_x32(tmem + lane_base + (g & 1) * 128 + h * 64 + 32,
+                             *reinterpret_cast<uint32_t(*)[32]>(v + 32));
           tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            sc[c * 32 + i] = __uint_as_float(v[i]) * sl2;
-            sc[c * 32 + 32 + i] = __uint_as_float(v2[i]) * sl2;
-          }
         }
         if (j == qt) {  // diagonal tile: key index > query index is masked
 #pragma unroll
-          for (int i = 0; i < TILE; ++i)
-            if (i > r) sc[i] = -INFINITY;
+          for (int i = 0; i < TILE / 2; ++i)
+            if (h * 64 + i > r) sv[i] = __float_as_uint(-INFINITY);
         }
-        // row max as a tree (short dependency chains)
+        // row max of this half (raw scores; the scale is positive) as a
+        // tree, then across the two halves
         float mx8[8];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) mx8[k] = sc[k];
+        for (int k = 0; k < 8; ++k) mx8[k] = __uint_as_float(sv[k]);
 #pragma unroll
-        for (int i = 8; i < TILE; i += 8)
+        for (int i = 8; i < TILE / 2; i += 8)
 #pragma unroll
-          for (int k = 0; k < 8; ++k) mx8[k] = fmaxf(mx8[k], sc[i + k]);
-        const float mx = fmaxf(m, fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                                        fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]))));
-        const float alpha = ex2(m - mx);  // 0 on the first tile (m = -inf)
+          for (int k = 0; k < 8; ++k) mx8[k] = fmaxf(mx8[k], __uint_as_float(sv[i + k]));
+        const float mxh = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                                fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+        float* rm = red_max + (g & 1) * 2 * TILE;
+        rm[h * TILE + r] = mxh;
+        named_barrier_sync(1 + q, 64);
+        const float mx2 = fmaxf(rm[r], rm[TILE + r]) * sl2;
+        const bool move = mx2 > m + kRescale;
+        if (j > 0 && __any_sync(0xffffffffu, move)) {
+          // rescale this warp's rows of O once the previous P V is done
+          const float alpha = move ? ex2_approx(m - mx2) : 1.f;
+          bool wo = mbar_wait(o_full + ((g - 1) & 1), ((g - 1) >> 1) & 1, status, abort_flag, 7);
+          if (!__all_sync(0xffffffffu, wo)) { ok = false; break; }
+          tc_fence_after();
+          uint32_t ov[32];
+          tmem_ld_32x32b_x32(o_cols, ov);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
+          tmem_st_32x32b_x32(o_cols, ov);
+          tmem_st_wait();
+          l *= alpha;
+        }
+        if (move) m = mx2;
         float rs8[8];
 #pragma unroll
         for (int k = 0; k < 8; ++k) rs8[k] = 0.f;
         uint8_t* pt = sP + (g & 1) * 2 * TILE_BYTES;
 #pragma unroll
-        for (int ch = 0; ch < TILE / 8; ++ch) {
+        for (int ch = 0; ch < TILE / 16; ++ch) {
           float pv[8];
 #pragma unroll
           for (int k = 0; k < 8; ++k) {
-            pv[k] = ex2(sc[ch * 8 + k] - mx);
+            pv[k] = ex2_approx(fmaf(__uint_as_float(sv[ch * 8 + k]), sl2, -m));
             rs8[k] += pv[k];
           }
-          st_tile_chunk(pt, r, ch, pv);
+          st_tile_chunk(pt, r, h * 8 + ch, pv);
         }
-        const float rs = ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
-        l = l * alpha + rs;
-        m = mx;
+        l += ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
         fence_async_smem();
         tc_fence_before();
         mbar_arrive(p_full + (g & 1));
-        if (j > 0 && !consume_o(g - 1, alpha_prev)) { ok = false; break; }
-        alpha_prev = alpha;
       }
-      if (!ok || !consume_o(g - 1, alpha_prev)) {
-        ok = false;
-        break;
-      }
+      if (!ok) break;
+      // the item's last P V, then O / l
+      bool wo = mbar_wait(o_full + ((g - 1) & 1), ((g - 1) >> 1) & 1, status, abort_flag, 7);
+      if (!__all_sync(0xffffffffu, wo)) { ok = false; break; }
+      tc_fence_after();
+      uint32_t ov[32];
+      tmem_ld_32x32b_x32(o_cols, ov);
+      tmem_ld_wait();
+      red_sum[h * TILE + r] = l;
+      named_barrier_sync(1 + q, 64);
+      const float lt = red_sum[r] + red_sum[TILE + r];
       const int t = qt * TILE + r;
       if (t < T) {
-        const float inv = 1.0f / l;
-        const long long off = (static_cast<long long>(it.b) * T + t) * C + it.h * HD;
+        const float inv = 1.0f / lt;
+        const long long off = (static_cast<long long>(it.b) * T + t) * C + it.h * HD + h * 32;
         if (out_f32) {
           float4* dst = reinterpret_cast<float4*>(static_cast<float*>(out_ptr) + off);
 #pragma unroll
-          for (int ch = 0; ch < HD / 4; ++ch)
-            dst[ch] = make_float4(o[ch * 4] * inv, o[ch * 4 + 1] * inv, o[ch * 4 + 2] * inv, o[ch * 4 + 3] * inv);
+          for (int ch = 0; ch < HD / 8; ++ch)
+            dst[ch] = make_float4(__uint_as_float(ov[ch * 4]) * inv, __uint_as_float(ov[ch * 4 + 1]) * inv,
+                                  __uint_as_float(ov[ch * 4 + 2]) * inv, __uint_as_float(ov[ch * 4 + 3]) * inv);
         } else {
           __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(out_ptr) + off;
 #pragma unroll
-          for (int ch = 0; ch < HD / 8; ++ch) {
+          for (int ch = 0; ch < HD / 16; ++ch) {
             uint4 u;
-            u.x = pack_bf16x2(o[ch * 8 + 0] * inv, o[ch * 8 + 1] * inv);
-            u.y = pack_bf16x2(o[ch * 8 + 2] * inv, o[ch * 8 + 3] * inv);
-            u.z = pack_bf16x2(o[ch * 8 + 4] * inv, o[ch * 8 + 5] * inv);
-            u.w = pack_bf16x2(o[ch * 8 + 6] * inv, o[ch * 8 + 7] * inv);
+            u.x = pack_bf16x2(__uint_as_float(ov[ch * 8 + 0]) * inv, __uint_as_float(ov[ch * 8 + 1]) * inv);
+            u.y = pack_bf16x2(__uint_as_float(ov[ch * 8 + 2]) * inv, __uint_as_float(ov[ch * 8 + 3]) * inv);
+            u.z = pack_bf16x2(__uint_as_float(ov[ch * 8 + 4]) * inv, __uint_as_float(ov[ch * 8 + 5]) * inv);
+            u.w = pack_bf16x2(__uint_as_float(ov[ch * 8 + 6]) * inv, __uint_as_float(ov[ch * 8 + 7]) * inv);
             reinterpret_cast<uint4*>(dst)[ch] = u;
           }
         }
         // natural-log LSE: (m2 + log2 l) * ln 2
-        lse[static_cast<long long>(it.bh) * T + t] = (m + __log2f(l)) * 0.6931471805599453f;
+        if (h == 0) lse[static_cast<long long>(it.bh) * T + t] = (m + __log2f(lt)) * 0.6931471805599453f;
       }
+      // the partner has read red_sum before either side writes it again
+      named_barrier_sync(1 + q, 64);
     }
     tc_fence_before();
   }
@@ -516,7 +531,7 @@ __device__ __forceinline__ void bwd_p_ds(const uint32_t* sv, const uint32_t* dv,
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
       const int tq = tq0 + c * 8 + k;
-      float pv = ex2(fmaf(__uint_as_float(sv[c * 8 + k]), sl2, -l2[k]));
+      float pv = ex2_approx(fmaf(__uint_as_float(sv[c * 8 + k]), sl2, -l2[k]));
       if (kMask && (tq < key || tq >= T)) pv = 0.f;  // causal (query before key) and padded queries
       p[k] = pv;
       ds[k] = pv * (__uint_as_float(dv[c * 8 + k]) - dd[k]);
@@ -909,7 +924,7 @@ int llmk_attention_forward(void* out, llmk_dtype out_dtype, float* lse, const vo
   LLMK_TRY(set_smem(reinterpret_cast<const void*>(attn_fwd_kernel), FwdSmem::BYTES));
   const int nq = (T + TILE - 1) / TILE;
   const int grid = std::min(nq * B * NH, num_sms());  // persistent: one CTA per SM
-  attn_fwd_kernel<<<grid, 192, FwdSmem::BYTES, static_cast<cudaStream_t>(stream)>>>(
+  attn_fwd_kernel<<<grid, 320, FwdSmem::BYTES, static_cast<cudaStream_t>(stream)>>>(
       tm, out, out_dtype == LLMK_F32 ? 1 : 0, lse, B, T, NH, C, device_status_ptr());
   count_launch();
   LLMK_CUDA(cudaGetLastError());
