@@ -10,13 +10,12 @@
 // {3C, T, B} with a {64, 128, 1} box serves Q, K, V, dO and O tiles: rows past
 // T of a batch read as zeros.
 //
-// Forward: persistent, one CTA per SM walking (128-query tile, head, batch)
-// items heaviest first; warp 0 = TMA, warp 1 = tcgen05 issuer (S = Q K^T
-// into TMEM, O_part = P V), warps 2..5 = softmax (thread = query row): exp2
-// online softmax, P -> smem (bf16, 128B-swizzled K-major), O accumulated in
-// registers from O_part. S, P and O_part are double-buffered and Q is
-// double-buffered across items, so the MMAs of tile j+1 (or of the next
-// item) overlap the softmax of tile j.
+// Forward: persistent, one CTA per SM walking (pair of 128-query tiles,
+// head, batch) items heaviest first; warp 0 = TMA, warp 1 = tcgen05 issuer
+// (S = Q K^T into TMEM, O += P V in TMEM), warps 2..9 = softmax of the two
+// tiles (thread = query row): exp2 online softmax with lazy rescaling, P ->
+// smem (bf16, 128B-swizzled K-major). The two tiles share each K/V load and
+// alternate on the tensor core, so one's softmax overlaps the other's MMAs.
 //
 // Backward: one CTA per (128-key tile, head, batch) walking query tiles from
 // the diagonal down. S^T = K Q^T and dP^T = V dO^T land in TMEM; 16 softmax
@@ -54,16 +53,6 @@ __device__ __forceinline__ void st_tile_chunk(uint8_t* tile, int r, int chunk, c
 }
 
 // ------------------------------------------------------------------ forward
-struct FwdSmem {
-  static constexpr int kStages = 3;
-  static constexpr int Q_OFF = 0;                                    // 2 x Q (double-buffered across items)
-  static constexpr int KV_OFF = 2 * TILE_BYTES;                      // stages x (K, V)
-  static constexpr int P_OFF = KV_OFF + kStages * 2 * TILE_BYTES;    // 2 x [128 x 128] bf16
-  static constexpr int RED_OFF = P_OFF + 2 * 2 * TILE_BYTES;        // row max / sum exchange, 3 KB
-  static constexpr int BAR_OFF = RED_OFF + 3 * 2 * TILE * 4;
-  static constexpr size_t BYTES = BAR_OFF + 256 + 1024;
-};
-
 // Work item w (0 .. nq*B*NH-1) of the attention kernels: query
 // (forward) or key (backward) tile `tile` of head bh. Items are ordered by
 // decreasing work, and CTA c walks items c, c + gridDim.x, ... .
@@ -80,7 +69,26 @@ __device__ __forceinline__ AttnItem fwd_item(int w, int nq, int B, int NH) {
   return it;
 }
 
-__global__ void __launch_bounds__(320, 1)
+// ------------------------------------------------------------------ forward
+// CTA = 10 warps: warp 0 TMA, warp 1 tcgen05 issuer, warps 2..5 the softmax
+// of query tile A = 2p of pair item p, warps 6..9 of tile B = 2p+1 (thread =
+// query row = TMEM lane). Both tiles of a pair belong to one (batch, head)
+// and share every K/V tile the TMA brings in (B needs one more: its
+// diagonal). Each tile has one S buffer (128 TMEM columns) and one O
+// accumulator (64 columns) in TMEM and one P buffer in shared memory; the
+// issuer alternates the tiles (PV_A(j), S_A(j+1), PV_B(j), S_B(j+1)), so one
+// tile's softmax runs while the other's MMAs do.
+struct FwdSmem {
+  static constexpr int kStages = 3;
+  static constexpr int Q_OFF = 0;                                  // 2 items x (Q_A, Q_B)
+  static constexpr int KV_OFF = 4 * TILE_BYTES;                    // stages x (K, V)
+  static constexpr int P_OFF = KV_OFF + kStages * 2 * TILE_BYTES;  // P_A, P_B: [128 x 128] bf16
+  static constexpr int BAR_OFF = P_OFF + 2 * 2 * TILE_BYTES;
+  static constexpr size_t BYTES = BAR_OFF + 256 + 1024;
+};
+constexpr int kFwdThreads = 320;
+
+__global__ void __launch_bounds__(kFwdThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, void* __restrict__ out_ptr, int out_f32,
                     float* __restrict__ lse, int B, int T, int NH, int C, unsigned int* status) {
   using S = FwdSmem;
@@ -90,27 +98,30 @@ __global__ void __launch_bounds__(320, 1)
   uint8_t* sKV = smem + S::KV_OFF;
   uint8_t* sP = smem + S::P_OFF;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::BAR_OFF);
-  uint64_t* q_full = bars;                       // [2]
-  uint64_t* q_empty = q_full + 2;                // [2]
-  uint64_t* kv_full = q_empty + 2;               // [2]
-  uint64_t* kv_empty = kv_full + S::kStages;     // [2]
-  uint64_t* s_full = kv_empty + S::kStages;      // [2]
-  uint64_t* p_full = s_full + 2;                 // [2]
-  uint64_t* o_full = p_full + 2;                 // [2]
-  uint64_t* done = o_full + 2;
+  uint64_t* q_full = bars;                       // [item parity][A, B]
+  uint64_t* q_empty = q_full + 4;                // [item parity][A, B]
+  uint64_t* kv_full = q_empty + 4;               // [stages]
+  uint64_t* kv_empty = kv_full + S::kStages;     // [stages]
+  uint64_t* s_full = kv_empty + S::kStages;      // [A, B]
+  uint64_t* p_full = s_full + 2;                 // [A, B]
+  uint64_t* pv_done = p_full + 2;                // [A, B]: the tile's latest P V is done
+  uint64_t* done = pv_done + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int nq = (T + TILE - 1) / TILE;
-  const int n_items = nq * B * NH;
+  const int np = (nq + 1) / 2;
+  const int n_items = np * B * NH;
   const int warp = warp_id(), lane = lane_id();
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < 4; ++i) {
       mbar_init(q_full + i, 1);
       mbar_init(q_empty + i, 1);
+    }
+    for (int i = 0; i < 2; ++i) {
       mbar_init(s_full + i, 1);
-      mbar_init(p_full + i, 256);
-      mbar_init(o_full + i, 1);
+      mbar_init(p_full + i, 128);
+      mbar_init(pv_done + i, 1);
     }
     for (int s = 0; s < S::kStages; ++s) {
       mbar_init(kv_full + s, 1);
@@ -128,10 +139,10 @@ __global__ void __launch_bounds__(320, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  // TMEM columns: S[0] 0..127, S[1] 128..255, O 256..319
-  // Buffers and barrier phases follow two running counters shared by all roles:
-  // the item count n (Q buffer n&1) and the key-tile step count g over all
-  // items (S / P / O_part buffer g&1, KV stage g%kStages).
+  // TMEM columns of tile X (0 = A, 1 = B): S at 192X .. 192X+127, O at
+  // 192X+128 .. 192X+191. Barrier phases follow counters every role keeps
+  // alike: items n (Q buffers n&1), K/V tiles over all items (stages), and
+  // per tile the key tiles processed so far (s_full / p_full / pv_done).
 
   if (warp == 0) {
     if (lane == 0) {
@@ -141,12 +152,18 @@ __global__ void __launch_bounds__(320, 1)
       bool ok = true;
       int n = 0;
       for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x, ++n) {
-        const AttnItem it = fwd_item(w, nq, B, NH);
-        const int qb = n & 1;
-        if (!mbar_wait(q_empty + qb, ((n >> 1) & 1) ^ 1u, status, abort_flag, 1)) break;
-        mbar_arrive_expect_tx(q_full + qb, TILE_BYTES);
-        tma_load_3d(sQ + qb * TILE_BYTES, &tm_qkv, q_full + qb, it.h * HD, it.tile * TILE, it.b);
-        for (int j = 0; j <= it.tile; ++j) {
+        const AttnItem it = fwd_item(w, np, B, NH);
+        const int p = it.tile;
+        const bool has_b = 2 * p + 1 < nq;
+        const int nkv = 2 * p + 1 + (has_b ? 1 : 0);
+        for (int x = 0; x < 2; ++x) {
+          // tile B of an odd last pair lies past T and reads as zeros
+          const int qb = (n & 1) * 2 + x;
+          if (!mbar_wait(q_empty + qb, ((n >> 1) & 1) ^ 1u, status, abort_flag, 1)) { ok = false; break; }
+          mbar_arrive_expect_tx(q_full + qb, TILE_BYTES);
+          tma_load_3d(sQ + qb * TILE_BYTES, &tm_qkv, q_full + qb, it.h * HD, (2 * p + x) * TILE, it.b);
+        }
+        for (int j = 0; j < nkv && ok; ++j) {
           if (!mbar_wait(kv_empty + stage, phase ^ 1u, status, abort_flag, 1)) { ok = false; break; }
           uint8_t* sK = sKV + stage * 2 * TILE_BYTES;
           mbar_arrive_expect_tx(kv_full + stage, 2 * TILE_BYTES);
@@ -160,143 +177,157 @@ __global__ void __launch_bounds__(320, 1)
     if (lane == 0) {
       // S = Q K^T: M=128 queries, N=128 keys, both K-major (hd contiguous).
       const uint32_t idesc_s = idesc_f32acc(128, 128, kFmtBF16, false, false);
-      // O_part = P V: M=128 queries, N=64 hd, K=128 keys; V is [keys][hd] = N-major.
+      // O += P V: M=128 queries, N=64 hd, K=128 keys; V is [keys][hd] = N-major.
       const uint32_t idesc_o = idesc_f32acc(128, HD, kFmtBF16, false, true);
-      // The key-tile steps of all this CTA's items form one sequence; S of
-      // step g+1 is issued before O_part of step g so the tensor core works
-      // while the softmax warps turn S(g) into P(g).
-      struct Step {
-        int w, j, n;  // item, key tile within it, item count
-      };
-      auto next_step = [&](Step st) -> Step {
-        const AttnItem it = fwd_item(st.w, nq, B, NH);
-        if (st.j < it.tile) return {st.w, st.j + 1, st.n};
-        return {st.w + static_cast<int>(gridDim.x), 0, st.n + 1};
-      };
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t cp[2] = {0, 0};  // P tiles consumed per query tile
       bool ok = true;
-      int kst = 0;        // KV stage of the step whose S was issued last
-      uint32_t kph = 0;
-      Step cur{static_cast<int>(blockIdx.x), 0, 0};
-      auto issue_s = [&](const Step& st, uint32_t g) -> bool {
-        // Q of a new item
-        if (st.j == 0) {
-          if (!mbar_wait(q_full + (st.n & 1), (st.n >> 1) & 1, status, abort_flag, 2)) return false;
-        }
-        if (!mbar_wait(kv_full + kst, kph, status, abort_flag, 3)) return false;
-        tc_fence_after();
-        const uint32_t q_addr = smem_u32(sQ + (st.n & 1) * TILE_BYTES);
-        const uint32_t k_addr = smem_u32(sKV + kst * 2 * TILE_BYTES);
-        const uint32_t d = tmem + (g & 1) * 128;
+      int n = 0;
+      auto issue_s = [&](int x, int st, int qb) {
+        const uint32_t q_addr = smem_u32(sQ + qb * TILE_BYTES);
+        const uint32_t k_addr = smem_u32(sKV + st * 2 * TILE_BYTES);
+        const uint32_t d = tmem + x * 192;
 #pragma unroll
         for (int ks = 0; ks < HD / 16; ++ks)
           mma_f16_ss(d, sdesc_sw128(q_addr + ks * 32, 16, 1024), sdesc_sw128(k_addr + ks * 32, 16, 1024), idesc_s,
                      ks > 0);
-        mma_commit(s_full + (g & 1));
-        // the item's last S: its Q buffer is free once these MMAs are done
-        if (st.j == fwd_item(st.w, nq, B, NH).tile) mma_commit(q_empty + (st.n & 1));
-        return true;
+        mma_commit(s_full + x);
       };
-      uint32_t g = 0;
-      if (cur.w < n_items) ok = issue_s(cur, 0);
-      while (cur.w < n_items && ok) {
-        const int st = kst;
-        const Step nxt = next_step(cur);
-        if (++kst == S::kStages) { kst = 0; kph ^= 1u; }
-        if (nxt.w < n_items) {
-          if (!issue_s(nxt, g + 1)) { ok = false; break; }
-        }
-        if (!mbar_wait(p_full + (g & 1), (g >> 1) & 1, status, abort_flag, 4)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t p_addr = smem_u32(sP + (g & 1) * 2 * TILE_BYTES);
+      auto issue_pv = [&](int x, int st, bool acc) {
+        const uint32_t p_addr = smem_u32(sP + x * 2 * TILE_BYTES);
         const uint32_t v_addr = smem_u32(sKV + st * 2 * TILE_BYTES + TILE_BYTES);
-        // O accumulates in TMEM across the item's key tiles
-        const uint32_t d = tmem + 256;
+        const uint32_t d = tmem + x * 192 + 128;
 #pragma unroll
         for (int ks = 0; ks < TILE / 16; ++ks) {
           const uint64_t a = sdesc_sw128(p_addr + (ks >> 2) * TILE_BYTES + (ks & 3) * 32, 16, 1024);
           const uint64_t bd = sdesc_sw128(v_addr + ks * 2048, TILE_BYTES, 1024);
-          mma_f16_ss(d, a, bd, idesc_o, (ks > 0 || cur.j > 0) ? 1u : 0u);
+          mma_f16_ss(d, a, bd, idesc_o, (ks > 0 || acc) ? 1u : 0u);
         }
-        mma_commit(o_full + (g & 1));
-        mma_commit(kv_empty + st);
-        cur = nxt;
-        ++g;
+        mma_commit(pv_done + x);
+      };
+      for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x, ++n) {
+        const AttnItem it = fwd_item(w, np, B, NH);
+        const int p = it.tile;
+        const bool has_b = 2 * p + 1 < nq;
+        const int na = 2 * p + 1, nkv = na + (has_b ? 1 : 0);
+        const int q0 = (n & 1) * 2;
+        if (!mbar_wait(q_full + q0, (n >> 1) & 1, status, abort_flag, 2) ||
+            !mbar_wait(q_full + q0 + 1, (n >> 1) & 1, status, abort_flag, 2)) { ok = false; break; }
+        if (!mbar_wait(kv_full + stage, phase, status, abort_flag, 3)) { ok = false; break; }
+        tc_fence_after();
+        // S_x(k) is issued as soon as the softmax has read S_x(k-1), ahead of
+        // P V_x(k-1); after the tile's last S its Q buffer is free.
+        issue_s(0, stage, q0);
+        if (na == 1) mma_commit(q_empty + q0);
+        if (has_b) issue_s(1, stage, q0 + 1);
+        for (int j = 0; j < nkv; ++j) {
+          const int st = stage;
+          if (++stage == S::kStages) { stage = 0; phase ^= 1u; }
+          bool next_ready = false;  // K/V tile j+1 (now at `stage`) has landed
+          for (int x = 0; x < 2; ++x) {
+            const int nx = x == 0 ? na : (has_b ? nkv : 0);
+            if (j >= nx) continue;
+            if (!mbar_wait(p_full + x, cp[x] & 1u, status, abort_flag, 4)) { ok = false; break; }
+            ++cp[x];
+            tc_fence_after();
+            if (j + 1 < nx) {
+              if (!next_ready) {
+                if (!mbar_wait(kv_full + stage, phase, status, abort_flag, 3)) { ok = false; break; }
+                tc_fence_after();
+                next_ready = true;
+              }
+              issue_s(x, stage, q0 + x);
+              if (j + 2 == nx) mma_commit(q_empty + q0 + x);
+            }
+            issue_pv(x, st, j > 0);
+          }
+          if (!ok) break;
+          mma_commit(kv_empty + st);  // K_j, V_j read by every MMA issued so far
+        }
+        // tile B of an odd last pair: its (zero) Q buffer is free
+        if (ok && !has_b) mma_commit(q_empty + q0 + 1);
       }
       mma_commit(done);
       mbar_wait(done, 0, status, nullptr, 5);
     }
     __syncwarp();
   } else {
-    // Softmax warps 2..9: warp w may read TMEM lane quarter q = w % 4 (query
-    // rows 32q..32q+31) and owns key-column half h = (w-2)/4 of every S tile
-    // (and output columns 32h..32h+31 of O). The two warps of a quarter meet
-    // at named barrier 1+q to combine their row maxima (double-buffered by
-    // step parity) and, at the end of an item, their row sums.
+    const int x = (warp - 2) >> 2;  // query tile of the pair
     const int q = warp & 3;
-    const int h = (warp - 2) >> 2;
     const int r = q * 32 + lane;  // query row within the tile (= TMEM lane)
     const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
-    float* red_max = reinterpret_cast<float*>(smem + S::RED_OFF);  // [2 parity][2 halves][128 rows]
-    float* red_sum = red_max + 2 * 2 * TILE;                        // [2 halves][128 rows]
+    const uint32_t s_cols = tmem + lane_base + x * 192;
+    const uint32_t o_cols = s_cols + 128;
     const float sl2 = 0.125f * 1.4426950408889634f;  // softmax scale * log2(e)
-    // O (fp32, TMEM columns 256..319) accumulates P V over the item's key
-    // tiles. Exponents use a running reference m (log2 domain) that moves only
-    // when a tile's row maximum exceeds it by more than kRescale: then the
-    // warp waits for the previous P V, rescales its O columns and l in place.
-    // Otherwise P stays below 2^kRescale, well inside bf16 / fp32 range.
+    // O accumulates P V over the tile's key tiles in TMEM. Exponents use a
+    // running reference m (log2 domain) that moves only when a tile's row
+    // maximum exceeds it by more than kRescale: then the warp rescales its O
+    // rows and l in place once the previous P V is done. Otherwise P stays
+    // below 2^kRescale, well inside bf16 and fp32 range.
     constexpr float kRescale = 8.f;
-    const uint32_t o_cols = tmem + lane_base + 256 + h * 32;
+    uint8_t* pt = sP + x * 2 * TILE_BYTES;
     bool ok = true;
-    uint32_t g = 0;
-    for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x) {
-      const AttnItem it = fwd_item(w, nq, B, NH);
-      const int qt = it.tile, n_kv = qt + 1;
+    uint32_t cs = 0;  // S tiles consumed
+    int n = 0;        // items
+    for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x, ++n) {
+      const AttnItem it = fwd_item(w, np, B, NH);
+      const int tile = 2 * it.tile + x;
+      if (tile >= nq) continue;  // tile B of an odd last pair
       float m = -INFINITY, l = 0.f;
-      for (int j = 0; j < n_kv; ++j, ++g) {
-        bool wt = mbar_wait(s_full + (g & 1), (g >> 1) & 1, status, abort_flag, 6);
+      for (int j = 0; j <= tile; ++j) {
+        bool wt = mbar_wait(s_full + x, cs & 1u, status, abort_flag, 6);
+        ++cs;
         if (!__all_sync(0xffffffffu, wt)) { ok = false; break; }
         tc_fence_after();
-        uint32_t sv[TILE / 2];  // raw scores of this half row
-        {
-          uint32_t* v = sv;
-          tmem_ld_32x32b_x32(tmem + lane_base + (g & 1) * 128 + h * 64, *reinterpret_cast<uint32_t(*)[32]>(v));
-          tmem_ld_32x32b_x32(tmem + lane_base + (g & 1) * 128 + h * 64 + 32,
-                             *reinterpret_cast<uint32_t(*)[32]>(v + 32));
-          tmem_ld_wait();
-        }
-        if (j == qt) {  // diagonal tile: key index > query index is masked
+        // The row's 128 scores in two halves of 64 (registers): the row max
+        // over both, then P of the half still in registers, then the other
+        // half is read from TMEM again.
+        uint32_t sv[TILE / 2];
+        auto load_half = [&](int hh) {
 #pragma unroll
-          for (int i = 0; i < TILE / 2; ++i)
-            if (h * 64 + i > r) sv[i] = __float_as_uint(-INFINITY);
-        }
-        // row max of this half (raw scores; the scale is positive) as a
-        // tree, then across the two halves
+          for (int c = 0; c < TILE / 2; c += 32)
+            tmem_ld_32x32b_x32(s_cols + hh * 64 + c, *reinterpret_cast<uint32_t(*)[32]>(sv + c));
+          tmem_ld_wait();
+          if (j == tile) {  // diagonal tile: key index > query index is masked
+#pragma unroll
+            for (int i = 0; i < TILE / 2; ++i)
+              if (hh * 64 + i > r) sv[i] = __float_as_uint(-INFINITY);
+          }
+        };
+        // row max (raw scores; the scale is positive) as a tree
         float mx8[8];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) mx8[k] = __uint_as_float(sv[k]);
+        for (int k = 0; k < 8; ++k) mx8[k] = -INFINITY;
 #pragma unroll
-        for (int i = 8; i < TILE / 2; i += 8)
+        for (int hh = 0; hh < 2; ++hh) {
+          load_half(hh);
 #pragma unroll
-          for (int k = 0; k < 8; ++k) mx8[k] = fmaxf(mx8[k], __uint_as_float(sv[i + k]));
-        const float mxh = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                                fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
-        float* rm = red_max + (g & 1) * 2 * TILE;
-        rm[h * TILE + r] = mxh;
-        named_barrier_sync(1 + q, 64);
-        const float mx2 = fmaxf(rm[r], rm[TILE + r]) * sl2;
+          for (int i = 0; i < TILE / 2; i += 8)
+#pragma unroll
+            for (int k = 0; k < 8; ++k) mx8[k] = fmaxf(mx8[k], __uint_as_float(sv[i + k]));
+        }
+        const float mx2 = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                                fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]))) * sl2;
+        // P V of the previous S tile (of this or the previous item) must be
+        // done before O is rescaled or P overwritten
+        if (cs > 1) {
+          bool wp = mbar_wait(pv_done + x, (cs - 2) & 1u, status, abort_flag, 7);
+          if (!__all_sync(0xffffffffu, wp)) { ok = false; break; }
+          tc_fence_after();
+        }
         const bool move = mx2 > m + kRescale;
         if (j > 0 && __any_sync(0xffffffffu, move)) {
-          // rescale this warp's rows of O once the previous P V is done
           const float alpha = move ? ex2_approx(m - mx2) : 1.f;
-          bool wo = mbar_wait(o_full + ((g - 1) & 1), ((g - 1) >> 1) & 1, status, abort_flag, 7);
-          if (!__all_sync(0xffffffffu, wo)) { ok = false; break; }
-          tc_fence_after();
-          uint32_t ov[32];
-          tmem_ld_32x32b_x32(o_cols, ov);
-          tmem_ld_wait();
+#pragma unroll 1
+          for (int c = 0; c < HD; c += 32) {
+            uint32_t ov[32];
+            tmem_ld_32x32b_x32(o_cols + c, ov);
+            tmem_ld_wait();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
-          tmem_st_32x32b_x32(o_cols, ov);
+            for (int i = 0; i < 32; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
+            tmem_st_32x32b_x32(o_cols + c, ov);
+          }
           tmem_st_wait();
           l *= alpha;
         }
@@ -304,47 +335,48 @@ __global__ void __launch_bounds__(320, 1)
         float rs8[8];
 #pragma unroll
         for (int k = 0; k < 8; ++k) rs8[k] = 0.f;
-        uint8_t* pt = sP + (g & 1) * 2 * TILE_BYTES;
 #pragma unroll
-        for (int ch = 0; ch < TILE / 16; ++ch) {
-          float pv[8];
+        for (int hh = 1; hh >= 0; --hh) {
+          if (hh == 0) load_half(0);
 #pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            pv[k] = ex2_approx(fmaf(__uint_as_float(sv[ch * 8 + k]), sl2, -m));
-            rs8[k] += pv[k];
+          for (int ch = 0; ch < TILE / 16; ++ch) {
+            float pv[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              pv[k] = ex2_approx(fmaf(__uint_as_float(sv[ch * 8 + k]), sl2, -m));
+              rs8[k] += pv[k];
+            }
+            st_tile_chunk(pt, r, hh * 8 + ch, pv);
           }
-          st_tile_chunk(pt, r, h * 8 + ch, pv);
         }
         l += ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
         fence_async_smem();
         tc_fence_before();
-        mbar_arrive(p_full + (g & 1));
+        mbar_arrive(p_full + x);
       }
       if (!ok) break;
-      // the item's last P V, then O / l
-      bool wo = mbar_wait(o_full + ((g - 1) & 1), ((g - 1) >> 1) & 1, status, abort_flag, 7);
+      // the tile's last P V, then O / l
+      bool wo = mbar_wait(pv_done + x, (cs - 1) & 1u, status, abort_flag, 7);
       if (!__all_sync(0xffffffffu, wo)) { ok = false; break; }
       tc_fence_after();
-      uint32_t ov[32];
-      tmem_ld_32x32b_x32(o_cols, ov);
+      uint32_t ov[HD];
+      tmem_ld_32x32b_x32(o_cols, *reinterpret_cast<uint32_t(*)[32]>(ov));
+      tmem_ld_32x32b_x32(o_cols + 32, *reinterpret_cast<uint32_t(*)[32]>(ov + 32));
       tmem_ld_wait();
-      red_sum[h * TILE + r] = l;
-      named_barrier_sync(1 + q, 64);
-      const float lt = red_sum[r] + red_sum[TILE + r];
-      const int t = qt * TILE + r;
+      const int t = tile * TILE + r;
       if (t < T) {
-        const float inv = 1.0f / lt;
-        const long long off = (static_cast<long long>(it.b) * T + t) * C + it.h * HD + h * 32;
+        const float inv = 1.0f / l;
+        const long long off = (static_cast<long long>(it.b) * T + t) * C + it.h * HD;
         if (out_f32) {
           float4* dst = reinterpret_cast<float4*>(static_cast<float*>(out_ptr) + off);
 #pragma unroll
-          for (int ch = 0; ch < HD / 8; ++ch)
+          for (int ch = 0; ch < HD / 4; ++ch)
             dst[ch] = make_float4(__uint_as_float(ov[ch * 4]) * inv, __uint_as_float(ov[ch * 4 + 1]) * inv,
                                   __uint_as_float(ov[ch * 4 + 2]) * inv, __uint_as_float(ov[ch * 4 + 3]) * inv);
         } else {
           __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(out_ptr) + off;
 #pragma unroll
-          for (int ch = 0; ch < HD / 16; ++ch) {
+          for (int ch = 0; ch < HD / 8; ++ch) {
             uint4 u;
             u.x = pack_bf16x2(__uint_as_float(ov[ch * 8 + 0]) * inv, __uint_as_float(ov[ch * 8 + 1]) * inv);
             u.y = pack_bf16x2(__uint_as_float(ov[ch * 8 + 2]) * inv, __uint_as_float(ov[ch * 8 + 3]) * inv);
@@ -354,10 +386,9 @@ __global__ void __launch_bounds__(320, 1)
           }
         }
         // natural-log LSE: (m2 + log2 l) * ln 2
-        if (h == 0) lse[static_cast<long long>(it.bh) * T + t] = (m + __log2f(lt)) * 0.6931471805599453f;
+        lse[static_cast<long long>(it.bh) * T + t] = (m + __log2f(l)) * 0.6931471805599453f;
       }
-      // the partner has read red_sum before either side writes it again
-      named_barrier_sync(1 + q, 64);
+      tc_fence_before();
     }
     tc_fence_before();
   }
@@ -922,9 +953,9 @@ int llmk_attention_forward(void* out, llmk_dtype out_dtype, float* lse, const vo
   LLMK_TRY(make_tmap_3d(&tm, qkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, C3, T, B, static_cast<uint64_t>(C3) * 2,
                         static_cast<uint64_t>(T) * C3 * 2, HD, TILE, 1));
   LLMK_TRY(set_smem(reinterpret_cast<const void*>(attn_fwd_kernel), FwdSmem::BYTES));
-  const int nq = (T + TILE - 1) / TILE;
-  const int grid = std::min(nq * B * NH, num_sms());  // persistent: one CTA per SM
-  attn_fwd_kernel<<<grid, 320, FwdSmem::BYTES, static_cast<cudaStream_t>(stream)>>>(
+  const int np = ((T + TILE - 1) / TILE + 1) / 2;  // pairs of query tiles
+  const int grid = std::min(np * B * NH, num_sms());  // persistent: one CTA per SM
+  attn_fwd_kernel<<<grid, kFwdThreads, FwdSmem::BYTES, static_cast<cudaStream_t>(stream)>>>(
       tm, out, out_dtype == LLMK_F32 ? 1 : 0, lse, B, T, NH, C, device_status_ptr());
   count_launch();
   LLMK_CUDA(cudaGetLastError());
