@@ -105,7 +105,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   uint64_t* s_full = kv_empty + S::kStages;      // [A, B]
   uint64_t* p_full = s_full + 2;                 // [A, B]
   uint64_t* pv_done = p_full + 2;                // [A, B]: the tile's latest P V is done
-  uint64_t* done = pv_done + 2;
+  uint64_t* s_free = pv_done + 2;                // [A, B]: the softmax has read S
+  uint64_t* done = s_free + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -122,6 +123,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       mbar_init(s_full + i, 1);
       mbar_init(p_full + i, 128);
       mbar_init(pv_done + i, 1);
+      mbar_init(s_free + i, 128);
     }
     for (int s = 0; s < S::kStages; ++s) {
       mbar_init(kv_full + s, 1);
@@ -182,6 +184,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       uint32_t cp[2] = {0, 0};  // P tiles consumed per query tile
+      uint32_t cf[2] = {0, 0};  // S tiles released per query tile
       bool ok = true;
       int n = 0;
       auto issue_s = [&](int x, int st, int qb) {
@@ -225,21 +228,30 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           const int st = stage;
           if (++stage == S::kStages) { stage = 0; phase ^= 1u; }
           bool next_ready = false;  // K/V tile j+1 (now at `stage`) has landed
+          // S_x(j+1) as soon as the softmax has read S_x(j) ...
+          for (int x = 0; x < 2; ++x) {
+            const int nx = x == 0 ? na : (has_b ? nkv : 0);
+            if (j >= nx) continue;
+            if (!mbar_wait(s_free + x, cf[x] & 1u, status, abort_flag, 8)) { ok = false; break; }
+            ++cf[x];
+            if (j + 1 < nx) {
+              if (!next_ready) {
+                if (!mbar_wait(kv_full + stage, phase, status, abort_flag, 3)) { ok = false; break; }
+                next_ready = true;
+              }
+              tc_fence_after();
+              issue_s(x, stage, q0 + x);
+              if (j + 2 == nx) mma_commit(q_empty + q0 + x);
+            }
+          }
+          if (!ok) break;
+          // ... and P V_x(j) once P_x(j) is in shared memory
           for (int x = 0; x < 2; ++x) {
             const int nx = x == 0 ? na : (has_b ? nkv : 0);
             if (j >= nx) continue;
             if (!mbar_wait(p_full + x, cp[x] & 1u, status, abort_flag, 4)) { ok = false; break; }
             ++cp[x];
             tc_fence_after();
-            if (j + 1 < nx) {
-              if (!next_ready) {
-                if (!mbar_wait(kv_full + stage, phase, status, abort_flag, 3)) { ok = false; break; }
-                tc_fence_after();
-                next_ready = true;
-              }
-              issue_s(x, stage, q0 + x);
-              if (j + 2 == nx) mma_commit(q_empty + q0 + x);
-            }
             issue_pv(x, st, j > 0);
           }
           if (!ok) break;
@@ -280,35 +292,28 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         ++cs;
         if (!__all_sync(0xffffffffu, wt)) { ok = false; break; }
         tc_fence_after();
-        // The row's 128 scores in two halves of 64 (registers): the row max
-        // over both, then P of the half still in registers, then the other
-        // half is read from TMEM again.
-        uint32_t sv[TILE / 2];
-        auto load_half = [&](int hh) {
+        // the row's 128 scores in registers; S_x is then free for the next tile
+        uint32_t sv[TILE];
 #pragma unroll
-          for (int c = 0; c < TILE / 2; c += 32)
-            tmem_ld_32x32b_x32(s_cols + hh * 64 + c, *reinterpret_cast<uint32_t(*)[32]>(sv + c));
-          tmem_ld_wait();
-          if (j == tile) {  // diagonal tile: key index > query index is masked
+        for (int c = 0; c < TILE; c += 32)
+          tmem_ld_32x32b_x32(s_cols + c, *reinterpret_cast<uint32_t(*)[32]>(sv + c));
+        tmem_ld_wait();
+        tc_fence_before();
+        mbar_arrive(s_free + x);
+        if (j == tile) {  // diagonal tile: key index > query index is masked
 #pragma unroll
-            for (int i = 0; i < TILE / 2; ++i)
-              if (hh * 64 + i > r) sv[i] = __float_as_uint(-INFINITY);
-          }
-        };
-        // row max (raw scores; the scale is positive) as a tree
-        float mx8[8];
-#pragma unroll
-        for (int k = 0; k < 8; ++k) mx8[k] = -INFINITY;
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          load_half(hh);
-#pragma unroll
-          for (int i = 0; i < TILE / 2; i += 8)
-#pragma unroll
-            for (int k = 0; k < 8; ++k) mx8[k] = fmaxf(mx8[k], __uint_as_float(sv[i + k]));
+          for (int i = 0; i < TILE; ++i)
+            if (i > r) sv[i] = __float_as_uint(-INFINITY);
         }
-        const float mx2 = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                                fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]))) * sl2;
+        // row max (raw scores; the scale is positive) as a tree
+        float mx4[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) mx4[k] = __uint_as_float(sv[k]);
+#pragma unroll
+        for (int i = 4; i < TILE; i += 4)
+#pragma unroll
+          for (int k = 0; k < 4; ++k) mx4[k] = fmaxf(mx4[k], __uint_as_float(sv[i + k]));
+        const float mx2 = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * sl2;
         // P V of the previous S tile (of this or the previous item) must be
         // done before O is rescaled or P overwritten
         if (cs > 1) {
@@ -320,13 +325,13 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         if (j > 0 && __any_sync(0xffffffffu, move)) {
           const float alpha = move ? ex2_approx(m - mx2) : 1.f;
 #pragma unroll 1
-          for (int c = 0; c < HD; c += 32) {
-            uint32_t ov[32];
-            tmem_ld_32x32b_x32(o_cols + c, ov);
+          for (int c = 0; c < HD; c += 16) {
+            uint32_t ov[16];
+            tmem_ld_32x32b_x16(o_cols + c, ov);
             tmem_ld_wait();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
-            tmem_st_32x32b_x32(o_cols + c, ov);
+            for (int i = 0; i < 16; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
+            tmem_st_32x32b_x16(o_cols + c, ov);
           }
           tmem_st_wait();
           l *= alpha;
@@ -336,18 +341,18 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 #pragma unroll
         for (int k = 0; k < 8; ++k) rs8[k] = 0.f;
 #pragma unroll
-        for (int hh = 1; hh >= 0; --hh) {
-          if (hh == 0) load_half(0);
+        for (int ch = 0; ch < TILE / 8; ++ch) {
+          uint32_t pk[4];
 #pragma unroll
-          for (int ch = 0; ch < TILE / 16; ++ch) {
-            float pv[8];
-#pragma unroll
-            for (int k = 0; k < 8; ++k) {
-              pv[k] = ex2_approx(fmaf(__uint_as_float(sv[ch * 8 + k]), sl2, -m));
-              rs8[k] += pv[k];
-            }
-            st_tile_chunk(pt, r, hh * 8 + ch, pv);
+          for (int k = 0; k < 4; ++k) {
+            const float p0 = ex2_approx(fmaf(__uint_as_float(sv[ch * 8 + 2 * k]), sl2, -m));
+            const float p1 = ex2_approx(fmaf(__uint_as_float(sv[ch * 8 + 2 * k + 1]), sl2, -m));
+            rs8[2 * k] += p0;
+            rs8[2 * k + 1] += p1;
+            pk[k] = pack_bf16x2(p0, p1);
           }
+          *reinterpret_cast<uint4*>(pt + (ch >> 3) * TILE_BYTES + sw128(r, ch & 7)) =
+              make_uint4(pk[0], pk[1], pk[2], pk[3]);
         }
         l += ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
         fence_async_smem();
