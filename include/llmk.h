@@ -27,7 +27,7 @@
 extern "C" {
 #endif
 
-typedef enum llmk_dtype { LLMK_F32 = 0, LLMK_BF16 = 1 } llmk_dtype;
+typedef enum llmk_dtype { LLMK_F32 = 0, LLMK_BF16 = 1, LLMK_F16 = 2 } llmk_dtype;
 
 /* Operand precision of the tensor-core contractions.
  *   LLMK_MATH_BF16: A/B operands are bf16 in memory, fp32 accumulation.
@@ -137,29 +137,32 @@ int llmk_colsum(float* dbias, const void* x, llmk_dtype x_dtype, int M, int N, i
 int llmk_colsum_noalloc(float* dbias, const void* x, llmk_dtype x_dtype, int M, int N, int accumulate, void* stream);
 
 /* ------------------------------------------------------------ attention */
-/* Causal multi-head attention, head size 64, bf16 tensor-core operands, fp32
- * softmax and accumulation. qkv: (B, T, C3) bf16, Q|K|V blocks of C = C3/3
- * columns, head h at columns h*64 of each block. out: (B, T, C) in out_dtype
- * (bf16, or fp32 to skip the output rounding). lse: (B, NH, T) fp32
- * natural-log logsumexp of the scaled scores (scale 1/8). Any T >= 1.
+/* Causal multi-head attention, head size 64, 16-bit tensor-core operands
+ * (qkv_dtype: LLMK_BF16, or LLMK_F16 for 3 more mantissa bits where values
+ * stay inside fp16 range), fp32 softmax and accumulation. qkv: (B, T, C3),
+ * Q|K|V blocks of C = C3/3 columns, head h at columns h*64 of each block.
+ * out: (B, T, C) in out_dtype (qkv_dtype, or fp32 to skip the output
+ * rounding). lse: (B, NH, T) fp32 natural-log logsumexp of the scaled scores
+ * (scale 1/8). Any T >= 1.
  * Replaces gpt2cuda::BatchCausalAttentionForward, gpt2/cuda/attention.cu:119-133
  * (AttentionForwardCUDA, kernel/flash_attn/flash_fwd_launch.cuh:18-68, which
  * requires T % 128 == 0). */
-int llmk_attention_forward(void* out, llmk_dtype out_dtype, float* lse, const void* qkv, int B, int T, int C3, int NH,
-                           void* stream);
+int llmk_attention_forward(void* out, llmk_dtype out_dtype, float* lse, const void* qkv, llmk_dtype qkv_dtype, int B,
+                           int T, int C3, int NH, void* stream);
 
 /* Gradient of llmk_attention_forward. dout, out (B, T, C) and dqkv (B, T, C3)
- * are in io_dtype (bf16, or fp32: D = rowsum(dO * O) and the dQ/dK/dV stores
- * then skip bf16 rounding; dO still enters the MMAs as bf16). qkv is bf16.
+ * are in io_dtype (qkv_dtype, or fp32: D = rowsum(dO * O) and the dQ/dK/dV
+ * stores then skip the 16-bit rounding; dO still enters the MMAs in
+ * qkv_dtype). qkv is in qkv_dtype (LLMK_BF16 or LLMK_F16), as in the forward.
  * dqkv is OVERWRITTEN (dQ, dK and dV); the reference accumulates dQ and
  * overwrites dK/dV (flash_bwd_kernel.cuh:377-472) on buffers its callers zero
  * first. workspace >= llmk_attention_backward_workspace(): D, an fp32 dQ
- * accumulator and a bf16 copy of dO.
+ * accumulator and a 16-bit copy of dO.
  * Replaces gpt2cuda::BatchCausalAttentionBackward, gpt2/cuda/attention.cu:135-148. */
 size_t llmk_attention_backward_workspace(int B, int T, int C3, int NH);
 int llmk_attention_backward(void* dqkv, const void* dout, const void* out, llmk_dtype io_dtype, const void* qkv,
-                            const float* lse, int B, int T, int C3, int NH, void* workspace, size_t workspace_bytes,
-                            void* stream);
+                            llmk_dtype qkv_dtype, const float* lse, int B, int T, int C3, int NH, void* workspace,
+                            size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------ layernorm */
 /* out = (inp - mean) * rstd * gamma + beta over rows of C (eps 1e-5, two-pass

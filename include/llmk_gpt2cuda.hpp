@@ -12,7 +12,7 @@
 //
 // Precision: the reference's fp32 GEMMs run as TF32 on the tensor cores
 // (its CUTLASS Sm80 kernels are TF32, gpt2/cuda/matmul.cu:195-220); attention
-// runs the bf16 tcgen05 kernels on bf16 copies of its fp32 operands (the
+// runs the tcgen05 kernels on fp16 copies of its fp32 operands (the
 // reference's FA-2 rounds to tf32/fp16/bf16 internally, config.cuh:56,163-165).
 #pragma once
 
@@ -94,9 +94,10 @@ void BatchCausalAttentionForward(Vec& outputs, Vec& logsumexp, const Vec& inputs
                                  cudaStream_t stream) {
   const long long n_in = 1LL * B * T * C3;
   void* qkv = llmk_detail::scratch(n_in * 2, 1);
-  llmk_detail::check(llmk_cast(qkv, LLMK_BF16, inputs.data(), LLMK_F32, n_in, stream), "BatchCausalAttentionForward");
-  llmk_detail::check(llmk_attention_forward(outputs.data(), LLMK_F32, logsumexp.data(), qkv, B, T, C3, NH, stream),
-                     "BatchCausalAttentionForward");
+  llmk_detail::check(llmk_cast(qkv, LLMK_F16, inputs.data(), LLMK_F32, n_in, stream), "BatchCausalAttentionForward");
+  llmk_detail::check(
+      llmk_attention_forward(outputs.data(), LLMK_F32, logsumexp.data(), qkv, LLMK_F16, B, T, C3, NH, stream),
+      "BatchCausalAttentionForward");
 }
 
 // gpt2/cuda/attention.cu:135-148. d_inputs (B,T,3C) accumulates dQ, dK, dV;
@@ -113,9 +114,9 @@ void BatchCausalAttentionBackward(Vec& d_inputs, Vec& att_D, const Vec& d_output
   float* dq32 = reinterpret_cast<float*>(base + n_in * 2);
   void* work = base + n_in * 6;
   const char* w = "BatchCausalAttentionBackward";
-  llmk_detail::check(llmk_cast(qkv, LLMK_BF16, inputs.data(), LLMK_F32, n_in, stream), w);
-  llmk_detail::check(llmk_attention_backward(dq32, d_outputs.data(), outputs.data(), LLMK_F32, qkv, logsumexp.data(), B,
-                                             T, C3, NH, work, ws, stream),
+  llmk_detail::check(llmk_cast(qkv, LLMK_F16, inputs.data(), LLMK_F32, n_in, stream), w);
+  llmk_detail::check(llmk_attention_backward(dq32, d_outputs.data(), outputs.data(), LLMK_F32, qkv, LLMK_F16,
+                                             logsumexp.data(), B, T, C3, NH, work, ws, stream),
                      w);
   llmk_detail::check(llmk_residual_forward(d_inputs.data(), d_inputs.data(), dq32, LLMK_F32, n_in, stream), w);
 }

@@ -26,6 +26,7 @@
 // next query tile runs. D = rowsum(dO * O) and the final dQ scaling run as
 // small pre/post kernels.
 #include <algorithm>
+#include <type_traits>
 
 #include "ptx.cuh"
 #include "runtime.h"
@@ -41,14 +42,16 @@ constexpr int TILE_BYTES = TILE * HD * 2;  // 16 KB: one [128 x 64] bf16 tile, 1
 // 128B-swizzled atom column (TMA SWIZZLE_128B / UMMA SWIZZLE_128B pattern).
 __device__ __forceinline__ uint32_t sw128(int r, int c) { return r * 128 + ((c ^ (r & 7)) << 4); }
 
-// Writes 8 fp32 as bf16 into row r, chunk c of a [128 x 128] bf16 K-major
-// tile stored as two 16 KB atom columns.
+// Writes 8 fp32 as the 16-bit operand type (kF16: fp16, else bf16) into row
+// r, chunk c of a [128 x 128] 16-bit K-major tile stored as two 16 KB atom
+// columns.
+template <bool kF16>
 __device__ __forceinline__ void st_tile_chunk(uint8_t* tile, int r, int chunk, const float* v) {
   uint4 u;
-  u.x = pack_bf16x2(v[0], v[1]);
-  u.y = pack_bf16x2(v[2], v[3]);
-  u.z = pack_bf16x2(v[4], v[5]);
-  u.w = pack_bf16x2(v[6], v[7]);
+  u.x = pack16x2<kF16>(v[0], v[1]);
+  u.y = pack16x2<kF16>(v[2], v[3]);
+  u.z = pack16x2<kF16>(v[4], v[5]);
+  u.w = pack16x2<kF16>(v[6], v[7]);
   *reinterpret_cast<uint4*>(tile + (chunk >> 3) * TILE_BYTES + sw128(r, chunk & 7)) = u;
 }
 
@@ -88,6 +91,7 @@ struct FwdSmem {
 };
 constexpr int kFwdThreads = 320;
 
+template <bool kF16>
 __global__ void __launch_bounds__(kFwdThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, void* __restrict__ out_ptr, int out_f32,
                     float* __restrict__ lse, int B, int T, int NH, int C, unsigned int* status) {
@@ -178,9 +182,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       // S = Q K^T: M=128 queries, N=128 keys, both K-major (hd contiguous).
-      const uint32_t idesc_s = idesc_f32acc(128, 128, kFmtBF16, false, false);
+      constexpr uint32_t kFmt = kF16 ? kFmtF16 : kFmtBF16;
+      const uint32_t idesc_s = idesc_f32acc(128, 128, kFmt, false, false);
       // O += P V: M=128 queries, N=64 hd, K=128 keys; V is [keys][hd] = N-major.
-      const uint32_t idesc_o = idesc_f32acc(128, HD, kFmtBF16, false, true);
+      const uint32_t idesc_o = idesc_f32acc(128, HD, kFmt, false, true);
       int stage = 0;
       uint32_t phase = 0;
       uint32_t cp[2] = {0, 0};  // P tiles consumed per query tile
@@ -349,7 +354,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             const float p1 = ex2_approx(fmaf(__uint_as_float(sv[ch * 8 + 2 * k + 1]), sl2, -m));
             rs8[2 * k] += p0;
             rs8[2 * k + 1] += p1;
-            pk[k] = pack_bf16x2(p0, p1);
+            pk[k] = pack16x2<kF16>(p0, p1);
           }
           *reinterpret_cast<uint4*>(pt + (ch >> 3) * TILE_BYTES + sw128(r, ch & 7)) =
               make_uint4(pk[0], pk[1], pk[2], pk[3]);
@@ -379,14 +384,14 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             dst[ch] = make_float4(__uint_as_float(ov[ch * 4]) * inv, __uint_as_float(ov[ch * 4 + 1]) * inv,
                                   __uint_as_float(ov[ch * 4 + 2]) * inv, __uint_as_float(ov[ch * 4 + 3]) * inv);
         } else {
-          __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(out_ptr) + off;
+          uint16_t* dst = static_cast<uint16_t*>(out_ptr) + off;
 #pragma unroll
           for (int ch = 0; ch < HD / 8; ++ch) {
             uint4 u;
-            u.x = pack_bf16x2(__uint_as_float(ov[ch * 8 + 0]) * inv, __uint_as_float(ov[ch * 8 + 1]) * inv);
-            u.y = pack_bf16x2(__uint_as_float(ov[ch * 8 + 2]) * inv, __uint_as_float(ov[ch * 8 + 3]) * inv);
-            u.z = pack_bf16x2(__uint_as_float(ov[ch * 8 + 4]) * inv, __uint_as_float(ov[ch * 8 + 5]) * inv);
-            u.w = pack_bf16x2(__uint_as_float(ov[ch * 8 + 6]) * inv, __uint_as_float(ov[ch * 8 + 7]) * inv);
+            u.x = pack16x2<kF16>(__uint_as_float(ov[ch * 8 + 0]) * inv, __uint_as_float(ov[ch * 8 + 1]) * inv);
+            u.y = pack16x2<kF16>(__uint_as_float(ov[ch * 8 + 2]) * inv, __uint_as_float(ov[ch * 8 + 3]) * inv);
+            u.z = pack16x2<kF16>(__uint_as_float(ov[ch * 8 + 4]) * inv, __uint_as_float(ov[ch * 8 + 5]) * inv);
+            u.w = pack16x2<kF16>(__uint_as_float(ov[ch * 8 + 6]) * inv, __uint_as_float(ov[ch * 8 + 7]) * inv);
             reinterpret_cast<uint4*>(dst)[ch] = u;
           }
         }
@@ -415,6 +420,16 @@ __device__ __forceinline__ void load8f(const __nv_bfloat16* p, float* v) {
     v[2 * i + 1] = u.y;
   }
 }
+__device__ __forceinline__ void load8f(const __half* p, float* v) {
+  uint4 a = *reinterpret_cast<const uint4*>(p);
+  const __half2* x = reinterpret_cast<const __half2*>(&a);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 u = __half22float2(x[i]);
+    v[2 * i] = u.x;
+    v[2 * i + 1] = u.y;
+  }
+}
 __device__ __forceinline__ void load8f(const float* p, float* v) {
   float4 a = reinterpret_cast<const float4*>(p)[0], b = reinterpret_cast<const float4*>(p)[1];
   v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
@@ -424,10 +439,11 @@ __device__ __forceinline__ void load8f(const float* p, float* v) {
 // (b,t), and zeroes the row's dq_acc. One warp per row: lane l reads the
 // 16-byte chunks l, l+32, ... of dO and O (8 chunks per head, so each head's
 // sum is a reduction over 8 consecutive lanes). With fp32 dO / O (IoT =
-// float) it also writes the bf16 copy of dO the MMAs read (dout16).
-template <typename IoT>
+// float) it also writes the 16-bit copy of dO the MMAs read (dout16, fp16
+// when kF16, else bf16).
+template <typename IoT, bool kF16>
 __global__ void __launch_bounds__(256) attn_bwd_pre_kernel(float* __restrict__ D, float* __restrict__ dq_acc,
-                                                           __nv_bfloat16* __restrict__ dout16,
+                                                           uint16_t* __restrict__ dout16,
                                                            const IoT* __restrict__ dout, const IoT* __restrict__ o,
                                                            int B, int T, int NH, int C) {
   const long long bt = blockIdx.x * 8LL + (threadIdx.x >> 5);  // row (b, t)
@@ -448,10 +464,10 @@ __global__ void __launch_bounds__(256) attn_bwd_pre_kernel(float* __restrict__ D
       for (int i = 0; i < 8; ++i) s += x[i] * y[i];
       if constexpr (sizeof(IoT) == 4) {
         uint4 u;
-        u.x = pack_bf16x2(x[0], x[1]);
-        u.y = pack_bf16x2(x[2], x[3]);
-        u.z = pack_bf16x2(x[4], x[5]);
-        u.w = pack_bf16x2(x[6], x[7]);
+        u.x = pack16x2<kF16>(x[0], x[1]);
+        u.y = pack16x2<kF16>(x[2], x[3]);
+        u.z = pack16x2<kF16>(x[4], x[5]);
+        u.w = pack16x2<kF16>(x[6], x[7]);
         *reinterpret_cast<uint4*>(dout16 + bt * C + 8 * c) = u;
       }
     }
@@ -465,8 +481,8 @@ __global__ void __launch_bounds__(256) attn_bwd_pre_kernel(float* __restrict__ D
   for (int k = lane; k < C / 4; k += 32) z[k] = make_float4(0.f, 0.f, 0.f, 0.f);
 }
 
-// dqkv[:, :, 0:C] = dq_acc * scale (bf16 or fp32)
-template <typename IoT>
+// dqkv[:, :, 0:C] = dq_acc * scale (fp32, or 16-bit: fp16 when kF16, else bf16)
+template <typename IoT, bool kF16>
 __global__ void attn_bwd_post_kernel(IoT* __restrict__ dqkv, const float* __restrict__ dq_acc, int BT, int C,
                                      float scale) {
   const long long n8 = static_cast<long long>(BT) * C / 8;
@@ -483,10 +499,10 @@ __global__ void attn_bwd_post_kernel(IoT* __restrict__ dqkv, const float* __rest
       d[1] = make_float4(bb.x * scale, bb.y * scale, bb.z * scale, bb.w * scale);
     } else {
       uint4 u;
-      u.x = pack_bf16x2(a.x * scale, a.y * scale);
-      u.y = pack_bf16x2(a.z * scale, a.w * scale);
-      u.z = pack_bf16x2(bb.x * scale, bb.y * scale);
-      u.w = pack_bf16x2(bb.z * scale, bb.w * scale);
+      u.x = pack16x2<kF16>(a.x * scale, a.y * scale);
+      u.y = pack16x2<kF16>(a.z * scale, a.w * scale);
+      u.z = pack16x2<kF16>(bb.x * scale, bb.y * scale);
+      u.w = pack16x2<kF16>(bb.z * scale, bb.w * scale);
       *reinterpret_cast<uint4*>(dqkv + bt * 3 * C + c) = u;
     }
   }
@@ -551,7 +567,7 @@ __device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, 
 // LSE2 / D of those columns (smem, read as broadcast vectors). kMask: the
 // diagonal tile (query < key masked) or a tile reaching past T (padded
 // queries masked).
-template <bool kMask, int kCols>
+template <bool kMask, int kCols, bool kF16>
 __device__ __forceinline__ void bwd_p_ds(const uint32_t* sv, const uint32_t* dv, const float* ld_l2,
                                          const float* ld_d, int tq0, int key, int T, uint8_t* p_tile,
                                          uint8_t* ds_tile, int r, int chunk0) {
@@ -572,11 +588,12 @@ __device__ __forceinline__ void bwd_p_ds(const uint32_t* sv, const uint32_t* dv,
       p[k] = pv;
       ds[k] = pv * (__uint_as_float(dv[c * 8 + k]) - dd[k]);
     }
-    st_tile_chunk(p_tile, r, chunk0 + c, p);
-    st_tile_chunk(ds_tile, r, chunk0 + c, ds);
+    st_tile_chunk<kF16>(p_tile, r, chunk0 + c, p);
+    st_tile_chunk<kF16>(ds_tile, r, chunk0 + c, ds);
   }
 }
 
+template <bool kF16>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_do,
                     void* __restrict__ dqkv_ptr, int io_f32, float* __restrict__ dq_acc,
@@ -696,12 +713,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       // S^T = K Q^T and dP^T = V dO^T: M=128 keys, N=128 q, K=64 (all K-major).
-      const uint32_t idesc_s = idesc_f32acc(128, 128, kFmtBF16, false, false);
+      constexpr uint32_t kFmt = kF16 ? kFmtF16 : kFmtBF16;
+      const uint32_t idesc_s = idesc_f32acc(128, 128, kFmt, false, false);
       // dV += P^T dO, dK += dS^T Q: M=128 keys, N=64, K=128 q; B is [q][hd] = N-major.
-      const uint32_t idesc_kv = idesc_f32acc(128, HD, kFmtBF16, false, true);
+      const uint32_t idesc_kv = idesc_f32acc(128, HD, kFmt, false, true);
       // dQ = dS K: M=128 q, N=64, K=128 keys; A = dS^T stored [keys][q] = M-major;
       // B = K stored [keys][hd] = N-major.
-      const uint32_t idesc_q = idesc_f32acc(128, HD, kFmtBF16, true, true);
+      const uint32_t idesc_q = idesc_f32acc(128, HD, kFmt, true, true);
       const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV);
       auto issue_sdp = [&](int st) {
         const uint32_t q_addr = smem_u32(sQD + st * 2 * TILE_BYTES);
@@ -826,14 +844,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
               dst[ch] = make_float4(__uint_as_float(x[ch * 4]) * sc, __uint_as_float(x[ch * 4 + 1]) * sc,
                                     __uint_as_float(x[ch * 4 + 2]) * sc, __uint_as_float(x[ch * 4 + 3]) * sc);
           } else {
-            __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(dqkv_ptr) + off;
+            uint16_t* dst = static_cast<uint16_t*>(dqkv_ptr) + off;
 #pragma unroll
             for (int ch = 0; ch < 2; ++ch) {
               uint4 u;
-              u.x = pack_bf16x2(__uint_as_float(x[ch * 8 + 0]) * sc, __uint_as_float(x[ch * 8 + 1]) * sc);
-              u.y = pack_bf16x2(__uint_as_float(x[ch * 8 + 2]) * sc, __uint_as_float(x[ch * 8 + 3]) * sc);
-              u.z = pack_bf16x2(__uint_as_float(x[ch * 8 + 4]) * sc, __uint_as_float(x[ch * 8 + 5]) * sc);
-              u.w = pack_bf16x2(__uint_as_float(x[ch * 8 + 6]) * sc, __uint_as_float(x[ch * 8 + 7]) * sc);
+              u.x = pack16x2<kF16>(__uint_as_float(x[ch * 8 + 0]) * sc, __uint_as_float(x[ch * 8 + 1]) * sc);
+              u.y = pack16x2<kF16>(__uint_as_float(x[ch * 8 + 2]) * sc, __uint_as_float(x[ch * 8 + 3]) * sc);
+              u.z = pack16x2<kF16>(__uint_as_float(x[ch * 8 + 4]) * sc, __uint_as_float(x[ch * 8 + 5]) * sc);
+              u.w = pack16x2<kF16>(__uint_as_float(x[ch * 8 + 6]) * sc, __uint_as_float(x[ch * 8 + 7]) * sc);
               reinterpret_cast<uint4*>(dst)[ch] = u;
             }
           }
@@ -892,10 +910,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         const int tq0 = qt * TILE + cq * kBwdCols;
         const float* ld = sLD + stage * 2 * TILE + cq * kBwdCols;
         if (qt == kt || qt * TILE + TILE > T)
-          bwd_p_ds<true, kBwdCols>(sv, dv, ld, ld + TILE, tq0, k0 + r, T, p_tile, p_tile + 2 * TILE_BYTES, r,
+          bwd_p_ds<true, kBwdCols, kF16>(sv, dv, ld, ld + TILE, tq0, k0 + r, T, p_tile, p_tile + 2 * TILE_BYTES, r,
                                    cq * kBwdCols / 8);
         else
-          bwd_p_ds<false, kBwdCols>(sv, dv, ld, ld + TILE, tq0, k0 + r, T, p_tile, p_tile + 2 * TILE_BYTES, r,
+          bwd_p_ds<false, kBwdCols, kF16>(sv, dv, ld, ld + TILE, tq0, k0 + r, T, p_tile, p_tile + 2 * TILE_BYTES, r,
                                     cq * kBwdCols / 8);
         fence_async_smem();
         tc_fence_before();
@@ -921,14 +939,22 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   }
 }
 
+// Raises a kernel's dynamic shared memory limit once per (kernel, device).
 int set_smem(const void* k, size_t bytes) {
-  static bool done_fwd[64] = {}, done_bwd[64] = {};
+  static const void* kernels[8] = {};
+  static bool done[8][64] = {};
   int dev = 0;
   LLMK_CUDA(cudaGetDevice(&dev));
-  bool* d = (k == reinterpret_cast<const void*>(attn_fwd_kernel)) ? done_fwd : done_bwd;
-  if (dev < 64 && !d[dev]) {
+  int slot = 0;
+  while (slot < 8 && kernels[slot] && kernels[slot] != k) ++slot;
+  if (slot == 8 || dev >= 64) {
     LLMK_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes)));
-    d[dev] = true;
+    return LLMK_OK;
+  }
+  kernels[slot] = k;
+  if (!done[slot][dev]) {
+    LLMK_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes)));
+    done[slot][dev] = true;
   }
   return LLMK_OK;
 }
@@ -947,20 +973,25 @@ using namespace llmk;
 
 extern "C" {
 
-int llmk_attention_forward(void* out, llmk_dtype out_dtype, float* lse, const void* qkv, int B, int T, int C3, int NH,
-                           void* stream) {
+int llmk_attention_forward(void* out, llmk_dtype out_dtype, float* lse, const void* qkv, llmk_dtype qkv_dtype, int B,
+                           int T, int C3, int NH, void* stream) {
   if (!out || !lse || !qkv) return fail(LLMK_ERR_INVALID_ARG, "attention_forward: null pointer");
   LLMK_TRY(check_shapes(B, T, C3, NH));
-  if (out_dtype != LLMK_BF16 && out_dtype != LLMK_F32) return fail(LLMK_ERR_UNSUPPORTED, "attention_forward: out dtype");
+  if (qkv_dtype != LLMK_BF16 && qkv_dtype != LLMK_F16)
+    return fail(LLMK_ERR_UNSUPPORTED, "attention_forward: qkv dtype (bf16 or fp16)");
+  if (out_dtype != qkv_dtype && out_dtype != LLMK_F32)
+    return fail(LLMK_ERR_UNSUPPORTED, "attention_forward: out dtype (qkv's or fp32)");
   if (!aligned16(out) || !aligned16(qkv)) return fail(LLMK_ERR_UNSUPPORTED, "attention_forward: alignment");
+  const bool f16 = qkv_dtype == LLMK_F16;
   const int C = C3 / 3;
   CUtensorMap tm;
-  LLMK_TRY(make_tmap_3d(&tm, qkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, C3, T, B, static_cast<uint64_t>(C3) * 2,
-                        static_cast<uint64_t>(T) * C3 * 2, HD, TILE, 1));
-  LLMK_TRY(set_smem(reinterpret_cast<const void*>(attn_fwd_kernel), FwdSmem::BYTES));
+  LLMK_TRY(make_tmap_3d(&tm, qkv, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, C3, T, B,
+                        static_cast<uint64_t>(C3) * 2, static_cast<uint64_t>(T) * C3 * 2, HD, TILE, 1));
+  auto kern = f16 ? attn_fwd_kernel<true> : attn_fwd_kernel<false>;
+  LLMK_TRY(set_smem(reinterpret_cast<const void*>(kern), FwdSmem::BYTES));
   const int np = ((T + TILE - 1) / TILE + 1) / 2;  // pairs of query tiles
   const int grid = std::min(np * B * NH, num_sms());  // persistent: one CTA per SM
-  attn_fwd_kernel<<<grid, kFwdThreads, FwdSmem::BYTES, static_cast<cudaStream_t>(stream)>>>(
+  kern<<<grid, kFwdThreads, FwdSmem::BYTES, static_cast<cudaStream_t>(stream)>>>(
       tm, out, out_dtype == LLMK_F32 ? 1 : 0, lse, B, T, NH, C, device_status_ptr());
   count_launch();
   LLMK_CUDA(cudaGetLastError());
@@ -970,7 +1001,7 @@ int llmk_attention_forward(void* out, llmk_dtype out_dtype, float* lse, const vo
 static size_t attn_ws_parts(int B, int T, int C, int NH, size_t* dq_off, size_t* do16_off) {
   const size_t d = ((static_cast<size_t>(B) * NH * T * sizeof(float) + 255) / 256) * 256;
   const size_t dq = ((static_cast<size_t>(B) * T * C * sizeof(float) + 255) / 256) * 256;
-  const size_t do16 = static_cast<size_t>(B) * T * C * sizeof(__nv_bfloat16);
+  const size_t do16 = static_cast<size_t>(B) * T * C * 2;
   if (dq_off) *dq_off = d;
   if (do16_off) *do16_off = d + dq;
   return d + dq + do16;
@@ -981,53 +1012,73 @@ size_t llmk_attention_backward_workspace(int B, int T, int C3, int NH) {
   return attn_ws_parts(B, T, C3 / 3, NH, nullptr, nullptr);
 }
 
-int llmk_attention_backward(void* dqkv, const void* dout, const void* out, llmk_dtype io_dtype, const void* qkv,
-                            const float* lse, int B, int T, int C3, int NH, void* workspace, size_t workspace_bytes,
-                            void* stream) {
-  if (!dqkv || !dout || !out || !qkv || !lse) return fail(LLMK_ERR_INVALID_ARG, "attention_backward: null pointer");
-  LLMK_TRY(check_shapes(B, T, C3, NH));
-  if (io_dtype != LLMK_BF16 && io_dtype != LLMK_F32) return fail(LLMK_ERR_UNSUPPORTED, "attention_backward: io dtype");
-  if (!aligned16(dqkv) || !aligned16(dout) || !aligned16(out) || !aligned16(qkv))
-    return fail(LLMK_ERR_UNSUPPORTED, "attention_backward: alignment");
-  if (!workspace || workspace_bytes < llmk_attention_backward_workspace(B, T, C3, NH) || !aligned16(workspace))
-    return fail(LLMK_ERR_WORKSPACE, "attention_backward: workspace too small");
+}  // extern "C"
+
+namespace {
+
+template <bool kF16>
+int attention_backward_t(void* dqkv, const void* dout, const void* out, bool f32, const void* qkv, const float* lse,
+                         int B, int T, int C3, int NH, void* workspace, cudaStream_t s) {
+  using T16 = typename std::conditional<kF16, __half, __nv_bfloat16>::type;
   const int C = C3 / 3;
-  const bool f32 = io_dtype == LLMK_F32;
   size_t dq_off, do16_off;
   attn_ws_parts(B, T, C, NH, &dq_off, &do16_off);
   float* Dv = static_cast<float*>(workspace);
   float* dq = reinterpret_cast<float*>(static_cast<char*>(workspace) + dq_off);
-  __nv_bfloat16* do16 = reinterpret_cast<__nv_bfloat16*>(static_cast<char*>(workspace) + do16_off);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint16_t* do16 = reinterpret_cast<uint16_t*>(static_cast<char*>(workspace) + do16_off);
   const long long rows = static_cast<long long>(B) * T;  // one warp per (b, t)
   const int pre_grid = static_cast<int>((rows + 7) / 8);
   if (f32)
-    attn_bwd_pre_kernel<float><<<pre_grid, 256, 0, s>>>(Dv, dq, do16, static_cast<const float*>(dout),
-                                                        static_cast<const float*>(out), B, T, NH, C);
+    attn_bwd_pre_kernel<float, kF16><<<pre_grid, 256, 0, s>>>(Dv, dq, do16, static_cast<const float*>(dout),
+                                                              static_cast<const float*>(out), B, T, NH, C);
   else
-    attn_bwd_pre_kernel<__nv_bfloat16><<<pre_grid, 256, 0, s>>>(
-        Dv, dq, nullptr, static_cast<const __nv_bfloat16*>(dout), static_cast<const __nv_bfloat16*>(out), B, T, NH, C);
-  // the MMAs read dO as bf16: the caller's buffer, or the copy the pre-pass made
+    attn_bwd_pre_kernel<T16, kF16><<<pre_grid, 256, 0, s>>>(Dv, dq, nullptr, static_cast<const T16*>(dout),
+                                                            static_cast<const T16*>(out), B, T, NH, C);
+  // the MMAs read dO in the operand type: the caller's buffer, or the copy the pre-pass made
   const void* dout_mma = f32 ? static_cast<const void*>(do16) : dout;
+  const CUtensorMapDataType dt = kF16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   CUtensorMap tq, td;
-  LLMK_TRY(make_tmap_3d(&tq, qkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, C3, T, B, static_cast<uint64_t>(C3) * 2,
-                        static_cast<uint64_t>(T) * C3 * 2, HD, TILE, 1));
-  LLMK_TRY(make_tmap_3d(&td, dout_mma, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, C, T, B, static_cast<uint64_t>(C) * 2,
-                        static_cast<uint64_t>(T) * C * 2, HD, TILE, 1));
-  LLMK_TRY(set_smem(reinterpret_cast<const void*>(attn_bwd_kernel), BwdSmem::BYTES));
+  LLMK_TRY(make_tmap_3d(&tq, qkv, dt, C3, T, B, static_cast<uint64_t>(C3) * 2, static_cast<uint64_t>(T) * C3 * 2, HD,
+                        TILE, 1));
+  LLMK_TRY(make_tmap_3d(&td, dout_mma, dt, C, T, B, static_cast<uint64_t>(C) * 2, static_cast<uint64_t>(T) * C * 2, HD,
+                        TILE, 1));
+  LLMK_TRY(set_smem(reinterpret_cast<const void*>(attn_bwd_kernel<kF16>), BwdSmem::BYTES));
   const int nk = (T + TILE - 1) / TILE;
   // one CTA per key-tile item: the hardware scheduler balances the uneven
   // items better than a static persistent assignment (measured)
   const int grid = nk * B * NH;
-  attn_bwd_kernel<<<grid, kBwdThreads, BwdSmem::BYTES, s>>>(tq, td, dqkv, f32 ? 1 : 0, dq, lse, Dv, B, T, NH, C,
-                                                             device_status_ptr());
+  attn_bwd_kernel<kF16><<<grid, kBwdThreads, BwdSmem::BYTES, s>>>(tq, td, dqkv, f32 ? 1 : 0, dq, lse, Dv, B, T, NH, C,
+                                                                  device_status_ptr());
   const long long n8 = static_cast<long long>(B) * T * C / 8;
   const int pg = static_cast<int>(std::min<long long>((n8 + 255) / 256, 148LL * 16));
-  if (f32) attn_bwd_post_kernel<float><<<pg, 256, 0, s>>>(static_cast<float*>(dqkv), dq, B * T, C, 0.125f);
-  else attn_bwd_post_kernel<__nv_bfloat16><<<pg, 256, 0, s>>>(static_cast<__nv_bfloat16*>(dqkv), dq, B * T, C, 0.125f);
+  if (f32) attn_bwd_post_kernel<float, kF16><<<pg, 256, 0, s>>>(static_cast<float*>(dqkv), dq, B * T, C, 0.125f);
+  else attn_bwd_post_kernel<T16, kF16><<<pg, 256, 0, s>>>(static_cast<T16*>(dqkv), dq, B * T, C, 0.125f);
   count_launch(3);
   LLMK_CUDA(cudaGetLastError());
   return LLMK_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int llmk_attention_backward(void* dqkv, const void* dout, const void* out, llmk_dtype io_dtype, const void* qkv,
+                            llmk_dtype qkv_dtype, const float* lse, int B, int T, int C3, int NH, void* workspace,
+                            size_t workspace_bytes, void* stream) {
+  if (!dqkv || !dout || !out || !qkv || !lse) return fail(LLMK_ERR_INVALID_ARG, "attention_backward: null pointer");
+  LLMK_TRY(check_shapes(B, T, C3, NH));
+  if (qkv_dtype != LLMK_BF16 && qkv_dtype != LLMK_F16)
+    return fail(LLMK_ERR_UNSUPPORTED, "attention_backward: qkv dtype (bf16 or fp16)");
+  if (io_dtype != qkv_dtype && io_dtype != LLMK_F32)
+    return fail(LLMK_ERR_UNSUPPORTED, "attention_backward: io dtype (qkv's or fp32)");
+  if (!aligned16(dqkv) || !aligned16(dout) || !aligned16(out) || !aligned16(qkv))
+    return fail(LLMK_ERR_UNSUPPORTED, "attention_backward: alignment");
+  if (!workspace || workspace_bytes < llmk_attention_backward_workspace(B, T, C3, NH) || !aligned16(workspace))
+    return fail(LLMK_ERR_WORKSPACE, "attention_backward: workspace too small");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool f32 = io_dtype == LLMK_F32;
+  if (qkv_dtype == LLMK_F16) return attention_backward_t<true>(dqkv, dout, out, f32, qkv, lse, B, T, C3, NH, workspace, s);
+  return attention_backward_t<false>(dqkv, dout, out, f32, qkv, lse, B, T, C3, NH, workspace, s);
 }
 
 }  // extern "C"

@@ -38,6 +38,12 @@ __device__ __forceinline__ float4 ld4(const __nv_bfloat16* p) {
   return make_float4(a.x, a.y, b.x, b.y);
 }
 __device__ __forceinline__ void st4(float* p, float4 v) { *reinterpret_cast<float4*>(p) = v; }
+__device__ __forceinline__ void st4(__half* p, float4 v) {
+  uint2 u;
+  u.x = pack_f16x2(v.x, v.y);
+  u.y = pack_f16x2(v.z, v.w);
+  *reinterpret_cast<uint2*>(p) = u;
+}
 __device__ __forceinline__ void st4(__nv_bfloat16* p, float4 v) {
   uint2 u;
   u.x = pack_bf16x2(v.x, v.y);
@@ -745,6 +751,10 @@ int llmk_cast(void* out, llmk_dtype out_dtype, const void* in, llmk_dtype in_dty
   const int g = grid_for(n / 4, 256);
   if (in_dtype == LLMK_F32 && out_dtype == LLMK_BF16)
     cast_kernel<<<g, 256, 0, s>>>(static_cast<__nv_bfloat16*>(out), static_cast<const float*>(in), n / 4);
+  else if (in_dtype == LLMK_F32 && out_dtype == LLMK_F16)
+    cast_kernel<<<g, 256, 0, s>>>(static_cast<__half*>(out), static_cast<const float*>(in), n / 4);
+  else if (in_dtype == LLMK_F16 || out_dtype == LLMK_F16)
+    return fail(LLMK_ERR_UNSUPPORTED, "cast: fp16 only as an fp32 -> fp16 cast");
   else if (in_dtype == LLMK_BF16 && out_dtype == LLMK_F32)
     cast_kernel<<<g, 256, 0, s>>>(static_cast<float*>(out), static_cast<const __nv_bfloat16*>(in), n / 4);
   else if (in_dtype == LLMK_F32)

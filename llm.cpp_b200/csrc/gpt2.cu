@@ -2,9 +2,11 @@
 // reference's gpt2cuda::GPT2 and gpt2cuda::Layer (gpt2/cuda/gpt2cuda.h:34-190,
 // gpt2/cuda/layer.cuh:5-102) with replicated data parallelism over NCCL.
 //
-// Precision: fp32 master parameters, gradients and AdamW state; a bf16 copy
-// of the parameters feeds the tensor-core GEMMs; activations that feed GEMMs
-// or attention are bf16, the residual stream and its gradient are fp32.
+// Precision (bf16 mode): fp32 master parameters, gradients and AdamW state; a
+// bf16 copy of the parameters feeds the tensor-core GEMMs; activations that
+// feed GEMMs or attention are bf16, the residual stream and its gradient are
+// fp32. TF32 mode keeps every activation fp32 (TF32 GEMMs) and gives the
+// attention MMAs an fp16 copy of q, k, v.
 //
 // Memory layout (HBM): parameters live LAYER-MAJOR in one flat buffer —
 // [wte | wpe | layer 0 {ln1w ln1b qkvw qkvb attprojw attprojb ln2w ln2b fcw
@@ -19,6 +21,7 @@
 // gpt2/cuda/layer.cu:151-266, with bias, residual add, GELU and GELU-backward
 // fused into the GEMM epilogues and softmax + cross-entropy fused into one
 // pass that turns logits into dlogits in place.
+#include <cuda_fp16.h>
 #include <nccl.h>
 
 #include <algorithm>
@@ -26,6 +29,7 @@
 #include <cmath>
 #include <cstring>
 #include <string>
+#include <type_traits>
 #include <vector>
 
 #include "llmk.h"
@@ -58,6 +62,7 @@ void tensor_sizes(const llmk_gpt2_config& c, size_t s[16]) {
 
 template <typename T>
 int dalloc(T** p, size_t n) {
+  static_assert(!std::is_void<T>::value, "dalloc counts elements of a typed pointer");
   return cuda_check(cudaMalloc(reinterpret_cast<void**>(p), std::max<size_t>(n, 1) * sizeof(T)), "cudaMalloc");
 }
 
@@ -75,8 +80,7 @@ struct LayerActs {
   float *ln1_mean, *ln1_rstd, *ln2_mean, *ln2_rstd, *lse, *res2, *res3;
   // GEMM operands in the activation dtype (bf16, or fp32 in tf32 mode)
   void *ln1, *qkv, *atty, *ln2, *fch_pre, *fch_gelu;
-  // tf32 mode only: bf16 copy of q, k, v for the attention MMAs
-  __nv_bfloat16* qkv16;
+  __half* qkv16;  // tf32 mode only: fp16 copy of q, k, v for the attention MMAs
 };
 
 struct llmk_gpt2 {
@@ -549,16 +553,16 @@ int llmk_gpt2_forward(llmk_gpt2* g, const int* d_inputs, const int* d_targets) {
     LLMK_TRY(op.gemm(KC_GEMM_FWD, a.qkv, adt, 3 * C, a.ln1, 0, C, W(p.qkvw), 0, C, BT, 3 * C, C, &e1, nullptr, 0));
     if (bf) {
       TimedScope ts(g, KC_ATTN_FWD, attn_flop);
-      LLMK_TRY(llmk_attention_forward(a.atty, LLMK_BF16, a.lse, a.qkv, B, T, 3 * C, NH, s));
+      LLMK_TRY(llmk_attention_forward(a.atty, LLMK_BF16, a.lse, a.qkv, LLMK_BF16, B, T, 3 * C, NH, s));
     } else {
       // the attention MMAs take bf16 operands: round q, k, v once; the output
       // leaves the kernel in fp32
       {
         TimedScope ts(g, KC_CAST, bt_c * 3.0 * 6.0);
-        LLMK_TRY(llmk_cast(a.qkv16, LLMK_BF16, a.qkv, LLMK_F32, static_cast<long long>(BT) * 3 * C, s));
+        LLMK_TRY(llmk_cast(a.qkv16, LLMK_F16, a.qkv, LLMK_F32, static_cast<long long>(BT) * 3 * C, s));
       }
       TimedScope ts(g, KC_ATTN_FWD, attn_flop);
-      LLMK_TRY(llmk_attention_forward(a.atty, LLMK_F32, a.lse, a.qkv16, B, T, 3 * C, NH, s));
+      LLMK_TRY(llmk_attention_forward(a.atty, LLMK_F32, a.lse, a.qkv16, LLMK_F16, B, T, 3 * C, NH, s));
     }
     llmk_epilogue e2 = epi(P + p.attprojb, x, C);  // residual add fused
     LLMK_TRY(op.gemm(KC_GEMM_FWD, a.res2, LLMK_F32, C, a.atty, 0, C, W(p.attprojw), 0, C, BT, C, C, &e2, nullptr, 0));
@@ -665,10 +669,11 @@ int llmk_gpt2_backward(llmk_gpt2* g) {
     LLMK_TRY(op.gemm(KC_GEMM_DW, G + p.attprojw, LLMK_F32, C, dres_op, 1, C, a.atty, 1, C, C, C, BT, nullptr, ws, wsb));
     LLMK_TRY(op.gemm(KC_GEMM_DINP, g->datty, adt, C, dres_op, 0, C, W(p.attprojw), 1, C, BT, C, C, nullptr, nullptr, 0));
     // attention
-    // (tf32 mode: fp32 dO, O and dqkv; q, k, v from the bf16 copy the forward made)
+    // (tf32 mode: fp32 dO, O and dqkv; q, k, v from the fp16 copy the forward made)
     {
       TimedScope ts(g, KC_ATTN_BWD, attn_flop);
-      LLMK_TRY(llmk_attention_backward(g->dqkv, g->datty, a.atty, adt, bf ? a.qkv : a.qkv16, a.lse, B, T, 3 * C, NH,
+      LLMK_TRY(llmk_attention_backward(g->dqkv, g->datty, a.atty, adt, bf ? static_cast<const void*>(a.qkv) : a.qkv16,
+                                       bf ? LLMK_BF16 : LLMK_F16, a.lse, B, T, 3 * C, NH,
                                        ws, wsb, s));
     }
     // qkv: dW = dqkv^T ln1, db = colsum(dqkv), dln1 = dqkv Wqkv

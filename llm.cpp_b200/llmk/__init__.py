@@ -14,7 +14,7 @@ import os
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(os.path.dirname(_HERE), "libllmk.so")
 
-F32, BF16 = 0, 1
+F32, BF16, F16 = 0, 1, 2
 MATH_BF16, MATH_TF32 = 1, 2
 EPI_ACCUMULATE, EPI_GELU, EPI_GELU_BWD, EPI_AUX_F32 = 1, 2, 4, 8
 ACCUM_DINP, ACCUM_DWEIGHT, ACCUM_DBIAS, ACCUM_DPARAM = 1, 2, 4, 8
@@ -67,9 +67,9 @@ SIGNATURES: dict[str, tuple] = {
     "llmk_colsum_workspace": (sz, [i32, i32]),
     "llmk_colsum": (i32, [vp, vp, i32, i32, i32, i32, vp, sz, vp]),
     "llmk_colsum_noalloc": (i32, [vp, vp, i32, i32, i32, i32, vp]),
-    "llmk_attention_forward": (i32, [vp, i32, vp, vp, i32, i32, i32, i32, vp]),
+    "llmk_attention_forward": (i32, [vp, i32, vp, vp, i32, i32, i32, i32, i32, vp]),
     "llmk_attention_backward_workspace": (sz, [i32, i32, i32, i32]),
-    "llmk_attention_backward": (i32, [vp, vp, vp, i32, vp, vp, i32, i32, i32, i32, vp, sz, vp]),
+    "llmk_attention_backward": (i32, [vp, vp, vp, i32, vp, i32, vp, i32, i32, i32, i32, vp, sz, vp]),
     "llmk_layernorm_forward": (i32, [vp, i32, vp, vp, vp, vp, vp, i32, i32, vp]),
     "llmk_layernorm_backward_workspace": (sz, [i32, i32]),
     "llmk_layernorm_backward": (i32, [vp, vp, vp, vp, vp, vp, i32, vp, vp, vp, vp, i32, i32, i32, vp, sz, vp]),
@@ -184,6 +184,8 @@ def dtype_code(t) -> int:
         return BF16
     if t.dtype == torch.float32:
         return F32
+    if t.dtype == torch.float16:
+        return F16
     raise TypeError(f"unsupported dtype {t.dtype}")
 
 

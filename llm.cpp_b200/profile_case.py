@@ -62,7 +62,7 @@ def main() -> None:
         lse = torch.empty(Bb, NH, T, device=dev)
         s = llmk.stream_ptr()
         run = lambda: llmk.call("llmk_attention_forward", out.data_ptr(), llmk.BF16, lse.data_ptr(), qkv.data_ptr(),
-                                Bb, T, 3 * C, NH, s)
+                                llmk.BF16, Bb, T, 3 * C, NH, s)
         flop = 4.0 * Bb * NH * 64 * T * (T + 1) / 2
     elif a.case == "attnbwd":
         Bb, T, NH = (a.dims + [8, 1024, 12][len(a.dims):])[:3]
@@ -75,10 +75,10 @@ def main() -> None:
         lse = torch.empty(Bb, NH, T, device=dev)
         wsb = llmk.lib().llmk_attention_backward_workspace(Bb, T, 3 * C, NH)
         ws = torch.empty(wsb // 4 + 64, device=dev)
-        llmk.call("llmk_attention_forward", out.data_ptr(), llmk.BF16, lse.data_ptr(), qkv.data_ptr(), Bb, T, 3 * C,
-                  NH, s)
+        llmk.call("llmk_attention_forward", out.data_ptr(), llmk.BF16, lse.data_ptr(), qkv.data_ptr(), llmk.BF16, Bb, T,
+                  3 * C, NH, s)
         run = lambda: llmk.call("llmk_attention_backward", dqkv.data_ptr(), dout.data_ptr(), out.data_ptr(), llmk.BF16,
-                                qkv.data_ptr(), lse.data_ptr(), Bb, T, 3 * C, NH, ws.data_ptr(), wsb, s)
+                                qkv.data_ptr(), llmk.BF16, lse.data_ptr(), Bb, T, 3 * C, NH, ws.data_ptr(), wsb, s)
         # S = QK^T, dP = dO V^T, dV += P^T dO, dK += dS^T Q, dQ += dS K over the causal half
         flop = 10.0 * Bb * NH * 64 * T * (T + 1) / 2
     elif a.case == "gemmset":

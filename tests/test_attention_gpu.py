@@ -1,8 +1,10 @@
 """tcgen05 causal flash attention vs the oracle (reference CPU algorithm).
 
-Inputs are seeded N(0,1) from the oracle's generator, rounded to bf16 for
-the device; the oracle consumes the same rounded values in fp32. Tolerance:
-max relative error 1e-2 (the BF16 bar of the hot path) on O, LSE, dQ, dK, dV.
+Inputs are seeded N(0,1) from the oracle's generator, rounded to the 16-bit
+operand type for the device; the oracle consumes the same rounded values in
+fp32. Tolerance: max relative error 1e-2 (the BF16 bar of the hot path) on O,
+LSE, dQ, dK, dV with bf16 operands; 3e-3 with fp16 operands (the operand
+type of the TF32 training mode: 3 more mantissa bits in Q, K, V, P, dO, dS).
 """
 import numpy as np
 import pytest
@@ -18,37 +20,50 @@ def _bf16_round(x):
     return torch.from_numpy(x).bfloat16().float().numpy()
 
 
-def _run_gpu(qkv_np, dout_np, B, T, C, NH, dev, io="bf16"):
-    """One forward + backward through the C ABI. io: dtype of O, dO and dqkv."""
+def _round(x, op):
+    import torch
+    t = torch.from_numpy(x)
+    return (t.half() if op == "f16" else t.bfloat16()).float().numpy()
+
+
+TOL = {"bf16": 1e-2, "f16": 3e-3}
+
+
+def _run_gpu(qkv_np, dout_np, B, T, C, NH, dev, io="bf16", op="bf16"):
+    """One forward + backward through the C ABI. op: operand type of qkv
+    ("bf16" / "f16"); io: dtype of O, dO and dqkv ("f32" or the operand type)."""
     import torch
     import llmk
-    tdt, code = (torch.bfloat16, llmk.BF16) if io == "bf16" else (torch.float32, llmk.F32)
-    qkv = torch.from_numpy(qkv_np).to(dev).bfloat16().contiguous()
+    odt, ocode = (torch.float16, llmk.F16) if op == "f16" else (torch.bfloat16, llmk.BF16)
+    tdt, code = (odt, ocode) if io != "f32" else (torch.float32, llmk.F32)
+    qkv = torch.from_numpy(qkv_np).to(dev).to(odt).contiguous()
     dout = torch.from_numpy(dout_np).to(dev).to(tdt).contiguous()
     out = torch.full((B, T, C), float("nan"), device=dev, dtype=tdt)
     lse = torch.full((B, NH, T), float("nan"), device=dev)
     s = llmk.stream_ptr()
-    llmk.call("llmk_attention_forward", out.data_ptr(), code, lse.data_ptr(), qkv.data_ptr(), B, T, 3 * C, NH, s)
+    llmk.call("llmk_attention_forward", out.data_ptr(), code, lse.data_ptr(), qkv.data_ptr(), ocode, B, T, 3 * C, NH,
+              s)
     ws_b = llmk.lib().llmk_attention_backward_workspace(B, T, 3 * C, NH)
     ws = torch.empty(ws_b // 4 + 64, device=dev)
     dqkv = torch.full((B, T, 3 * C), float("nan"), device=dev, dtype=tdt)
-    llmk.call("llmk_attention_backward", dqkv.data_ptr(), dout.data_ptr(), out.data_ptr(), code, qkv.data_ptr(),
+    llmk.call("llmk_attention_backward", dqkv.data_ptr(), dout.data_ptr(), out.data_ptr(), code, qkv.data_ptr(), ocode,
               lse.data_ptr(), B, T, 3 * C, NH, ws.data_ptr(), ws_b, s)
     torch.cuda.synchronize()
     assert llmk.device_status() == 0
     return out.float().cpu().numpy(), lse.cpu().numpy(), dqkv.float().cpu().numpy()
 
 
-@pytest.mark.parametrize("io", ["bf16", "f32"])
-# (4, 600, 12): 240 work items over at most 148 persistent CTAs, so CTAs walk
-# several items of different lengths with a ragged last tile
+@pytest.mark.parametrize("op,io", [("bf16", "bf16"), ("bf16", "f32"), ("f16", "f16"), ("f16", "f32")])
+# (4, 600, 12): 120 pair items over at most 148 persistent CTAs with a ragged
+# last tile; (1, 384, 2): an odd number of query tiles (a pair without B)
 @pytest.mark.parametrize("B,T,NH", [(1, 128, 1), (2, 256, 2), (1, 200, 3), (2, 64, 2), (1, 384, 2), (1, 1, 1),
                                     (4, 600, 12)])
-def test_attention_vs_oracle(cuda_dev, B, T, NH, io):
+def test_attention_vs_oracle(cuda_dev, B, T, NH, op, io):
     C = 64 * NH
-    qkv = _bf16_round(O.normal((B, T, 3 * C), 100 + T))
-    dout = _bf16_round(O.normal((B, T, C), 200 + T))
-    out_g, lse_g, dqkv_g = _run_gpu(qkv, dout, B, T, C, NH, cuda_dev, io)
+    qkv = _round(O.normal((B, T, 3 * C), 100 + T), op)
+    dout = _round(O.normal((B, T, C), 200 + T), op)
+    out_g, lse_g, dqkv_g = _run_gpu(qkv, dout, B, T, C, NH, cuda_dev, io, op)
+    tol = TOL[op]
     out_o = np.zeros((B, T, C), np.float32)
     att = np.zeros((B, NH, T, T), np.float32)
     lse_o = np.zeros((B, NH, T), np.float32)
@@ -56,14 +71,14 @@ def test_attention_vs_oracle(cuda_dev, B, T, NH, io):
     dqkv_o = np.zeros((B, T, 3 * C), np.float32)
     # the backward's dO.O uses the device's bf16 O, as the kernel does
     O.orc().orc_attention_backward(dqkv_o, O.f32a(dout), O.f32a(qkv), att, B, T, C, NH)
-    assert max_rel_err(out_g, out_o) < 1e-2, max_rel_err(out_g, out_o)
-    assert max_rel_err(lse_g, lse_o) < 1e-2
+    assert max_rel_err(out_g, out_o) < tol, max_rel_err(out_g, out_o)
+    assert max_rel_err(lse_g, lse_o) < tol
     # relative to the largest gradient entry of dQ|dK|dV: for T = 1 the true dQ
     # and dK are exactly zero (softmax over one key), so a per-part scale is empty
     scale = np.abs(dqkv_o).max()
     for name, sl in (("dq", slice(0, C)), ("dk", slice(C, 2 * C)), ("dv", slice(2 * C, 3 * C))):
         e = np.abs(dqkv_g[..., sl] - dqkv_o[..., sl]).max() / scale
-        assert e < 1e-2, f"{name} max_rel={e:.3e}"
+        assert e < tol, f"{name} max_rel={e:.3e}"
 
 
 def test_attention_config2_vs_torch(cuda_dev):
@@ -99,8 +114,8 @@ def test_attention_rejects_head_size(cuda_dev):
     out = torch.zeros(1, 128, 96, device=cuda_dev, dtype=torch.bfloat16)
     lse = torch.zeros(1, 3, 128, device=cuda_dev)
     with pytest.raises(llmk.LlmkError) as e:
-        llmk.call("llmk_attention_forward", out.data_ptr(), llmk.BF16, lse.data_ptr(), qkv.data_ptr(), 1, 128, 288, 3,
-                  llmk.stream_ptr())
+        llmk.call("llmk_attention_forward", out.data_ptr(), llmk.BF16, lse.data_ptr(), qkv.data_ptr(), llmk.BF16, 1,
+                  128, 288, 3, llmk.stream_ptr())
     assert e.value.code == 2
 
 

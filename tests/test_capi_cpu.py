@@ -39,7 +39,7 @@ def test_argument_validation_without_gpu(llmk_lib):
     import llmk
     L = llmk.lib()
     assert L.llmk_gemm(None, 0, 0, None, 0, 0, None, 0, 0, llmk.MATH_BF16, 1, 1, 1, None, None, 0, None) == 1
-    assert L.llmk_attention_forward(None, llmk.BF16, None, None, 1, 64, 192, 1, None) == 1
+    assert L.llmk_attention_forward(None, llmk.BF16, None, None, llmk.BF16, 1, 64, 192, 1, None) == 1
     assert b"null" in L.llmk_last_error()
     assert L.llmk_status_string(4) == b"device wait timed out"
     assert L.llmk_matmul_backward_workspace(8192, 768, 2304, llmk.MATH_BF16) > 0
