@@ -42,19 +42,6 @@ constexpr int TILE_BYTES = TILE * HD * 2;  // 16 KB: one [128 x 64] bf16 tile, 1
 // 128B-swizzled atom column (TMA SWIZZLE_128B / UMMA SWIZZLE_128B pattern).
 __device__ __forceinline__ uint32_t sw128(int r, int c) { return r * 128 + ((c ^ (r & 7)) << 4); }
 
-// Writes 8 fp32 as the 16-bit operand type (kF16: fp16, else bf16) into row
-// r, chunk c of a [128 x 128] 16-bit K-major tile stored as two 16 KB atom
-// columns.
-template <bool kF16>
-__device__ __forceinline__ void st_tile_chunk(uint8_t* tile, int r, int chunk, const float* v) {
-  uint4 u;
-  u.x = pack16x2<kF16>(v[0], v[1]);
-  u.y = pack16x2<kF16>(v[2], v[3]);
-  u.z = pack16x2<kF16>(v[4], v[5]);
-  u.w = pack16x2<kF16>(v[6], v[7]);
-  *reinterpret_cast<uint4*>(tile + (chunk >> 3) * TILE_BYTES + sw128(r, chunk & 7)) = u;
-}
-
 // ------------------------------------------------------------------ forward
 // Work item w (0 .. nq*B*NH-1) of the attention kernels: query
 // (forward) or key (backward) tile `tile` of head bh. Items are ordered by
@@ -512,13 +499,13 @@ __global__ void attn_bwd_post_kernel(IoT* __restrict__ dqkv, const float* __rest
 // runtime alignment pad: the dynamic shared memory is declared 1024-byte
 // aligned (the 128B-swizzle atom) and the kernel checks that it is.
 struct BwdSmem {
-  static constexpr int kStages = 2;
+  static constexpr int kStages = 3;
   static constexpr int K_OFF = 0;
   static constexpr int V_OFF = TILE_BYTES;
   static constexpr int QD_OFF = 2 * TILE_BYTES;                    // stages x (Q_i, dO_i)
-  static constexpr int PD_OFF = QD_OFF + kStages * 2 * TILE_BYTES;  // 2 x (P^T, dS^T) [128 keys x 128 q]
+  static constexpr int PD_OFF = QD_OFF + kStages * 2 * TILE_BYTES;  // P^T, dS^T [128 keys x 128 q]
   static constexpr int PD_BYTES = 4 * TILE_BYTES;
-  static constexpr int LD_OFF = PD_OFF + 2 * PD_BYTES;             // stages x (LSE2[128], D[128]) fp32
+  static constexpr int LD_OFF = PD_OFF + PD_BYTES;                 // stages x (LSE[128], D[128]) fp32
   static constexpr int BAR_OFF = LD_OFF + kStages * 2 * TILE * 4;
   static constexpr size_t BYTES = BAR_OFF + 256;
   static_assert(BYTES <= 232448, "backward smem");
@@ -561,35 +548,37 @@ __device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, 
                : "memory");
 }
 
-// P^T = exp2(S^T * scale*log2e - LSE2) and dS^T = P^T (dP^T - D) for one
-// thread's key row `key` and kCols query columns tq0.., written as 16-byte
-// chunks chunk0.. of row r of the swizzled P^T / dS^T tiles. ld: the tile's
-// LSE2 / D of those columns (smem, read as broadcast vectors). kMask: the
-// diagonal tile (query < key masked) or a tile reaching past T (padded
-// queries masked).
+// P^T = exp2(S^T * scale*log2e - LSE*log2e) and dS^T = P^T (dP^T - D) for
+// one thread's key row `key` and kCols query columns tq0.., packed as pairs
+// of the 16-bit operand type into pk / dk. ld_lse / ld_d: the tile's LSE
+// (natural log) / D of those columns (smem, read as broadcast vectors).
+// kMask: the diagonal tile (query < key masked) or a tile reaching past T
+// (padded queries masked).
 template <bool kMask, int kCols, bool kF16>
-__device__ __forceinline__ void bwd_p_ds(const uint32_t* sv, const uint32_t* dv, const float* ld_l2,
-                                         const float* ld_d, int tq0, int key, int T, uint8_t* p_tile,
-                                         uint8_t* ds_tile, int r, int chunk0) {
+__device__ __forceinline__ void bwd_p_ds(const uint32_t* sv, const uint32_t* dv, const float* ld_lse,
+                                         const float* ld_d, int tq0, int key, int T, uint32_t* pk, uint32_t* dk) {
   const float sl2 = 0.125f * 1.4426950408889634f;
 #pragma unroll
   for (int c = 0; c < kCols / 8; ++c) {
     float l2[8], dd[8];
-    *reinterpret_cast<float4*>(l2) = reinterpret_cast<const float4*>(ld_l2 + c * 8)[0];
-    *reinterpret_cast<float4*>(l2 + 4) = reinterpret_cast<const float4*>(ld_l2 + c * 8)[1];
+    *reinterpret_cast<float4*>(l2) = reinterpret_cast<const float4*>(ld_lse + c * 8)[0];
+    *reinterpret_cast<float4*>(l2 + 4) = reinterpret_cast<const float4*>(ld_lse + c * 8)[1];
     *reinterpret_cast<float4*>(dd) = reinterpret_cast<const float4*>(ld_d + c * 8)[0];
     *reinterpret_cast<float4*>(dd + 4) = reinterpret_cast<const float4*>(ld_d + c * 8)[1];
     float p[8], ds[8];
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
       const int tq = tq0 + c * 8 + k;
-      float pv = ex2_approx(fmaf(__uint_as_float(sv[c * 8 + k]), sl2, -l2[k]));
+      float pv = ex2_approx(fmaf(__uint_as_float(sv[c * 8 + k]), sl2, -l2[k] * 1.4426950408889634f));
       if (kMask && (tq < key || tq >= T)) pv = 0.f;  // causal (query before key) and padded queries
       p[k] = pv;
       ds[k] = pv * (__uint_as_float(dv[c * 8 + k]) - dd[k]);
     }
-    st_tile_chunk<kF16>(p_tile, r, chunk0 + c, p);
-    st_tile_chunk<kF16>(ds_tile, r, chunk0 + c, ds);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      pk[c * 4 + k] = pack16x2<kF16>(p[2 * k], p[2 * k + 1]);
+      dk[c * 4 + k] = pack16x2<kF16>(ds[2 * k], ds[2 * k + 1]);
+    }
   }
 }
 
@@ -609,20 +598,20 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   uint8_t* sK = smem + S::K_OFF;
   uint8_t* sV = smem + S::V_OFF;
   uint8_t* sQD = smem + S::QD_OFF;
-  uint8_t* sPD = smem + S::PD_OFF;  // buffer b: P^T at b*PD_BYTES, dS^T 2 tiles further
+  uint8_t* sPD = smem + S::PD_OFF;  // P^T, dS^T 2 tiles further
   float* sLD = reinterpret_cast<float*>(smem + S::LD_OFF);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::BAR_OFF);
   uint64_t* kv_full = bars;                       // K, V of an item loaded
   uint64_t* kv_empty = bars + 1;                  // an item's last gradient MMAs done (K, V free)
-  uint64_t* qd_full = bars + 2;                   // [2] Q_i, dO_i
-  uint64_t* qd_empty = qd_full + S::kStages;      // [2]
+  uint64_t* qd_full = bars + 2;                   // [stages] Q_i, dO_i
+  uint64_t* qd_empty = qd_full + S::kStages;      // [stages]
   uint64_t* sdp_full = qd_empty + S::kStages;     // S^T and dP^T in TMEM
   uint64_t* sdp_free = sdp_full + 1;              // S^T / dP^T read into registers (one arrival per warp)
-  uint64_t* ps_full = sdp_free + 1;               // [2] P^T, dS^T of step parity b in smem
+  uint64_t* ps_full = sdp_free + 1;               // [2] P^T, dS^T of a step of parity b in smem
   uint64_t* grad_done = ps_full + 2;              // [2] gradient MMAs of step parity b done
   uint64_t* dq_free = grad_done + 2;              // [2] dQ TMEM buffer b read
   uint64_t* dkv_free = dq_free + 2;               // an item's dK / dV TMEM read
-  uint64_t* ld_full = dkv_free + 1;               // [2] LSE2 / D of a ring stage staged
+  uint64_t* ld_full = dkv_free + 1;               // [stages] LSE / D of a ring stage staged
   uint64_t* done = ld_full + S::kStages;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -688,14 +677,26 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           tma_load_3d(sq, &tm_qkv, qd_full + stage, it.h * HD, q0, it.b);
           tma_load_3d(sq + TILE_BYTES, &tm_do, qd_full + stage, it.h * HD, q0, it.b);
         }
+        // LSE and D of the tile's queries: two 512-byte bulk copies for a full,
+        // 16-byte aligned tile (the common case), plain loads otherwise
         float* ld = sLD + stage * 2 * TILE;
-        for (int k = lane; k < TILE; k += 32) {
-          const int t = q0 + k;
-          ld[k] = t < T ? lse_bh[t] * 1.4426950408889634f : 0.f;
-          ld[TILE + k] = t < T ? d_bh[t] : 0.f;
+        const bool bulk = q0 + TILE <= T && (reinterpret_cast<uintptr_t>(lse_bh + q0) & 15u) == 0 &&
+                          (reinterpret_cast<uintptr_t>(d_bh + q0) & 15u) == 0;
+        if (bulk) {
+          if (lane == 0) {
+            mbar_arrive_expect_tx(ld_full + stage, 2 * TILE * 4);
+            bulk_load_1d(ld, lse_bh + q0, TILE * 4, ld_full + stage);
+            bulk_load_1d(ld + TILE, d_bh + q0, TILE * 4, ld_full + stage);
+          }
+        } else {
+          for (int k = lane; k < TILE; k += 32) {
+            const int t = q0 + k;
+            ld[k] = t < T ? lse_bh[t] : 0.f;
+            ld[TILE + k] = t < T ? d_bh[t] : 0.f;
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(ld_full + stage);
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(ld_full + stage);
         if (++stage == S::kStages) { stage = 0; phase ^= 1u; }
         if (i == 0) {
           // K, V of this item once the previous item's gradient MMAs are done
@@ -771,7 +772,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           tc_fence_after();
           const uint32_t q_addr = smem_u32(sQD + stage * 2 * TILE_BYTES);
           const uint32_t do_addr = q_addr + TILE_BYTES;
-          const uint32_t p_addr = smem_u32(sPD + pb * S::PD_BYTES), ds_addr = p_addr + 2 * TILE_BYTES;
+          const uint32_t p_addr = smem_u32(sPD), ds_addr = p_addr + 2 * TILE_BYTES;
 #pragma unroll
           for (int ks = 0; ks < TILE / 16; ++ks) {
             const uint32_t koff = (ks >> 2) * TILE_BYTES + (ks & 3) * 32;  // K (= q) offset in a [128 x 128] K-major tile
@@ -904,17 +905,29 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(sdp_free);
-        // P^T / dS^T buffer pb was last read by the gradient MMAs of step g-2,
-        // which finished before this warp flushed that step's dQ
-        uint8_t* p_tile = sPD + pb * S::PD_BYTES;
+        // P^T / dS^T of this warp's query columns, packed in registers
         const int tq0 = qt * TILE + cq * kBwdCols;
         const float* ld = sLD + stage * 2 * TILE + cq * kBwdCols;
+        uint32_t pk[kBwdCols / 2], dk[kBwdCols / 2];
         if (qt == kt || qt * TILE + TILE > T)
-          bwd_p_ds<true, kBwdCols, kF16>(sv, dv, ld, ld + TILE, tq0, k0 + r, T, p_tile, p_tile + 2 * TILE_BYTES, r,
-                                   cq * kBwdCols / 8);
+          bwd_p_ds<true, kBwdCols, kF16>(sv, dv, ld, ld + TILE, tq0, k0 + r, T, pk, dk);
         else
-          bwd_p_ds<false, kBwdCols, kF16>(sv, dv, ld, ld + TILE, tq0, k0 + r, T, p_tile, p_tile + 2 * TILE_BYTES, r,
-                                    cq * kBwdCols / 8);
+          bwd_p_ds<false, kBwdCols, kF16>(sv, dv, ld, ld + TILE, tq0, k0 + r, T, pk, dk);
+        // the single P^T / dS^T buffer: the previous step's gradient MMAs have read it
+        if (have_prev) {
+          const uint32_t gp = g - 1;
+          bool gd = mbar_wait(grad_done + (gp & 1), (gp >> 1) & 1, status, abort_flag, 17);
+          if (!__all_sync(0xffffffffu, gd)) { ok = false; break; }
+          tc_fence_after();
+        }
+#pragma unroll
+        for (int c = 0; c < kBwdCols / 8; ++c) {
+          const int chunk = cq * kBwdCols / 8 + c;
+          const uint32_t off = (chunk >> 3) * TILE_BYTES + sw128(r, chunk & 7);
+          *reinterpret_cast<uint4*>(sPD + off) = make_uint4(pk[c * 4], pk[c * 4 + 1], pk[c * 4 + 2], pk[c * 4 + 3]);
+          *reinterpret_cast<uint4*>(sPD + 2 * TILE_BYTES + off) =
+              make_uint4(dk[c * 4], dk[c * 4 + 1], dk[c * 4 + 2], dk[c * 4 + 3]);
+        }
         fence_async_smem();
         tc_fence_before();
         __syncwarp();
