@@ -22,8 +22,8 @@
 // warps (4 per TMEM lane quarter, 32 query columns each) form P^T and
 // dS^T = P^T (dP^T - D) in smem (double-buffered); then dV += P^T dO and
 // dK += dS^T Q accumulate in TMEM, dQ_i = dS K lands in one of two TMEM
-// buffers and is added to an fp32 workspace with vector reductions while the
-// next query tile runs. D = rowsum(dO * O) and the final dQ scaling run as
+// buffers and is staged in smem and added to an fp32 workspace by TMA
+// reduce-adds while the next query tile runs. D = rowsum(dO * O) and the final dQ scaling run as
 // small pre/post kernels.
 #include <algorithm>
 #include <type_traits>
@@ -499,13 +499,14 @@ __global__ void attn_bwd_post_kernel(IoT* __restrict__ dqkv, const float* __rest
 // runtime alignment pad: the dynamic shared memory is declared 1024-byte
 // aligned (the 128B-swizzle atom) and the kernel checks that it is.
 struct BwdSmem {
-  static constexpr int kStages = 3;
+  static constexpr int kStages = 2;
   static constexpr int K_OFF = 0;
   static constexpr int V_OFF = TILE_BYTES;
   static constexpr int QD_OFF = 2 * TILE_BYTES;                    // stages x (Q_i, dO_i)
   static constexpr int PD_OFF = QD_OFF + kStages * 2 * TILE_BYTES;  // P^T, dS^T [128 keys x 128 q]
   static constexpr int PD_BYTES = 4 * TILE_BYTES;
-  static constexpr int LD_OFF = PD_OFF + PD_BYTES;                 // stages x (LSE[128], D[128]) fp32
+  static constexpr int DQ_OFF = PD_OFF + PD_BYTES;                 // dQ staging: 2 x [128 q x 32] fp32, 128B-swizzled
+  static constexpr int LD_OFF = DQ_OFF + 2 * TILE_BYTES;           // stages x (LSE[128], D[128]) fp32
   static constexpr int BAR_OFF = LD_OFF + kStages * 2 * TILE * 4;
   static constexpr size_t BYTES = BAR_OFF + 256;
   static_assert(BYTES <= 232448, "backward smem");
@@ -519,11 +520,11 @@ struct BwdSmem {
 //
 // A CTA walks key-tile items c, c + gridDim.x, ... (most query tiles first);
 // the launch uses one CTA per item. The query-tile steps g of a CTA's items
-// form one sequence. P^T / dS^T
-// (smem) and dQ (TMEM) are double-buffered by step parity, so the softmax
-// warps turn S^T / dP^T of step g into P^T / dS^T while the gradient MMAs of
-// step g-1 run, and then add dQ of step g-1 to the fp32 accumulator with
-// vector reductions straight from registers.
+// form one sequence. The softmax warps turn S^T / dP^T of step g into P^T /
+// dS^T in registers while the gradient MMAs of step g-1 run, write them to
+// the single smem P^T / dS^T buffer once those MMAs are done, and then stage
+// dQ of step g-1 (TMEM, double-buffered by step parity) for the TMA
+// reduce-adds into the fp32 accumulator.
 #ifndef LLMK_BWD_SOFTMAX_WARPS
 #define LLMK_BWD_SOFTMAX_WARPS 16
 #endif
@@ -543,11 +544,6 @@ __device__ __forceinline__ AttnItem bwd_item(int w, int B, int NH) {
   return it;
 }
 
-__device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, float d) {
-  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d)
-               : "memory");
-}
-
 // P^T = exp2(S^T * scale*log2e - LSE*log2e) and dS^T = P^T (dP^T - D) for
 // one thread's key row `key` and kCols query columns tq0.., packed as pairs
 // of the 16-bit operand type into pk / dk. ld_lse / ld_d: the tile's LSE
@@ -557,27 +553,37 @@ __device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, 
 template <bool kMask, int kCols, bool kF16>
 __device__ __forceinline__ void bwd_p_ds(const uint32_t* sv, const uint32_t* dv, const float* ld_lse,
                                          const float* ld_d, int tq0, int key, int T, uint32_t* pk, uint32_t* dk) {
-  const float sl2 = 0.125f * 1.4426950408889634f;
+  const float sl2 = 0.125f * kLog2e;
+  const uint64_t sl2x2 = f2_pack(sl2, sl2), nlog2e = f2_pack(-kLog2e, -kLog2e);
 #pragma unroll
   for (int c = 0; c < kCols / 8; ++c) {
-    float l2[8], dd[8];
-    *reinterpret_cast<float4*>(l2) = reinterpret_cast<const float4*>(ld_lse + c * 8)[0];
-    *reinterpret_cast<float4*>(l2 + 4) = reinterpret_cast<const float4*>(ld_lse + c * 8)[1];
-    *reinterpret_cast<float4*>(dd) = reinterpret_cast<const float4*>(ld_d + c * 8)[0];
-    *reinterpret_cast<float4*>(dd + 4) = reinterpret_cast<const float4*>(ld_d + c * 8)[1];
-    float p[8], ds[8];
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const int tq = tq0 + c * 8 + k;
-      float pv = ex2_approx(fmaf(__uint_as_float(sv[c * 8 + k]), sl2, -l2[k] * 1.4426950408889634f));
-      if (kMask && (tq < key || tq >= T)) pv = 0.f;  // causal (query before key) and padded queries
-      p[k] = pv;
-      ds[k] = pv * (__uint_as_float(dv[c * 8 + k]) - dd[k]);
-    }
+    // (LSE, D) of 8 query columns as 4 pairs each, from the broadcast smem rows
+    uint64_t l2[4], dd[4];
+    *reinterpret_cast<uint4*>(l2) = reinterpret_cast<const uint4*>(ld_lse + c * 8)[0];
+    *reinterpret_cast<uint4*>(l2 + 2) = reinterpret_cast<const uint4*>(ld_lse + c * 8)[1];
+    *reinterpret_cast<uint4*>(dd) = reinterpret_cast<const uint4*>(ld_d + c * 8)[0];
+    *reinterpret_cast<uint4*>(dd + 2) = reinterpret_cast<const uint4*>(ld_d + c * 8)[1];
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      pk[c * 4 + k] = pack16x2<kF16>(p[2 * k], p[2 * k + 1]);
-      dk[c * 4 + k] = pack16x2<kF16>(ds[2 * k], ds[2 * k + 1]);
+      const int i = c * 8 + 2 * k;
+      // x = S * scale * log2e - LSE * log2e, two columns at a time
+      const uint64_t x = f2_fma(f2_pack(__uint_as_float(sv[i]), __uint_as_float(sv[i + 1])), sl2x2,
+                                f2_mul(l2[k], nlog2e));
+      float x0, x1;
+      f2_unpack(x, x0, x1);
+      float p0 = ex2_approx(x0), p1 = ex2_approx(x1);
+      if (kMask) {  // causal (query before key) and padded queries
+        const int tq = tq0 + i;
+        if (tq < key || tq >= T) p0 = 0.f;
+        if (tq + 1 < key || tq + 1 >= T) p1 = 0.f;
+      }
+      // dS = P (dP - D)
+      const uint64_t pp = f2_pack(p0, p1);
+      const uint64_t t = f2_fma(dd[k], f2_pack(-1.f, -1.f), f2_pack(__uint_as_float(dv[i]), __uint_as_float(dv[i + 1])));
+      float d0, d1;
+      f2_unpack(f2_mul(pp, t), d0, d1);
+      pk[c * 4 + k] = pack16x2<kF16>(p0, p1);
+      dk[c * 4 + k] = pack16x2<kF16>(d0, d1);
     }
   }
 }
@@ -585,6 +591,7 @@ __device__ __forceinline__ void bwd_p_ds(const uint32_t* sv, const uint32_t* dv,
 template <bool kF16>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_do,
+                    const __grid_constant__ CUtensorMap tm_dq,
                     void* __restrict__ dqkv_ptr, int io_f32, float* __restrict__ dq_acc,
                     const float* __restrict__ lse, const float* __restrict__ Dvec, int B, int T, int NH, int C,
                     unsigned int* status) {
@@ -600,6 +607,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   uint8_t* sQD = smem + S::QD_OFF;
   uint8_t* sPD = smem + S::PD_OFF;  // P^T, dS^T 2 tiles further
   float* sLD = reinterpret_cast<float*>(smem + S::LD_OFF);
+  uint8_t* sDQ = smem + S::DQ_OFF;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::BAR_OFF);
   uint64_t* kv_full = bars;                       // K, V of an item loaded
   uint64_t* kv_empty = bars + 1;                  // an item's last gradient MMAs done (K, V free)
@@ -612,7 +620,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   uint64_t* dq_free = grad_done + 2;              // [2] dQ TMEM buffer b read
   uint64_t* dkv_free = dq_free + 2;               // an item's dK / dV TMEM read
   uint64_t* ld_full = dkv_free + 1;               // [stages] LSE / D of a ring stage staged
-  uint64_t* done = ld_full + S::kStages;
+  uint64_t* dqs_full = ld_full + S::kStages;      // dQ staging written (one arrival per softmax warp)
+  uint64_t* dqs_free = dqs_full + 1;              // the previous dQ reduce-adds have read the staging
+  uint64_t* done = dqs_free + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -636,6 +646,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       mbar_init(dq_free + b2, kBwdSoftmaxWarps);
     }
     mbar_init(dkv_free, kBwdSoftmaxWarps);
+    mbar_init(dqs_full, kBwdSoftmaxWarps);
+    mbar_init(dqs_free, 1);
     mbar_init(done, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -803,22 +815,44 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const int r = q * 32 + lane;     // key row within the tile for S^T/dP^T/dK/dV; query row for dQ
     const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
     // dQ of step gg (TMEM buffer gg&1, lane = query row, columns cq*16..+16)
-    // added to the fp32 accumulator with vector reductions
-    auto flush_dq = [&](uint32_t gg, int b, int h, int qt) {
+    // staged in smem (two 128B-swizzled [128 x 32] fp32 halves) by all the
+    // softmax warps, then added to the fp32 accumulator by two TMA
+    // reduce-adds that one thread (warp 2, lane 0) issues; rows past T are
+    // clipped by the tensor map. dqs_free: the previous reduce-adds have
+    // read the staging; dqs_full: every warp has written it.
+    uint32_t nflush = 0;
+    auto flush_dq = [&](uint32_t gg, int b, int h, int qt) -> bool {
       uint32_t v[kBwdGradCols];
 #pragma unroll
       for (int c16 = 0; c16 < kBwdGradCols; c16 += 16)
         tmem_ld_32x32b_x16(tmem + lane_base + 384 + (gg & 1) * HD + cq * kBwdGradCols + c16,
                            *reinterpret_cast<uint32_t(*)[16]>(v + c16));
       tmem_ld_wait();
-      const int tq = qt * TILE + r;
-      if (tq < T) {
-        float* dst = dq_acc + (static_cast<long long>(b) * T + tq) * C + h * HD + cq * kBwdGradCols;
-#pragma unroll
-        for (int k = 0; k < kBwdGradCols / 4; ++k)
-          red_add_v4(dst + 4 * k, __uint_as_float(v[4 * k]), __uint_as_float(v[4 * k + 1]),
-                     __uint_as_float(v[4 * k + 2]), __uint_as_float(v[4 * k + 3]));
+      const bool issuer = warp == 2 && lane == 0;
+      const uint32_t f = nflush++;
+      if (issuer && f > 0) {
+        bulk_wait_read0();
+        mbar_arrive(dqs_free);
       }
+      bool fr = mbar_wait(dqs_free, (f & 1) ^ 1u, status, abort_flag, 23);
+      if (!__all_sync(0xffffffffu, fr)) return false;
+      const int col0 = cq * kBwdGradCols;  // of the 64 dQ columns
+      uint8_t* half = sDQ + (col0 >> 5) * TILE_BYTES;
+#pragma unroll
+      for (int k = 0; k < kBwdGradCols / 4; ++k) {
+        const int chunk = ((col0 & 31) >> 2) + k;  // 16-byte chunk of the 128-byte row
+        *reinterpret_cast<uint4*>(half + sw128(r, chunk)) = make_uint4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+      }
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(dqs_full);
+      if (issuer) {
+        if (!mbar_wait(dqs_full, f & 1, status, abort_flag, 24)) return false;
+        tma_reduce_add_3d(&tm_dq, sDQ, h * HD, qt * TILE, b);
+        tma_reduce_add_3d(&tm_dq, sDQ + TILE_BYTES, h * HD + 32, qt * TILE, b);
+        bulk_commit();
+      }
+      return true;
     };
     // dK (scaled) and dV of key tile kt, columns cq*16..+16: TMEM lane = key row.
     // tcgen05.ld is warp-collective (.sync.aligned): every lane loads, only
@@ -872,7 +906,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       bool gd = mbar_wait(grad_done + (gp & 1), (gp >> 1) & 1, status, abort_flag, 17);
       if (!__all_sync(0xffffffffu, gd)) return false;
       tc_fence_after();
-      flush_dq(gp, pbb, phh, pqt);
+      if (!flush_dq(gp, pbb, phh, pqt)) return false;
       if (prev_last) drain_dkv(pbb, phh, pkt);
       tc_fence_before();
       __syncwarp();
@@ -943,6 +977,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
     }
     if (ok && have_prev) finish_prev();
+    if (warp == 2 && lane == 0) bulk_wait0();  // the dQ reduce-adds are complete before the CTA exits
     tc_fence_before();
   }
   __syncthreads();
@@ -1055,12 +1090,15 @@ int attention_backward_t(void* dqkv, const void* dout, const void* out, bool f32
                         TILE, 1));
   LLMK_TRY(make_tmap_3d(&td, dout_mma, dt, C, T, B, static_cast<uint64_t>(C) * 2, static_cast<uint64_t>(T) * C * 2, HD,
                         TILE, 1));
+  CUtensorMap tdq;  // fp32 dQ accumulator (B, T, C), [128 x 32] boxes for the reduce-adds
+  LLMK_TRY(make_tmap_3d(&tdq, dq, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, C, T, B, static_cast<uint64_t>(C) * 4,
+                        static_cast<uint64_t>(T) * C * 4, 32, TILE, 1));
   LLMK_TRY(set_smem(reinterpret_cast<const void*>(attn_bwd_kernel<kF16>), BwdSmem::BYTES));
   const int nk = (T + TILE - 1) / TILE;
   // one CTA per key-tile item: the hardware scheduler balances the uneven
   // items better than a static persistent assignment (measured)
   const int grid = nk * B * NH;
-  attn_bwd_kernel<kF16><<<grid, kBwdThreads, BwdSmem::BYTES, s>>>(tq, td, dqkv, f32 ? 1 : 0, dq, lse, Dv, B, T, NH, C,
+  attn_bwd_kernel<kF16><<<grid, kBwdThreads, BwdSmem::BYTES, s>>>(tq, td, tdq, dqkv, f32 ? 1 : 0, dq, lse, Dv, B, T, NH, C,
                                                                   device_status_ptr());
   const long long n8 = static_cast<long long>(B) * T * C / 8;
   const int pg = static_cast<int>(std::min<long long>((n8 + 255) / 256, 148LL * 16));
