@@ -43,9 +43,8 @@ constexpr int TILE_BYTES = TILE * HD * 2;  // 16 KB: one [128 x 64] bf16 tile, 1
 __device__ __forceinline__ uint32_t sw128(int r, int c) { return r * 128 + ((c ^ (r & 7)) << 4); }
 
 // ------------------------------------------------------------------ forward
-// Work item w (0 .. nq*B*NH-1) of the attention kernels: query
-// (forward) or key (backward) tile `tile` of head bh. Items are ordered by
-// decreasing work, and CTA c walks items c, c + gridDim.x, ... .
+// Work item w of the attention kernels: query-tile pair (forward) or key
+// tile (backward) `tile` of head bh. Items are ordered by decreasing work.
 struct AttnItem {
   int tile, b, h, bh;
 };
@@ -57,6 +56,16 @@ __device__ __forceinline__ AttnItem fwd_item(int w, int nq, int B, int NH) {
   it.b = it.bh / NH;
   it.h = it.bh % NH;
   return it;
+}
+
+// The k-th item of this CTA in the forward's static schedule: rounds of
+// gridDim.x items, alternate rounds in reverse CTA order (items are sorted by
+// decreasing work, so a CTA that takes a heavy item in one round takes a light
+// one in the next). n_items when the CTA has no k-th item.
+__device__ __forceinline__ int fwd_slot(int k, int n_items) {
+  const int g = static_cast<int>(gridDim.x), c = static_cast<int>(blockIdx.x);
+  const int w = k * g + ((k & 1) ? g - 1 - c : c);
+  return w < n_items ? w : n_items;
 }
 
 // ------------------------------------------------------------------ forward
@@ -144,7 +153,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       uint32_t phase = 0;
       bool ok = true;
       int n = 0;
-      for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x, ++n) {
+      for (int w = fwd_slot(0, n_items); w < n_items && ok; w = fwd_slot(n + 1, n_items), ++n) {
         const AttnItem it = fwd_item(w, np, B, NH);
         const int p = it.tile;
         const bool has_b = 2 * p + 1 < nq;
@@ -201,7 +210,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         }
         mma_commit(pv_done + x);
       };
-      for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x, ++n) {
+      for (int w = fwd_slot(0, n_items); w < n_items && ok; w = fwd_slot(n + 1, n_items), ++n) {
         const AttnItem it = fwd_item(w, np, B, NH);
         const int p = it.tile;
         const bool has_b = 2 * p + 1 < nq;
@@ -274,7 +283,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     bool ok = true;
     uint32_t cs = 0;  // S tiles consumed
     int n = 0;        // items
-    for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x, ++n) {
+    for (int w = fwd_slot(0, n_items); w < n_items && ok; w = fwd_slot(n + 1, n_items), ++n) {
       const AttnItem it = fwd_item(w, np, B, NH);
       const int tile = 2 * it.tile + x;
       if (tile >= nq) continue;  // tile B of an odd last pair
