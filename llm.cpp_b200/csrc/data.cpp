@@ -160,6 +160,10 @@ int llmk_loader_destroy(llmk_loader* l) {
 int llmk_loader_next(llmk_loader* l, int* inputs, int* targets) {
   if (!l || !inputs || !targets) return fail(LLMK_ERR_INVALID_ARG, "loader_next: null argument");
   if (l->sample_idx >= l->shard_samples) LLMK_TRY(advance(l));
+  // After a Resume into a shard with more samples than the last shuffled
+  // order holds, the reference would index past that order; refuse instead.
+  if (l->shuffle && l->sample_idx >= l->sample_order.size())
+    return fail(LLMK_ERR_INVALID_ARG, "loader_next: resumed position is outside the shuffled sample order");
   const size_t idx = l->shuffle ? static_cast<size_t>(l->sample_order[l->sample_idx]) : l->sample_idx;
   const size_t bt = l->B * l->T;
   const long long off = static_cast<long long>(llmk_loader::kHeaderInts) * 4 +
