@@ -338,23 +338,30 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           l *= alpha;
         }
         if (move) m = mx2;
-        float rs8[8];
+        // P = 2^(S * scale * log2e - m) two columns at a time (packed fp32
+        // pairs), row sum in 8 running partial sums (4 packed pairs)
+        const uint64_t sl2x2 = f2_pack(sl2, sl2), negm2 = f2_pack(-m, -m);
+        uint64_t rs2[4];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) rs8[k] = 0.f;
+        for (int k = 0; k < 4; ++k) rs2[k] = f2_pack(0.f, 0.f);
 #pragma unroll
         for (int ch = 0; ch < TILE / 8; ++ch) {
           uint32_t pk[4];
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
-            const float p0 = ex2_approx(fmaf(__uint_as_float(sv[ch * 8 + 2 * k]), sl2, -m));
-            const float p1 = ex2_approx(fmaf(__uint_as_float(sv[ch * 8 + 2 * k + 1]), sl2, -m));
-            rs8[2 * k] += p0;
-            rs8[2 * k + 1] += p1;
+            const int i = ch * 8 + 2 * k;
+            float x0, x1;
+            f2_unpack(f2_fma(f2_pack(__uint_as_float(sv[i]), __uint_as_float(sv[i + 1])), sl2x2, negm2), x0, x1);
+            const float p0 = ex2_approx(x0), p1 = ex2_approx(x1);
+            rs2[k] = f2_add(rs2[k], f2_pack(p0, p1));
             pk[k] = pack16x2<kF16>(p0, p1);
           }
           *reinterpret_cast<uint4*>(pt + (ch >> 3) * TILE_BYTES + sw128(r, ch & 7)) =
               make_uint4(pk[0], pk[1], pk[2], pk[3]);
         }
+        float rs8[8];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) f2_unpack(rs2[k], rs8[2 * k], rs8[2 * k + 1]);
         l += ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
         fence_async_smem();
         tc_fence_before();
