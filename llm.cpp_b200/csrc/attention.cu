@@ -17,14 +17,15 @@
 // smem (bf16, 128B-swizzled K-major). The two tiles share each K/V load and
 // alternate on the tensor core, so one's softmax overlaps the other's MMAs.
 //
-// Backward: one CTA per (128-key tile, head, batch) walking query tiles from
-// the diagonal down. S^T = K Q^T and dP^T = V dO^T land in TMEM; 16 softmax
-// warps (4 per TMEM lane quarter, 32 query columns each) form P^T and
-// dS^T = P^T (dP^T - D) in smem (double-buffered); then dV += P^T dO and
+// Backward: persistent, one CTA per SM walking (128-key tile, head, batch)
+// items; each walks query tiles from the diagonal down. S^T = K Q^T and
+// dP^T = V dO^T land in TMEM; 16 softmax warps (4 per TMEM lane quarter, 32
+// query columns each) form P^T and dS^T = P^T (dP^T - D) in registers and then
+// in smem once the previous tile's gradient MMAs are done; dV += P^T dO and
 // dK += dS^T Q accumulate in TMEM, dQ_i = dS K lands in one of two TMEM
 // buffers and is staged in smem and added to an fp32 workspace by TMA
-// reduce-adds while the next query tile runs. D = rowsum(dO * O) and the final dQ scaling run as
-// small pre/post kernels.
+// reduce-adds while the next query tile runs. D = rowsum(dO * O) and the
+// final dQ scaling run as small pre/post kernels.
 #include <algorithm>
 #include <type_traits>
 
@@ -58,11 +59,11 @@ __device__ __forceinline__ AttnItem fwd_item(int w, int nq, int B, int NH) {
   return it;
 }
 
-// The k-th item of this CTA in the forward's static schedule: rounds of
-// gridDim.x items, alternate rounds in reverse CTA order (items are sorted by
-// decreasing work, so a CTA that takes a heavy item in one round takes a light
-// one in the next). n_items when the CTA has no k-th item.
-__device__ __forceinline__ int fwd_slot(int k, int n_items) {
+// The k-th item of this CTA in the persistent kernels' static schedule:
+// rounds of gridDim.x items, alternate rounds in reverse CTA order (items are
+// sorted by decreasing work, so a CTA that takes a heavy item in one round
+// takes a light one in the next). n_items when the CTA has no k-th item.
+__device__ __forceinline__ int sched_slot(int k, int n_items) {
   const int g = static_cast<int>(gridDim.x), c = static_cast<int>(blockIdx.x);
   const int w = k * g + ((k & 1) ? g - 1 - c : c);
   return w < n_items ? w : n_items;
@@ -153,7 +154,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       uint32_t phase = 0;
       bool ok = true;
       int n = 0;
-      for (int w = fwd_slot(0, n_items); w < n_items && ok; w = fwd_slot(n + 1, n_items), ++n) {
+      for (int w = sched_slot(0, n_items); w < n_items && ok; w = sched_slot(n + 1, n_items), ++n) {
         const AttnItem it = fwd_item(w, np, B, NH);
         const int p = it.tile;
         const bool has_b = 2 * p + 1 < nq;
@@ -210,7 +211,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         }
         mma_commit(pv_done + x);
       };
-      for (int w = fwd_slot(0, n_items); w < n_items && ok; w = fwd_slot(n + 1, n_items), ++n) {
+      for (int w = sched_slot(0, n_items); w < n_items && ok; w = sched_slot(n + 1, n_items), ++n) {
         const AttnItem it = fwd_item(w, np, B, NH);
         const int p = it.tile;
         const bool has_b = 2 * p + 1 < nq;
@@ -283,7 +284,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     bool ok = true;
     uint32_t cs = 0;  // S tiles consumed
     int n = 0;        // items
-    for (int w = fwd_slot(0, n_items); w < n_items && ok; w = fwd_slot(n + 1, n_items), ++n) {
+    for (int w = sched_slot(0, n_items); w < n_items && ok; w = sched_slot(n + 1, n_items), ++n) {
       const AttnItem it = fwd_item(w, np, B, NH);
       const int tile = 2 * it.tile + x;
       if (tile >= nq) continue;  // tile B of an odd last pair
@@ -534,9 +535,9 @@ struct BwdSmem {
 // column group (w-2)/4 of every tile it touches: kBwdSoftmaxWarps/4 warps
 // share each lane quarter and split its columns.
 //
-// A CTA walks key-tile items c, c + gridDim.x, ... (most query tiles first);
-// the launch uses one CTA per item. The query-tile steps g of a CTA's items
-// form one sequence. The softmax warps turn S^T / dP^T of step g into P^T /
+// A persistent CTA (one per SM) walks key-tile items in the snake-order
+// schedule (sched_slot; most query tiles first). The query-tile steps g of a
+// CTA's items form one sequence. The softmax warps turn S^T / dP^T of step g into P^T /
 // dS^T in registers while the gradient MMAs of step g-1 run, write them to
 // the single smem P^T / dS^T buffer once those MMAs are done, and then stage
 // dQ of step g-1 (TMEM, double-buffered by step parity) for the TMA
@@ -690,7 +691,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     uint32_t phase = 0;
     bool ok = true;
     int n = 0;
-    for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x, ++n) {
+    for (int w = sched_slot(0, n_items); w < n_items && ok; w = sched_slot(n + 1, n_items), ++n) {
       const AttnItem it = bwd_item(w, B, NH);
       const int kt = it.tile, nqi = nk - kt;
       const float* lse_bh = lse + static_cast<long long>(it.bh) * T;
@@ -769,7 +770,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       uint32_t g = 0;
       bool issued = false;  // S^T / dP^T of step g already issued
       int n = 0;
-      for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x, ++n) {
+      for (int w = sched_slot(0, n_items); w < n_items && ok; w = sched_slot(n + 1, n_items), ++n) {
         const int nqi = nk - bwd_item(w, B, NH).tile;
         for (int j = 0; j < nqi; ++j, ++g) {
           const int nst = stage + 1 == S::kStages ? 0 : stage + 1;
@@ -932,7 +933,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
       return true;
     };
-    for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x) {
+    for (int w = sched_slot(0, n_items), nw = 0; w < n_items && ok; w = sched_slot(++nw, n_items)) {
       const AttnItem it = bwd_item(w, B, NH);
       const int kt = it.tile, nqi = nk - kt, k0 = kt * TILE;
       for (int j = 0; j < nqi; ++j, ++g) {
@@ -1111,9 +1112,10 @@ int attention_backward_t(void* dqkv, const void* dout, const void* out, bool f32
                         static_cast<uint64_t>(T) * C * 4, 32, TILE, 1));
   LLMK_TRY(set_smem(reinterpret_cast<const void*>(attn_bwd_kernel<kF16>), BwdSmem::BYTES));
   const int nk = (T + TILE - 1) / TILE;
-  // one CTA per key-tile item: the hardware scheduler balances the uneven
-  // items better than a static persistent assignment (measured)
-  const int grid = nk * B * NH;
+  // persistent: one CTA per SM walking key-tile items in the snake-order
+  // schedule, so an item's dK / dV drain and K / V load overlap the next
+  // item's first query tile
+  const int grid = std::min(nk * B * NH, num_sms());
   attn_bwd_kernel<kF16><<<grid, kBwdThreads, BwdSmem::BYTES, s>>>(tq, td, tdq, dqkv, f32 ? 1 : 0, dq, lse, Dv, B, T, NH, C,
                                                                   device_status_ptr());
   const long long n8 = static_cast<long long>(B) * T * C / 8;
