@@ -392,6 +392,65 @@ __global__ void __launch_bounds__(1024) encoder_sort_kernel(unsigned int* __rest
   }
   for (int i = threadIdx.x; i < BT; i += blockDim.x) sorted[i] = key[i];
 }
+// The same network for n = kPer * 1024 keys, with the stages whose partner
+// distance j is below kPer run in registers on each thread's kPer
+// consecutive keys (one shared-memory round trip and one barrier per merge
+// size instead of one per stage). Shared memory holds one pad word per 32
+// keys, so the threads' strided register loads and the passes' consecutive
+// accesses both avoid bank conflicts.
+__device__ __forceinline__ int sort_pad(int i) { return i + (i >> 5); }
+
+template <int kPer>
+__global__ void __launch_bounds__(1024) encoder_sort_reg_kernel(unsigned int* __restrict__ sorted,
+                                                                const int* __restrict__ tokens, int BT) {
+  constexpr int n = kPer * 1024;
+  extern __shared__ unsigned int key[];  // n + n / 32 words
+  for (int i = threadIdx.x; i < n; i += 1024)
+    key[sort_pad(i)] = i < BT ? (static_cast<unsigned int>(tokens[i]) << 15) | static_cast<unsigned int>(i) : 0xFFFFFFFFu;
+  __syncthreads();
+  const int base = threadIdx.x * kPer;
+  unsigned int r[kPer];
+  for (int k = 2; k <= n; k <<= 1) {
+    for (int j = k >> 1; j >= kPer; j >>= 1) {
+      for (int i = threadIdx.x; i < n; i += 1024) {
+        const int ixj = i ^ j;
+        if (ixj > i) {
+          const unsigned int a = key[sort_pad(i)], b = key[sort_pad(ixj)];
+          const bool ascending = (i & k) == 0;
+          if ((a > b) == ascending) {
+            key[sort_pad(i)] = b;
+            key[sort_pad(ixj)] = a;
+          }
+        }
+      }
+      __syncthreads();
+    }
+#pragma unroll
+    for (int e = 0; e < kPer; ++e) r[e] = key[sort_pad(base + e)];
+#pragma unroll
+    for (int j = kPer / 2; j > 0; j >>= 1) {
+      if (j < k) {
+#pragma unroll
+        for (int e = 0; e < kPer; ++e) {
+          if ((e & j) == 0) {
+            const int f = e | j;
+            const bool ascending = ((base + e) & k) == 0;
+            const unsigned int a = r[e], b = r[f];
+            if ((a > b) == ascending) {
+              r[e] = b;
+              r[f] = a;
+            }
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < kPer; ++e) key[sort_pad(base + e)] = r[e];
+    __syncthreads();
+  }
+  for (int i = threadIdx.x; i < BT; i += 1024) sorted[i] = key[sort_pad(i)];
+}
+
 // dwte[tok,:] += sum of dout rows of the positions holding tok, in position
 // order: the first sorted key of each run of equal tokens sums its run.
 __global__ void encoder_bwd_wte_sorted_kernel(float* __restrict__ dwte, const float* __restrict__ dout,
@@ -793,11 +852,18 @@ int llmk_encoder_backward(float* dwte, float* dwpe, const float* dout, const int
     // sort (token, position) keys once, then one pass over runs of equal tokens
     int n = 1;
     while (n < BT) n <<= 1;
-    const size_t smem = static_cast<size_t>(n) * sizeof(unsigned int);
-    LLMK_CUDA(cudaFuncSetAttribute(encoder_sort_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   static_cast<int>(smem)));
     unsigned int* sorted = static_cast<unsigned int*>(workspace);
-    encoder_sort_kernel<<<1, 1024, smem, s>>>(sorted, tokens, BT, n);
+    if (n == 8192 || n == 16384) {  // (32 keys a thread would spill registers)
+      const size_t smem = static_cast<size_t>(n + n / 32) * sizeof(unsigned int);
+      auto kern = n == 8192 ? encoder_sort_reg_kernel<8> : encoder_sort_reg_kernel<16>;
+      LLMK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+      kern<<<1, 1024, smem, s>>>(sorted, tokens, BT);
+    } else {
+      const size_t smem = static_cast<size_t>(n) * sizeof(unsigned int);
+      LLMK_CUDA(cudaFuncSetAttribute(encoder_sort_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(smem)));
+      encoder_sort_kernel<<<1, 1024, smem, s>>>(sorted, tokens, BT, n);
+    }
     encoder_bwd_wte_sorted_kernel<<<grid_for(static_cast<long long>(BT) * C / 4, 256), 256, 0, s>>>(dwte, dout, sorted,
                                                                                                    BT, C);
   } else {

@@ -213,9 +213,10 @@ def test_encoder_vs_oracle(cuda_dev):
     assert max_rel_err(dwpe.cpu(), torch.from_numpy(b)) < 1e-5
 
 
-@pytest.mark.parametrize("B,Tt,V", [(16, 1024, 50257), (33, 1024, 3000)])
+@pytest.mark.parametrize("B,Tt,V", [(16, 1024, 50257), (5, 1000, 3000), (20, 1000, 50257), (33, 1024, 3000)])
 def test_encoder_backward_sizes(cuda_dev, B, Tt, V):
-    """B*T = 16384 exercises the one-CTA sort path, B*T = 33792 the scan fallback."""
+    """One-CTA sort paths: B*T = 16384 (16 keys per thread in registers), 5000 (8 keys per thread, padded to
+    8192), 20000 (the shared-memory network, padded to 32768); B*T = 33792 takes the scan fallback."""
     import torch
     import llmk
     C = 128
