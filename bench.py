@@ -97,6 +97,13 @@ class ClockSampler:
                                       stderr=subprocess.DEVNULL)
         except Exception:
             self.p = None
+            return
+        # nvidia-smi takes a moment to start: begin timing once it is sampling
+        t0 = time.time()
+        while time.time() - t0 < 3.0 and self.p.poll() is None:
+            if os.path.getsize(self.f.name) > 0:
+                break
+            time.sleep(0.02)
 
     def stop(self) -> dict:
         if self.p is None:
@@ -234,7 +241,7 @@ def run_reference(args) -> None:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
