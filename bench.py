@@ -343,6 +343,14 @@ def main() -> None:
     line = None
     if rank == 0:
         peaks = measured_peaks()
+        # the burst GEMM peak while the step ran at the maximum SM clock, the
+        # sustained one when the power cap held the clock down
+        capped = "sw_power_cap" in (clocks.get("reasons") or []) or (
+            clocks.get("sm_mhz") and clocks.get("sm_max_mhz") and clocks["sm_mhz"] < 0.97 * clocks["sm_max_mhz"])
+        if capped and peaks.get("bf16_tflops_sustained"):
+            tpeak, tsrc = peaks["bf16_tflops_sustained"], " bf16 sustained (the step ran under the power cap)"
+        else:
+            tpeak, tsrc = peaks["bf16_tflops"], " bf16 burst (the step ran at the maximum SM clock)"
         roof = gemm_roofline(llmk, torch, BT)
         kernels = {}
         for name, c in classes.items():
@@ -350,7 +358,7 @@ def main() -> None:
                 continue
             tensor = c["unit"] == "flop"
             rate = c["work"] / (c["ms"] * 1e-3) / (1e12 if tensor else 1e9) if c["ms"] > 0 else 0.0
-            peak = peaks["bf16_tflops"] if tensor else peaks["hbm_gbs"]
+            peak = tpeak if tensor else peaks["hbm_gbs"]
             kernels[name] = {"ms_per_step": round(c["ms"] / args.steps, 4),
                              "share": round(c["ms"] / args.steps / timed_ms, 4),
                              "launches_per_step": c["launches"] // args.steps,
@@ -372,12 +380,12 @@ def main() -> None:
             "gpu_launches": int(launches),
             "loss": last_loss,
             "roofline": {"kernel": "gemm_tc_kernel (every GEMM of the step, timed live in the step)",
-                         "bound": "tensor", "achieved": round(achieved, 1), "peak": peaks["bf16_tflops"],
-                         "unit": "TFLOP/s", "frac": round(achieved / peaks["bf16_tflops"], 4),
+                         "bound": "tensor", "achieved": round(achieved, 1), "peak": tpeak,
+                         "unit": "TFLOP/s", "frac": round(achieved / tpeak, 4),
                          "traffic": GEMM_TRAFFIC_PER_LAUNCH,
                          "flop_per_launch": g["work"] / gemm_launches,
                          "launch_ms": g["ms"] / gemm_launches,
-                         "peak_source": peaks["source"] + " bf16 burst (the step runs at max SM clock)"},
+                         "peak_source": peaks["source"] + tsrc},
             "kernels": kernels,
             "gemm_ms_per_step": round(g["ms"] / args.steps, 3),
             "instrumented_ms_per_step": round(timed_ms, 3),
