@@ -1,32 +1,39 @@
-"""Benchmark: GPT-2 124M data-parallel training throughput on B200.
+"""Benchmark: GPT-2 data-parallel training throughput on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--model 124m|774m]
+    python bench.py --case NAME [dims ...] [--reps R]      (one kernel, for ncu captures)
 
-Workload (configuration 3 of the spec): GPT-2 124M (L=12, NH=12, C=768,
-V=50257 padded to 50304, maxT=1024), B=16 sequences of T=1024 tokens per GPU,
-bf16 GEMMs and attention with fp32 master weights and AdamW (lr 3e-4,
+Workload (configuration 3 of the spec, the default): GPT-2 124M (L=12, NH=12,
+C=768, V=50257 padded to 50304, maxT=1024), B=16 sequences of T=1024 tokens
+per GPU, bf16 GEMMs and attention with fp32 master weights and AdamW (lr 3e-4,
 betas 0.9/0.999, eps 1e-8, wd 0), seeded initialisation, synthetic uniform
-tokens seeded per rank (1337 + rank). One step = forward + backward (with
-the per-layer NCCL gradient all-reduce when N > 1) + AdamW, all on the native
-trainer of libllmk.so (include/llmk_gpt2.h), replayed as one captured CUDA
-graph per step (llmk_gpt2_use_graph).
+tokens seeded per rank (1337 + rank). `--model 774m` runs configuration 4
+instead (L=36, NH=20, C=1280, B=8 per GPU). One step = forward + backward
+(with the per-layer NCCL gradient all-reduce when N > 1) + AdamW on the
+native trainer of libllmk.so (include/llmk_gpt2.h), replayed as one captured
+CUDA graph per step (llmk_gpt2_use_graph).
 
 value: tokens/s of the whole job with tokens already resident in HBM,
 timed with CUDA events on the trainer's stream over exactly K steps between
 barriers, max over ranks. e2e: the same through llmk_gpt2_train_step from
 pinned host tokens to a host loss every step. roofline: the tcgen05 GEMM
 kernel over every GEMM of the step, timed live in the step (K further steps
-with CUDA events around each library call of the trainer); kernels: the same
-per kernel class with its share of the step and its fraction of the measured
-tensor or HBM peak; gemm_alone_*: each GEMM shape timed alone.
-cpu_baseline: the reference's own CPU training step (oracle/_ref, the
-llm.cpp sources built by oracle/Makefile) on a bounded sample, rank 0 only.
+with CUDA events around each library call of the trainer), against the
+measured bf16 burst peak; kernels: the same per kernel class with its share
+of the step and its fraction of the measured tensor or HBM peak.
+gemm_alone_*: each GEMM shape of the step timed alone. config1_gemm: the
+GEMM microbench of configuration 1 (BT = 8192, every layer shape, forward,
+input gradient, weight gradient and bias gradient, TF32 and BF16).
+config2_attention: causal attention forward and backward at B=8, NH=12,
+T=1024. cpu_baseline: the reference's own CPU training step (oracle/_ref,
+the llm.cpp sources built by oracle/Makefile) on configuration 0, rank 0 only.
 """
 from __future__ import annotations
 
 import argparse
 import json
 import os
+import platform
 import statistics
 import subprocess
 import sys
@@ -37,15 +44,20 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(ROOT, "llm.cpp_b200"))
 sys.path.insert(0, ROOT)
 
-CFG = dict(max_seq_len=1024, vocab_size=50257, padded_vocab_size=50304, num_layers=12, num_heads=12, channels=768)
-B_PER_GPU, T = 16, 1024
+MODELS = {
+    "124m": dict(cfg=dict(max_seq_len=1024, vocab_size=50257, padded_vocab_size=50304, num_layers=12, num_heads=12,
+                          channels=768), B=16, name="gpt2-124M", config="config 3"),
+    "774m": dict(cfg=dict(max_seq_len=1024, vocab_size=50257, padded_vocab_size=50304, num_layers=36, num_heads=20,
+                          channels=1280), B=8, name="gpt2-774M", config="config 4"),
+}
+T = 1024
 LR = 3e-4
-METRIC = "GPT-2 124M train tokens/sec (B=16/GPU, T=1024)"
-# Reference CPU sample: training steps of the same model at B=1, T=256. Its
-# attention backward is O(T^3) per head (gpt2/attention.cpp:104-113), so one
-# step at T=1024 would take tens of minutes; T=256 steps take a few seconds
-# each and overstate, not understate, the reference's throughput at T=1024.
-REF_SAMPLE = dict(B=1, T=256)
+# Reference CPU sample: configuration 0 of the spec (GPT-2 124M, B=4, T=64),
+# 20 steps, median of steps 1-19 (step 0 pays the first-touch costs). A
+# step at the GPU arm's T=1024 would take tens of minutes on the CPU: its
+# attention backward is O(T^3) per head (gpt2/attention.cpp:104-113), so the
+# T=64 sample overstates the reference's throughput at T=1024.
+REF_SAMPLE = dict(B=4, T=64, steps=20)
 # DRAM bytes (read + write) per gemm_tc_kernel launch of one training step:
 # an ncu capture of every GEMM shape of the step at BT = 8192 gave 56.8 MB per
 # launch on average; all shapes scale with BT, so 113.5 MB at BT = 16384
@@ -53,13 +65,19 @@ REF_SAMPLE = dict(B=1, T=256)
 GEMM_TRAFFIC_PER_LAUNCH = 113.5e6
 
 
-def seeded_init_params(seed: int):
+def metric_name(model: str) -> str:
+    m = MODELS[model]
+    return f"GPT-2 {m['name'].split('-')[1]} train tokens/sec (B={m['B']}/GPU, T={T})"
+
+
+def seeded_init_params(cfg: dict, seed: int):
     """GPT-2 init of the spec (N(0,0.02), projections / sqrt(2L), biases 0, LN 1/0,
     padded vocab rows 0), drawn on the device with torch's generator. The
     bench only needs a valid initialisation of the architecture; parity runs
     use the oracle's generator (tests/)."""
     import torch
-    L, C, Vp, V, maxT = CFG["num_layers"], CFG["channels"], CFG["padded_vocab_size"], CFG["vocab_size"], CFG["max_seq_len"]
+    L, C, Vp, V, maxT = cfg["num_layers"], cfg["channels"], cfg["padded_vocab_size"], cfg["vocab_size"], \
+        cfg["max_seq_len"]
     sizes = [Vp * C, maxT * C, L * C, L * C, L * 3 * C * C, L * 3 * C, L * C * C, L * C, L * C, L * C, L * 4 * C * C,
              L * 4 * C, L * 4 * C * C, L * C, C, C]
     g = torch.Generator(device="cuda").manual_seed(seed)
@@ -139,24 +157,49 @@ def measured_peaks() -> dict:
     if os.path.exists(p):
         d = json.load(open(p))
         return {"bf16_tflops": d["bf16_tflops"], "bf16_tflops_sustained": d.get("bf16_tflops_sustained"),
-                "hbm_gbs": d["hbm_gbs"], "source": "measured"}
-    return {"bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "hbm_gbs": 6650.0, "source": "fallback"}
+                "hbm_gbs": d["hbm_gbs"], "sm_max_mhz": d.get("sm_max_mhz"), "source": "measured"}
+    return {"bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "hbm_gbs": 6650.0, "sm_max_mhz": 1965.0,
+            "source": "fallback"}
 
 
-def gemm_roofline(llmk, torch, BT: int, reps: int = 5) -> dict:
+def cpu_model() -> str:
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return platform.processor() or "unknown"
+
+
+# ------------------------------------------------------------------ timing helpers
+def time_calls(torch, fn, reps: int, warm: int = 2) -> float:
+    """ms per call of fn() with CUDA events on the current stream."""
+    for _ in range(warm):
+        fn()
+    s = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(s)
+    for _ in range(reps):
+        fn()
+    e1.record(s)
+    e1.synchronize()
+    return e0.elapsed_time(e1) / reps
+
+
+def gemm_roofline(llmk, torch, cfg: dict, BT: int, reps: int = 5) -> dict:
     """Times the tcgen05 GEMM alone on every GEMM shape of one training step
     (fwd / dinp / dweight of QKV, attproj, FC, FCproj and the tied lm_head at
     BT tokens) with CUDA events on the launching stream."""
-    C, Vp = CFG["channels"], CFG["padded_vocab_size"]
+    C, Vp, L = cfg["channels"], cfg["padded_vocab_size"], cfg["num_layers"]
     dev = "cuda"
     shapes = []  # (name, M, N, K, a_trans, b_trans, count per step)
-    L = CFG["num_layers"]
     for name, IC, OC in [("qkv", C, 3 * C), ("attproj", C, C), ("fc", C, 4 * C), ("fcproj", 4 * C, C)]:
         shapes += [(f"{name}.fwd", BT, OC, IC, 0, 0, L), (f"{name}.dinp", BT, IC, OC, 0, 1, L),
                    (f"{name}.dweight", OC, IC, BT, 1, 1, L)]
     shapes += [("lm_head.fwd", BT, Vp, C, 0, 0, 1), ("lm_head.dinp", BT, C, Vp, 0, 1, 1),
                ("lm_head.dweight", Vp, C, BT, 1, 1, 1)]
-    s = torch.cuda.current_stream()
     per = {}
     tot_flop = tot_ms = 0.0
     for name, M, N, K, at, bt, cnt in shapes:
@@ -165,16 +208,7 @@ def gemm_roofline(llmk, torch, BT: int, reps: int = 5) -> dict:
         D = torch.empty(M, N, device=dev, dtype=torch.float32 if "dweight" in name else torch.bfloat16)
         wsb = llmk.lib().llmk_gemm_workspace(M, N, K, llmk.MATH_BF16)
         ws = torch.empty(max(wsb // 4, 1), device=dev)
-        for _ in range(2):
-            llmk.gemm(D, A, B, a_trans=at, b_trans=bt, M=M, N=N, K=K, workspace=ws)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        torch.cuda.synchronize()
-        e0.record(s)
-        for _ in range(reps):
-            llmk.gemm(D, A, B, a_trans=at, b_trans=bt, M=M, N=N, K=K, workspace=ws)
-        e1.record(s)
-        e1.synchronize()
-        ms = e0.elapsed_time(e1) / reps
+        ms = time_calls(torch, lambda: llmk.gemm(D, A, B, a_trans=at, b_trans=bt, M=M, N=N, K=K, workspace=ws), reps)
         flop = 2.0 * M * N * K
         per[name] = {"tflops": round(flop / ms / 1e9, 1), "ms": round(ms, 4)}
         tot_flop += flop * cnt
@@ -184,9 +218,88 @@ def gemm_roofline(llmk, torch, BT: int, reps: int = 5) -> dict:
             "achieved_tflops": tot_flop / tot_ms / 1e9}
 
 
-def reference_step_time(threads: int, steps: int = 3) -> dict:
-    """The reference's own CPU training step (oracle/_ref/libref.so) on the
-    REF_SAMPLE batch: `steps` steps of one model; median tokens/s."""
+def config1_gemm(llmk, torch, reps: int = 5) -> dict:
+    """Configuration 1: the GPT-2 124M layer GEMMs at BT = 8192 (QKV, attention
+    projection, FC, FC projection, lm_head), each as forward (with bias, except
+    the lm_head), input gradient, weight gradient (K = BT) and bias gradient
+    (column sum of dout), in TF32 (fp32 operands and outputs) and BF16 (bf16
+    operands, bf16 activations out, fp32 weight gradients) — the forms of
+    llmk_matmul_forward / llmk_matmul_backward. Inputs N(0,1) from a seed."""
+    BT, C, Vp = 8192, 768, 50304
+    shapes = [("qkv", C, 3 * C), ("attproj", C, C), ("fc", C, 4 * C), ("fcproj", 4 * C, C), ("lm_head", C, Vp)]
+    out = {}
+    g = torch.Generator(device="cuda").manual_seed(1)
+    for mode, math, dt in (("tf32", llmk.MATH_TF32, torch.float32), ("bf16", llmk.MATH_BF16, torch.bfloat16)):
+        res = {}
+        flop_all = ms_all = 0.0
+        for name, IC, OC in shapes:
+            x = torch.randn(BT, IC, device="cuda", generator=g).to(dt)
+            W = torch.randn(OC, IC, device="cuda", generator=g).to(dt)
+            bias = None if name == "lm_head" else torch.randn(OC, device="cuda", generator=g)
+            dout = torch.randn(BT, OC, device="cuda", generator=g).to(dt)
+            y = torch.empty(BT, OC, device="cuda", dtype=dt)
+            dx = torch.empty(BT, IC, device="cuda", dtype=dt)
+            dW = torch.empty(OC, IC, device="cuda", dtype=torch.float32)
+            db = torch.empty(OC, device="cuda", dtype=torch.float32)
+            wsb = max(llmk.lib().llmk_gemm_workspace(OC, IC, BT, math), llmk.lib().llmk_colsum_workspace(BT, OC))
+            ws = torch.empty(wsb // 4 + 64, device="cuda")
+            flop = 2.0 * BT * IC * OC
+            f_ms = time_calls(torch, lambda: llmk.gemm(y, x, W, math=math, bias=bias), reps)
+            i_ms = time_calls(torch, lambda: llmk.gemm(dx, dout, W, b_trans=True, math=math, M=BT, N=IC, K=OC), reps)
+            w_ms = time_calls(torch, lambda: llmk.gemm(dW, dout, x, a_trans=True, b_trans=True, math=math, M=OC, N=IC,
+                                                       K=BT, workspace=ws), reps)
+            r = {"fwd_tflops": round(flop / f_ms / 1e9, 1), "dinp_tflops": round(flop / i_ms / 1e9, 1),
+                 "dweight_tflops": round(flop / w_ms / 1e9, 1), "fwd_ms": round(f_ms, 4), "dinp_ms": round(i_ms, 4),
+                 "dweight_ms": round(w_ms, 4)}
+            flop_all += 3 * flop
+            ms_all += f_ms + i_ms + w_ms
+            if bias is not None:
+                b_ms = time_calls(torch, lambda: llmk.call("llmk_colsum", db.data_ptr(), dout.data_ptr(),
+                                                           llmk.dtype_code(dout), BT, OC, 0, ws.data_ptr(), wsb,
+                                                           llmk.stream_ptr()), reps)
+                r["dbias_ms"] = round(b_ms, 4)
+                r["dbias_gbs"] = round(BT * OC * dout.element_size() / b_ms / 1e6, 1)
+                ms_all += b_ms
+            res[name] = r
+            del x, W, bias, dout, y, dx, dW, db, ws
+        res["all_forms"] = {"tflop": round(flop_all / 1e12, 4), "ms": round(ms_all, 4),
+                            "tflops": round(flop_all / ms_all / 1e9, 1)}
+        out[mode] = res
+    torch.cuda.empty_cache()
+    return out
+
+
+def config2_attention(llmk, torch, reps: int = 5) -> dict:
+    """Configuration 2: causal attention forward and backward, B=8, NH=12,
+    T=1024, head size 64, bf16 operands; FLOPs of the causal half
+    (forward 4*hd*T(T+1)/2, backward 10*hd*T(T+1)/2 per (b, h))."""
+    Bb, Tt, NH = 8, 1024, 12
+    C = 64 * NH
+    g = torch.Generator(device="cuda").manual_seed(2)
+    qkv = torch.randn(Bb, Tt, 3 * C, device="cuda", generator=g).bfloat16()
+    dout = torch.randn(Bb, Tt, C, device="cuda", generator=g).bfloat16()
+    out = torch.empty(Bb, Tt, C, device="cuda", dtype=torch.bfloat16)
+    dqkv = torch.empty_like(qkv)
+    lse = torch.empty(Bb, NH, Tt, device="cuda")
+    wsb = llmk.lib().llmk_attention_backward_workspace(Bb, Tt, 3 * C, NH)
+    ws = torch.empty(wsb // 4 + 64, device="cuda")
+    s = llmk.stream_ptr()
+    fwd = lambda: llmk.call("llmk_attention_forward", out.data_ptr(), llmk.BF16, lse.data_ptr(), qkv.data_ptr(),
+                            llmk.BF16, Bb, Tt, 3 * C, NH, s)
+    bwd = lambda: llmk.call("llmk_attention_backward", dqkv.data_ptr(), dout.data_ptr(), out.data_ptr(), llmk.BF16,
+                            qkv.data_ptr(), llmk.BF16, lse.data_ptr(), Bb, Tt, 3 * C, NH, ws.data_ptr(), wsb, s)
+    f_ms = time_calls(torch, fwd, reps)
+    b_ms = time_calls(torch, bwd, reps)
+    pairs = Bb * NH * 64 * Tt * (Tt + 1) / 2
+    return {"fwd_ms": round(f_ms, 4), "fwd_tflops": round(4 * pairs / f_ms / 1e9, 1), "bwd_ms": round(b_ms, 4),
+            "bwd_tflops": round(10 * pairs / b_ms / 1e9, 1)}
+
+
+# ------------------------------------------------------------------ reference CPU arm
+def reference_step_time(threads: int) -> dict:
+    """The reference's own CPU training step (oracle/_ref/libref*.so, the ISA
+    build the host supports) on configuration 0: REF_SAMPLE steps of one
+    model, tokens/s of the median step after the first."""
     import numpy as np
     import oracle as O
     if not O.ref_available():
@@ -194,7 +307,7 @@ def reference_step_time(threads: int, steps: int = 3) -> dict:
     os.environ["OMP_NUM_THREADS"] = str(threads)
     cfg = O.config()
     params = O.init_params(cfg, 1337)
-    Bs, Ts = REF_SAMPLE["B"], REF_SAMPLE["T"]
+    Bs, Ts, steps = REF_SAMPLE["B"], REF_SAMPLE["T"], REF_SAMPLE["steps"]
     toks = O.tokens(Bs * Ts + 1, cfg.vocab_size, 1337)
     with tempfile.TemporaryDirectory() as d:
         ck = os.path.join(d, "gpt2_124m.bin")
@@ -211,9 +324,11 @@ def reference_step_time(threads: int, steps: int = 3) -> dict:
             os.dup2(saved, 1)
             os.close(saved)
     per_step = [Bs * Ts / (x / 1e3) for x in ms]
-    return {"value": statistics.median(per_step), "per_step": per_step, "step_s": statistics.median(ms) / 1e3,
-            "sample": f"{steps} reference training steps of GPT-2 124M at B={Bs}, T={Ts} ({Bs * Ts} tokens each), "
-                      f"median"}
+    return {"value": statistics.median(per_step[1:]), "per_step": per_step, "losses": losses.tolist(),
+            "build": O.ref_build(), "cpu": cpu_model(),
+            "sample": f"configuration 0: {steps} reference training steps of GPT-2 124M at B={Bs}, T={Ts} "
+                      f"({Bs * Ts} tokens each), tokens/s of the median of steps 1-{steps - 1}; reference built "
+                      f"{O.ref_build()}; CPU {cpu_model()}"}
 
 
 def run_reference(args) -> None:
@@ -221,58 +336,90 @@ def run_reference(args) -> None:
     if rank != 0:
         return
     threads = os.cpu_count() or 1
-    r = reference_step_time(threads, steps=args.warmup + args.steps)
+    r = reference_step_time(threads)
     if "unavailable" in r:
         print(json.dumps({"impl": "reference", "unavailable": r["unavailable"]}))
         return
-    v = statistics.median(r["per_step"][args.warmup:])
-    line = {"metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": REF_SAMPLE["B"] * REF_SAMPLE["T"] / v * 1e3,
+    v = r["value"]
+    m = MODELS[args.model]
+    line = {"metric": metric_name(args.model), "value": v, "unit": "tokens/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": REF_SAMPLE["B"] * REF_SAMPLE["T"] / v * 1e3,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "impl": "reference",
-            "config": {"workload": "gpt2-124M train step (config 3), reference CPU sample", "model": "gpt2-124M",
-                       "global_batch": REF_SAMPLE["B"], "seq_len": REF_SAMPLE["T"], "parallelism": "cpu"},
+            "config": {"workload": f"{m['name']} train step ({m['config']}), reference CPU sample on configuration 0",
+                       "model": m["name"], "global_batch": REF_SAMPLE["B"], "seq_len": REF_SAMPLE["T"],
+                       "parallelism": "cpu"},
             "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": threads, "kind": "reference",
                              "sample": r["sample"]},
             "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line))
 
 
-def main() -> None:
-    ap = argparse.ArgumentParser()
-    ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=30)
-    ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--no-cpu-baseline", action="store_true")
-    args = ap.parse_args()
-    if args.impl == "reference":
-        run_reference(args)
-        return
+# ------------------------------------------------------------------ NCCL record
+def nccl_summary(path: str) -> dict:
+    """Version, channel count and NVLS use from one rank's NCCL_DEBUG=INFO log."""
+    info = {"log": os.path.basename(path)}
+    try:
+        lines = open(path, errors="replace").read().splitlines()
+    except OSError:
+        return {"unavailable": "no NCCL debug log"}
+    chans, nvls = set(), None
+    for ln in lines:
+        if "NCCL version" in ln and "version" not in info:
+            info["version"] = ln.split("NCCL version", 1)[1].strip().split()[0]
+        if " Channel " in ln and "/" in ln:
+            try:
+                chans.add(int(ln.split(" Channel ", 1)[1].split("/")[0]))
+            except ValueError:
+                pass
+        if "NVLS" in ln:
+            if "multicast support is available" in ln or "NVLS comm" in ln:
+                nvls = True
+            elif "not available" in ln or "disabled" in ln.lower():
+                nvls = False if nvls is None else nvls
+        if "coll channels" in ln and "coll_channels_line" not in info:
+            info["coll_channels_line"] = ln.split("NCCL INFO", 1)[-1].strip()[:200]
+    info["channels_seen"] = len(chans)
+    info["nvls"] = nvls
+    info["env"] = {k: v for k, v in os.environ.items() if k.startswith("NCCL_") and k not in ("NCCL_DEBUG_FILE",)}
+    return info
 
+
+# ------------------------------------------------------------------ main arm
+def run_ours(args) -> None:
     import numpy as np
     import torch
     import torch.distributed as dist
     import datetime
+    import zlib
     import llmk
 
+    spec = MODELS[args.model]
+    cfg, B = spec["cfg"], spec["B"]
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    nccl_log = None
+    if world > 1:
+        nccl_log = os.path.join(tempfile.gettempdir(), f"llmk_nccl_{os.getpid()}.log")
+        os.environ.setdefault("NCCL_DEBUG", "INFO")
+        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT,TUNING")
+        os.environ["NCCL_DEBUG_FILE"] = nccl_log
     torch.cuda.set_device(local)
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
-    model = llmk.GPT2(B_PER_GPU, T, **CFG)
-    params = seeded_init_params(1337)
+    model = llmk.GPT2(B, T, **cfg)
+    params = seeded_init_params(cfg, 1337)
     model.load_parameters(params)
+    del params
     if world > 1:
         obj = [llmk.nccl_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(obj, src=0)
         model.enable_dp(obj[0], rank, world)
         model.broadcast_parameters(0)
-    BT = B_PER_GPU * T
+    BT = B * T
     rng = np.random.default_rng(1337 + rank)
-    toks = rng.integers(0, CFG["vocab_size"], size=BT + 1, dtype=np.int32)
+    toks = rng.integers(0, cfg["vocab_size"], size=BT + 1, dtype=np.int32)
     inp_h, tgt_h = toks[:-1].copy(), toks[1:].copy()
     model.train_step(inp_h, tgt_h, 0.0, t=1, want_loss=False)  # tokens now resident in the model's buffers
     d_in, d_tg = model.buffers()
@@ -284,14 +431,17 @@ def main() -> None:
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
+            torch.cuda.synchronize()
 
     t = 1
     for _ in range(args.warmup):
         model.step_device(d_in, d_tg, LR, t)
         t += 1
-    barrier()
+    # the clock sampler starts before the barrier (it can take a moment to
+    # come up), so every rank leaves the barrier and starts timing together
     sampler = ClockSampler(local)
     sampler.start()
+    barrier()
     n0 = llmk.lib().llmk_launch_count()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
@@ -306,6 +456,7 @@ def main() -> None:
     # per-kernel-class device time inside the training step: the same K steps
     # again, with CUDA events on the trainer stream around every library call
     # (kept out of the timed region above; the events add a little device time)
+    barrier()
     model.set_timing(True)
     ei0, ei1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ei0.record(stream)
@@ -332,26 +483,37 @@ def main() -> None:
     e2e_ms = ee0.elapsed_time(ee1) / e2e_steps
     e2e_wall_ms = (time.perf_counter() - w0) * 1e3 / e2e_steps
     e2e_ms = max(e2e_ms, e2e_wall_ms)
+    dp = None
     if world > 1:
         v = torch.tensor([ms, e2e_ms], device="cuda")
         dist.all_reduce(v, op=dist.ReduceOp.MAX)
         ms, e2e_ms = v.tolist()
+        # replicas must hold bit-identical parameters after every step
+        p = model.read_parameters()
+        mine = torch.tensor([float(zlib.crc32(p.tobytes())), float(np.float64(p).sum())], dtype=torch.float64,
+                            device="cuda")
+        allv = [torch.zeros_like(mine) for _ in range(world)]
+        dist.all_gather(allv, mine)
+        allv = [x.tolist() for x in allv]
+        dp = {"dp_consistent": all(x == allv[0] for x in allv), "param_crc32": [int(x[0]) for x in allv],
+              "param_sum": allv[0][1]}
+        del p
     tokens_per_step = BT * world
     value = tokens_per_step / (ms / 1e3)
     e2e_value = tokens_per_step / (e2e_ms / 1e3)
 
-    line = None
     if rank == 0:
         peaks = measured_peaks()
-        # the burst GEMM peak while the step ran at the maximum SM clock, the
-        # sustained one when the power cap held the clock down
-        capped = "sw_power_cap" in (clocks.get("reasons") or []) or (
-            clocks.get("sm_mhz") and clocks.get("sm_max_mhz") and clocks["sm_mhz"] < 0.97 * clocks["sm_max_mhz"])
-        if capped and peaks.get("bf16_tflops_sustained"):
-            tpeak, tsrc = peaks["bf16_tflops_sustained"], " bf16 sustained (the step ran under the power cap)"
-        else:
-            tpeak, tsrc = peaks["bf16_tflops"], " bf16 burst (the step ran at the maximum SM clock)"
-        roof = gemm_roofline(llmk, torch, BT)
+        tpeak = peaks["bf16_tflops"]
+        sm_max = clocks.get("sm_max_mhz") or peaks.get("sm_max_mhz") or 1965.0
+        sm_med = clocks.get("sm_mhz")
+        clock_scale = (sm_med / sm_max) if sm_med else None
+        extras = {}
+        if not args.no_extras:
+            extras["gemm_alone"] = gemm_roofline(llmk, torch, cfg, BT)
+            if args.model == "124m":
+                extras["config1_gemm"] = config1_gemm(llmk, torch)
+                extras["config2_attention"] = config2_attention(llmk, torch)
         kernels = {}
         for name, c in classes.items():
             if c["calls"] == 0:
@@ -369,12 +531,13 @@ def main() -> None:
         gemm_launches = max(g["launches"], 1)
         achieved = g["work"] / (g["ms"] * 1e-3) / 1e12
         line = {
-            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded uniform tokens, seeded init)",
-            "config": {"workload": "gpt2-124M train step (config 3)", "model": "gpt2-124M",
-                       "global_batch": B_PER_GPU * world, "seq_len": T, "parallelism": f"dp{world}",
-                       "l2": "working set larger than L2 (about 7 GB of activations per step)"},
+            "metric": metric_name(args.model), "value": value, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded uniform tokens, seeded init)",
+            "config": {"workload": f"{spec['name']} train step ({spec['config']})", "model": spec["name"],
+                       "global_batch": B * world, "seq_len": T, "parallelism": f"dp{world}",
+                       "l2": "working set larger than L2 (GBs of activations per step)"},
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": 2 * BT * 4,
                     "d2h_bytes_per_step": 4},
             "gpu_launches": int(launches),
@@ -382,19 +545,28 @@ def main() -> None:
             "roofline": {"kernel": "gemm_tc_kernel (every GEMM of the step, timed live in the step)",
                          "bound": "tensor", "achieved": round(achieved, 1), "peak": tpeak,
                          "unit": "TFLOP/s", "frac": round(achieved / tpeak, 4),
-                         "traffic": GEMM_TRAFFIC_PER_LAUNCH,
+                         "traffic": GEMM_TRAFFIC_PER_LAUNCH * (BT / 16384) if args.model == "124m" else None,
                          "flop_per_launch": g["work"] / gemm_launches,
                          "launch_ms": g["ms"] / gemm_launches,
-                         "peak_source": peaks["source"] + tsrc},
+                         "peak_source": peaks["source"] + " bf16 burst (cuBLAS 8192^3 at the clock the driver saw)",
+                         "frac_at_sampled_clock": round(achieved / (tpeak * clock_scale), 4) if clock_scale else None,
+                         "sampled_clock_note": "frac_at_sampled_clock divides by the burst peak scaled by the "
+                                               "median sampled SM clock over the maximum SM clock"},
             "kernels": kernels,
             "gemm_ms_per_step": round(g["ms"] / args.steps, 3),
             "instrumented_ms_per_step": round(timed_ms, 3),
-            "gemm_alone_tflops": roof["per_gemm"],
-            "gemm_alone_step_ms": round(roof["step_gemm_ms"], 3),
-            "gemm_alone_tflops_avg": round(roof["achieved_tflops"], 1),
             "clocks": clocks,
         }
-        if not args.no_cpu_baseline:
+        if "gemm_alone" in extras:
+            ga = extras.pop("gemm_alone")
+            line["gemm_alone_tflops"] = ga["per_gemm"]
+            line["gemm_alone_step_ms"] = round(ga["step_gemm_ms"], 3)
+            line["gemm_alone_tflops_avg"] = round(ga["achieved_tflops"], 1)
+        line.update(extras)
+        if dp is not None:
+            line.update(dp)
+            line["nccl"] = nccl_summary(nccl_log)
+        if not args.no_cpu_baseline and world == 1:
             cb = reference_step_time(os.cpu_count() or 1)
             if "unavailable" in cb:
                 line["cpu_baseline"] = {"value": None, "unavailable": cb["unavailable"]}
@@ -406,6 +578,227 @@ def main() -> None:
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+# ------------------------------------------------------------------ single-kernel cases
+CASES = ["gemm", "attn", "attnbwd", "gemmset", "lmxent", "step", "lnfwd", "lnbwd", "adamw", "colsum", "encoder"]
+
+
+def run_case(args) -> None:
+    """One kernel (or one training step) on a small case, for ncu captures:
+    inputs allocated once, one warm-up launch, R timed launches, the CUDA-event
+    time per launch printed; exits 0. Default sizes hold operands larger than
+    the 126 MB L2 but only a few GB, so a `ncu -k <kernel> -c 1..3` capture of
+    them ends quickly.
+
+      gemm    [M N K] [--trans A B] [--out-bf16]   one llmk_gemm, bf16 operands
+      attn    [B T NH]                            llmk_attention_forward, bf16
+      attnbwd [B T NH]                            llmk_attention_backward, bf16
+      gemmset [BT]   every GEMM shape of one GPT-2 124M step (fwd, dinp, dweight)
+      lmxent  [BT] [--variant fused|unfused|gemm] lm_head + softmax + cross-entropy
+      step    [B T]                               one graph-replayed training step
+      lnfwd   [N C]  llmk_layernorm_forward, fp32 in, bf16 out
+      lnbwd   [N C]  llmk_layernorm_backward with the bf16 mirror and column sums
+      adamw   [n]    llmk_adamw over n parameters with the bf16 mirror
+      colsum  [M N]  llmk_colsum of a bf16 matrix
+      encoder [B T C] llmk_encoder_forward + llmk_encoder_backward
+    """
+    import numpy as np
+    import torch
+    import llmk
+    a = args
+    torch.cuda.set_device(0)
+    dev = "cuda"
+    s = llmk.stream_ptr()
+    flop = 0.0
+    nbytes = 0.0
+    if a.case == "gemm":
+        M, N, K = (a.dims + [16384, 4096, 768][len(a.dims):])[:3]
+        at, bt = a.trans
+        A = torch.randn((K, M) if at else (M, K), device=dev).bfloat16()
+        B = torch.randn((K, N) if bt else (N, K), device=dev).bfloat16()
+        D = torch.empty(M, N, device=dev, dtype=torch.bfloat16 if a.out_bf16 else torch.float32)
+        wsb = llmk.lib().llmk_gemm_workspace(M, N, K, llmk.MATH_BF16)
+        ws = torch.empty(max(wsb // 4, 1), device=dev)
+        run = lambda: llmk.gemm(D, A, B, a_trans=at, b_trans=bt, M=M, N=N, K=K, workspace=ws)
+        flop = 2.0 * M * N * K
+    elif a.case in ("attn", "attnbwd"):
+        Bb, Tt, NH = (a.dims + [8, 1024, 12][len(a.dims):])[:3]
+        C = 64 * NH
+        qkv = torch.randn(Bb, Tt, 3 * C, device=dev).bfloat16()
+        out = torch.empty(Bb, Tt, C, device=dev, dtype=torch.bfloat16)
+        lse = torch.empty(Bb, NH, Tt, device=dev)
+        fwd = lambda: llmk.call("llmk_attention_forward", out.data_ptr(), llmk.BF16, lse.data_ptr(), qkv.data_ptr(),
+                                llmk.BF16, Bb, Tt, 3 * C, NH, s)
+        if a.case == "attn":
+            run = fwd
+            flop = 4.0 * Bb * NH * 64 * Tt * (Tt + 1) / 2
+        else:
+            dout = torch.randn(Bb, Tt, C, device=dev).bfloat16()
+            dqkv = torch.empty(Bb, Tt, 3 * C, device=dev, dtype=torch.bfloat16)
+            wsb = llmk.lib().llmk_attention_backward_workspace(Bb, Tt, 3 * C, NH)
+            ws = torch.empty(wsb // 4 + 64, device=dev)
+            fwd()
+            run = lambda: llmk.call("llmk_attention_backward", dqkv.data_ptr(), dout.data_ptr(), out.data_ptr(),
+                                    llmk.BF16, qkv.data_ptr(), llmk.BF16, lse.data_ptr(), Bb, Tt, 3 * C, NH,
+                                    ws.data_ptr(), wsb, s)
+            flop = 10.0 * Bb * NH * 64 * Tt * (Tt + 1) / 2
+    elif a.case == "gemmset":
+        BT = (a.dims + [16384])[0]
+        C, Vp = 768, 50304
+        shapes = []
+        for IC, OC in [(C, 3 * C), (C, C), (C, 4 * C), (4 * C, C)]:
+            shapes += [(BT, OC, IC, 0, 0), (BT, IC, OC, 0, 1), (OC, IC, BT, 1, 1)]
+        shapes += [(BT, Vp, C, 0, 0), (BT, C, Vp, 0, 1), (Vp, C, BT, 1, 1)]
+        bufs = []
+        for (M, N, K, at, bt) in shapes:
+            A = torch.randn((K, M) if at else (M, K), device=dev).bfloat16()
+            B = torch.randn((K, N) if bt else (N, K), device=dev).bfloat16()
+            D = torch.empty(M, N, device=dev, dtype=torch.float32 if at else torch.bfloat16)
+            wsb = llmk.lib().llmk_gemm_workspace(M, N, K, llmk.MATH_BF16)
+            bufs.append((A, B, D, torch.empty(max(wsb // 4, 1), device=dev), M, N, K, at, bt))
+
+        def run():
+            for (A, B, D, ws, M, N, K, at, bt) in bufs:
+                llmk.gemm(D, A, B, a_trans=at, b_trans=bt, M=M, N=N, K=K, workspace=ws)
+        flop = sum(2.0 * M * N * K for (_, _, _, _, M, N, K, _, _) in bufs)
+    elif a.case == "lmxent":
+        BT = (a.dims + [16384])[0]
+        C, V, Vp = 768, 50257, 50304
+        x = torch.randn(BT, C, device=dev).bfloat16()
+        W = (torch.randn(Vp, C, device=dev) * 0.05).bfloat16()
+        tg = torch.randint(0, V, (BT,), device=dev, dtype=torch.int32)
+        logits = torch.empty(BT, Vp, device=dev, dtype=torch.bfloat16)
+        losses = torch.empty(BT, device=dev)
+        wsb = llmk.lib().llmk_matmul_softmax_workspace(BT, Vp)
+        ws = torch.empty(wsb // 4 + 4, device=dev)
+        if a.variant == "fused":
+            run = lambda: llmk.call("llmk_matmul_crossentropy_forward", losses.data_ptr(), logits.data_ptr(),
+                                    llmk.BF16, x.data_ptr(), W.data_ptr(), None, tg.data_ptr(), BT, C, Vp, V,
+                                    1.0 / BT, 1, llmk.MATH_BF16, ws.data_ptr(), wsb, s)
+        elif a.variant == "unfused":
+            def run():
+                llmk.gemm(logits, x, W)
+                llmk.call("llmk_softmax_crossentropy", losses.data_ptr(), logits.data_ptr(), logits.data_ptr(),
+                          llmk.BF16, tg.data_ptr(), BT, V, Vp, 1.0 / BT, s)
+        else:
+            run = lambda: llmk.gemm(logits, x, W)
+        flop = 2.0 * BT * Vp * C
+    elif a.case in ("lnfwd", "lnbwd"):
+        N, C = (a.dims + [16384, 768][len(a.dims):])[:2]
+        x = torch.randn(N, C, device=dev)
+        w = torch.randn(C, device=dev)
+        b = torch.randn(C, device=dev)
+        out = torch.empty(N, C, device=dev, dtype=torch.bfloat16)
+        mean = torch.empty(N, device=dev)
+        rstd = torch.empty(N, device=dev)
+        llmk.call("llmk_layernorm_forward", out.data_ptr(), llmk.BF16, mean.data_ptr(), rstd.data_ptr(), x.data_ptr(),
+                  w.data_ptr(), b.data_ptr(), N, C, s)
+        if a.case == "lnfwd":
+            run = lambda: llmk.call("llmk_layernorm_forward", out.data_ptr(), llmk.BF16, mean.data_ptr(),
+                                    rstd.data_ptr(), x.data_ptr(), w.data_ptr(), b.data_ptr(), N, C, s)
+            nbytes = N * C * (4 + 2) + 8 * N
+        else:
+            dout = torch.randn(N, C, device=dev)
+            dres = torch.randn(N, C, device=dev)
+            mirror = torch.empty(N, C, device=dev, dtype=torch.bfloat16)
+            dw = torch.zeros(C, device=dev)
+            db = torch.zeros(C, device=dev)
+            cs = torch.zeros(C, device=dev)
+            wsb = llmk.lib().llmk_layernorm_backward_workspace(N, C)
+            ws = torch.empty(wsb // 4 + 64, device=dev)
+            run = lambda: llmk.call("llmk_layernorm_backward", dres.data_ptr(), mirror.data_ptr(), dw.data_ptr(),
+                                    db.data_ptr(), cs.data_ptr(), dout.data_ptr(), llmk.F32, x.data_ptr(),
+                                    w.data_ptr(), mean.data_ptr(), rstd.data_ptr(), N, C, llmk.ACCUM_DINP,
+                                    ws.data_ptr(), wsb, s)
+            nbytes = N * C * (4 + 4 + 8 + 2) + 8 * N
+    elif a.case == "adamw":
+        n = (a.dims + [124475904])[0]
+        p = torch.randn(n, device=dev) * 0.02
+        g = torch.randn(n, device=dev) * 1e-3
+        m = torch.zeros(n, device=dev)
+        v = torch.zeros(n, device=dev)
+        pb = torch.empty(n, device=dev, dtype=torch.bfloat16)
+        run = lambda: llmk.call("llmk_adamw", p.data_ptr(), pb.data_ptr(), g.data_ptr(), m.data_ptr(), v.data_ptr(),
+                                n, 3e-4, 0.9, 0.999, 1e-8, 0.0, 1, 1.0, s)
+        nbytes = n * 30.0
+    elif a.case == "colsum":
+        M, N = (a.dims + [16384, 3072][len(a.dims):])[:2]
+        x = torch.randn(M, N, device=dev).bfloat16()
+        out = torch.empty(N, device=dev)
+        wsb = llmk.lib().llmk_colsum_workspace(M, N)
+        ws = torch.empty(wsb // 4 + 64, device=dev)
+        run = lambda: llmk.call("llmk_colsum", out.data_ptr(), x.data_ptr(), llmk.BF16, M, N, 0, ws.data_ptr(), wsb, s)
+        nbytes = M * N * 2.0
+    elif a.case == "encoder":
+        Bb, Tt, C = (a.dims + [16, 1024, 768][len(a.dims):])[:3]
+        Vp = 50304
+        tok = torch.randint(0, 50257, (Bb * Tt,), device=dev, dtype=torch.int32)
+        wte = torch.randn(Vp, C, device=dev)
+        wpe = torch.randn(1024, C, device=dev)
+        out = torch.empty(Bb * Tt, C, device=dev)
+        dwte = torch.zeros(Vp, C, device=dev)
+        dwpe = torch.zeros(1024, C, device=dev)
+        wsb = llmk.lib().llmk_encoder_backward_workspace(Bb, Tt)
+        ws = torch.empty(wsb // 4 + 64, device=dev)
+
+        def run():
+            llmk.call("llmk_encoder_forward", out.data_ptr(), tok.data_ptr(), wte.data_ptr(), wpe.data_ptr(), Bb, Tt, C,
+                      s)
+            llmk.call("llmk_encoder_backward", dwte.data_ptr(), dwpe.data_ptr(), out.data_ptr(), tok.data_ptr(), Bb,
+                      Tt, C, Vp, ws.data_ptr(), wsb, s)
+        nbytes = 2 * Bb * Tt * C * 12.0
+    else:  # step
+        Bb, Tt = (a.dims + [16, 1024][len(a.dims):])[:2]
+        m = llmk.GPT2(Bb, Tt)
+        m.load_parameters((np.random.default_rng(0).standard_normal(m.n) * 0.02).astype(np.float32))
+        toks = np.random.default_rng(1).integers(0, 50257, size=Bb * Tt + 1, dtype=np.int32)
+        m.train_step(toks[:-1], toks[1:], 0.0, t=1, want_loss=False)
+        d_in, d_tg = m.buffers()
+        m.use_graph(True)
+        torch.cuda.set_stream(torch.cuda.ExternalStream(m.stream))
+        state = {"t": 2}
+
+        def run():
+            m.step_device(d_in, d_tg, 3e-4, state["t"])
+            state["t"] += 1
+    n0 = llmk.lib().llmk_launch_count()
+    run()
+    torch.cuda.synchronize()
+    print(f"llmk launches before the timed region: {llmk.lib().llmk_launch_count()}, "
+          f"per launch of the case: {llmk.lib().llmk_launch_count() - n0}")
+    ms = time_calls(torch, run, a.reps, warm=0)
+    extra = ""
+    if flop:
+        extra = f", {flop / ms / 1e9:.1f} TFLOP/s"
+    elif nbytes:
+        extra = f", {nbytes / ms / 1e6:.1f} GB/s (algorithmic bytes)"
+    tag = f"{a.case}/{a.variant}" if a.case == "lmxent" else a.case
+    print(f"{tag} {a.dims}: {ms:.4f} ms per launch{extra}; device status {llmk.device_status()}")
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--model", default="124m", choices=sorted(MODELS))
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true", help="skip the per-shape GEMM and attention microbenches")
+    ap.add_argument("--case", choices=CASES, help="run one kernel on a small case instead (for ncu captures)")
+    ap.add_argument("dims", nargs="*", type=int)
+    ap.add_argument("--trans", nargs=2, type=int, default=[0, 0])
+    ap.add_argument("--reps", type=int, default=3)
+    ap.add_argument("--out-bf16", action="store_true")
+    ap.add_argument("--variant", choices=["fused", "unfused", "gemm"], default="fused")
+    args = ap.parse_args()
+    if args.case:
+        run_case(args)
+    elif args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
 
 
 if __name__ == "__main__":

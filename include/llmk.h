@@ -111,8 +111,9 @@ int llmk_matmul_backward(void* dinp, llmk_dtype dinp_dtype, float* dweight, floa
                          const void* inp, const void* weight, int BT, int C, int OC, llmk_math math, int flags,
                          void* workspace, size_t workspace_bytes, void* stream);
 
-/* dbias[N] (+)= sum over M rows of x[M,N] (x fp32 or bf16), deterministic
- * two-pass reduction through `workspace`.
+/* dbias[N] (+)= sum over M rows of x[M,N] (x fp32 or bf16; other dtypes are
+ * rejected with LLMK_ERR_UNSUPPORTED), deterministic two-pass reduction
+ * through `workspace`.
  * Replaces kernel::MatrixColSumCUDA, gpt2/cuda/matmul.cu:180-187. */
 size_t llmk_colsum_workspace(int M, int N);
 int llmk_colsum(float* dbias, const void* x, llmk_dtype x_dtype, int M, int N, int accumulate, void* workspace,
@@ -124,14 +125,20 @@ int llmk_colsum(float* dbias, const void* x, llmk_dtype x_dtype, int M, int N, i
  * not stall its stream (cudaMalloc can synchronise the device). It takes no
  * workspace: its partial sums live in a fixed array inside the library (1 MiB,
  * held by every GPU that loads the library until the process exits), so it
- * calls no cudaMalloc / cudaFree and allocates nothing. Limit: the partial
- * sums of one call (about 2 x SMs / ceil(N / 256) rows of N floats) must fit
- * in 262144 floats; larger M x N is rejected with LLMK_ERR_UNSUPPORTED (use
- * llmk_colsum). The first call on a device looks up the array's device
- * address with that device current; make that first call before any stream
- * capture. All calls share the array: calls that can overlap on the GPU
- * (different streams, or different host threads on one device) race and must
- * be serialised by the caller. Results equal llmk_colsum's.
+ * calls no cudaMalloc / cudaFree and allocates nothing.
+ * Limit: N <= 262144 columns (one row chunk holds N partial sums); larger N
+ * is rejected with LLMK_ERR_UNSUPPORTED (use llmk_colsum). Any M is
+ * accepted: the rows are split into min(llmk_colsum's chunk count,
+ * 262144 / N) chunks, where llmk_colsum uses about 8 x SMs / ceil(N / 256)
+ * chunks of at least 64 rows. x must be fp32 or bf16.
+ * Results match llmk_colsum's to fp32 rounding; they are bitwise equal when
+ * the chunk count is not capped by the array (both sum the same chunks in the
+ * same order).
+ * The first call on a device looks up the array's device address with that
+ * device current (again after a device reset gave the device a new context);
+ * make that first call before any stream capture. All calls share the array:
+ * calls that can overlap on the GPU (different streams, or different host
+ * threads on one device) race and must be serialised by the caller.
  * No counterpart in the reference: its column sum takes no scratch
  * (gpt2/cuda/matmul.cu:26-187). */
 int llmk_colsum_noalloc(float* dbias, const void* x, llmk_dtype x_dtype, int M, int N, int accumulate, void* stream);
@@ -225,6 +232,26 @@ int llmk_encoder_backward(float* dwte, float* dwpe, const float* dout, const int
  * gpt2/cuda/gpt2cuda.cu:325,342,398). */
 int llmk_softmax_crossentropy(float* losses, void* dlogits, const void* logits, llmk_dtype dtype, const int* targets,
                               int BT, int V, int Vp, float dscale, void* stream);
+/* The three ops of the reference's unfused lm_head tail, one each (rows =
+ * B*T, row stride ld = Vp, first V columns live; fp32 or bf16):
+ * llmk_softmax_forward: probs[row, :V] = softmax(logits[row, :V]); columns
+ * [V, ld) are left untouched. Replaces gpt2cuda::BatchSoftmaxForward
+ * (gpt2/cuda/softmax.cu:13-91, softmax.cuh:8). */
+int llmk_softmax_forward(void* probs, const void* logits, llmk_dtype dtype, int rows, int V, int ld, void* stream);
+/* llmk_crossentropy_forward: losses[row] (+)= -log(probs[row, target[row]])
+ * (accumulate != 0 adds, as the reference does; a target outside [0, ld)
+ * gives NaN). Replaces gpt2cuda::BatchCrossEntropyForward
+ * (gpt2/cuda/cross_entropy.cu:24-29, cross_entropy.cuh:9). */
+int llmk_crossentropy_forward(float* losses, const void* probs, llmk_dtype dtype, const int* targets, int rows, int ld,
+                              int accumulate, void* stream);
+/* llmk_crossentropy_softmax_backward: dlogits[row, c] (+)= (probs[row, c] -
+ * [c == target[row]]) * scale for c < V; [V, ld) untouched. Replaces
+ * gpt2cuda::BatchCrossEntropySoftmaxBackward (gpt2/cuda/cross_entropy.cu:7-21,
+ * cross_entropy.cuh:8), whose kernel computes (2 * dlogits + probs - onehot)
+ * * scale: the same values on the zeroed buffer its caller passes
+ * (gpt2cuda.cu ZeroGrad); accumulate = 0 overwrites. */
+int llmk_crossentropy_softmax_backward(void* dlogits, const void* probs, llmk_dtype dtype, const int* targets,
+                                       int rows, int V, int ld, float scale, int accumulate, void* stream);
 /* ------------------------------- fused lm_head + softmax / cross-entropy */
 /* logits[BT, Vp] = inp[BT, C] * W[Vp, C]^T (+ bias) on the tensor cores
  * (inp and W in the math mode's operand type: bf16, or fp32 for TF32), with

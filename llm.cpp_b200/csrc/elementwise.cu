@@ -496,7 +496,10 @@ __global__ void encoder_links_kernel(int* __restrict__ first_of, int* __restrict
 // onehot) * dscale on columns < V and 0 on [V, ld) (the reference's
 // CrossEntropySoftmaxBackward with scale 1/(B*T), gpt2/cuda/gpt2cuda.cu:398).
 // dlogits may alias logits.
-template <typename T>
+// kSoftmaxOnly: no targets or losses; `dlogits` receives softmax on the
+// columns < V, and [V, ld) is left untouched (the reference's
+// BatchSoftmaxForward, gpt2/cuda/softmax.cu:13-91, writes only the first V).
+template <typename T, bool kSoftmaxOnly = false>
 __global__ void __launch_bounds__(512) softmax_xent_kernel(float* __restrict__ losses, T* dlogits, const T* logits,
                                                            const int* __restrict__ targets, int V, int ld,
                                                            float dscale) {
@@ -548,12 +551,26 @@ __global__ void __launch_bounds__(512) softmax_xent_kernel(float* __restrict__ l
   }
   __syncthreads();
   const float S = bcast[1];
+  const float inv = 1.0f / S;
+  if constexpr (kSoftmaxOnly) {
+    T* d = dlogits + row * ld;
+    for (int i = tid; i < v4; i += nt) {
+      float4 v = ld4(x + 4 * i);
+      st4(d + 4 * i, make_float4(__expf(v.x - M) * inv, __expf(v.y - M) * inv, __expf(v.z - M) * inv,
+                                 __expf(v.w - M) * inv));
+    }
+    for (int i = 4 * v4 + tid; i < V; i += nt) {
+      const float g = __expf(to_f(x[i]) - M) * inv;
+      if constexpr (sizeof(T) == 4) d[i] = g;
+      else d[i] = __float2bfloat16(g);
+    }
+    return;
+  }
   const int tgt = targets[row];
   const float lse = M + logf(S);
   if (tid == 0) losses[row] = lse - to_f(x[tgt]);
   if (dlogits == nullptr) return;
   T* d = dlogits + row * ld;
-  const float inv = 1.0f / S;
   for (int i = tid; i < v4; i += nt) {
     float4 v = ld4(x + 4 * i);
     float4 p = make_float4(__expf(v.x - M) * inv, __expf(v.y - M) * inv, __expf(v.z - M) * inv,
@@ -572,6 +589,37 @@ __global__ void __launch_bounds__(512) softmax_xent_kernel(float* __restrict__ l
     if (i < V) g = (__expf(to_f(x[i]) - M) * inv - (i == tgt ? 1.f : 0.f)) * dscale;
     if constexpr (sizeof(T) == 4) d[i] = g;
     else d[i] = __float2bfloat16(g);
+  }
+}
+
+// losses[row] (+)= -log(probs[row, targets[row]]) — the reference's
+// CrossEntropyForward over probabilities (gpt2/cuda/cross_entropy.cu:24-29,
+// which accumulates). A target outside [0, ld) gives NaN for that row.
+template <typename T>
+__global__ void xent_from_probs_kernel(float* __restrict__ losses, const T* __restrict__ probs,
+                                       const int* __restrict__ targets, int rows, int ld, int accumulate) {
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= rows) return;
+  const int t = targets[r];
+  const float l = (t >= 0 && t < ld) ? -logf(to_f(probs[static_cast<long long>(r) * ld + t])) : __int_as_float(0x7fc00000);
+  losses[r] = accumulate ? losses[r] + l : l;
+}
+
+// dlogits[row, c] = (accumulate ? dlogits[row, c] : 0) + (probs[row, c] -
+// [c == target]) * scale on the columns c < V; [V, ld) untouched.
+template <typename T>
+__global__ void xent_softmax_backward_kernel(T* __restrict__ dlogits, const T* __restrict__ probs,
+                                             const int* __restrict__ targets, int V, int ld, float scale,
+                                             int accumulate) {
+  const long long row = blockIdx.y;
+  const int t = targets[row];
+  const T* p = probs + row * ld;
+  T* d = dlogits + row * ld;
+  for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < V; c += gridDim.x * blockDim.x) {
+    float g = (to_f(p[c]) - (c == t ? 1.f : 0.f)) * scale;
+    if (accumulate) g += to_f(d[c]);
+    if constexpr (sizeof(T) == 4) d[c] = g;
+    else d[c] = __float2bfloat16(g);
   }
 }
 
@@ -892,6 +940,69 @@ int llmk_softmax_crossentropy(float* losses, void* dlogits, const void* logits, 
     softmax_xent_kernel<float><<<BT, 512, 0, s>>>(losses, static_cast<float*>(dlogits),
                                                   static_cast<const float*>(logits), targets, V, Vp, dscale);
   count_launch();
+  LLMK_CUDA(cudaGetLastError());
+  return LLMK_OK;
+}
+
+int llmk_softmax_forward(void* probs, const void* logits, llmk_dtype dtype, int rows, int V, int ld, void* stream) {
+  if (!probs || !logits || rows <= 0 || V <= 0 || ld < V) return fail(LLMK_ERR_INVALID_ARG, "softmax_forward");
+  if (dtype != LLMK_F32 && dtype != LLMK_BF16) return fail(LLMK_ERR_UNSUPPORTED, "softmax_forward: fp32 or bf16");
+  if (ld % 8 || !a16(logits) || !a16(probs)) return fail(LLMK_ERR_UNSUPPORTED, "softmax_forward: ld % 8, 16-byte rows");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == LLMK_BF16)
+    softmax_xent_kernel<__nv_bfloat16, true><<<rows, 512, 0, s>>>(
+        nullptr, static_cast<__nv_bfloat16*>(probs), static_cast<const __nv_bfloat16*>(logits), nullptr, V, ld, 1.f);
+  else
+    softmax_xent_kernel<float, true><<<rows, 512, 0, s>>>(nullptr, static_cast<float*>(probs),
+                                                          static_cast<const float*>(logits), nullptr, V, ld, 1.f);
+  count_launch();
+  LLMK_CUDA(cudaGetLastError());
+  return LLMK_OK;
+}
+
+int llmk_crossentropy_forward(float* losses, const void* probs, llmk_dtype dtype, const int* targets, int rows, int ld,
+                              int accumulate, void* stream) {
+  if (!losses || !probs || !targets || rows <= 0 || ld <= 0) return fail(LLMK_ERR_INVALID_ARG, "crossentropy_forward");
+  if (dtype != LLMK_F32 && dtype != LLMK_BF16) return fail(LLMK_ERR_UNSUPPORTED, "crossentropy_forward: fp32 or bf16");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int blocks = (rows + 255) / 256;
+  if (dtype == LLMK_BF16)
+    xent_from_probs_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(
+        losses, static_cast<const __nv_bfloat16*>(probs), targets, rows, ld, accumulate);
+  else
+    xent_from_probs_kernel<float><<<blocks, 256, 0, s>>>(losses, static_cast<const float*>(probs), targets, rows, ld,
+                                                         accumulate);
+  count_launch();
+  LLMK_CUDA(cudaGetLastError());
+  return LLMK_OK;
+}
+
+int llmk_crossentropy_softmax_backward(void* dlogits, const void* probs, llmk_dtype dtype, const int* targets,
+                                       int rows, int V, int ld, float scale, int accumulate, void* stream) {
+  if (!dlogits || !probs || !targets || rows <= 0 || V <= 0 || ld < V)
+    return fail(LLMK_ERR_INVALID_ARG, "crossentropy_softmax_backward");
+  if (dtype != LLMK_F32 && dtype != LLMK_BF16)
+    return fail(LLMK_ERR_UNSUPPORTED, "crossentropy_softmax_backward: fp32 or bf16");
+  if (rows > 65535 * 1024) return fail(LLMK_ERR_UNSUPPORTED, "crossentropy_softmax_backward: too many rows");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // rows on grid.y (chunks of 65535), columns on grid.x
+  const int cx = std::min((V + 255) / 256, 16);
+  for (int r0 = 0; r0 < rows; r0 += 65535) {
+    const int n = std::min(65535, rows - r0);
+    dim3 grid(cx, n);
+    const size_t off = static_cast<size_t>(r0) * ld * (dtype == LLMK_BF16 ? 2 : 4);
+    if (dtype == LLMK_BF16)
+      xent_softmax_backward_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(
+          reinterpret_cast<__nv_bfloat16*>(static_cast<char*>(dlogits) + off),
+          reinterpret_cast<const __nv_bfloat16*>(static_cast<const char*>(probs) + off), targets + r0, V, ld, scale,
+          accumulate);
+    else
+      xent_softmax_backward_kernel<float><<<grid, 256, 0, s>>>(
+          reinterpret_cast<float*>(static_cast<char*>(dlogits) + off),
+          reinterpret_cast<const float*>(static_cast<const char*>(probs) + off), targets + r0, V, ld, scale,
+          accumulate);
+    count_launch();
+  }
   LLMK_CUDA(cudaGetLastError());
   return LLMK_OK;
 }

@@ -119,11 +119,20 @@ size_t colsum_workspace(int M, int N) {
 // Scratch of llmk_colsum_noalloc: a fixed device array that every GPU loading
 // this library holds until the process exits (1 MiB). Host code must not pass
 // `g_colsum_noalloc_scratch` itself to a kernel (on the host it names a
-// host-side stand-in); it passes the device address fetched once per device.
+// host-side stand-in); it passes the device address that SymbolCache looks
+// up with cudaGetSymbolAddress once per device (and again after a device
+// reset gave the device a new context).
 constexpr int kColsumNoAllocFloats = 1 << 18;
 static __device__ __align__(256) float g_colsum_noalloc_scratch[kColsumNoAllocFloats];
-static float* g_colsum_noalloc_ptr[64] = {};
-static std::mutex g_colsum_noalloc_mu;
+static cudaError_t lookup_colsum_noalloc(void** p) { return cudaGetSymbolAddress(p, g_colsum_noalloc_scratch); }
+static SymbolCache g_colsum_noalloc_addr(lookup_colsum_noalloc);
+
+// The column sums read fp32 or bf16; anything else is refused rather than
+// reinterpreted.
+static int colsum_dtype_ok(llmk_dtype t, const char* what) {
+  if (t == LLMK_F32 || t == LLMK_BF16) return LLMK_OK;
+  return fail(LLMK_ERR_UNSUPPORTED, std::string(what) + ": x must be fp32 or bf16");
+}
 
 }  // namespace llmk
 
@@ -136,6 +145,7 @@ size_t llmk_colsum_workspace(int M, int N) { return colsum_workspace(M, N); }
 int llmk_colsum(float* dbias, const void* x, llmk_dtype x_dtype, int M, int N, int accumulate, void* workspace,
                 size_t workspace_bytes, void* stream) {
   if (!dbias || !x || M <= 0 || N <= 0) return fail(LLMK_ERR_INVALID_ARG, "colsum: bad arguments");
+  LLMK_TRY(colsum_dtype_ok(x_dtype, "colsum"));
   if (N % 8 || !aligned16(x)) return fail(LLMK_ERR_UNSUPPORTED, "colsum: N % 8 == 0 and 16-byte alignment required");
   if (!workspace || workspace_bytes < colsum_workspace(M, N))
     return fail(LLMK_ERR_WORKSPACE, "colsum: workspace too small");
@@ -148,33 +158,21 @@ int llmk_colsum(float* dbias, const void* x, llmk_dtype x_dtype, int M, int N, i
 // scratch array with that device current; later calls reuse it.
 int llmk_colsum_noalloc(float* dbias, const void* x, llmk_dtype x_dtype, int M, int N, int accumulate, void* stream) {
   if (!dbias || !x || M <= 0 || N <= 0) return fail(LLMK_ERR_INVALID_ARG, "colsum_noalloc: bad arguments");
+  LLMK_TRY(colsum_dtype_ok(x_dtype, "colsum_noalloc"));
   if (N % 8 || !aligned16(x))
     return fail(LLMK_ERR_UNSUPPORTED, "colsum_noalloc: N % 8 == 0 and 16-byte alignment required");
-  // as many row chunks as the fixed scratch holds (at least one)
+  // One row chunk needs N partial sums: N up to the array's size is
+  // accepted, with as many row chunks (any M) as the array holds.
+  if (N > kColsumNoAllocFloats)
+    return fail(LLMK_ERR_UNSUPPORTED, "colsum_noalloc: N = " + std::to_string(N) + " exceeds the fixed scratch of " +
+                                          std::to_string(kColsumNoAllocFloats) +
+                                          " floats (use llmk_colsum with a caller workspace)");
   const int max_chunks = static_cast<int>(std::min<size_t>(colsum_chunks(M, N), kColsumNoAllocFloats / N));
-  const size_t need = static_cast<size_t>(std::max(max_chunks, 1)) * N;
-  if (max_chunks < 1 || need > static_cast<size_t>(kColsumNoAllocFloats))
-    return fail(LLMK_ERR_UNSUPPORTED,
-                "colsum_noalloc: M x N needs " + std::to_string(need) + " scratch floats, more than the fixed " +
-                    std::to_string(kColsumNoAllocFloats) + " (use llmk_colsum with a caller workspace)");
-  int dev = 0;
-  LLMK_CUDA(cudaGetDevice(&dev));
-  if (dev < 0 || dev >= 64) return fail(LLMK_ERR_UNSUPPORTED, "colsum_noalloc: device index out of range");
-  float* scratch = nullptr;
-  {
-    std::lock_guard<std::mutex> lk(g_colsum_noalloc_mu);
-    if (!g_colsum_noalloc_ptr[dev]) {
-      void* p = nullptr;
-      cudaError_t e = cudaGetSymbolAddress(&p, g_colsum_noalloc_scratch);
-      if (e != cudaSuccess || p == nullptr)
-        return fail(LLMK_ERR_CUDA, std::string("colsum_noalloc: cudaGetSymbolAddress: ") + cudaGetErrorString(e));
-      g_colsum_noalloc_ptr[dev] = static_cast<float*>(p);
-    }
-    scratch = g_colsum_noalloc_ptr[dev];
-  }
+  void* scratch = nullptr;
+  LLMK_TRY(g_colsum_noalloc_addr.get(&scratch));
   // Pass 1 overwrites every partial that pass 2 reads, so nothing in the
   // shared scratch has to start at zero.
-  return colsum_launch(dbias, x, x_dtype == LLMK_BF16, M, N, accumulate, scratch,
+  return colsum_launch(dbias, x, x_dtype == LLMK_BF16, M, N, accumulate, static_cast<float*>(scratch),
                        static_cast<cudaStream_t>(stream), max_chunks);
 }
 

@@ -16,9 +16,29 @@ std::atomic<unsigned long long> g_launches{0};
 constexpr int kMaxDevices = 64;
 // One status word per device, in device global memory of this module.
 __device__ unsigned int g_device_status;
-unsigned int* g_status_ptr[kMaxDevices] = {};
 int g_num_sms[kMaxDevices] = {};
 std::mutex g_mu;
+
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+CtxGetCurrentFn g_ctx_get = nullptr;
+bool g_ctx_get_tried = false;
+
+// The current CUDA context (the device's primary context once the runtime
+// has touched it), fetched through the runtime's driver entry point; nullptr
+// when it cannot be queried. Caller holds g_mu.
+CUcontext current_context_locked() {
+  if (!g_ctx_get_tried) {
+    g_ctx_get_tried = true;
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_ctx_get = reinterpret_cast<CtxGetCurrentFn>(fn);
+  }
+  CUcontext ctx = nullptr;
+  if (g_ctx_get) g_ctx_get(&ctx);
+  return ctx;
+}
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -50,16 +70,37 @@ int cuda_check(cudaError_t e, const char* what) {
   return fail(LLMK_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
 }
 
-unsigned int* device_status_ptr() {
+int SymbolCache::get(void** out) {
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  LLMK_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) return fail(LLMK_ERR_UNSUPPORTED, "device index out of range");
+  // No device call here: this runs on every kernel launch, also inside stream
+  // capture. Before the runtime has made a context current the context reads
+  // as null; the lookup below creates it, and the next call refreshes the
+  // entry once under the real context.
   std::lock_guard<std::mutex> lk(g_mu);
-  if (!g_status_ptr[dev]) {
+  const CUcontext ctx = current_context_locked();
+  if (!ptr_[dev] || ctx_[dev] != static_cast<void*>(ctx)) {
     void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_device_status) != cudaSuccess) return nullptr;
-    g_status_ptr[dev] = static_cast<unsigned int*>(p);
+    const cudaError_t e = lookup_(&p);
+    if (e != cudaSuccess || p == nullptr)
+      return fail(LLMK_ERR_CUDA, std::string("cudaGetSymbolAddress: ") + cudaGetErrorString(e));
+    ptr_[dev] = p;
+    ctx_[dev] = ctx;
   }
-  return g_status_ptr[dev];
+  *out = ptr_[dev];
+  return LLMK_OK;
+}
+
+namespace {
+cudaError_t lookup_status(void** p) { return cudaGetSymbolAddress(p, g_device_status); }
+SymbolCache g_status_cache(lookup_status);
+}  // namespace
+
+unsigned int* device_status_ptr() {
+  void* p = nullptr;
+  if (g_status_cache.get(&p) != LLMK_OK) return nullptr;
+  return static_cast<unsigned int*>(p);
 }
 
 int num_sms() {

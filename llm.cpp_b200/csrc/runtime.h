@@ -22,6 +22,27 @@ int cuda_check(cudaError_t e, const char* what);
 // LLMK_DEV_TIMEOUT into it). Never null after a successful call.
 unsigned int* device_status_ptr();
 
+// Device address of a file-scope __device__ array, looked up with
+// cudaGetSymbolAddress once per device and context and cached. A module's
+// symbols get new addresses when the device's primary context is destroyed
+// (cudaDeviceReset) and created again, so the cache is keyed on the current
+// context as well as the device and is refreshed when that context changes.
+// `lookup` calls cudaGetSymbolAddress on the symbol in its own translation
+// unit (host code only ever sees a host-side stand-in of the array).
+class SymbolCache {
+ public:
+  using Lookup = cudaError_t (*)(void**);
+  explicit SymbolCache(Lookup lookup) : lookup_(lookup) {}
+  // Device address for the current device; LLMK_OK or LLMK_ERR_*.
+  int get(void** out);
+
+ private:
+  static constexpr int kDevices = 64;
+  Lookup lookup_;
+  void* ptr_[kDevices] = {};
+  void* ctx_[kDevices] = {};
+};
+
 // Number of SMs of the current device (cached per device).
 int num_sms();
 

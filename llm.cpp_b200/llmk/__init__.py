@@ -82,6 +82,9 @@ SIGNATURES: dict[str, tuple] = {
     "llmk_encoder_backward_workspace": (sz, [i32, i32]),
     "llmk_encoder_backward": (i32, [vp, vp, vp, vp, i32, i32, i32, i32, vp, sz, vp]),
     "llmk_softmax_crossentropy": (i32, [vp, vp, vp, i32, vp, i32, i32, i32, f32, vp]),
+    "llmk_softmax_forward": (i32, [vp, vp, i32, i32, i32, i32, vp]),
+    "llmk_crossentropy_forward": (i32, [vp, vp, i32, vp, i32, i32, i32, vp]),
+    "llmk_crossentropy_softmax_backward": (i32, [vp, vp, i32, vp, i32, i32, i32, f32, i32, vp]),
     "llmk_matmul_softmax_workspace": (sz, [i32, i32]),
     "llmk_matmul_softmax_forward": (i32, [vp, vp, i32, vp, vp, vp, i32, i32, i32, i32, i32, vp, sz, vp]),
     "llmk_matmul_crossentropy_forward": (i32, [vp, vp, i32, vp, vp, vp, vp, i32, i32, i32, i32, f32, i32, i32, vp, sz,

@@ -15,7 +15,34 @@ import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_LIB = os.path.join(HERE, "liboracle.so")
-REF_LIB = os.path.join(HERE, "_ref", "libref.so")
+REF_LIB = os.path.join(HERE, "_ref", "libref.so")          # -march=x86-64-v3
+REF_LIB_V4 = os.path.join(HERE, "_ref", "libref_v4.so")    # -march=x86-64-v4 (AVX-512)
+_AVX512 = ("avx512f", "avx512bw", "avx512cd", "avx512dq", "avx512vl")
+
+
+def _host_has_avx512() -> bool:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("flags"):
+                    flags = set(line.split(":", 1)[1].split())
+                    return all(x in flags for x in _AVX512)
+    except OSError:
+        pass
+    return False
+
+
+def ref_path() -> str:
+    """The reference build for this host: the AVX-512 one when the CPU has it."""
+    if os.path.exists(REF_LIB_V4) and _host_has_avx512():
+        return REF_LIB_V4
+    return REF_LIB
+
+
+def ref_build() -> str:
+    """Compiler flags of the reference build ref() loads."""
+    isa = "-march=x86-64-v4" if ref_path() == REF_LIB_V4 else "-march=x86-64-v3"
+    return f"g++ -O3 {isa} -ffast-math -fopenmp (CMakeLists.txt Release flags, ISA level of the host)"
 
 fp = np.ctypeslib.ndpointer(dtype=np.float32, flags="C_CONTIGUOUS")
 ip = np.ctypeslib.ndpointer(dtype=np.int32, flags="C_CONTIGUOUS")
@@ -109,15 +136,16 @@ def orc():
 
 
 def ref_available() -> bool:
-    return os.path.exists(REF_LIB)
+    return os.path.exists(ref_path())
 
 
 def ref():
     global _ref
     if _ref is None:
         if not ref_available():
-            raise OSError(f"{REF_LIB} not built (run `make -C oracle ref` where the reference tree exists)")
-        _ref = _load(REF_LIB, _REF_SIGS)
+            raise OSError(f"{REF_LIB} not built (run `make -C oracle ref REF=<reference root>` where the "
+                          f"reference tree exists)")
+        _ref = _load(ref_path(), _REF_SIGS)
     return _ref
 
 

@@ -11,7 +11,7 @@ run) and writes tests/golden/reference_unit_vectors.json:
 Numbers come from Eigen comma initialisers (`x << a, b, ...;`) and brace
 initialisers (`Matf{{...},{...}}`, `VecBTC v{Matf{...}, Matf{...}}`), in
 row-major order, which is the order Eigen fills them. The values are the
-PyTorch outputs the reference's notebooks produced (SURVEY: tests/gpt2/*_note.ipynb).
+PyTorch outputs the reference's notebooks produced (tests/gpt2/*_note.ipynb in the reference tree).
 """
 from __future__ import annotations
 
@@ -86,4 +86,7 @@ def main(root: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("LLMK_REFERENCE_DIR")
+    if not root:
+        sys.exit("usage: extract_reference_goldens.py REFERENCE_ROOT (or set LLMK_REFERENCE_DIR)")
+    main(root)

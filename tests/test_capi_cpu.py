@@ -55,6 +55,14 @@ def test_argument_validation_without_gpu(llmk_lib):
                                               llmk.MATH_BF16, None, 0, None) == 5
     assert L.llmk_matmul_softmax_forward(fake, fake, llmk.BF16, fake, fake, None, 8, 64, 510, 500, llmk.MATH_BF16,
                                          fake, 1 << 20, None) == 2  # Vp % 8
+    # the column sums read fp32 or bf16 only: fp16 is refused, not read as fp32
+    assert L.llmk_colsum(fake, fake, llmk.F16, 64, 64, 0, fake, 1 << 20, None) == 2
+    assert b"fp32 or bf16" in L.llmk_last_error()
+    assert L.llmk_colsum_noalloc(fake, fake, llmk.F16, 64, 64, 0, None) == 2
+    assert L.llmk_colsum_noalloc(fake, fake, 7, 64, 64, 0, None) == 2
+    # the no-allocation column sum accepts up to 262144 columns, refused above before any device call
+    assert L.llmk_colsum_noalloc(fake, fake, llmk.F32, 64, (1 << 18) + 8, 0, None) == 2
+    assert b"exceeds the fixed scratch" in L.llmk_last_error()
 
 
 def test_dp_buckets_partition_parameters(llmk_lib):

@@ -5,9 +5,18 @@ test_config0_loss_trajectory: configuration 0 of the benchmark spec (GPT-2
 The expected losses are the reference's own (llm.cpp gpt2/*.cpp compiled and
 run by tests/golden/make_fixtures.py). In TF32 mode (fp32 activations, TF32
 GEMMs: the reference GPU path's precision) the bar is |L_gpu - L_ref| / L_ref
-<= 0.5% at every step. The bf16 mode (bf16 GEMM operands and activations) is
-held to 2%: this run overfits one batch from loss 11 to 2 in 20 steps, and
-bf16 rounding of every activation compounds over the steps.
+<= 0.5% at every step, for both modes: TF32 (fp32 activations, TF32 GEMMs:
+the reference GPU path's precision) and bf16 (bf16 GEMM operands and
+activations, fp32 master weights: what the benchmark runs).
+
+The bf16 run has little margin (about 0.5% at its worst step, measured on a
+B200). That is bf16 arithmetic, not a kernel fault: the run overfits one batch
+from loss 11 to 2 in 20 steps, so any rounding perturbation grows along the
+trajectory. tests/golden/bf16_drift.py replays the same 20 steps in fp32
+torch on the CPU with bf16 rounding at the points the device rounds; its
+committed result (tests/golden/gpt2_124m_b4t64_bf16_drift.json) shows 0.3-0.6%
+worst-step drift from rounding the weights alone, the activations alone, or
+everything, against 0.003% for the unrounded fp32 replay.
 """
 import json
 import os
@@ -28,7 +37,7 @@ def _model(llmk, cfg, B, T, math):
                      channels=cfg.channels, math=math)
 
 
-@pytest.mark.parametrize("mathname,bar", [("tf32", 5e-3), ("bf16", 2e-2)])
+@pytest.mark.parametrize("mathname,bar", [("tf32", 5e-3), ("bf16", 5e-3)])
 def test_config0_loss_trajectory(cuda_dev, mathname, bar):
     import llmk
     math = llmk.MATH_TF32 if mathname == "tf32" else llmk.MATH_BF16
@@ -172,4 +181,93 @@ def test_graph_steps_match_eager(cuda_dev, mathname):
     (l0, p0), (l1, p1) = runs
     assert np.allclose(l0, l1, rtol=1e-5, atol=0), (l0, l1)
     assert np.abs(p1 - p0).max() / np.abs(p0).max() < 1e-4
+    assert llmk.device_status() == 0
+
+
+_CONFIG3_REF = {}
+
+
+def _config3_oracle():
+    """The oracle's loss and gradients of one GPT-2 124M step at T = 1024
+    (configuration 3's sequence length and model; B = 1, seed 31)."""
+    if not _CONFIG3_REF:
+        cfg = O.config()
+        B, T = 1, 1024
+        params = O.init_params(cfg, 31)
+        toks = O.tokens(B * T + 1, cfg.vocab_size, 31)
+        ref = O.Model(cfg, params, B, T)
+        loss = ref.forward(toks[:-1], toks[1:])
+        ref.zero_grad()
+        ref.backward()
+        _CONFIG3_REF.update(cfg=cfg, B=B, T=T, params=params, toks=toks, loss=loss, grads=ref.grads())
+        del ref
+    return _CONFIG3_REF
+
+
+@pytest.mark.parametrize("mathname,ltol,gtol", [("bf16", 1e-2, 5e-2), ("tf32", 1e-3, 1e-2)])
+def test_config3_step_vs_oracle(cuda_dev, mathname, ltol, gtol):
+    """Configuration 3's model at its full sequence length: one GPT-2 124M
+    training step (B = 1, T = 1024) through the native trainer against the
+    oracle — loss and every parameter gradient (norm-wise relative error, the
+    reference tests' isApprox metric; the max relative error is printed)."""
+    import llmk
+    math = llmk.MATH_TF32 if mathname == "tf32" else llmk.MATH_BF16
+    r = _config3_oracle()
+    cfg, B, T = r["cfg"], r["B"], r["T"]
+    m = _model(llmk, cfg, B, T, math)
+    m.load_parameters(r["params"])
+    loss = m.train_step(r["toks"][:-1], r["toks"][1:], 0.0, t=1)
+    g = m.read_gradients()
+    m.close()
+    assert abs(loss - r["loss"]) / r["loss"] < ltol, (loss, r["loss"])
+    names = ["wte", "wpe", "ln1w", "ln1b", "qkvw", "qkvb", "attprojw", "attprojb", "ln2w", "ln2b", "fcw", "fcb",
+             "fcprojw", "fcprojb", "lnfw", "lnfb"]
+    off = 0
+    report = {}
+    for name, n in zip(names, O.param_sizes(cfg)):
+        a, b = g[off:off + n].astype(np.float64), r["grads"][off:off + n].astype(np.float64)
+        off += n
+        nrm = np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30)
+        mx = np.abs(a - b).max() / max(np.abs(b).max(), 1e-30)
+        report[name] = (nrm, mx)
+    print(mathname, f"loss {loss:.6f} oracle {r['loss']:.6f}",
+          {k: f"{v[0]:.1e}/{v[1]:.1e}" for k, v in report.items()})
+    for name, (nrm, mx) in report.items():
+        assert nrm < gtol, f"{name}: norm-rel err {nrm:.3e}"
+    assert llmk.device_status() == 0
+
+
+@pytest.mark.parametrize("mathname,tol", [("bf16", 5e-2), ("tf32", 1e-2)])
+def test_774m_shape_gradients_vs_oracle(cuda_dev, mathname, tol):
+    """Configuration 4's layer shape (C = 1280, NH = 20, head size 64: K = 1280
+    GEMMs, 20-head attention, 1280-wide LayerNorms) in a 2-layer model, one
+    step against the oracle: loss and every gradient tensor."""
+    import llmk
+    math = llmk.MATH_TF32 if mathname == "tf32" else llmk.MATH_BF16
+    cfg = O.config(max_seq_len=256, vocab_size=1000, padded_vocab_size=1024, num_layers=2, num_heads=20,
+                   channels=1280)
+    B, T = 2, 256
+    params = O.init_params(cfg, 41)
+    toks = O.tokens(B * T + 1, cfg.vocab_size, 41)
+    ref = O.Model(cfg, params, B, T)
+    loss_ref = ref.forward(toks[:-1], toks[1:])
+    ref.zero_grad()
+    ref.backward()
+    g_ref = ref.grads()
+    m = _model(llmk, cfg, B, T, math)
+    m.load_parameters(params)
+    loss = m.train_step(toks[:-1], toks[1:], 0.0, t=1)
+    g = m.read_gradients()
+    m.close()
+    assert abs(loss - loss_ref) / loss_ref < (1e-3 if mathname == "tf32" else 1e-2), (loss, loss_ref)
+    names = ["wte", "wpe", "ln1w", "ln1b", "qkvw", "qkvb", "attprojw", "attprojb", "ln2w", "ln2b", "fcw", "fcb",
+             "fcprojw", "fcprojb", "lnfw", "lnfb"]
+    off = 0
+    for name, n in zip(names, O.param_sizes(cfg)):
+        a, b = g[off:off + n].astype(np.float64), g_ref[off:off + n].astype(np.float64)
+        off += n
+        if name == "wpe":  # rows beyond T have zero gradient in both
+            a, b = a[:T * cfg.channels], b[:T * cfg.channels]
+        nrm = np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30)
+        assert nrm < tol, f"{name}: norm-rel err {nrm:.3e}"
     assert llmk.device_status() == 0
