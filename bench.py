@@ -34,6 +34,7 @@ import argparse
 import json
 import os
 import platform
+import re
 import statistics
 import subprocess
 import sys
@@ -363,7 +364,7 @@ def nccl_summary(path: str) -> dict:
         lines = open(path, errors="replace").read().splitlines()
     except OSError:
         return {"unavailable": "no NCCL debug log"}
-    chans, nvls = set(), None
+    chans, nvls, algos = set(), None, {}
     for ln in lines:
         if "NCCL version" in ln and "version" not in info:
             info["version"] = ln.split("NCCL version", 1)[1].strip().split()[0]
@@ -379,7 +380,13 @@ def nccl_summary(path: str) -> dict:
                 nvls = False if nvls is None else nvls
         if "coll channels" in ln and "coll_channels_line" not in info:
             info["coll_channels_line"] = ln.split("NCCL INFO", 1)[-1].strip()[:200]
+        # the tuner's per-call choice (NCCL_DEBUG_SUBSYS=TUNING): "... Algo <a> proto <p> ..."
+        ma, mp = re.search(r"[Aa]lgo[ =:]+(\w+)", ln), re.search(r"[Pp]roto(?:col)?[ =:]+(\w+)", ln)
+        if ma and mp:
+            key = f"{ma.group(1)}/{mp.group(1)}"
+            algos[key] = algos.get(key, 0) + 1
     info["channels_seen"] = len(chans)
+    info["algo_proto_counts"] = algos
     info["nvls"] = nvls
     info["env"] = {k: v for k, v in os.environ.items() if k.startswith("NCCL_") and k not in ("NCCL_DEBUG_FILE",)}
     return info
@@ -596,7 +603,7 @@ def run_case(args) -> None:
       attnbwd [B T NH]                            llmk_attention_backward, bf16
       gemmset [BT]   every GEMM shape of one GPT-2 124M step (fwd, dinp, dweight)
       lmxent  [BT] [--variant fused|unfused|gemm] lm_head + softmax + cross-entropy
-      step    [B T]                               one graph-replayed training step
+      step    [B T]                               one eager training step
       lnfwd   [N C]  llmk_layernorm_forward, fp32 in, bf16 out
       lnbwd   [N C]  llmk_layernorm_backward with the bf16 mirror and column sums
       adamw   [n]    llmk_adamw over n parameters with the bf16 mirror
@@ -755,7 +762,7 @@ def run_case(args) -> None:
         toks = np.random.default_rng(1).integers(0, 50257, size=Bb * Tt + 1, dtype=np.int32)
         m.train_step(toks[:-1], toks[1:], 0.0, t=1, want_loss=False)
         d_in, d_tg = m.buffers()
-        m.use_graph(True)
+        # eager (one launch per kernel, as the committed launch lists count them)
         torch.cuda.set_stream(torch.cuda.ExternalStream(m.stream))
         state = {"t": 2}
 

@@ -117,6 +117,8 @@ struct llmk_gpt2 {
   int rank = 0, world = 1;
   std::vector<cudaEvent_t> layer_done;
   cudaEvent_t embed_done = nullptr, comm_done = nullptr, h2d_done = nullptr;
+  // data parallel: lnf bucket issued, every bucket but the embeddings reduced
+  cudaEvent_t lnf_done = nullptr, layers_reduced = nullptr;
   unsigned long long steps = 0;
   // per-kernel-class timing (llmk_gpt2_set_timing): event pairs on `stream`
   struct Mark {
@@ -275,6 +277,8 @@ void free_all(llmk_gpt2* g) {
   for (auto e : g->layer_done) cudaEventDestroy(e);
   if (g->embed_done) cudaEventDestroy(g->embed_done);
   if (g->comm_done) cudaEventDestroy(g->comm_done);
+  if (g->lnf_done) cudaEventDestroy(g->lnf_done);
+  if (g->layers_reduced) cudaEventDestroy(g->layers_reduced);
   if (g->h2d_done) cudaEventDestroy(g->h2d_done);
   for (auto e : g->tev) cudaEventDestroy(e);
   if (g->graph_exec) cudaGraphExecDestroy(g->graph_exec);
@@ -340,6 +344,8 @@ int alloc_all(llmk_gpt2* g) {
   for (auto& e : g->layer_done) LLMK_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
   LLMK_CUDA(cudaEventCreateWithFlags(&g->embed_done, cudaEventDisableTiming));
   LLMK_CUDA(cudaEventCreateWithFlags(&g->comm_done, cudaEventDisableTiming));
+  LLMK_CUDA(cudaEventCreateWithFlags(&g->lnf_done, cudaEventDisableTiming));
+  LLMK_CUDA(cudaEventCreateWithFlags(&g->layers_reduced, cudaEventDisableTiming));
   LLMK_CUDA(cudaEventCreateWithFlags(&g->h2d_done, cudaEventDisableTiming));
   return LLMK_OK;
 }
@@ -643,6 +649,8 @@ int llmk_gpt2_backward(llmk_gpt2* g) {
   // the column sums of the new dres are the last layer's fcproj bias gradient
   LLMK_TRY(op.ln_bwd(g->dres, dres_mirror, G + g->off_lnfw, G + g->off_lnfb, L > 0 ? G + g->lp[L - 1].fcprojb : nullptr,
                      g->dln, xL, P + g->off_lnfw, g->lnf_mean, g->lnf_rstd, BT, C, 0, ws, wsb));
+  // the final LayerNorm's gradients are final now: reduce them first
+  LLMK_TRY(allreduce_bucket(g, g->lnf_done, g->off_lnfw, g->off_lnfw + 2 * static_cast<size_t>(C)));
   for (int l = L - 1; l >= 0; --l) {
     // Layer::Backward (gpt2/cuda/layer.cu:180-266); dres = d(layer output)
     const LayerParams& p = g->lp[l];
@@ -695,36 +703,50 @@ int llmk_gpt2_backward(llmk_gpt2* g) {
     TimedScope ts(g, KC_ENCODER, bt_c * 12.0 + 8.0 * static_cast<double>(T) * C + 4.0 * BT);
     LLMK_TRY(llmk_encoder_backward(G + g->off_wte, G + g->off_wpe, g->dres, g->inputs, B, T, C, Vp, ws, wsb, s));
   }
-  // wte/wpe bucket, then lnf bucket
+  // Everything but the embeddings is reduced once the comm stream passes
+  // here; the wte/wpe bucket (the encoder backward's scatter completes it)
+  // goes last, and llmk_gpt2_update updates every other parameter while it
+  // is still being reduced.
+  if (g->world > 1) LLMK_CUDA(cudaEventRecord(g->layers_reduced, g->comm_stream));
   LLMK_TRY(allreduce_bucket(g, g->embed_done, g->off_wte, g->off_wpe + g->tsize[llmk::WPE]));
-  if (g->world > 1) {
-    LLMK_TRY(nccl_check(ncclAllReduce(G + g->off_lnfw, G + g->off_lnfw, 2 * C, ncclFloat, ncclSum, g->comm,
-                                      g->comm_stream),
-                        "ncclAllReduce"));
-    LLMK_CUDA(cudaEventRecord(g->comm_done, g->comm_stream));
-    LLMK_CUDA(cudaStreamWaitEvent(s, g->comm_done, 0));
-  }
+  if (g->world > 1) LLMK_CUDA(cudaEventRecord(g->comm_done, g->comm_stream));
   return LLMK_OK;
 }
 
-// AdamW over the flat buffer with its hyperparameters read from g->hp_dev
-// (the form a captured graph replays).
-static int update_device_hparams(llmk_gpt2* g) {
-  TimedScope ts(g, KC_ADAMW, static_cast<double>(g->nparams) * (28.0 + (g->params_bf16 ? 2.0 : 0.0)));
-  LLMK_TRY(llmk_adamw_device_hparams(g->params, g->params_bf16, g->grads, g->m, g->v,
-                                     static_cast<long long>(g->nparams), g->hp_dev, g->stream));
-  return LLMK_OK;
+// AdamW over the flat buffer: one multi-tensor launch (the reference launches
+// one AdamW per tensor, gpt2cuda.cu:434-441), gradients averaged over ranks.
+// Under data parallelism it runs in two ranges: every parameter but the
+// embeddings as soon as their buckets are reduced, then wte / wpe once
+// their bucket is — so that update overlaps the embedding all-reduce, the
+// one the backward cannot hide. hp: the hyperparameters in device memory
+// (the form a captured graph replays), or nullptr to pass them by value.
+static int adamw_ranges(llmk_gpt2* g, const float* hp, float lr, float beta1, float beta2, float eps,
+                        float weight_decay, int t) {
+  const float scale = 1.0f / static_cast<float>(g->world);
+  auto range = [&](size_t begin, size_t end) -> int {
+    // p, g, m, v read; p, m, v written; plus the bf16 mirror in bf16 mode
+    TimedScope ts(g, KC_ADAMW, static_cast<double>(end - begin) * (28.0 + (g->params_bf16 ? 2.0 : 0.0)));
+    __nv_bfloat16* pb = g->params_bf16 ? g->params_bf16 + begin : nullptr;
+    const long long n = static_cast<long long>(end - begin);
+    if (hp)
+      return llmk_adamw_device_hparams(g->params + begin, pb, g->grads + begin, g->m + begin, g->v + begin, n, hp,
+                                       g->stream);
+    return llmk_adamw(g->params + begin, pb, g->grads + begin, g->m + begin, g->v + begin, n, lr, beta1, beta2, eps,
+                      weight_decay, t, scale, g->stream);
+  };
+  if (g->world <= 1) return range(0, g->nparams);
+  const size_t emb_end = g->off_wpe + g->tsize[llmk::WPE];  // [wte | wpe] lead the flat buffer
+  LLMK_CUDA(cudaStreamWaitEvent(g->stream, g->layers_reduced, 0));
+  LLMK_TRY(range(emb_end, g->nparams));
+  LLMK_CUDA(cudaStreamWaitEvent(g->stream, g->comm_done, 0));
+  return range(0, emb_end);
 }
+
+static int update_device_hparams(llmk_gpt2* g) { return adamw_ranges(g, g->hp_dev, 0.f, 0.f, 0.f, 0.f, 0.f, 1); }
 
 int llmk_gpt2_update(llmk_gpt2* g, float lr, float beta1, float beta2, float eps, float weight_decay, int t) {
   if (!g || t < 1) return fail(LLMK_ERR_INVALID_ARG, "gpt2_update");
-  // one multi-tensor launch over the flat buffer (the reference launches one
-  // AdamW per tensor, gpt2cuda.cu:434-441); gradients are averaged over ranks
-  const float scale = 1.0f / static_cast<float>(g->world);
-  // p, g, m, v read; p, m, v written; plus the bf16 mirror in bf16 mode
-  TimedScope ts(g, KC_ADAMW, static_cast<double>(g->nparams) * (28.0 + (g->params_bf16 ? 2.0 : 0.0)));
-  LLMK_TRY(llmk_adamw(g->params, g->params_bf16, g->grads, g->m, g->v, static_cast<long long>(g->nparams), lr, beta1,
-                      beta2, eps, weight_decay, t, scale, g->stream));
+  LLMK_TRY(adamw_ranges(g, nullptr, lr, beta1, beta2, eps, weight_decay, t));
   ++g->steps;
   return LLMK_OK;
 }
