@@ -409,8 +409,9 @@ def run_ours(args) -> None:
     nccl_log = None
     if world > 1:
         nccl_log = os.path.join(tempfile.gettempdir(), f"llmk_nccl_{os.getpid()}.log")
-        os.environ.setdefault("NCCL_DEBUG", "INFO")
-        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT,TUNING")
+        # NCCL's own record of its choices, into a per-process file (not stdout)
+        os.environ["NCCL_DEBUG"] = "INFO"
+        os.environ["NCCL_DEBUG_SUBSYS"] = "INIT,TUNING"
         os.environ["NCCL_DEBUG_FILE"] = nccl_log
     torch.cuda.set_device(local)
     if world > 1:

@@ -87,6 +87,13 @@ struct llmk_gpt2 {
   llmk_gpt2_config cfg{};
   int B = 0, T = 0, device = 0;
   cudaStream_t stream = nullptr, comm_stream = nullptr;
+  // backward: weight gradients and bias column sums run on aux_stream beside
+  // the input-gradient chain on `stream` (own workspace), forked and joined
+  // with events
+  cudaStream_t aux_stream = nullptr;
+  cudaEvent_t ev_fork = nullptr, ev_j1 = nullptr, ev_j2 = nullptr, ev_j3 = nullptr;
+  void* workspace2 = nullptr;
+  size_t workspace2_bytes = 0;
   bool own_stream = false;
   size_t nparams = 0;
   size_t tsize[16] = {};
@@ -170,18 +177,20 @@ int timing_event(llmk_gpt2* g) {
 // stream while timing is on; a no-op otherwise.
 struct TimedScope {
   llmk_gpt2* g;
+  cudaStream_t st;
   int idx = -1;
-  TimedScope(llmk_gpt2* model, int cls, double work) : g(model) {
+  TimedScope(llmk_gpt2* model, int cls, double work, cudaStream_t stream = nullptr)
+      : g(model), st(stream ? stream : model->stream) {
     if (!g->timing) return;
     const int e0 = timing_event(g);
-    if (e0 < 0 || cudaEventRecord(g->tev[e0], g->stream) != cudaSuccess) return;
+    if (e0 < 0 || cudaEventRecord(g->tev[e0], st) != cudaSuccess) return;
     idx = static_cast<int>(g->marks.size());
     g->marks.push_back({cls, work, e0, -1, llmk_launch_count()});
   }
   ~TimedScope() {
     if (idx < 0) return;
     const int e1 = timing_event(g);
-    if (e1 < 0 || cudaEventRecord(g->tev[e1], g->stream) != cudaSuccess) {
+    if (e1 < 0 || cudaEventRecord(g->tev[e1], st) != cudaSuccess) {
       g->marks.resize(idx);
       return;
     }
@@ -285,6 +294,10 @@ void free_all(llmk_gpt2* g) {
   f(g->hp_dev);
   if (g->comm) ncclCommDestroy(g->comm);
   if (g->comm_stream) cudaStreamDestroy(g->comm_stream);
+  if (g->aux_stream) cudaStreamDestroy(g->aux_stream);
+  for (cudaEvent_t e : {g->ev_fork, g->ev_j1, g->ev_j2, g->ev_j3})
+    if (e) cudaEventDestroy(e);
+  f(g->workspace2);
   if (g->own_stream && g->stream) cudaStreamDestroy(g->stream);
 }
 
@@ -345,6 +358,16 @@ int alloc_all(llmk_gpt2* g) {
   LLMK_CUDA(cudaEventCreateWithFlags(&g->embed_done, cudaEventDisableTiming));
   LLMK_CUDA(cudaEventCreateWithFlags(&g->comm_done, cudaEventDisableTiming));
   LLMK_CUDA(cudaEventCreateWithFlags(&g->lnf_done, cudaEventDisableTiming));
+  for (cudaEvent_t* e : {&g->ev_fork, &g->ev_j1, &g->ev_j2, &g->ev_j3})
+    LLMK_CUDA(cudaEventCreateWithFlags(e, cudaEventDisableTiming));
+  // the side stream's workspace: split-K partials of every weight gradient and the column sums
+  size_t ws2 = 0;
+  for (int oc : {3 * iC, iC, 4 * iC}) ws2 = std::max(ws2, llmk_gemm_workspace(oc, iC, iBT, g->math));
+  ws2 = std::max(ws2, llmk_gemm_workspace(iC, 4 * iC, iBT, g->math));
+  ws2 = std::max(ws2, llmk_gemm_workspace(iVp, iC, iBT, g->math));
+  ws2 = std::max(ws2, llmk_colsum_workspace(iBT, 4 * iC));
+  g->workspace2_bytes = ws2;
+  LLMK_CUDA(cudaMalloc(&g->workspace2, std::max<size_t>(ws2, 256)));
   LLMK_CUDA(cudaEventCreateWithFlags(&g->layers_reduced, cudaEventDisableTiming));
   LLMK_CUDA(cudaEventCreateWithFlags(&g->h2d_done, cudaEventDisableTiming));
   return LLMK_OK;
@@ -362,11 +385,14 @@ llmk_epilogue epi(const float* bias = nullptr, const float* residual = nullptr, 
   return e;
 }
 
-// Gradient all-reduce of one contiguous bucket on the comm stream, after `ev`.
-int allreduce_bucket(llmk_gpt2* g, cudaEvent_t ev, size_t begin, size_t end) {
+// Gradient all-reduce of one contiguous bucket on the comm stream, after `ev`
+// (recorded on the model stream) and, when given, `aux_ev` (already recorded
+// on the side stream).
+int allreduce_bucket(llmk_gpt2* g, cudaEvent_t ev, size_t begin, size_t end, cudaEvent_t aux_ev = nullptr) {
   if (g->world <= 1) return LLMK_OK;
   LLMK_CUDA(cudaEventRecord(ev, g->stream));
   LLMK_CUDA(cudaStreamWaitEvent(g->comm_stream, ev, 0));
+  if (aux_ev) LLMK_CUDA(cudaStreamWaitEvent(g->comm_stream, aux_ev, 0));
   return nccl_check(ncclAllReduce(g->grads + begin, g->grads + begin, end - begin, ncclFloat, ncclSum, g->comm,
                                   g->comm_stream),
                     "ncclAllReduce");
@@ -411,6 +437,8 @@ int llmk_gpt2_create(llmk_gpt2** out, const llmk_gpt2_config* cfg, int B, int T,
   }
   if (rc == LLMK_OK)
     rc = llmk::cuda_check(cudaStreamCreateWithFlags(&g->comm_stream, cudaStreamNonBlocking), "cudaStreamCreate");
+  if (rc == LLMK_OK)
+    rc = llmk::cuda_check(cudaStreamCreateWithFlags(&g->aux_stream, cudaStreamNonBlocking), "cudaStreamCreate");
   if (rc == LLMK_OK) {
     layout(g);
     rc = alloc_all(g);
@@ -503,12 +531,12 @@ struct StepOps {
   double ae;  // activation element size
   int gemm(int cls, void* D, llmk_dtype dt, long long ldd, const void* A, int at, long long lda, const void* Bm,
            int bt, long long ldb, int M, int N, int K, const llmk_epilogue* e, void* w, size_t wb) const {
-    TimedScope ts(g, cls, 2.0 * M * N * K);
+    TimedScope ts(g, cls, 2.0 * M * N * K, s);
     return llmk_gemm(D, dt, ldd, A, at, lda, Bm, bt, ldb, mm, M, N, K, e, w, wb, s);
   }
   int ln_fwd(void* out, llmk_dtype dt, float* mean, float* rstd, const float* x, const float* w, const float* b,
              int N, int C) const {
-    TimedScope ts(g, KC_LN_FWD, static_cast<double>(N) * C * (4.0 + ae) + 8.0 * N + 8.0 * C);
+    TimedScope ts(g, KC_LN_FWD, static_cast<double>(N) * C * (4.0 + ae) + 8.0 * N + 8.0 * C, s);
     return llmk_layernorm_forward(out, dt, mean, rstd, x, w, b, N, C, s);
   }
   int ln_bwd(float* dinp, void* mirror, float* dw, float* db, float* colsum, const float* dout, const float* x,
@@ -516,9 +544,13 @@ struct StepOps {
              size_t wsb) const {
     const double dres = (flags & LLMK_ACCUM_DINP) ? 8.0 : 4.0;
     TimedScope ts(g, KC_LN_BWD,
-                  static_cast<double>(N) * C * (4.0 + 4.0 + dres + (mirror ? 2.0 : 0.0)) + 8.0 * N + 16.0 * C);
+                  static_cast<double>(N) * C * (4.0 + 4.0 + dres + (mirror ? 2.0 : 0.0)) + 8.0 * N + 16.0 * C, s);
     return llmk_layernorm_backward(dinp, mirror, dw, db, colsum, dout, LLMK_F32, x, w, mean, rstd, N, C, flags, ws,
                                    wsb, s);
+  }
+  int colsum(float* db, const void* x, llmk_dtype dt, int M, int N, void* ws, size_t wsb) const {
+    TimedScope ts(g, KC_COLSUM, static_cast<double>(M) * N * ae + 4.0 * N, s);
+    return llmk_colsum(db, x, dt, M, N, 0, ws, wsb, s);
   }
 };
 }  // namespace
@@ -642,9 +674,28 @@ int llmk_gpt2_backward(llmk_gpt2* g) {
     TimedScope ts(g, KC_OTHER, static_cast<double>(g->tsize[llmk::WPE]) * 4.0);
     LLMK_TRY(llmk_gpt2_zero_grad(g));
   }
-  // lm_head backward (gpt2cuda.cu:402): dlnf = dlogits * wte; dwte = dlogits^T * lnf
+  // Two streams: the input-gradient chain (dinp GEMMs, LayerNorm and
+  // attention backward) on `s`; every weight gradient and bias column sum on
+  // the side stream `a` with its own workspace, so they fill the gaps and
+  // tails of the chain. fork: `a` waits for `s` to reach this point. A join
+  // event marks where `a` is done reading something `s` overwrites next: the
+  // bf16 residual gradient (dres_op) is rewritten by each LayerNorm backward.
+  cudaStream_t a = g->aux_stream;
+  const StepOps opa{g, a, mm, static_cast<double>(g->ae)};
+  void* ws2 = g->workspace2;
+  const size_t wsb2 = g->workspace2_bytes;
+  auto fork = [&]() -> int {
+    LLMK_CUDA(cudaEventRecord(g->ev_fork, s));
+    LLMK_CUDA(cudaStreamWaitEvent(a, g->ev_fork, 0));
+    return LLMK_OK;
+  };
+  auto mark = [&](cudaEvent_t ev) -> int { return llmk::cuda_check(cudaEventRecord(ev, a), "cudaEventRecord"); };
+  auto wait_mark = [&](cudaEvent_t ev) -> int { return llmk::cuda_check(cudaStreamWaitEvent(s, ev, 0), "cudaStreamWaitEvent"); };
+  // lm_head backward (gpt2cuda.cu:402): dlnf = dlogits * wte on s; dwte = dlogits^T * lnf on a
+  LLMK_TRY(fork());
+  LLMK_TRY(opa.gemm(KC_GEMM_LMHEAD, G + g->off_wte, LLMK_F32, C, g->logits, 1, Vp, g->lnf, 1, C, Vp, C, BT, nullptr,
+                    ws2, wsb2));
   LLMK_TRY(op.gemm(KC_GEMM_LMHEAD, g->dln, LLMK_F32, C, g->logits, 0, Vp, W(g->off_wte), 1, C, BT, C, Vp, nullptr, nullptr, 0));
-  LLMK_TRY(op.gemm(KC_GEMM_LMHEAD, G + g->off_wte, LLMK_F32, C, g->logits, 1, Vp, g->lnf, 1, C, Vp, C, BT, nullptr, ws, wsb));
   const float* xL = L > 0 ? g->acts[L - 1].res3 : g->encoded;
   // the column sums of the new dres are the last layer's fcproj bias gradient
   LLMK_TRY(op.ln_bwd(g->dres, dres_mirror, G + g->off_lnfw, G + g->off_lnfb, L > 0 ? G + g->lp[L - 1].fcprojb : nullptr,
@@ -654,50 +705,60 @@ int llmk_gpt2_backward(llmk_gpt2* g) {
   for (int l = L - 1; l >= 0; --l) {
     // Layer::Backward (gpt2/cuda/layer.cu:180-266); dres = d(layer output)
     const LayerParams& p = g->lp[l];
-    LayerActs& a = g->acts[l];
+    LayerActs& a_ = g->acts[l];
     const float* x = l > 0 ? g->acts[l - 1].res3 : g->encoded;
-    // fcproj: dW = dres^T fch_gelu, dfch = (dres Wfcproj) * gelu'(fch_pre); its bias
+    // fcproj: dW = dres^T fch_gelu (a), dfch = (dres Wfcproj) * gelu'(fch_pre) (s); its bias
     // gradient colsum(dres) came out of the LayerNorm backward that produced dres
-    LLMK_TRY(op.gemm(KC_GEMM_DW, G + p.fcprojw, LLMK_F32, 4 * C, dres_op, 1, C, a.fch_gelu, 1, 4 * C, C, 4 * C, BT, nullptr, ws,
-                     wsb));
-    llmk_epilogue eg = epi(nullptr, nullptr, 0, a.fch_pre, 4 * C, LLMK_EPI_GELU_BWD | aux_f32);
+    LLMK_TRY(fork());
+    LLMK_TRY(opa.gemm(KC_GEMM_DW, G + p.fcprojw, LLMK_F32, 4 * C, dres_op, 1, C, a_.fch_gelu, 1, 4 * C, C, 4 * C, BT,
+                      nullptr, ws2, wsb2));
+    LLMK_TRY(mark(g->ev_j1));  // dres_op read
+    llmk_epilogue eg = epi(nullptr, nullptr, 0, a_.fch_pre, 4 * C, LLMK_EPI_GELU_BWD | aux_f32);
     LLMK_TRY(op.gemm(KC_GEMM_DINP, g->dfch, adt, 4 * C, dres_op, 0, C, W(p.fcprojw), 1, 4 * C, BT, 4 * C, C, &eg, nullptr, 0));
-    // fc: dW = dfch^T ln2, db = colsum(dfch), dln2 = dfch Wfc
-    LLMK_TRY(op.gemm(KC_GEMM_DW, G + p.fcw, LLMK_F32, C, g->dfch, 1, 4 * C, a.ln2, 1, C, 4 * C, C, BT, nullptr, ws, wsb));
-    {
-      TimedScope ts(g, KC_COLSUM, bt_c * 4.0 * g->ae + 16.0 * C);
-      LLMK_TRY(llmk_colsum(G + p.fcb, g->dfch, adt, BT, 4 * C, 0, ws, wsb, s));
-    }
+    // fc: dW = dfch^T ln2, db = colsum(dfch) (a); dln2 = dfch Wfc (s)
+    LLMK_TRY(fork());
+    LLMK_TRY(opa.gemm(KC_GEMM_DW, G + p.fcw, LLMK_F32, C, g->dfch, 1, 4 * C, a_.ln2, 1, C, 4 * C, C, BT, nullptr, ws2,
+                      wsb2));
+    LLMK_TRY(opa.colsum(G + p.fcb, g->dfch, adt, BT, 4 * C, ws2, wsb2));
     LLMK_TRY(op.gemm(KC_GEMM_DINP, g->dln, LLMK_F32, C, g->dfch, 0, 4 * C, W(p.fcw), 1, C, BT, C, 4 * C, nullptr, nullptr, 0));
     // ln2: dres += LN2 backward (dres becomes d(res2)); its column sums are the
     // attproj bias gradient
-    LLMK_TRY(op.ln_bwd(g->dres, dres_mirror, G + p.ln2w, G + p.ln2b, G + p.attprojb, g->dln, a.res2, P + p.ln2w,
-                       a.ln2_mean, a.ln2_rstd, BT, C, LLMK_ACCUM_DINP, ws, wsb));
-    // attproj: dW = dres^T atty, datty = dres Wproj
-    LLMK_TRY(op.gemm(KC_GEMM_DW, G + p.attprojw, LLMK_F32, C, dres_op, 1, C, a.atty, 1, C, C, C, BT, nullptr, ws, wsb));
+    LLMK_TRY(wait_mark(g->ev_j1));
+    LLMK_TRY(op.ln_bwd(g->dres, dres_mirror, G + p.ln2w, G + p.ln2b, G + p.attprojb, g->dln, a_.res2, P + p.ln2w,
+                       a_.ln2_mean, a_.ln2_rstd, BT, C, LLMK_ACCUM_DINP, ws, wsb));
+    // attproj: dW = dres^T atty (a), datty = dres Wproj (s)
+    LLMK_TRY(fork());
+    LLMK_TRY(opa.gemm(KC_GEMM_DW, G + p.attprojw, LLMK_F32, C, dres_op, 1, C, a_.atty, 1, C, C, C, BT, nullptr, ws2,
+                      wsb2));
+    LLMK_TRY(mark(g->ev_j2));  // dres_op read
     LLMK_TRY(op.gemm(KC_GEMM_DINP, g->datty, adt, C, dres_op, 0, C, W(p.attprojw), 1, C, BT, C, C, nullptr, nullptr, 0));
     // attention
     // (tf32 mode: fp32 dO, O and dqkv; q, k, v from the fp16 copy the forward made)
     {
       TimedScope ts(g, KC_ATTN_BWD, attn_flop);
-      LLMK_TRY(llmk_attention_backward(g->dqkv, g->datty, a.atty, adt, bf ? static_cast<const void*>(a.qkv) : a.qkv16,
-                                       bf ? LLMK_BF16 : LLMK_F16, a.lse, B, T, 3 * C, NH,
+      LLMK_TRY(llmk_attention_backward(g->dqkv, g->datty, a_.atty, adt, bf ? static_cast<const void*>(a_.qkv) : a_.qkv16,
+                                       bf ? LLMK_BF16 : LLMK_F16, a_.lse, B, T, 3 * C, NH,
                                        ws, wsb, s));
     }
-    // qkv: dW = dqkv^T ln1, db = colsum(dqkv), dln1 = dqkv Wqkv
-    LLMK_TRY(op.gemm(KC_GEMM_DW, G + p.qkvw, LLMK_F32, C, g->dqkv, 1, 3 * C, a.ln1, 1, C, 3 * C, C, BT, nullptr, ws, wsb));
-    {
-      TimedScope ts(g, KC_COLSUM, bt_c * 3.0 * g->ae + 12.0 * C);
-      LLMK_TRY(llmk_colsum(G + p.qkvb, g->dqkv, adt, BT, 3 * C, 0, ws, wsb, s));
-    }
+    // qkv: dW = dqkv^T ln1, db = colsum(dqkv) (a); dln1 = dqkv Wqkv (s)
+    LLMK_TRY(fork());
+    LLMK_TRY(opa.gemm(KC_GEMM_DW, G + p.qkvw, LLMK_F32, C, g->dqkv, 1, 3 * C, a_.ln1, 1, C, 3 * C, C, BT, nullptr, ws2,
+                      wsb2));
+    LLMK_TRY(opa.colsum(G + p.qkvb, g->dqkv, adt, BT, 3 * C, ws2, wsb2));
+    LLMK_TRY(mark(g->ev_j3));  // this layer's weight and bias gradients are final
     LLMK_TRY(op.gemm(KC_GEMM_DINP, g->dln, LLMK_F32, C, g->dqkv, 0, 3 * C, W(p.qkvw), 1, C, BT, C, 3 * C, nullptr, nullptr, 0));
     // ln1: dres += LN1 backward (dres becomes d(layer input)); its column sums are
     // the previous layer's fcproj bias gradient
+    LLMK_TRY(wait_mark(g->ev_j2));
     LLMK_TRY(op.ln_bwd(g->dres, dres_mirror, G + p.ln1w, G + p.ln1b, l > 0 ? G + g->lp[l - 1].fcprojb : nullptr, g->dln,
-                       x, P + p.ln1w, a.ln1_mean, a.ln1_rstd, BT, C, LLMK_ACCUM_DINP, ws, wsb));
+                       x, P + p.ln1w, a_.ln1_mean, a_.ln1_rstd, BT, C, LLMK_ACCUM_DINP, ws, wsb));
     // this layer's gradients are final: reduce them while the layers below run
-    LLMK_TRY(allreduce_bucket(g, g->layer_done[l], p.begin, p.end));
+    LLMK_TRY(allreduce_bucket(g, g->layer_done[l], p.begin, p.end, g->ev_j3));
   }
+  // the side stream rejoins before the encoder adds into dwte (the lm_head's
+  // weight gradient) and before the step ends
+  LLMK_TRY(mark(g->ev_j1));
+  LLMK_TRY(wait_mark(g->ev_j1));
   // encoder backward (gpt2cuda.cu:413): dwte += scatter, dwpe += sum over batch
   {
     TimedScope ts(g, KC_ENCODER, bt_c * 12.0 + 8.0 * static_cast<double>(T) * C + 4.0 * BT);
