@@ -680,11 +680,15 @@ int llmk_gpt2_backward(llmk_gpt2* g) {
   // tails of the chain. fork: `a` waits for `s` to reach this point. A join
   // event marks where `a` is done reading something `s` overwrites next: the
   // bf16 residual gradient (dres_op) is rewritten by each LayerNorm backward.
-  cudaStream_t a = g->aux_stream;
+  // With per-kernel-class timing on, everything runs on `s`: the events then
+  // time each library call alone, not two overlapping ones (the step
+  // without timing is what runs concurrently).
+  cudaStream_t a = g->timing ? s : g->aux_stream;
   const StepOps opa{g, a, mm, static_cast<double>(g->ae)};
   void* ws2 = g->workspace2;
   const size_t wsb2 = g->workspace2_bytes;
   auto fork = [&]() -> int {
+    if (a == s) return LLMK_OK;
     LLMK_CUDA(cudaEventRecord(g->ev_fork, s));
     LLMK_CUDA(cudaStreamWaitEvent(a, g->ev_fork, 0));
     return LLMK_OK;
