@@ -517,9 +517,12 @@ __global__ void attn_bwd_post_kernel(IoT* __restrict__ dqkv, const float* __rest
 // aligned (the 128B-swizzle atom) and the kernel checks that it is.
 struct BwdSmem {
   static constexpr int kStages = 2;
+  // K, V of two items (by item parity: buffer b holds K at 2b tiles, V one
+  // tile further), so the next item's K / V arrive while this item runs
   static constexpr int K_OFF = 0;
   static constexpr int V_OFF = TILE_BYTES;
-  static constexpr int QD_OFF = 2 * TILE_BYTES;                    // stages x (Q_i, dO_i)
+  static constexpr int KV_BYTES = 2 * TILE_BYTES;
+  static constexpr int QD_OFF = 2 * KV_BYTES;                      // stages x (Q_i, dO_i)
   static constexpr int PD_OFF = QD_OFF + kStages * 2 * TILE_BYTES;  // P^T, dS^T [128 keys x 128 q]
   static constexpr int PD_BYTES = 4 * TILE_BYTES;
   static constexpr int DQ_OFF = PD_OFF + PD_BYTES;                 // dQ staging: 2 x [128 q x 32] fp32, 128B-swizzled
@@ -620,15 +623,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   }
   uint8_t* smem = smem_bwd;
   uint8_t* sK = smem + S::K_OFF;
-  uint8_t* sV = smem + S::V_OFF;
   uint8_t* sQD = smem + S::QD_OFF;
   uint8_t* sPD = smem + S::PD_OFF;  // P^T, dS^T 2 tiles further
   float* sLD = reinterpret_cast<float*>(smem + S::LD_OFF);
   uint8_t* sDQ = smem + S::DQ_OFF;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::BAR_OFF);
-  uint64_t* kv_full = bars;                       // K, V of an item loaded
-  uint64_t* kv_empty = bars + 1;                  // an item's last gradient MMAs done (K, V free)
-  uint64_t* qd_full = bars + 2;                   // [stages] Q_i, dO_i
+  uint64_t* kv_full = bars;                       // [2] K, V of an item of parity b loaded
+  uint64_t* kv_empty = bars + 2;                  // [2] that item's last gradient MMAs done (buffer b free)
+  uint64_t* qd_full = bars + 4;                   // [stages] Q_i, dO_i
   uint64_t* qd_empty = qd_full + S::kStages;      // [stages]
   uint64_t* sdp_full = qd_empty + S::kStages;     // S^T and dP^T in TMEM
   uint64_t* sdp_free = sdp_full + 1;              // S^T / dP^T read into registers (one arrival per warp)
@@ -648,8 +650,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   const int warp = warp_id(), lane = lane_id();
 
   if (threadIdx.x == 0) {
-    mbar_init(kv_full, 1);
-    mbar_init(kv_empty, 1);
+    for (int b2 = 0; b2 < 2; ++b2) {
+      mbar_init(kv_full + b2, 1);
+      mbar_init(kv_empty + b2, 1);
+    }
     for (int s = 0; s < S::kStages; ++s) {
       mbar_init(qd_full + s, 1);
       mbar_init(qd_empty + s, 1);
@@ -696,6 +700,20 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       const int kt = it.tile, nqi = nk - kt;
       const float* lse_bh = lse + static_cast<long long>(it.bh) * T;
       const float* d_bh = Dvec + static_cast<long long>(it.bh) * T;
+      {
+        // K, V of this item into buffer n&1 once the item two back (its
+        // previous user) has finished its gradient MMAs; this runs as soon as
+        // the previous item's Q / dO loads are issued, a step or two ahead
+        const int kb = n & 1;
+        bool wt = mbar_wait(kv_empty + kb, ((n >> 1) & 1) ^ 1u, status, abort_flag, 19);
+        if (!__all_sync(0xffffffffu, wt)) { ok = false; break; }
+        if (lane == 0) {
+          uint8_t* kv = sK + kb * S::KV_BYTES;
+          mbar_arrive_expect_tx(kv_full + kb, 2 * TILE_BYTES);
+          tma_load_3d(kv, &tm_qkv, kv_full + kb, C + it.h * HD, kt * TILE, it.b);
+          tma_load_3d(kv + TILE_BYTES, &tm_qkv, kv_full + kb, 2 * C + it.h * HD, kt * TILE, it.b);
+        }
+      }
       for (int i = 0; i < nqi; ++i) {
         const int q0 = (kt + i) * TILE;
         bool wt = mbar_wait(qd_empty + stage, phase ^ 1u, status, abort_flag, 8);
@@ -727,17 +745,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           if (lane == 0) mbar_arrive(ld_full + stage);
         }
         if (++stage == S::kStages) { stage = 0; phase ^= 1u; }
-        if (i == 0) {
-          // K, V of this item once the previous item's gradient MMAs are done
-          // (after its first Q / dO tile, which only needs a free ring stage)
-          wt = mbar_wait(kv_empty, (n & 1) ^ 1u, status, abort_flag, 19);
-          if (!__all_sync(0xffffffffu, wt)) { ok = false; break; }
-          if (lane == 0) {
-            mbar_arrive_expect_tx(kv_full, 2 * TILE_BYTES);
-            tma_load_3d(sK, &tm_qkv, kv_full, C + it.h * HD, kt * TILE, it.b);
-            tma_load_3d(sV, &tm_qkv, kv_full, 2 * C + it.h * HD, kt * TILE, it.b);
-          }
-        }
       }
     }
   } else if (warp == 1) {
@@ -750,8 +757,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       // dQ = dS K: M=128 q, N=64, K=128 keys; A = dS^T stored [keys][q] = M-major;
       // B = K stored [keys][hd] = N-major.
       const uint32_t idesc_q = idesc_f32acc(128, HD, kFmt, true, true);
-      const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV);
-      auto issue_sdp = [&](int st) {
+      auto issue_sdp = [&](int st, int kb) {
+        const uint32_t k_addr = smem_u32(sK) + kb * S::KV_BYTES, v_addr = k_addr + TILE_BYTES;
         const uint32_t q_addr = smem_u32(sQD + st * 2 * TILE_BYTES);
         const uint32_t do_addr = q_addr + TILE_BYTES;
 #pragma unroll
@@ -772,25 +779,35 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       int n = 0;
       for (int w = sched_slot(0, n_items); w < n_items && ok; w = sched_slot(n + 1, n_items), ++n) {
         const int nqi = nk - bwd_item(w, B, NH).tile;
+        const int kb = n & 1;
+        const bool has_next = sched_slot(n + 1, n_items) < n_items;
+        const uint32_t k_addr = smem_u32(sK) + kb * S::KV_BYTES;
         for (int j = 0; j < nqi; ++j, ++g) {
           const int nst = stage + 1 == S::kStages ? 0 : stage + 1;
           const uint32_t nph = stage + 1 == S::kStages ? phase ^ 1u : phase;
           const uint32_t pb = g & 1;
           if (!issued) {
             // first step of an item: its K, V, and the S^T / dP^T TMEM of the previous step
-            if ((j == 0 && !mbar_wait(kv_full, n & 1, status, abort_flag, 9)) ||
+            if ((j == 0 && !mbar_wait(kv_full + kb, (n >> 1) & 1, status, abort_flag, 9)) ||
                 !mbar_wait(qd_full + stage, phase, status, abort_flag, 10) ||
                 (g > 0 && !mbar_wait(sdp_free, (g - 1) & 1, status, abort_flag, 11))) { ok = false; break; }
             tc_fence_after();
-            issue_sdp(stage);
+            issue_sdp(stage, kb);
           }
           issued = false;
-          if (j + 1 < nqi) {
-            // next step of this item as soon as the softmax warps hold this one in registers
+          if (j + 1 < nqi || has_next) {
+            // the next step, of this item or the first of the next one (its K, V
+            // in the other buffer), as soon as the softmax warps hold this one
+            // in registers
+            const int nkb = j + 1 < nqi ? kb : kb ^ 1;
             if (!mbar_wait(sdp_free, g & 1, status, abort_flag, 11) ||
-                !mbar_wait(qd_full + nst, nph, status, abort_flag, 10)) { ok = false; break; }
+                !mbar_wait(qd_full + nst, nph, status, abort_flag, 10) ||
+                (j + 1 == nqi && !mbar_wait(kv_full + nkb, ((n + 1) >> 1) & 1, status, abort_flag, 9))) {
+              ok = false;
+              break;
+            }
             tc_fence_after();
-            issue_sdp(nst);
+            issue_sdp(nst, nkb);
             issued = true;
           }
           // P^T / dS^T of this step in smem; dQ buffer pb read (step g-2); at an
@@ -817,7 +834,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                        sdesc_sw128(k_addr + ks * 2048, TILE_BYTES, 1024), idesc_q, ks > 0);
           mma_commit(grad_done + pb);
           mma_commit(qd_empty + stage);
-          if (j + 1 == nqi) mma_commit(kv_empty);
+          if (j + 1 == nqi) mma_commit(kv_empty + kb);
           stage = nst;
           phase = nph;
         }
