@@ -604,7 +604,7 @@ def run_case(args) -> None:
       attnbwd [B T NH]                            llmk_attention_backward, bf16
       gemmset [BT]   every GEMM shape of one GPT-2 124M step (fwd, dinp, dweight)
       lmxent  [BT] [--variant fused|unfused|gemm] lm_head + softmax + cross-entropy
-      step    [B T]                               one eager training step
+      step    [B T] [--model 124m|774m]           one eager training step
       lnfwd   [N C]  llmk_layernorm_forward, fp32 in, bf16 out
       lnbwd   [N C]  llmk_layernorm_backward with the bf16 mirror and column sums
       adamw   [n]    llmk_adamw over n parameters with the bf16 mirror
@@ -764,8 +764,8 @@ def run_case(args) -> None:
                       Tt, C, Vp, ws.data_ptr(), wsb, s)
         nbytes = 2 * Bb * Tt * C * 12.0
     else:  # step
-        Bb, Tt = (a.dims + [16, 1024][len(a.dims):])[:2]
-        m = llmk.GPT2(Bb, Tt)
+        Bb, Tt = (a.dims + [MODELS[a.model]["B"], 1024][len(a.dims):])[:2]
+        m = llmk.GPT2(Bb, Tt, **MODELS[a.model]["cfg"])
         m.load_parameters((np.random.default_rng(0).standard_normal(m.n) * 0.02).astype(np.float32))
         toks = np.random.default_rng(1).integers(0, 50257, size=Bb * Tt + 1, dtype=np.int32)
         m.train_step(toks[:-1], toks[1:], 0.0, t=1, want_loss=False)

@@ -132,8 +132,11 @@ __global__ void __launch_bounds__(256) layernorm_fwd_kernel(OutT* __restrict__ o
 // the rows it handles, dgamma (dy*xhat), dbeta (dy) and the column sums of the
 // final dinp into its own smem slice [3][C]; the block then reduces the
 // slices in warp order into partial[block][3][C]. kV as in the forward.
+// Wide rows (kV >= 8, C >= 1024) hold 3 x kV float4 per lane and 96 KB+ of
+// warp slices per block, so only one block fits an SM anyway: they get the
+// whole register file instead of spilling under a two-blocks-per-SM bound.
 template <typename DoutT, int kV>
-__global__ void __launch_bounds__(256, 2) layernorm_bwd_kernel(float* __restrict__ dinp, __nv_bfloat16* __restrict__ dinp_bf16,
+__global__ void __launch_bounds__(256, (kV >= 8 ? 1 : 2)) layernorm_bwd_kernel(float* __restrict__ dinp, __nv_bfloat16* __restrict__ dinp_bf16,
                                                             float* __restrict__ partial, const DoutT* __restrict__ dout,
                                                             const float* __restrict__ inp,
                                                             const float* __restrict__ gamma,
