@@ -67,9 +67,10 @@ struct EpiParams {
 // for every other combination.
 //   kOpNone      store the accumulator (also split-K partial tiles)
 //   kOpBias      + bias
-//   kOpBiasRes   + bias + fp32 residual, fp32 D (the residual-stream GEMMs)
+//   kOpBiasRes   + bias + fp32 residual, fp32 D (the residual-stream GEMMs);
+//                the residual arrives by TMA loads (epilogue_operand_role)
 //   kOpBiasGelu  + bias, GELU, pre-activation by TMA store (aux type == D type)
-//   kOpGeluBwd   * GELU'(pre-activation), aux type == D type
+//   kOpGeluBwd   * GELU'(pre-activation), aux type == D type, loaded by TMA
 //   kOpStats     + bias, and the rows' softmax statistics (the logits GEMM)
 // Each is a kernel template argument: one kernel holds one program.
 enum : int { kOpNone = 0, kOpBias = 1, kOpBiasRes = 2, kOpBiasGelu = 3, kOpGeluBwd = 4, kOpGeneric = 5, kOpStats = 6 };
@@ -89,7 +90,12 @@ LLMK_GEMM_DISPATCH_DECL(gemm_dispatch_tf32_cta);
 namespace {
 
 
-template <bool kTF32, bool kAMN, bool kBMN, int kBN, bool kPair>
+// Staging buffers per epilogue warp: two (alternating TMA-store buffers), or
+// three for the programs whose drain reads a per-element operand of D's shape
+// (it arrives by TMA loads into the buffers, two chunks ahead of the drain).
+constexpr int op_bufs(int op) { return (op == kOpBiasRes || op == kOpGeluBwd) ? 3 : 2; }
+
+template <bool kTF32, bool kAMN, bool kBMN, int kBN, bool kPair, int kBufs = 2>
 struct Cfg {
   static constexpr int kElem = kTF32 ? 4 : 2;
   static constexpr int BM = 128;                   // accumulator rows per CTA
@@ -109,16 +115,20 @@ struct Cfg {
   static constexpr uint32_t kMNSbo = kTF32 ? 512 : 1024;
   static constexpr int kEpiWarps = 8;
   static constexpr int kThreads = 64 + 32 * kEpiWarps;
-  // Epilogue staging for TMA stores: 8 warps x 2 buffers x [32 rows x 128 B].
-  static constexpr int STAGING_BYTES = kEpiWarps * 2 * 4096;
+  // Epilogue staging for TMA stores: 8 warps x kBufs buffers x [32 rows x 128 B].
+  static constexpr int STAGING_BYTES = kEpiWarps * kBufs * 4096;
+  // barriers: the pipeline's at BAR_OFF, the operand loads' at BAR_OFF + 256
+  static constexpr int kBarBytes = 512;
   // as many operand stages as fit beside the staging buffers (227 KB per CTA)
-  static constexpr int kStagesFit = (232448 - 1024 - 256 - STAGING_BYTES) / STAGE_BYTES;
+  static constexpr int kStagesFit = (232448 - 1024 - kBarBytes - STAGING_BYTES) / STAGE_BYTES;
   static constexpr int kStages = kStagesFit > 8 ? 8 : kStagesFit;
   static constexpr int STAGING_OFF = kStages * STAGE_BYTES;
   static constexpr int BAR_OFF = STAGING_OFF + STAGING_BYTES;
-  static constexpr size_t SMEM = size_t(BAR_OFF) + 256 + 1024;
+  static constexpr size_t SMEM = size_t(BAR_OFF) + kBarBytes + 1024;
   static_assert(kBN == 128 || kBN == 256, "BN");
   static_assert(kStages >= 3, "stages");
+  static_assert(kBufs == 2 || kBufs == 3, "staging buffers");
+  static_assert(8 * (2 * 8 + 5) + 8 <= 256 && 256 + 8 * kEpiWarps * 3 <= kBarBytes, "barrier area");
   static_assert(!kBMN || BNC % kAtomMN == 0, "B atoms");
 };
 
@@ -211,21 +221,8 @@ __device__ __forceinline__ void epi_post8(const EpiParams& ep, long long gm, int
 }
 
 
-// Loads the 128 bytes of columns [gn0, gn0 + CW) of a row as eight 16-byte
-// pieces (one chunk's worth of an operand with D's element size); a piece
-// past column N reads the chunk's first piece instead (its columns are
-// computed but never stored: the tensor map clips them).
-template <int CW>
-__device__ __forceinline__ void chunk_load(const uint8_t* row, int gn0, int N, uint4* pre) {
-  constexpr int kEs = 128 / CW;  // element bytes: 2 (bf16 chunk of 64) or 4 (fp32 chunk of 32)
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const int col = gn0 + j * (16 / kEs);
-    pre[j] = *reinterpret_cast<const uint4*>(row + static_cast<long long>(col < N ? col : gn0) * kEs);
-  }
-}
-
-// Columns [8k, 8k + 8) of a chunk loaded by chunk_load, as floats.
+// Columns [8k, 8k + 8) of a chunk row held as eight 16-byte pieces (bf16: one
+// piece per group; fp32: two), as floats.
 template <bool kBF16>
 __device__ __forceinline__ void chunk_unpack8(const uint4* pre, int k, float* t) {
   if constexpr (kBF16) {
@@ -318,23 +315,14 @@ __device__ __forceinline__ void epilogue_cols(const EpiParams& ep, const CUtenso
                                               uint32_t tsrc, int row0, int n0, int c_begin, int c_end, int sp, int M,
                                               int N, int lane, uint8_t* stg, uint32_t& nstore) {
   constexpr int CW = kBF16 ? 64 : 32;  // columns per chunk
-  constexpr bool kChunkOperand = kOp == kOpBiasRes || kOp == kOpGeluBwd;
+  static_assert(op_bufs(kOp) == 2, "operand-loading programs drain in epilogue_operand_role");
   const long long gm = row0 + lane;
   const bool row_ok = gm < M && !ep.partial;
   float st_m = -INFINITY, st_s = 0.f;
-  // the row of the per-element operand (residual or GELU pre-activation)
-  const uint8_t* orow = nullptr;
-  if constexpr (kOp == kOpBiasRes) orow = reinterpret_cast<const uint8_t*>(ep.residual + gm * ep.ldr);
-  if constexpr (kOp == kOpGeluBwd) orow = reinterpret_cast<const uint8_t*>(ep.aux) + gm * ep.ldaux * (kBF16 ? 2 : 4);
 #pragma unroll 1
   for (int c0 = c_begin; c0 < c_end; c0 += CW) {
     const int gn0 = n0 + c0;
     if (gn0 >= N) break;
-    uint4 pre[kChunkOperand ? 8 : 1];
-    if constexpr (kChunkOperand) {
-      // issued before the TMEM read, so the load latency overlaps it
-      if (row_ok) chunk_load<CW>(orow, gn0, N, pre);
-    }
     float v[CW];
     {
       uint32_t r[32];
@@ -382,21 +370,10 @@ __device__ __forceinline__ void epilogue_cols(const EpiParams& ep, const CUtenso
 #pragma unroll
         for (int k = 0; k < CW / 8; ++k) {
           const int gc = gn0 + k * 8 < N ? gn0 + k * 8 : N - 8;
-          if constexpr (kOp == kOpBias || kOp == kOpBiasRes || kOp == kOpBiasGelu) {
+          if constexpr (kOp == kOpBias || kOp == kOpBiasGelu) {
             load8(ep.bias + gc, t);
 #pragma unroll
             for (int j = 0; j < 8; ++j) v[k * 8 + j] += t[j];
-          }
-          if constexpr (kOp == kOpBiasRes) {
-            chunk_unpack8<kBF16>(pre, k, t);
-#pragma unroll
-            for (int j = 0; j < 8; ++j) v[k * 8 + j] += t[j];
-          }
-          if constexpr (kOp == kOpGeluBwd) {
-            chunk_unpack8<kBF16>(pre, k, t);
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-              v[k * 8 + j] *= kBF16 ? gelu_tanh_grad_fast(t[j]) : gelu_tanh_grad(t[j]);
           }
         }
       }
@@ -437,12 +414,168 @@ __device__ __forceinline__ void epilogue_cols(const EpiParams& ep, const CUtenso
   }
 }
 
+// What the epilogue role of one warp needs to walk its tiles.
+struct EpiRole {
+  int unit, units, num_tiles, num_m, num_n, group_m;
+  int rank_rows;  // this CTA's first accumulator row inside a tile (rank * 128)
+  int q, half, lane, M, N;
+  uint32_t tmem_base;
+  unsigned int* status;
+  volatile int* abort_flag;
+};
+
+// Epilogue role of the programs whose drain reads a per-element operand of D's
+// shape: kOpBiasRes (D = acc + bias + residual, fp32) and kOpGeluBwd (D = acc *
+// GELU'(pre-activation), the pre-activation in D's type). The operand arrives
+// by TMA tile loads (box = one 4 KB chunk, 128B-swizzled exactly as the D chunk
+// is staged) into the warp's three staging buffers: chunk n's operand lands in
+// buffer n % 3, each lane reads its row from there (conflict-free: the swizzle
+// spreads a quarter-warp's 16-byte pieces over all banks), writes its result
+// over it, and one lane TMA-stores the buffer. Loads run two chunks ahead of
+// the drain and across tile boundaries: the load of chunk n + 2 goes into the
+// buffer of chunk n - 1 as soon as that chunk's store has finished reading it,
+// so the operand waits in shared memory when the accumulator is ready.
+// Rows / columns past M / N load as zeros and are clipped by D's tensor map.
+// tmX maps the operand with D's chunk box.
+template <bool kBF16, int kOp, int kBN, int kMmaM, bool kPair>
+__device__ __forceinline__ void epilogue_operand_role(const EpiParams& ep, const CUtensorMap* tmD,
+                                                      const CUtensorMap* tmX, const EpiRole& r, uint64_t* accf,
+                                                      uint64_t* acce, uint32_t acce_leader0, uint64_t* opbar,
+                                                      uint8_t* stg) {
+  constexpr int CW = kBF16 ? 64 : 32;  // columns per 4 KB chunk
+  const int lane = r.lane;
+  const int cb = r.half * (kBN / 2), ce = cb + kBN / 2;
+  // The load sequence (lane 0 only): tile lt, column lc of the next chunk to load.
+  int lt = r.unit, lc = cb;
+  uint32_t nload = 0;
+  auto issue = [&]() {
+    while (lt < r.num_tiles) {
+      int mb, nb, sp;
+      tile_coords(lt, r.num_m, r.num_n, r.group_m, mb, nb, sp);
+      if (lc < ce && nb * kBN + lc < r.N) {
+        const int j = static_cast<int>(nload % 3u);
+        mbar_arrive_expect_tx(opbar + j, 4096);
+        tma_load_2d(stg + j * 4096, tmX, opbar + j, nb * kBN + lc, mb * kMmaM + r.rank_rows + r.q * 32);
+        ++nload;
+        lc += CW;
+        return;
+      }
+      lt += r.units;
+      lc = cb;
+    }
+  };
+  if (lane == 0) {
+    issue();
+    issue();
+  }
+  uint32_t n = 0;  // chunks drained (= stores issued) by this warp
+  bool failed = false;
+  int local = 0;
+  for (int tile = r.unit; tile < r.num_tiles && !failed; tile += r.units, ++local) {
+    int mb, nb, sp;
+    tile_coords(tile, r.num_m, r.num_n, r.group_m, mb, nb, sp);
+    const int row0 = mb * kMmaM + r.rank_rows + r.q * 32;
+    const int n0 = nb * kBN;
+    const int acc = local & 1;
+    const uint32_t aphase = (local >> 1) & 1;
+    {
+      // while the tile's MMAs run, pull this lane's row segment of the operand
+      // into L2 (the chunk loads then find it there)
+      const long long gm = row0 + lane;
+      const int c0 = n0 + cb;
+      if (gm < r.M && c0 < r.N) {
+        const uint32_t ncol = static_cast<uint32_t>(min(kBN / 2, r.N - c0));
+        if constexpr (kOp == kOpBiasRes) prefetch_l2_bulk(ep.residual + gm * ep.ldr + c0, ncol * 4);
+        else prefetch_l2_bulk(reinterpret_cast<const uint8_t*>(ep.aux) + (gm * ep.ldaux + c0) * (kBF16 ? 2 : 4),
+                              ncol * (kBF16 ? 2 : 4));
+      }
+    }
+    bool ok = mbar_wait(accf + acc, aphase, r.status, r.abort_flag);
+    if (!__all_sync(0xffffffffu, ok)) { failed = true; break; }
+    tc_fence_after();
+    const uint32_t tsrc = r.tmem_base + (static_cast<uint32_t>(r.q * 32) << 16) + acc * kBN;
+#pragma unroll 1
+    for (int c0 = cb; c0 < ce; c0 += CW) {
+      const int gn0 = n0 + c0;
+      if (gn0 >= r.N) break;
+      float v[CW];
+      {
+        uint32_t t32[32];
+        tmem_ld_32x32b_x32(tsrc + c0, t32);
+        if constexpr (kBF16) {
+          uint32_t t32b[32];
+          tmem_ld_32x32b_x32(tsrc + c0 + 32, t32b);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[32 + j] = __uint_as_float(t32b[j]);
+        } else {
+          tmem_ld_wait();
+        }
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(t32[j]);
+      }
+      const int b = static_cast<int>(n % 3u);
+      uint8_t* buf = stg + b * 4096;
+      ok = mbar_wait(opbar + b, (n / 3u) & 1u, r.status, r.abort_flag);
+      if (!__all_sync(0xffffffffu, ok)) { failed = true; break; }
+      const int r7 = lane & 7;
+      uint4 pre[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) pre[j] = *reinterpret_cast<const uint4*>(buf + lane * 128 + ((j ^ r7) << 4));
+      float t[8];
+#pragma unroll
+      for (int k = 0; k < CW / 8; ++k) {
+        chunk_unpack8<kBF16>(pre, k, t);
+        if constexpr (kOp == kOpBiasRes) {
+          // column clamped into [0, N): no branch per group
+          const int gc = gn0 + k * 8 < r.N ? gn0 + k * 8 : r.N - 8;
+          float bb[8];
+          load8(ep.bias + gc, bb);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) v[k * 8 + j] = (v[k * 8 + j] + bb[j]) + t[j];  // (acc + bias) + residual
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) v[k * 8 + j] *= kBF16 ? gelu_tanh_grad_fast(t[j]) : gelu_tanh_grad(t[j]);
+        }
+      }
+      // chunk n - 1's store has read buffer (n + 2) % 3: load chunk n + 2 into it
+      if (lane == 0) {
+        bulk_wait_read0();
+        issue();
+      }
+      // the result goes over the operand, each lane on its own row
+#pragma unroll
+      for (int k = 0; k < CW / 8; ++k) stage8<kBF16>(buf, lane, k, v + k * 8);
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_2d(tmD, buf, gn0, row0);
+        bulk_commit();
+      }
+      ++n;
+    }
+    if (failed) break;
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) {
+      if (kPair) mbar_arrive_cluster(acce_leader0 + acc * 8);
+      else mbar_arrive(acce + acc);
+    }
+  }
+  // after a failed wait: let the loads still in flight land before the CTA exits
+  if (lane == 0) {
+    for (uint32_t i = n; i < nload; ++i) mbar_wait(opbar + i % 3u, (i / 3u) & 1u, nullptr, nullptr);
+  }
+  __syncwarp();
+}
+
 template <bool kTF32, bool kAMN, bool kBMN, int kBN, bool kPair, int kOp>
 __global__ void __launch_bounds__(Cfg<kTF32, kAMN, kBMN, kBN, kPair>::kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmD, const __grid_constant__ CUtensorMap tmX, EpiParams ep,
                    int M, int N, int K, int splits, int group_m, unsigned int* status) {
-  using C = Cfg<kTF32, kAMN, kBMN, kBN, kPair>;
+  using C = Cfg<kTF32, kAMN, kBMN, kBN, kPair, op_bufs(kOp)>;
+  constexpr bool kOperandLoads = op_bufs(kOp) == 3;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
@@ -452,6 +585,7 @@ __global__ void __launch_bounds__(Cfg<kTF32, kAMN, kBMN, kBN, kPair>::kThreads, 
   uint64_t* done = acce + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint64_t* opbar = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF + 256);  // 3 per epilogue warp
 
   const int warp = warp_id();
   const int lane = lane_id();
@@ -468,6 +602,9 @@ __global__ void __launch_bounds__(Cfg<kTF32, kAMN, kBMN, kBN, kPair>::kThreads, 
       mbar_init(acce + a, kPair ? 2 * C::kEpiWarps : C::kEpiWarps);
     }
     mbar_init(done, 1);
+    if constexpr (kOperandLoads) {
+      for (int i = 0; i < 3 * C::kEpiWarps; ++i) mbar_init(opbar + i, 1);
+    }
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -609,6 +746,21 @@ __global__ void __launch_bounds__(Cfg<kTF32, kAMN, kBMN, kBN, kPair>::kThreads, 
       mbar_wait(done, 0, status, nullptr);
     }
     __syncwarp();
+  } else if constexpr (kOperandLoads) {
+    const int ew = warp - 2;
+    EpiRole r;
+    r.unit = unit; r.units = units; r.num_tiles = num_tiles; r.num_m = num_m; r.num_n = num_n; r.group_m = group_m;
+    r.rank_rows = static_cast<int>(rank) * C::BM;
+    r.q = warp & 3; r.half = ew >> 2; r.lane = lane; r.M = M; r.N = N;
+    r.tmem_base = tmem_base; r.status = status; r.abort_flag = abort_flag;
+    const uint32_t acce_leader0 = kPair ? mapa_shared(smem_u32(acce), 0) : smem_u32(acce);
+    uint8_t* stg = smem + C::STAGING_OFF + ew * (3 * 4096);
+    if (kOp == kOpGeluBwd && ep.d_bf16)
+      epilogue_operand_role<true, kOp, kBN, C::kMmaM, kPair>(ep, &tmD, &tmX, r, accf, acce, acce_leader0,
+                                                             opbar + 3 * ew, stg);
+    else
+      epilogue_operand_role<false, kOp, kBN, C::kMmaM, kPair>(ep, &tmD, &tmX, r, accf, acce, acce_leader0,
+                                                              opbar + 3 * ew, stg);
   } else {
     const int ew = warp - 2;               // epilogue warp 0..7
     const int q = warp & 3;                // TMEM lane quarter this warp may access
@@ -663,8 +815,6 @@ __global__ void __launch_bounds__(Cfg<kTF32, kAMN, kBMN, kBN, kPair>::kThreads, 
           if (ep.aux_tma) epilogue_cols<false, true, kOpGeneric>(LLMK_EPI_ARGS);
           else epilogue_cols<false, false, kOpGeneric>(LLMK_EPI_ARGS);
         }
-      } else if constexpr (kOp == kOpBiasRes) {
-        epilogue_cols<false, false, kOpBiasRes>(LLMK_EPI_ARGS);  // fp32 D only
       } else if constexpr (kOp == kOpBiasGelu) {
         if (ep.d_bf16) epilogue_cols<true, true, kOpBiasGelu>(LLMK_EPI_ARGS);
         else epilogue_cols<false, true, kOpBiasGelu>(LLMK_EPI_ARGS);
@@ -735,7 +885,7 @@ int persistent_units(Kern kern, bool pair, size_t smem, int threads, int* units)
 template <bool kTF32, bool kAMN, bool kBMN, int kBN, bool kPair, int kOp>
 int launch_gemm(const void* A, long long lda, const void* B, long long ldb, int M, int N, int K, EpiParams ep,
                 int splits, cudaStream_t stream) {
-  using C = Cfg<kTF32, kAMN, kBMN, kBN, kPair>;
+  using C = Cfg<kTF32, kAMN, kBMN, kBN, kPair, op_bufs(kOp)>;
   auto kern = gemm_tc_kernel<kTF32, kAMN, kBMN, kBN, kPair, kOp>;
   static bool attr_done[64] = {};
   int dev = 0;
@@ -760,9 +910,16 @@ int launch_gemm(const void* A, long long lda, const void* B, long long ldb, int 
   } else {
     LLMK_TRY(make_tmap_2d(&td, ep.D, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, N, M, ep.ldd * 4, 32, 32));
   }
-  // GELU pre-activation map (same chunk boxes as D); a copy of D's otherwise
+  // GELU pre-activation map (same chunk boxes as D); for the operand-loading
+  // programs the residual's or the pre-activation's load map, with D's chunk
+  // box; a copy of D's otherwise
   CUtensorMap tx = td;
-  if (ep.aux_tma) {
+  if constexpr (kOp == kOpBiasRes) {
+    LLMK_TRY(make_tmap_2d(&tx, ep.residual, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, N, M, ep.ldr * 4, 32, 32));
+  } else if constexpr (kOp == kOpGeluBwd) {
+    if (ep.d_bf16) LLMK_TRY(make_tmap_2d(&tx, ep.aux, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, N, M, ep.ldaux * 2, 64, 32));
+    else LLMK_TRY(make_tmap_2d(&tx, ep.aux, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, N, M, ep.ldaux * 4, 32, 32));
+  } else if (ep.aux_tma) {
     if (ep.d_bf16) LLMK_TRY(make_tmap_2d(&tx, ep.aux, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, N, M, ep.ldaux * 2, 64, 32));
     else LLMK_TRY(make_tmap_2d(&tx, ep.aux, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, N, M, ep.ldaux * 4, 32, 32));
   }
