@@ -599,7 +599,7 @@ def run_case(args) -> None:
     the 126 MB L2 but only a few GB, so a `ncu -k <kernel> -c 1..3` capture of
     them ends quickly.
 
-      gemm    [M N K] [--trans A B] [--out-bf16] [--epi bias|residual|gelu]  one llmk_gemm, bf16 operands
+      gemm    [M N K] [--trans A B] [--out-bf16] [--epi bias|residual|gelu|gelubwd]  one llmk_gemm, bf16 operands
       attn    [B T NH]                            llmk_attention_forward, bf16
       attnbwd [B T NH]                            llmk_attention_backward, bf16
       gemmset [BT]   every GEMM shape of one GPT-2 124M step (fwd, dinp, dweight)
@@ -629,11 +629,16 @@ def run_case(args) -> None:
         wsb = llmk.lib().llmk_gemm_workspace(M, N, K, llmk.MATH_BF16)
         ws = torch.empty(max(wsb // 4, 1), device=dev)
         # the training step's epilogues: --epi bias | residual (bias + fp32 residual, the
-        # projections) | gelu (bias + GELU with the bf16 pre-activation stored, fc)
-        bias = torch.randn(N, device=dev) if a.epi else None
+        # projections) | gelu (bias + GELU with the bf16 pre-activation stored, fc) |
+        # gelubwd (times GELU' of a bf16 pre-activation, the FC-projection input gradient)
+        bias = torch.randn(N, device=dev) if a.epi in ("bias", "residual", "gelu") else None
         res = torch.randn(M, N, device=dev) if a.epi == "residual" else None
-        aux = torch.empty(M, N, device=dev, dtype=torch.bfloat16) if a.epi == "gelu" else None
-        flags = llmk.EPI_GELU if a.epi == "gelu" else 0
+        aux = None
+        if a.epi == "gelu":
+            aux = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+        elif a.epi == "gelubwd":
+            aux = torch.randn(M, N, device=dev).bfloat16()
+        flags = {"gelu": llmk.EPI_GELU, "gelubwd": llmk.EPI_GELU_BWD}.get(a.epi, 0)
         run = lambda: llmk.gemm(D, A, B, a_trans=at, b_trans=bt, M=M, N=N, K=K, workspace=ws, bias=bias,
                                 residual=res, aux=aux, flags=flags)
         flop = 2.0 * M * N * K
@@ -806,7 +811,7 @@ def main() -> None:
     ap.add_argument("--trans", nargs=2, type=int, default=[0, 0])
     ap.add_argument("--reps", type=int, default=3)
     ap.add_argument("--out-bf16", action="store_true")
-    ap.add_argument("--epi", choices=["bias", "residual", "gelu"], default=None,
+    ap.add_argument("--epi", choices=["bias", "residual", "gelu", "gelubwd"], default=None,
                     help="gemm case: the epilogue operands of the step's forward GEMMs")
     ap.add_argument("--variant", choices=["fused", "unfused", "gemm"], default="fused")
     args = ap.parse_args()
