@@ -454,6 +454,88 @@ __global__ void __launch_bounds__(1024) encoder_sort_reg_kernel(unsigned int* __
   for (int i = threadIdx.x; i < BT; i += 1024) sorted[i] = key[sort_pad(i)];
 }
 
+// The same sorted keys for BT <= 16384 and tokens below 2^16, by a stable
+// LSD radix sort on the token in one CTA: two passes of one 8-bit digit. A
+// pass counts each warp's digits (warp w owns 512-or-fewer consecutive keys),
+// scans the counts in (digit, warp) order into every warp's first slot per
+// digit, and lets each warp scatter its keys in order, 32 a round, ranking
+// equal digits inside a round by lane (match.any). Equal tokens therefore keep
+// their position order, and since the keys are distinct the result is the
+// bitonic network's array, in a few microseconds instead of ~100.
+constexpr int kRadixMaxBT = 16384;
+constexpr size_t kRadixSmem = (2 * kRadixMaxBT + 256 * 32 + 32) * sizeof(unsigned int);
+__global__ void __launch_bounds__(1024) encoder_radix_kernel(unsigned int* __restrict__ sorted,
+                                                             const int* __restrict__ tokens, int BT) {
+  extern __shared__ unsigned int rsm[];
+  unsigned int* src = rsm;                     // keys, kRadixMaxBT
+  unsigned int* dst = rsm + kRadixMaxBT;       // keys, kRadixMaxBT
+  unsigned int* cnt = rsm + 2 * kRadixMaxBT;   // [256 digits][32 warps], then 32 warp totals
+  unsigned int* wsum = cnt + 256 * 32;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const unsigned int lt = (1u << lane) - 1u;
+  for (int i = tid; i < BT; i += 1024) src[i] = (static_cast<unsigned int>(tokens[i]) << 15) | static_cast<unsigned int>(i);
+  const int per = (BT + 31) / 32;
+  const int w0 = min(BT, warp * per), w1 = min(BT, w0 + per);
+  for (int pass = 0; pass < 2; ++pass) {
+    const int shift = 15 + 8 * pass;
+    for (int i = tid; i < 256 * 32; i += 1024) cnt[i] = 0;
+    __syncthreads();
+    for (int i = w0 + lane; i < w1; i += 32) atomicAdd(&cnt[((src[i] >> shift) & 255u) * 32 + warp], 1u);
+    __syncthreads();
+    // exclusive scan of the 8192 counts: 8 consecutive per thread, then the
+    // thread totals across the block
+    unsigned int c8[8], run = 0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      c8[k] = run;
+      run += cnt[tid * 8 + k];
+    }
+    unsigned int inc = run;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const unsigned int y = __shfl_up_sync(0xffffffffu, inc, o);
+      if (lane >= o) inc += y;
+    }
+    if (lane == 31) wsum[warp] = inc;
+    __syncthreads();
+    if (warp == 0) {
+      unsigned int v = wsum[lane], vi = v;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const unsigned int y = __shfl_up_sync(0xffffffffu, vi, o);
+        if (lane >= o) vi += y;
+      }
+      wsum[lane] = vi - v;  // exclusive
+    }
+    __syncthreads();
+    const unsigned int base = wsum[warp] + inc - run;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) cnt[tid * 8 + k] = base + c8[k];
+    __syncthreads();
+    // stable scatter, 32 keys of this warp a round
+    for (int b0 = w0; b0 < w1; b0 += 32) {
+      const int i = b0 + lane;
+      const bool valid = i < w1;
+      const unsigned int key = valid ? src[i] : 0u;
+      const unsigned int d = valid ? (key >> shift) & 255u : 256u + static_cast<unsigned int>(lane);
+      const unsigned int peers = __match_any_sync(0xffffffffu, d);
+      unsigned int slot = 0;
+      if (valid) slot = cnt[d * 32 + warp] + __popc(peers & lt);
+      __syncwarp();
+      if (valid) {
+        dst[slot] = key;
+        if ((peers >> lane) == 1u) cnt[d * 32 + warp] = slot + 1;  // the group's last lane advances the slot
+      }
+      __syncwarp();
+    }
+    __syncthreads();
+    unsigned int* t = src;
+    src = dst;
+    dst = t;
+  }
+  for (int i = tid; i < BT; i += 1024) sorted[i] = src[i];
+}
+
 // dwte[tok,:] += sum of dout rows of the positions holding tok, in position
 // order: the first sorted key of each run of equal tokens sums its run.
 __global__ void encoder_bwd_wte_sorted_kernel(float* __restrict__ dwte, const float* __restrict__ dout,
@@ -904,7 +986,11 @@ int llmk_encoder_backward(float* dwte, float* dwpe, const float* dout, const int
     int n = 1;
     while (n < BT) n <<= 1;
     unsigned int* sorted = static_cast<unsigned int*>(workspace);
-    if (n == 8192 || n == 16384) {  // (32 keys a thread would spill registers)
+    if (BT <= kRadixMaxBT && V <= (1 << 16)) {
+      LLMK_CUDA(cudaFuncSetAttribute(encoder_radix_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(kRadixSmem)));
+      encoder_radix_kernel<<<1, 1024, kRadixSmem, s>>>(sorted, tokens, BT);
+    } else if (n == 8192 || n == 16384) {  // (32 keys a thread would spill registers)
       const size_t smem = static_cast<size_t>(n + n / 32) * sizeof(unsigned int);
       auto kern = n == 8192 ? encoder_sort_reg_kernel<8> : encoder_sort_reg_kernel<16>;
       LLMK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));

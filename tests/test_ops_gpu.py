@@ -213,10 +213,13 @@ def test_encoder_vs_oracle(cuda_dev):
     assert max_rel_err(dwpe.cpu(), torch.from_numpy(b)) < 1e-5
 
 
-@pytest.mark.parametrize("B,Tt,V", [(16, 1024, 50257), (5, 1000, 3000), (20, 1000, 50257), (33, 1024, 3000)])
+@pytest.mark.parametrize("B,Tt,V", [(16, 1024, 50257), (5, 1000, 3000), (16, 1024, 70000), (20, 1000, 50257),
+                                    (33, 1024, 3000)])
 def test_encoder_backward_sizes(cuda_dev, B, Tt, V):
-    """One-CTA sort paths: B*T = 16384 (16 keys per thread in registers), 5000 (8 keys per thread, padded to
-    8192), 20000 (the shared-memory network, padded to 32768); B*T = 33792 takes the scan fallback."""
+    """Sort paths: B*T = 16384 and 5000 with V < 2^16 (the one-CTA radix sort), 16384 with V = 70000 (the
+    bitonic network, 16 keys per thread in registers), 20000 (the shared-memory network, padded to 32768);
+    B*T = 33792 takes the scan fallback. dwte starts at zero, so the device's per-token sums in position
+    order must equal the oracle's sequential accumulation bit for bit."""
     import torch
     import llmk
     C = 128
@@ -234,6 +237,7 @@ def test_encoder_backward_sizes(cuda_dev, B, Tt, V):
     torch.cuda.synchronize()
     assert max_rel_err(dwte, a) < 1e-5
     assert max_rel_err(dwpe, b) < 1e-5
+    assert np.array_equal(dwte.cpu().numpy(), a)
 
 
 @pytest.mark.parametrize("dtname", ["f32", "bf16"])
