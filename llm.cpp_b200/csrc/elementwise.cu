@@ -336,12 +336,29 @@ __global__ void encoder_fwd_kernel(float* __restrict__ out, const int* __restric
 }
 // dwpe[t,:] += sum_b dout[b,t,:] in batch order (deterministic).
 __global__ void encoder_bwd_wpe_kernel(float* __restrict__ dwpe, const float* __restrict__ dout, int B, int T, int C) {
-  const long long n = static_cast<long long>(T) * C;
-  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+  // four columns a thread, four batch rows' loads in flight; the sum still
+  // runs over b in order
+  const long long n = static_cast<long long>(T) * C, n4 = n / 4;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n4;
        i += static_cast<long long>(gridDim.x) * blockDim.x) {
-    float s = 0.f;
-    for (int b = 0; b < B; ++b) s += dout[static_cast<long long>(b) * n + i];
-    dwpe[i] += s;
+    const float* p = dout + 4 * i;
+    float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+    int b = 0;
+    for (; b + 4 <= B; b += 4) {
+      float4 d[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) d[k] = ld4(p + static_cast<long long>(b + k) * n);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        s.x += d[k].x; s.y += d[k].y; s.z += d[k].z; s.w += d[k].w;
+      }
+    }
+    for (; b < B; ++b) {
+      const float4 d = ld4(p + static_cast<long long>(b) * n);
+      s.x += d.x; s.y += d.y; s.z += d.z; s.w += d.w;
+    }
+    const float4 o = ld4(dwpe + 4 * i);
+    st4(dwpe + 4 * i, make_float4(o.x + s.x, o.y + s.y, o.z + s.z, o.w + s.w));
   }
 }
 // dwte[tok,:] += dout[b,t,:]: positions sharing a token are summed in
@@ -980,7 +997,7 @@ int llmk_encoder_backward(float* dwte, float* dwpe, const float* dout, const int
     return fail(LLMK_ERR_WORKSPACE, "encoder_backward: workspace too small");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int BT = B * T;
-  encoder_bwd_wpe_kernel<<<grid_for(static_cast<long long>(T) * C, 256), 256, 0, s>>>(dwpe, dout, B, T, C);
+  encoder_bwd_wpe_kernel<<<grid_for(static_cast<long long>(T) * C / 4, 256), 256, 0, s>>>(dwpe, dout, B, T, C);
   if (BT <= kSortMaxBT && V < (1 << 17)) {
     // sort (token, position) keys once, then one pass over runs of equal tokens
     int n = 1;
