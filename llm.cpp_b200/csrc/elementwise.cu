@@ -15,6 +15,7 @@
 // AdamWKernel (adamw.cu:8-33).
 #include <algorithm>
 #include <cmath>
+#include <type_traits>
 
 #include "ptx.cuh"
 #include "runtime.h"
@@ -563,11 +564,35 @@ __global__ void encoder_bwd_wte_sorted_kernel(float* __restrict__ dwte, const fl
     const int idx = static_cast<int>(i / c4), c = static_cast<int>(i - static_cast<long long>(idx) * c4) * 4;
     const unsigned int tok = sorted[idx] >> 15;
     if (idx > 0 && (sorted[idx - 1] >> 15) == tok) continue;
+    // the run's rows added in position order, their loads in flight together:
+    // eight for the first block (most runs are short), 32 a block after that
+    // (frequent tokens make runs of thousands)
     float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int j = idx; j < BT && (sorted[j] >> 15) == tok; ++j) {
-      float4 d = ld4(dout + static_cast<long long>(sorted[j] & 0x7FFFu) * C + c);
-      s.x += d.x; s.y += d.y; s.z += d.z; s.w += d.w;
-    }
+    bool more = true;
+    int j = idx;
+    auto block = [&](auto ku) {
+      constexpr int kU = decltype(ku)::value;
+      unsigned int key[kU];
+      bool in[kU];
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        key[u] = j + u < BT ? sorted[j + u] : 0xFFFFFFFFu;
+        in[u] = (key[u] >> 15) == tok;
+      }
+      float4 d[kU];
+#pragma unroll
+      for (int u = 0; u < kU; ++u)
+        d[u] = in[u] ? ld4(dout + static_cast<long long>(key[u] & 0x7FFFu) * C + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int u = 0; u < kU; ++u)
+        if (in[u]) {
+          s.x += d[u].x; s.y += d[u].y; s.z += d[u].z; s.w += d[u].w;
+        }
+      more = in[kU - 1];
+      j += kU;
+    };
+    block(std::integral_constant<int, 8>{});
+    while (more) block(std::integral_constant<int, 32>{});
     float* dst = dwte + static_cast<long long>(tok) * C + c;
     float4 o = ld4(dst);
     st4(dst, make_float4(o.x + s.x, o.y + s.y, o.z + s.z, o.w + s.w));

@@ -240,6 +240,34 @@ def test_encoder_backward_sizes(cuda_dev, B, Tt, V):
     assert np.array_equal(dwte.cpu().numpy(), a)
 
 
+@pytest.mark.parametrize("B,Tt", [(16, 1024), (20, 1000)])
+def test_encoder_backward_frequent_tokens(cuda_dev, B, Tt):
+    """Text-like token counts: a few tokens take most positions (runs of thousands in the sorted order), as
+    frequent words do. The per-token sums must still run in position order: dwte bit-exact to the oracle."""
+    import torch
+    import llmk
+    C, V = 768, 50257
+    rng = np.random.default_rng(37)
+    tok = rng.integers(0, V, B * Tt).astype(np.int32)
+    hot = rng.random(B * Tt)
+    tok[hot < 0.30] = 11
+    tok[(hot >= 0.30) & (hot < 0.45)] = 13
+    tok[(hot >= 0.45) & (hot < 0.50)] = 50256
+    dout = O.normal((B * Tt, C), 38)
+    tokd, doutd = T(tok, cuda_dev), T(dout, cuda_dev)
+    dwte = torch.zeros(V, C, device=cuda_dev)
+    dwpe = torch.zeros(Tt, C, device=cuda_dev)
+    ws_b = llmk.lib().llmk_encoder_backward_workspace(B, Tt)
+    ws = torch.empty(ws_b // 4 + 16, device=cuda_dev)
+    llmk.call("llmk_encoder_backward", dwte.data_ptr(), dwpe.data_ptr(), doutd.data_ptr(), tokd.data_ptr(), B, Tt, C,
+              V, ws.data_ptr(), ws_b, llmk.stream_ptr())
+    a, b = np.zeros((V, C), np.float32), np.zeros((Tt, C), np.float32)
+    O.orc().orc_encoder_backward(a, b, dout, tok, B, Tt, C)
+    torch.cuda.synchronize()
+    assert np.array_equal(dwte.cpu().numpy(), a)
+    assert max_rel_err(dwpe, b) < 1e-5
+
+
 @pytest.mark.parametrize("dtname", ["f32", "bf16"])
 def test_softmax_crossentropy_vs_oracle(cuda_dev, dtname):
     import torch
