@@ -556,14 +556,25 @@ __global__ void __launch_bounds__(1024) encoder_radix_kernel(unsigned int* __res
 
 // dwte[tok,:] += sum of dout rows of the positions holding tok, in position
 // order: the first sorted key of each run of equal tokens sums its run.
+// Runs longer than this many positions (frequent tokens) are summed by
+// encoder_bwd_wte_long_kernel in 32 ordered segments instead of one thread's
+// sequential loop.
+constexpr int kLongRun = 64;
+
 __global__ void encoder_bwd_wte_sorted_kernel(float* __restrict__ dwte, const float* __restrict__ dout,
-                                              const unsigned int* __restrict__ sorted, int BT, int C) {
+                                              const unsigned int* __restrict__ sorted, int BT, int C,
+                                              int* __restrict__ long_runs) {
   const int c4 = C / 4;
   for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < static_cast<long long>(BT) * c4;
        i += static_cast<long long>(gridDim.x) * blockDim.x) {
     const int idx = static_cast<int>(i / c4), c = static_cast<int>(i - static_cast<long long>(idx) * c4) * 4;
     const unsigned int tok = sorted[idx] >> 15;
     if (idx > 0 && (sorted[idx - 1] >> 15) == tok) continue;
+    if (idx + kLongRun < BT && (sorted[idx + kLongRun] >> 15) == tok) {
+      // a long run: listed once (by its first column group) for the segmented kernel
+      if (c == 0) long_runs[1 + atomicAdd(long_runs, 1)] = idx;
+      continue;
+    }
     // the run's rows added in position order, their loads in flight together:
     // eight for the first block (most runs are short), 32 a block after that
     // (frequent tokens make runs of thousands)
@@ -596,6 +607,72 @@ __global__ void encoder_bwd_wte_sorted_kernel(float* __restrict__ dwte, const fl
     float* dst = dwte + static_cast<long long>(tok) * C + c;
     float4 o = ld4(dst);
     st4(dst, make_float4(o.x + s.x, o.y + s.y, o.z + s.z, o.w + s.w));
+  }
+}
+
+// dwte[tok,:] += the sum of one long run's dout rows (more than kLongRun
+// positions): a block per 128-column chunk and run of the list (blocks
+// stride over the runs); warp w sums the w-th of 32 equal contiguous segments
+// of the run in position order, and warp 0 adds the 32 segment sums in
+// segment order. Fixed segmentation and order:
+// the result is the same on every run (not the strictly sequential sum a
+// short run gets).
+__global__ void __launch_bounds__(1024) encoder_bwd_wte_long_kernel(float* __restrict__ dwte,
+                                                                    const float* __restrict__ dout,
+                                                                    const unsigned int* __restrict__ sorted, int BT,
+                                                                    int C, const int* __restrict__ long_runs) {
+  __shared__ float4 part[32][32];
+  __shared__ int run_end;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int c = blockIdx.y * 128 + lane * 4;
+  const int nruns = long_runs[0];
+  for (int r = blockIdx.x; r < nruns; r += gridDim.x) {
+    const int rs = long_runs[1 + r];
+    const unsigned int tok = sorted[rs] >> 15;
+    if (threadIdx.x == 0) {
+      // first index past the run: binary search over the sorted keys
+      int lo = rs + 1, hi = BT;
+      while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        if ((sorted[mid] >> 15) == tok) lo = mid + 1;
+        else hi = mid;
+      }
+      run_end = lo;
+    }
+    __syncthreads();
+    const int len = run_end - rs, seg = (len + 31) / 32;
+    const int j0 = rs + min(len, warp * seg), j1 = rs + min(len, (warp + 1) * seg);
+    float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (c < C) {
+      int j = j0;
+      for (; j + 8 <= j1; j += 8) {
+        float4 d[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) d[u] = ld4(dout + static_cast<long long>(sorted[j + u] & 0x7FFFu) * C + c);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          s.x += d[u].x; s.y += d[u].y; s.z += d[u].z; s.w += d[u].w;
+        }
+      }
+      for (; j < j1; ++j) {
+        const float4 d = ld4(dout + static_cast<long long>(sorted[j] & 0x7FFFu) * C + c);
+        s.x += d.x; s.y += d.y; s.z += d.z; s.w += d.w;
+      }
+    }
+    part[warp][lane] = s;
+    __syncthreads();
+    if (warp == 0 && c < C) {
+      float4 t = part[0][lane];
+#pragma unroll 1
+      for (int w = 1; w < 32; ++w) {
+        const float4 p = part[w][lane];
+        t.x += p.x; t.y += p.y; t.z += p.z; t.w += p.w;
+      }
+      float* dst = dwte + static_cast<long long>(tok) * C + c;
+      const float4 o = ld4(dst);
+      st4(dst, make_float4(o.x + t.x, o.y + t.y, o.z + t.z, o.w + t.w));
+    }
+    __syncthreads();  // part and run_end are rewritten for the next run
   }
 }
 
@@ -1043,8 +1120,14 @@ int llmk_encoder_backward(float* dwte, float* dwpe, const float* dout, const int
                                      static_cast<int>(smem)));
       encoder_sort_kernel<<<1, 1024, smem, s>>>(sorted, tokens, BT, n);
     }
+    // the list of long runs (a count, then their first sorted indices) in the
+    // workspace's second half
+    int* long_runs = static_cast<int*>(workspace) + BT;
+    LLMK_CUDA(cudaMemsetAsync(long_runs, 0, sizeof(int), s));
     encoder_bwd_wte_sorted_kernel<<<grid_for(static_cast<long long>(BT) * C / 4, 256), 256, 0, s>>>(dwte, dout, sorted,
-                                                                                                   BT, C);
+                                                                                                   BT, C, long_runs);
+    encoder_bwd_wte_long_kernel<<<dim3(16, (C + 127) / 128), 1024, 0, s>>>(dwte, dout, sorted, BT, C, long_runs);
+    count_launch(1);
   } else {
     int* first_of = static_cast<int*>(workspace);
     int* next_same = first_of + BT;

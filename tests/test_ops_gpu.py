@@ -243,7 +243,9 @@ def test_encoder_backward_sizes(cuda_dev, B, Tt, V):
 @pytest.mark.parametrize("B,Tt", [(16, 1024), (20, 1000)])
 def test_encoder_backward_frequent_tokens(cuda_dev, B, Tt):
     """Text-like token counts: a few tokens take most positions (runs of thousands in the sorted order), as
-    frequent words do. The per-token sums must still run in position order: dwte bit-exact to the oracle."""
+    frequent words do. Runs of up to 64 positions are summed in position order (bit-exact to the oracle's
+    sequential accumulation); longer runs in 32 ordered segments: within fp32 rounding of the oracle, and
+    the same bits on every call."""
     import torch
     import llmk
     C, V = 768, 50257
@@ -264,8 +266,19 @@ def test_encoder_backward_frequent_tokens(cuda_dev, B, Tt):
     a, b = np.zeros((V, C), np.float32), np.zeros((Tt, C), np.float32)
     O.orc().orc_encoder_backward(a, b, dout, tok, B, Tt, C)
     torch.cuda.synchronize()
-    assert np.array_equal(dwte.cpu().numpy(), a)
+    got = dwte.cpu().numpy()
+    counts = np.bincount(tok, minlength=V)
+    short = counts <= 64
+    assert np.array_equal(got[short], a[short])
+    assert max_rel_err(dwte, a) < 1e-5
     assert max_rel_err(dwpe, b) < 1e-5
+    # deterministic: a second call on zeroed gradients gives the same bits
+    dwte2 = torch.zeros(V, C, device=cuda_dev)
+    dwpe.zero_()
+    llmk.call("llmk_encoder_backward", dwte2.data_ptr(), dwpe.data_ptr(), doutd.data_ptr(), tokd.data_ptr(), B, Tt, C,
+              V, ws.data_ptr(), ws_b, llmk.stream_ptr())
+    torch.cuda.synchronize()
+    assert torch.equal(dwte2, dwte)
 
 
 @pytest.mark.parametrize("dtname", ["f32", "bf16"])
