@@ -6,8 +6,9 @@
 Workload (configuration 3 of the spec, the default): GPT-2 124M (L=12, NH=12,
 C=768, V=50257 padded to 50304, maxT=1024), B=16 sequences of T=1024 tokens
 per GPU, bf16 GEMMs and attention with fp32 master weights and AdamW (lr 3e-4,
-betas 0.9/0.999, eps 1e-8, wd 0), seeded initialisation, synthetic uniform
-tokens seeded per rank (1337 + rank). `--model 774m` runs configuration 4
+betas 0.9/0.999, eps 1e-8, wd 0), seeded initialisation, synthetic tokens
+seeded per rank (1337 + rank) with Zipf-law counts as text has (the k-th most
+frequent token ~ 1/k). `--model 774m` runs configuration 4
 instead (L=36, NH=20, C=1280, B=8 per GPU). One step = forward + backward
 (with the per-layer NCCL gradient all-reduce when N > 1) + AdamW on the
 native trainer of libllmk.so (include/llmk_gpt2.h), replayed as one captured
@@ -427,7 +428,13 @@ def run_ours(args) -> None:
         model.broadcast_parameters(0)
     BT = B * T
     rng = np.random.default_rng(1337 + rank)
-    toks = rng.integers(0, cfg["vocab_size"], size=BT + 1, dtype=np.int32)
+    # text-like token counts: Zipf's law over the vocabulary (frequency of the
+    # k-th most common token ~ 1/k, as in English text), ranks mapped to ids by
+    # a seeded permutation
+    V = cfg["vocab_size"]
+    zipf = 1.0 / np.arange(1, V + 1)
+    ids = np.random.default_rng(7).permutation(V).astype(np.int32)
+    toks = ids[rng.choice(V, size=BT + 1, p=zipf / zipf.sum())]
     inp_h, tgt_h = toks[:-1].copy(), toks[1:].copy()
     model.train_step(inp_h, tgt_h, 0.0, t=1, want_loss=False)  # tokens now resident in the model's buffers
     d_in, d_tg = model.buffers()
@@ -542,7 +549,7 @@ def run_ours(args) -> None:
             "metric": metric_name(args.model), "value": value, "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic (seeded uniform tokens, seeded init)",
+            "data": "synthetic (seeded tokens with Zipf-law counts as in text, seeded init)",
             "config": {"workload": f"{spec['name']} train step ({spec['config']})", "model": spec["name"],
                        "global_batch": B * world, "seq_len": T, "parallelism": f"dp{world}",
                        "l2": "working set larger than L2 (GBs of activations per step)"},
