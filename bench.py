@@ -760,7 +760,10 @@ def run_case(args) -> None:
     elif a.case == "encoder":
         Bb, Tt, C = (a.dims + [16, 1024, 768][len(a.dims):])[:3]
         Vp = 50304
-        tok = torch.randint(0, 50257, (Bb * Tt,), device=dev, dtype=torch.int32)
+        # token ids with Zipf-law counts, as the training step's synthetic batches have
+        zipf = 1.0 / np.arange(1, 50258)
+        ids = np.random.default_rng(7).permutation(50257).astype(np.int32)
+        tok = torch.from_numpy(ids[np.random.default_rng(1337).choice(50257, size=Bb * Tt, p=zipf / zipf.sum())]).to(dev)
         wte = torch.randn(Vp, C, device=dev)
         wpe = torch.randn(1024, C, device=dev)
         out = torch.empty(Bb * Tt, C, device=dev)
