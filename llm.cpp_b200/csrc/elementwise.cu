@@ -481,14 +481,17 @@ __global__ void __launch_bounds__(1024) encoder_sort_reg_kernel(unsigned int* __
 // their position order, and since the keys are distinct the result is the
 // bitonic network's array, in a few microseconds instead of ~100.
 constexpr int kRadixMaxBT = 16384;
-constexpr size_t kRadixSmem = (2 * kRadixMaxBT + 256 * 32 + 32) * sizeof(unsigned int);
+// digit counters [256 digits][32 warps] with a row stride of 33 words, so the
+// 32 lanes of a warp (one warp column, different digits) hit different banks
+constexpr int kRadixRow = 33;
+constexpr size_t kRadixSmem = (2 * kRadixMaxBT + 256 * kRadixRow + 32) * sizeof(unsigned int);
 __global__ void __launch_bounds__(1024) encoder_radix_kernel(unsigned int* __restrict__ sorted,
                                                              const int* __restrict__ tokens, int BT) {
   extern __shared__ unsigned int rsm[];
   unsigned int* src = rsm;                     // keys, kRadixMaxBT
   unsigned int* dst = rsm + kRadixMaxBT;       // keys, kRadixMaxBT
-  unsigned int* cnt = rsm + 2 * kRadixMaxBT;   // [256 digits][32 warps], then 32 warp totals
-  unsigned int* wsum = cnt + 256 * 32;
+  unsigned int* cnt = rsm + 2 * kRadixMaxBT;   // [256 digits][32 warps] (row stride 33), then 32 warp totals
+  unsigned int* wsum = cnt + 256 * kRadixRow;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const unsigned int lt = (1u << lane) - 1u;
   for (int i = tid; i < BT; i += 1024) src[i] = (static_cast<unsigned int>(tokens[i]) << 15) | static_cast<unsigned int>(i);
@@ -496,17 +499,19 @@ __global__ void __launch_bounds__(1024) encoder_radix_kernel(unsigned int* __res
   const int w0 = min(BT, warp * per), w1 = min(BT, w0 + per);
   for (int pass = 0; pass < 2; ++pass) {
     const int shift = 15 + 8 * pass;
-    for (int i = tid; i < 256 * 32; i += 1024) cnt[i] = 0;
+    for (int i = tid; i < 256 * kRadixRow; i += 1024) cnt[i] = 0;
     __syncthreads();
-    for (int i = w0 + lane; i < w1; i += 32) atomicAdd(&cnt[((src[i] >> shift) & 255u) * 32 + warp], 1u);
+    for (int i = w0 + lane; i < w1; i += 32) atomicAdd(&cnt[((src[i] >> shift) & 255u) * kRadixRow + warp], 1u);
     __syncthreads();
     // exclusive scan of the 8192 counts: 8 consecutive per thread, then the
     // thread totals across the block
+    // entry e = 8 tid + k is (digit e / 32, warp e % 32)
+    const int crow = (tid >> 2) * kRadixRow + (tid & 3) * 8;
     unsigned int c8[8], run = 0;
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
       c8[k] = run;
-      run += cnt[tid * 8 + k];
+      run += cnt[crow + k];
     }
     unsigned int inc = run;
 #pragma unroll
@@ -528,7 +533,7 @@ __global__ void __launch_bounds__(1024) encoder_radix_kernel(unsigned int* __res
     __syncthreads();
     const unsigned int base = wsum[warp] + inc - run;
 #pragma unroll
-    for (int k = 0; k < 8; ++k) cnt[tid * 8 + k] = base + c8[k];
+    for (int k = 0; k < 8; ++k) cnt[crow + k] = base + c8[k];
     __syncthreads();
     // stable scatter, 32 keys of this warp a round
     for (int b0 = w0; b0 < w1; b0 += 32) {
@@ -538,11 +543,11 @@ __global__ void __launch_bounds__(1024) encoder_radix_kernel(unsigned int* __res
       const unsigned int d = valid ? (key >> shift) & 255u : 256u + static_cast<unsigned int>(lane);
       const unsigned int peers = __match_any_sync(0xffffffffu, d);
       unsigned int slot = 0;
-      if (valid) slot = cnt[d * 32 + warp] + __popc(peers & lt);
+      if (valid) slot = cnt[d * kRadixRow + warp] + __popc(peers & lt);
       __syncwarp();
       if (valid) {
         dst[slot] = key;
-        if ((peers >> lane) == 1u) cnt[d * 32 + warp] = slot + 1;  // the group's last lane advances the slot
+        if ((peers >> lane) == 1u) cnt[d * kRadixRow + warp] = slot + 1;  // the group's last lane advances the slot
       }
       __syncwarp();
     }

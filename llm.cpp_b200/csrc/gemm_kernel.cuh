@@ -373,7 +373,9 @@ __device__ __forceinline__ void epilogue_cols(const EpiParams& ep, const CUtenso
           if constexpr (kOp == kOpBias || kOp == kOpBiasGelu) {
             load8(ep.bias + gc, t);
 #pragma unroll
-            for (int j = 0; j < 8; ++j) v[k * 8 + j] += t[j];
+            for (int j = 0; j < 8; j += 2)
+              f2_unpack(f2_add(f2_pack(v[k * 8 + j], v[k * 8 + j + 1]), f2_pack(t[j], t[j + 1])), v[k * 8 + j],
+                        v[k * 8 + j + 1]);
           }
         }
       }
@@ -390,8 +392,13 @@ __device__ __forceinline__ void epilogue_cols(const EpiParams& ep, const CUtenso
           tma_store_2d(tmX, stg, gn0, row0);
           bulk_commit();
         }
+        if constexpr (kBF16) {
 #pragma unroll
-        for (int j = 0; j < CW; ++j) v[j] = kBF16 ? gelu_tanh_fast(v[j]) : gelu_tanh(v[j]);
+          for (int j = 0; j < CW; j += 2) f2_unpack(gelu_tanh_fast2(f2_pack(v[j], v[j + 1])), v[j], v[j + 1]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < CW; ++j) v[j] = gelu_tanh(v[j]);
+        }
       }
     }
     if constexpr (!kAux || kOp == kOpBiasGelu) {
@@ -532,10 +539,22 @@ __device__ __forceinline__ void epilogue_operand_role(const EpiParams& ep, const
           float bb[8];
           load8(ep.bias + gc, bb);
 #pragma unroll
-          for (int j = 0; j < 8; ++j) v[k * 8 + j] = (v[k * 8 + j] + bb[j]) + t[j];  // (acc + bias) + residual
+          for (int j = 0; j < 8; j += 2) {  // (acc + bias) + residual
+            const uint64_t r = f2_add(f2_add(f2_pack(v[k * 8 + j], v[k * 8 + j + 1]), f2_pack(bb[j], bb[j + 1])),
+                                      f2_pack(t[j], t[j + 1]));
+            f2_unpack(r, v[k * 8 + j], v[k * 8 + j + 1]);
+          }
         } else {
+          if constexpr (kBF16) {
 #pragma unroll
-          for (int j = 0; j < 8; ++j) v[k * 8 + j] *= kBF16 ? gelu_tanh_grad_fast(t[j]) : gelu_tanh_grad(t[j]);
+            for (int j = 0; j < 8; j += 2) {
+              const uint64_t g = f2_mul(f2_pack(v[k * 8 + j], v[k * 8 + j + 1]), gelu_tanh_grad_fast2(f2_pack(t[j], t[j + 1])));
+              f2_unpack(g, v[k * 8 + j], v[k * 8 + j + 1]);
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[k * 8 + j] *= gelu_tanh_grad(t[j]);
+          }
         }
       }
       // chunk n - 1's store has read buffer (n + 2) % 3: load chunk n + 2 into it

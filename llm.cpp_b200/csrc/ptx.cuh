@@ -428,6 +428,39 @@ __device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
   return d;
 }
 
+// gelu_tanh_fast on two values with packed fp32x2 operations, the same IEEE
+// operations in the same order per value (the scalar form's multiply-add
+// contraction included), so the results are bit-identical to two calls of it.
+__device__ __forceinline__ uint64_t gelu_tanh_fast2(uint64_t x) {
+  const uint64_t t = f2_mul(f2_mul(f2_pack(0.044715f, 0.044715f), x), x);
+  const uint64_t u = f2_mul(f2_pack(0.7978845608f, 0.7978845608f), f2_fma(t, x, x));
+  const uint64_t hx = f2_mul(f2_pack(0.5f, 0.5f), x);
+  float u0, u1;
+  f2_unpack(u, u0, u1);
+  float th0, th1;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(th0) : "f"(u0));
+  asm("tanh.approx.f32 %0, %1;" : "=f"(th1) : "f"(u1));
+  return f2_fma(hx, f2_pack(th0, th1), hx);
+}
+
+// gelu_tanh_grad_fast on two values, operation for operation as the scalar
+// form evaluates it.
+__device__ __forceinline__ uint64_t gelu_tanh_grad_fast2(uint64_t x) {
+  const uint64_t one = f2_pack(1.f, 1.f), half = f2_pack(0.5f, 0.5f), k0 = f2_pack(0.7978845608f, 0.7978845608f);
+  const uint64_t x2 = f2_mul(x, x);
+  const uint64_t u = f2_mul(k0, f2_fma(f2_mul(f2_pack(0.044715f, 0.044715f), x2), x, x));
+  float u0, u1;
+  f2_unpack(u, u0, u1);
+  float th0, th1;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(th0) : "f"(u0));
+  asm("tanh.approx.f32 %0, %1;" : "=f"(th1) : "f"(u1));
+  const uint64_t th = f2_pack(th0, th1), nth = f2_pack(-th0, -th1);
+  const uint64_t sech2 = f2_fma(nth, th, one);
+  const uint64_t a = f2_mul(half, f2_add(one, th));
+  const uint64_t b = f2_mul(f2_mul(f2_mul(half, x), sech2), k0);
+  return f2_fma(b, f2_fma(f2_pack(0.134145f, 0.134145f), x2, one), a);
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
