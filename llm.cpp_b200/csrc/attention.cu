@@ -532,8 +532,9 @@ struct BwdSmem {
   static_assert(BYTES <= 232448, "backward smem");
 };
 
-// Backward CTA = 2 + kBwdSoftmaxWarps warps: warp 0 TMA, warp 1 tcgen05
-// issuer, the rest softmax-gradient warps. Warp w reads TMEM lanes
+// Backward CTA = 3 + kBwdSoftmaxWarps warps: warp 0 TMA, warp 1 tcgen05
+// issuer, warps 2.. the softmax-gradient warps, the last warp the dQ
+// reduce issuer. Softmax warp w reads TMEM lanes
 // 32*(w%4).. (key rows of S^T / dP^T / dK / dV, query rows of dQ) and owns
 // column group (w-2)/4 of every tile it touches: kBwdSoftmaxWarps/4 warps
 // share each lane quarter and split its columns.
@@ -544,12 +545,16 @@ struct BwdSmem {
 // dS^T in registers while the gradient MMAs of step g-1 run, write them to
 // the single smem P^T / dS^T buffer once those MMAs are done, and then stage
 // dQ of step g-1 (TMEM, double-buffered by step parity) for the TMA
-// reduce-adds into the fp32 accumulator.
+// reduce-adds into the fp32 accumulator, which the last warp issues once every
+// softmax warp has staged its part: the softmax warps never wait for one
+// another there, only (a step later) for those reduce-adds to have read the
+// staging.
 #ifndef LLMK_BWD_SOFTMAX_WARPS
 #define LLMK_BWD_SOFTMAX_WARPS 16
 #endif
 constexpr int kBwdSoftmaxWarps = LLMK_BWD_SOFTMAX_WARPS;  // 8 or 16
-constexpr int kBwdThreads = 64 + 32 * kBwdSoftmaxWarps;
+constexpr int kBwdDqWarp = 2 + kBwdSoftmaxWarps;            // the dQ reduce issuer
+constexpr int kBwdThreads = 32 * (kBwdDqWarp + 1);
 constexpr int kBwdCols = 4 * TILE / kBwdSoftmaxWarps;     // S^T columns per warp (64 or 32)
 constexpr int kBwdGradCols = HD * 4 / kBwdSoftmaxWarps;   // dQ / dK / dV columns per warp (32 or 16)
 static_assert(kBwdSoftmaxWarps == 8 || kBwdSoftmaxWarps == 16, "softmax warps");
@@ -843,6 +848,28 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       mbar_wait(done, 0, status, nullptr, 5);
     }
     __syncwarp();
+  } else if (warp == kBwdDqWarp) {
+    // dQ of every step, in the softmax warps' step order: once all of them
+    // have staged it (dqs_full), two TMA reduce-adds into the fp32
+    // accumulator; once those have read the staging, dqs_free.
+    if (lane == 0) {
+      uint32_t f = 0;
+      bool ok = true;
+      int n = 0;
+      for (int w = sched_slot(0, n_items); w < n_items && ok; w = sched_slot(++n, n_items)) {
+        const AttnItem it = bwd_item(w, B, NH);
+        for (int qt = it.tile; qt < nk; ++qt, ++f) {
+          if (!mbar_wait(dqs_full, f & 1, status, abort_flag, 24)) { ok = false; break; }
+          tma_reduce_add_3d(&tm_dq, sDQ, it.h * HD, qt * TILE, it.b);
+          tma_reduce_add_3d(&tm_dq, sDQ + TILE_BYTES, it.h * HD + 32, qt * TILE, it.b);
+          bulk_commit();
+          bulk_wait_read0();
+          mbar_arrive(dqs_free);
+        }
+      }
+      bulk_wait0();  // the reduce-adds are complete before the CTA exits
+    }
+    __syncwarp();
   } else {
     const int q = warp & 3;
     const int cq = (warp - 2) >> 2;  // column quarter
@@ -851,23 +878,18 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     // dQ of step gg (TMEM buffer gg&1, lane = query row, columns cq*16..+16)
     // staged in smem (two 128B-swizzled [128 x 32] fp32 halves) by all the
     // softmax warps, then added to the fp32 accumulator by two TMA
-    // reduce-adds that one thread (warp 2, lane 0) issues; rows past T are
-    // clipped by the tensor map. dqs_free: the previous reduce-adds have
-    // read the staging; dqs_full: every warp has written it.
+    // reduce-adds that the dQ warp issues; rows past T are clipped by the
+    // tensor map. dqs_free: the previous reduce-adds have read the staging;
+    // dqs_full: every softmax warp has written it.
     uint32_t nflush = 0;
-    auto flush_dq = [&](uint32_t gg, int b, int h, int qt) -> bool {
+    auto flush_dq = [&](uint32_t gg) -> bool {
       uint32_t v[kBwdGradCols];
 #pragma unroll
       for (int c16 = 0; c16 < kBwdGradCols; c16 += 16)
         tmem_ld_32x32b_x16(tmem + lane_base + 384 + (gg & 1) * HD + cq * kBwdGradCols + c16,
                            *reinterpret_cast<uint32_t(*)[16]>(v + c16));
       tmem_ld_wait();
-      const bool issuer = warp == 2 && lane == 0;
       const uint32_t f = nflush++;
-      if (issuer && f > 0) {
-        bulk_wait_read0();
-        mbar_arrive(dqs_free);
-      }
       bool fr = mbar_wait(dqs_free, (f & 1) ^ 1u, status, abort_flag, 23);
       if (!__all_sync(0xffffffffu, fr)) return false;
       const int col0 = cq * kBwdGradCols;  // of the 64 dQ columns
@@ -880,12 +902,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       fence_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(dqs_full);
-      if (issuer) {
-        if (!mbar_wait(dqs_full, f & 1, status, abort_flag, 24)) return false;
-        tma_reduce_add_3d(&tm_dq, sDQ, h * HD, qt * TILE, b);
-        tma_reduce_add_3d(&tm_dq, sDQ + TILE_BYTES, h * HD + 32, qt * TILE, b);
-        bulk_commit();
-      }
       return true;
     };
     // dK (scaled) and dV of key tile kt, columns cq*16..+16: TMEM lane = key row.
@@ -932,7 +948,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     int stage = 0;
     uint32_t phase = 0;
     bool have_prev = false, prev_last = false;
-    int pbb = 0, phh = 0, pqt = 0, pkt = 0;  // the previous step's batch, head, q tile and key tile
+    int pbb = 0, phh = 0, pkt = 0;  // the previous step's batch, head and key tile
     // the previous step's gradient MMAs are done: flush its dQ and, at an item
     // boundary, drain its item's dK / dV
     auto finish_prev = [&]() -> bool {
@@ -940,7 +956,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       bool gd = mbar_wait(grad_done + (gp & 1), (gp >> 1) & 1, status, abort_flag, 17);
       if (!__all_sync(0xffffffffu, gd)) return false;
       tc_fence_after();
-      if (!flush_dq(gp, pbb, phh, pqt)) return false;
+      if (!flush_dq(gp)) return false;
       if (prev_last) drain_dkv(pbb, phh, pkt);
       tc_fence_before();
       __syncwarp();
@@ -1006,12 +1022,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         prev_last = j + 1 == nqi;
         pbb = it.b;
         phh = it.h;
-        pqt = qt;
         pkt = kt;
       }
     }
     if (ok && have_prev) finish_prev();
-    if (warp == 2 && lane == 0) bulk_wait0();  // the dQ reduce-adds are complete before the CTA exits
     tc_fence_before();
   }
   __syncthreads();
