@@ -549,8 +549,12 @@ struct BwdSmem {
 // softmax warp has staged its part: the softmax warps never wait for one
 // another there, only (a step later) for those reduce-adds to have read the
 // staging.
+// Eight softmax warps (64 columns of each tile per warp, two per TMEM lane
+// quarter): measured 3.6 % faster per call than sixteen at B = 16, T = 1024 —
+// fewer arrivals per barrier phase and 168 registers a thread instead of the
+// 96 that sixteen warps leave (which spill more).
 #ifndef LLMK_BWD_SOFTMAX_WARPS
-#define LLMK_BWD_SOFTMAX_WARPS 16
+#define LLMK_BWD_SOFTMAX_WARPS 8
 #endif
 constexpr int kBwdSoftmaxWarps = LLMK_BWD_SOFTMAX_WARPS;  // 8 or 16
 constexpr int kBwdDqWarp = 2 + kBwdSoftmaxWarps;            // the dQ reduce issuer
