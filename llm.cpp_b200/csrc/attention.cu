@@ -19,12 +19,12 @@
 //
 // Backward: persistent, one CTA per SM walking (128-key tile, head, batch)
 // items; each walks query tiles from the diagonal down. S^T = K Q^T and
-// dP^T = V dO^T land in TMEM; 16 softmax warps (4 per TMEM lane quarter, 32
+// dP^T = V dO^T land in TMEM; 8 softmax warps (2 per TMEM lane quarter, 64
 // query columns each) form P^T and dS^T = P^T (dP^T - D) in registers and then
 // in smem once the previous tile's gradient MMAs are done; dV += P^T dO and
 // dK += dS^T Q accumulate in TMEM, dQ_i = dS K lands in one of two TMEM
 // buffers and is staged in smem and added to an fp32 workspace by TMA
-// reduce-adds while the next query tile runs. D = rowsum(dO * O) and the
+// reduce-adds (issued by a warp of their own) while the next query tile runs. D = rowsum(dO * O) and the
 // final dQ scaling run as small pre/post kernels.
 #include <algorithm>
 #include <type_traits>
