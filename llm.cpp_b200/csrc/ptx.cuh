@@ -428,9 +428,10 @@ __device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
   return d;
 }
 
-// gelu_tanh_fast on two values with packed fp32x2 operations, the same IEEE
-// operations in the same order per value (the scalar form's multiply-add
-// contraction included), so the results are bit-identical to two calls of it.
+// gelu_tanh_fast on two values with packed fp32x2 operations: the scalar
+// form's operations in its order per value, its inner multiply-add fused as
+// the compiler fuses it there (the FC forward's bf16 outputs matched the
+// scalar epilogue's bit for bit on the training step's shapes).
 __device__ __forceinline__ uint64_t gelu_tanh_fast2(uint64_t x) {
   const uint64_t t = f2_mul(f2_mul(f2_pack(0.044715f, 0.044715f), x), x);
   const uint64_t u = f2_mul(f2_pack(0.7978845608f, 0.7978845608f), f2_fma(t, x, x));
@@ -443,8 +444,9 @@ __device__ __forceinline__ uint64_t gelu_tanh_fast2(uint64_t x) {
   return f2_fma(hx, f2_pack(th0, th1), hx);
 }
 
-// gelu_tanh_grad_fast on two values, operation for operation as the scalar
-// form evaluates it.
+// gelu_tanh_grad_fast on two values: the scalar form's formula and order with
+// its multiply-adds written as explicit fused operations (results can differ
+// from the scalar function's in the last fp32 bit).
 __device__ __forceinline__ uint64_t gelu_tanh_grad_fast2(uint64_t x) {
   const uint64_t one = f2_pack(1.f, 1.f), half = f2_pack(0.5f, 0.5f), k0 = f2_pack(0.7978845608f, 0.7978845608f);
   const uint64_t x2 = f2_mul(x, x);
