@@ -14,7 +14,7 @@
 // head, batch) items heaviest first; warp 0 = TMA, warp 1 = tcgen05 issuer
 // (S = Q K^T into TMEM, O += P V in TMEM), warps 2..9 = softmax of the two
 // tiles (thread = query row): exp2 online softmax with lazy rescaling, P ->
-// smem (bf16, 128B-swizzled K-major). The two tiles share each K/V load and
+// TMEM (16-bit pairs, the P V MMA's A operand). The two tiles share each K/V load and
 // alternate on the tensor core, so one's softmax overlaps the other's MMAs.
 //
 // Backward: persistent, one CTA per SM walking (128-key tile, head, batch)
@@ -75,18 +75,22 @@ __device__ __forceinline__ int sched_slot(int k, int n_items) {
 // query row = TMEM lane). Both tiles of a pair belong to one (batch, head)
 // and share every K/V tile the TMA brings in (B needs one more: its
 // diagonal). Each tile has one S buffer (128 TMEM columns) and one O
-// accumulator (64 columns) in TMEM and one P buffer in shared memory; the
-// issuer alternates the tiles (PV_A(j), S_A(j+1), PV_B(j), S_B(j+1)), so one
+// accumulator (64 columns) in TMEM and its P tile in TMEM too (64 columns of
+// 16-bit pairs, the A operand of the P V MMA read straight from tensor memory);
+// the issuer alternates the tiles (PV_A(j), S_A(j+1), PV_B(j), S_B(j+1)), so one
 // tile's softmax runs while the other's MMAs do.
 struct FwdSmem {
   static constexpr int kStages = 3;
   static constexpr int Q_OFF = 0;                                  // 2 items x (Q_A, Q_B)
   static constexpr int KV_OFF = 4 * TILE_BYTES;                    // stages x (K, V)
-  static constexpr int P_OFF = KV_OFF + kStages * 2 * TILE_BYTES;  // P_A, P_B: [128 x 128] bf16
-  static constexpr int BAR_OFF = P_OFF + 2 * 2 * TILE_BYTES;
+  static constexpr int BAR_OFF = KV_OFF + kStages * 2 * TILE_BYTES;  // (P_A, P_B live in TMEM)
   static constexpr size_t BYTES = BAR_OFF + 256 + 1024;
 };
 constexpr int kFwdThreads = 320;
+// TMEM columns of the forward: tile x has S at 192x (128 columns) and O at
+// 192x + 128 (64 columns); P_x (bf16/fp16 pairs, the A operand of P V) at
+// kFwdPCol + 64x.
+constexpr uint32_t kFwdPCol = 384;
 
 template <bool kF16>
 __global__ void __launch_bounds__(kFwdThreads, 1)
@@ -97,7 +101,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem + S::Q_OFF;
   uint8_t* sKV = smem + S::KV_OFF;
-  uint8_t* sP = smem + S::P_OFF;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::BAR_OFF);
   uint64_t* q_full = bars;                       // [item parity][A, B]
   uint64_t* q_empty = q_full + 4;                // [item parity][A, B]
@@ -200,14 +203,14 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         mma_commit(s_full + x);
       };
       auto issue_pv = [&](int x, int st, bool acc) {
-        const uint32_t p_addr = smem_u32(sP + x * 2 * TILE_BYTES);
+        // A = P_x in TMEM (columns 384 + 64x: 128 keys as 64 packed pairs), 16 keys a K-step
+        const uint32_t p_tmem = tmem + kFwdPCol + x * (TILE / 2);
         const uint32_t v_addr = smem_u32(sKV + st * 2 * TILE_BYTES + TILE_BYTES);
         const uint32_t d = tmem + x * 192 + 128;
 #pragma unroll
         for (int ks = 0; ks < TILE / 16; ++ks) {
-          const uint64_t a = sdesc_sw128(p_addr + (ks >> 2) * TILE_BYTES + (ks & 3) * 32, 16, 1024);
           const uint64_t bd = sdesc_sw128(v_addr + ks * 2048, TILE_BYTES, 1024);
-          mma_f16_ss(d, a, bd, idesc_o, (ks > 0 || acc) ? 1u : 0u);
+          mma_f16_ts(d, p_tmem + ks * 8, bd, idesc_o, (ks > 0 || acc) ? 1u : 0u);
         }
         mma_commit(pv_done + x);
       };
@@ -273,6 +276,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
     const uint32_t s_cols = tmem + lane_base + x * 192;
     const uint32_t o_cols = s_cols + 128;
+    const uint32_t p_cols = tmem + lane_base + kFwdPCol + x * (TILE / 2);
     const float sl2 = 0.125f * 1.4426950408889634f;  // softmax scale * log2(e)
     // O accumulates P V over the tile's key tiles in TMEM. Exponents use a
     // running reference m (log2 domain) that moves only when a tile's row
@@ -280,7 +284,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     // rows and l in place once the previous P V is done. Otherwise P stays
     // below 2^kRescale, well inside bf16 and fp32 range.
     constexpr float kRescale = 8.f;
-    uint8_t* pt = sP + x * 2 * TILE_BYTES;
     bool ok = true;
     uint32_t cs = 0;  // S tiles consumed
     int n = 0;        // items
@@ -357,14 +360,13 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             rs2[k] = f2_add(rs2[k], f2_pack(p0, p1));
             pk[k] = pack16x2<kF16>(p0, p1);
           }
-          *reinterpret_cast<uint4*>(pt + (ch >> 3) * TILE_BYTES + sw128(r, ch & 7)) =
-              make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          tmem_st_32x32b_x4(p_cols + ch * 4, pk[0], pk[1], pk[2], pk[3]);
         }
         float rs8[8];
 #pragma unroll
         for (int k = 0; k < 4; ++k) f2_unpack(rs2[k], rs8[2 * k], rs8[2 * k + 1]);
         l += ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
-        fence_async_smem();
+        tmem_st_wait();
         tc_fence_before();
         mbar_arrive(p_full + x);
       }
