@@ -136,6 +136,36 @@ def test_gemm_epilogues(cuda_dev, M):
     assert llmk.device_status() == 0
 
 
+@pytest.mark.parametrize("M,N,K", [(600, 776, 192), (1000, 200, 136), (512, 3072, 768)])
+def test_gemm_operand_epilogues_ragged(cuda_dev, M, N, K):
+    """The two epilogue programs that take a per-element operand by TMA tile loads, on CTA-pair tiles with a
+    ragged last row block and column block (the operand's edge chunks load as zeros, D's edge stores are
+    clipped): bias + fp32 residual with a row stride wider than N (the residual GEMMs; K <= 1024 and
+    longer), and GELU-backward with B N-major and bf16 D / pre-activation (the FC-projection input
+    gradient)."""
+    import torch
+    import llmk
+    A, B, ref = _operands(torch, M, N, K, 0, 0, llmk.MATH_BF16, cuda_dev, seed=11)
+    ref = ref.float().to(cuda_dev)
+    g = torch.Generator(device="cpu").manual_seed(12)
+    bias = torch.randn(N, generator=g).to(cuda_dev)
+    res_full = torch.randn(M, N + 8, generator=g).to(cuda_dev)
+    res = res_full[:, :N]
+    D = torch.full((M, N), float("nan"), device=cuda_dev)
+    llmk.gemm(D, A, B, bias=bias, residual=res)
+    assert max_rel_err(D, ref + bias + res) < 1e-4
+    # GELU backward, B stored [K][N] (N-major) as the input-gradient GEMMs keep it
+    Bt = B.t().contiguous()
+    pre = (torch.randn(M, N, generator=g) * 2).bfloat16().to(cuda_dev)
+    Db = torch.full((M, N), float("nan"), device=cuda_dev, dtype=torch.bfloat16)
+    llmk.gemm(Db, A, Bt, b_trans=True, aux=pre, flags=llmk.EPI_GELU_BWD)
+    x = pre.float().requires_grad_(True)
+    torch.nn.functional.gelu(x, approximate="tanh").backward(ref)
+    assert max_rel_err(Db.float(), x.grad) < 1e-2
+    torch.cuda.synchronize()
+    assert llmk.device_status() == 0
+
+
 def test_gemm_rejects_misaligned(cuda_dev):
     import torch
     import llmk
