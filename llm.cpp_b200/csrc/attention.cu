@@ -233,31 +233,48 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           const int st = stage;
           if (++stage == S::kStages) { stage = 0; phase ^= 1u; }
           bool next_ready = false;  // K/V tile j+1 (now at `stage`) has landed
-          // S_x(j+1) as soon as the softmax has read S_x(j) ...
+          // S_x(j+1) once the softmax has read S_x(j), P V_x(j) once P_x(j) is
+          // in TMEM: each issued as soon as its barrier completes, whichever
+          // tile comes first
+          bool need_s[2], need_pv[2];
+          int nxs[2];
           for (int x = 0; x < 2; ++x) {
-            const int nx = x == 0 ? na : (has_b ? nkv : 0);
-            if (j >= nx) continue;
-            if (!mbar_wait(s_free + x, cf[x] & 1u, status, abort_flag, 8)) { ok = false; break; }
-            ++cf[x];
-            if (j + 1 < nx) {
-              if (!next_ready) {
-                if (!mbar_wait(kv_full + stage, phase, status, abort_flag, 3)) { ok = false; break; }
-                next_ready = true;
-              }
-              tc_fence_after();
-              issue_s(x, stage, q0 + x);
-              if (j + 2 == nx) mma_commit(q_empty + q0 + x);
-            }
+            nxs[x] = x == 0 ? na : (has_b ? nkv : 0);
+            need_s[x] = need_pv[x] = j < nxs[x];
           }
-          if (!ok) break;
-          // ... and P V_x(j) once P_x(j) is in shared memory
-          for (int x = 0; x < 2; ++x) {
-            const int nx = x == 0 ? na : (has_b ? nkv : 0);
-            if (j >= nx) continue;
-            if (!mbar_wait(p_full + x, cp[x] & 1u, status, abort_flag, 4)) { ok = false; break; }
-            ++cp[x];
-            tc_fence_after();
-            issue_pv(x, st, j > 0);
+          const long long c0 = clock64();
+          unsigned int polls = 0;
+          while (ok && (need_s[0] || need_s[1] || need_pv[0] || need_pv[1])) {
+            bool progressed = false;
+            for (int x = 0; x < 2; ++x) {
+              if (need_s[x] && mbar_peek(s_free + x, cf[x] & 1u)) {
+                ++cf[x];
+                need_s[x] = false;
+                progressed = true;
+                if (j + 1 < nxs[x]) {
+                  if (!next_ready) {
+                    if (!mbar_wait(kv_full + stage, phase, status, abort_flag, 3)) { ok = false; break; }
+                    next_ready = true;
+                  }
+                  tc_fence_after();
+                  issue_s(x, stage, q0 + x);
+                  if (j + 2 == nxs[x]) mma_commit(q_empty + q0 + x);
+                }
+              }
+              if (need_pv[x] && !need_s[x] && mbar_peek(p_full + x, cp[x] & 1u)) {
+                ++cp[x];
+                need_pv[x] = false;
+                progressed = true;
+                tc_fence_after();
+                issue_pv(x, st, j > 0);
+              }
+            }
+            if (!ok || progressed) continue;
+            if (*abort_flag || clock64() - c0 > kWaitLimitCycles || ++polls > kWaitLimitIters) {
+              if (!*abort_flag) atomicOr(status, LLMK_DEV_TIMEOUT | (1u << (8 + 4)));
+              *abort_flag = 1;
+              ok = false;
+            }
           }
           if (!ok) break;
           mma_commit(kv_empty + st);  // K_j, V_j read by every MMA issued so far

@@ -58,6 +58,20 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-blocking test of a phase (no suspend): for a thread that polls several
+// barriers and serves whichever completes first.
+__device__ __forceinline__ bool mbar_peek(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait for completion of the phase with the given parity. `abort` is a
 // CTA-shared flag: once any role of the CTA gave up, the others stop waiting.
 // `site` (0..23) names the wait in the status word (bit 8 + site) so a timeout
