@@ -28,6 +28,7 @@
 // final dQ scaling run as small pre/post kernels.
 #include <algorithm>
 #include <type_traits>
+#include <vector>
 
 #include "ptx.cuh"
 #include "runtime.h"
@@ -69,6 +70,20 @@ __device__ __forceinline__ int sched_slot(int k, int n_items) {
   return w < n_items ? w : n_items;
 }
 
+// The last round of a schedule whose items do not fill it: CTA c takes the
+// item of rank slot[c] in that round (-1: none), so the round's items go to
+// the CTAs with the least work after the full rounds. Filled on the host.
+constexpr int kMaxTailCtas = 256;
+struct SchedTail {
+  int16_t slot[kMaxTailCtas];
+};
+
+__device__ __forceinline__ int sched_slot_tail(int k, int n_items, int tail) {
+  const int g = static_cast<int>(gridDim.x), full = n_items / g;
+  if (k < full) return sched_slot(k, n_items);
+  return (k == full && tail >= 0) ? full * g + tail : n_items;
+}
+
 // ------------------------------------------------------------------ forward
 // CTA = 10 warps: warp 0 TMA, warp 1 tcgen05 issuer, warps 2..5 the softmax
 // of query tile A = 2p of pair item p, warps 6..9 of tile B = 2p+1 (thread =
@@ -77,8 +92,9 @@ __device__ __forceinline__ int sched_slot(int k, int n_items) {
 // diagonal). Each tile has one S buffer (128 TMEM columns) and one O
 // accumulator (64 columns) in TMEM and its P tile in TMEM too (64 columns of
 // 16-bit pairs, the A operand of the P V MMA read straight from tensor memory);
-// the issuer alternates the tiles (PV_A(j), S_A(j+1), PV_B(j), S_B(j+1)), so one
-// tile's softmax runs while the other's MMAs do.
+// the issuer serves the two tiles (S_x(j+1) once S_x(j) is read, PV_x(j) once
+// P_x(j) is written) in the order their barriers complete, so one tile's
+// softmax runs while the other's MMAs do.
 struct FwdSmem {
   static constexpr int kStages = 3;
   static constexpr int Q_OFF = 0;                                  // 2 items x (Q_A, Q_B)
@@ -95,8 +111,10 @@ constexpr uint32_t kFwdPCol = 384;
 template <bool kF16>
 __global__ void __launch_bounds__(kFwdThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, void* __restrict__ out_ptr, int out_f32,
-                    float* __restrict__ lse, int B, int T, int NH, int C, unsigned int* status) {
+                    float* __restrict__ lse, int B, int T, int NH, int C, unsigned int* status,
+                    const __grid_constant__ SchedTail tail) {
   using S = FwdSmem;
+  const int tail_slot = tail.slot[blockIdx.x];
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem + S::Q_OFF;
@@ -117,6 +135,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   const int nq = (T + TILE - 1) / TILE;
   const int np = (nq + 1) / 2;
   const int n_items = np * B * NH;
+  // this CTA's k-th item (n_items: none)
+  auto slot = [&](int k) { return sched_slot_tail(k, n_items, tail_slot); };
   const int warp = warp_id(), lane = lane_id();
   if (threadIdx.x == 0) {
     for (int i = 0; i < 4; ++i) {
@@ -157,7 +177,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       uint32_t phase = 0;
       bool ok = true;
       int n = 0;
-      for (int w = sched_slot(0, n_items); w < n_items && ok; w = sched_slot(n + 1, n_items), ++n) {
+      for (int w = slot(0); w < n_items && ok; w = slot(n + 1), ++n) {
         const AttnItem it = fwd_item(w, np, B, NH);
         const int p = it.tile;
         const bool has_b = 2 * p + 1 < nq;
@@ -214,7 +234,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         }
         mma_commit(pv_done + x);
       };
-      for (int w = sched_slot(0, n_items); w < n_items && ok; w = sched_slot(n + 1, n_items), ++n) {
+      for (int w = slot(0); w < n_items && ok; w = slot(n + 1), ++n) {
         const AttnItem it = fwd_item(w, np, B, NH);
         const int p = it.tile;
         const bool has_b = 2 * p + 1 < nq;
@@ -304,7 +324,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     bool ok = true;
     uint32_t cs = 0;  // S tiles consumed
     int n = 0;        // items
-    for (int w = sched_slot(0, n_items); w < n_items && ok; w = sched_slot(n + 1, n_items), ++n) {
+    for (int w = slot(0); w < n_items && ok; w = slot(n + 1), ++n) {
       const AttnItem it = fwd_item(w, np, B, NH);
       const int tile = 2 * it.tile + x;
       if (tile >= nq) continue;  // tile B of an odd last pair
@@ -559,7 +579,7 @@ struct BwdSmem {
 // share each lane quarter and split its columns.
 //
 // A persistent CTA (one per SM) walks key-tile items in the snake-order
-// schedule (sched_slot; most query tiles first). The query-tile steps g of a
+// schedule (sched_slot_tail; most query tiles first). The query-tile steps g of a
 // CTA's items form one sequence. The softmax warps turn S^T / dP^T of step g into P^T /
 // dS^T in registers while the gradient MMAs of step g-1 run, write them to
 // the single smem P^T / dS^T buffer once those MMAs are done, and then stage
@@ -642,8 +662,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                     const __grid_constant__ CUtensorMap tm_dq,
                     void* __restrict__ dqkv_ptr, int io_f32, float* __restrict__ dq_acc,
                     const float* __restrict__ lse, const float* __restrict__ Dvec, int B, int T, int NH, int C,
-                    unsigned int* status) {
+                    unsigned int* status, const __grid_constant__ SchedTail tail) {
   using S = BwdSmem;
+  const int tail_slot = tail.slot[blockIdx.x];
   extern __shared__ __align__(1024) uint8_t smem_bwd[];
   if ((smem_u32(smem_bwd) & 1023u) != 0) {  // uniform: every thread returns before any barrier
     if (threadIdx.x == 0) atomicOr(status, LLMK_DEV_SMEM_ALIGN);
@@ -675,6 +696,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 
   const int nk = (T + TILE - 1) / TILE;
   const int n_items = nk * B * NH;
+  // this CTA's k-th item (n_items: none)
+  auto slot = [&](int k) { return sched_slot_tail(k, n_items, tail_slot); };
   const int warp = warp_id(), lane = lane_id();
 
   if (threadIdx.x == 0) {
@@ -723,7 +746,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     uint32_t phase = 0;
     bool ok = true;
     int n = 0;
-    for (int w = sched_slot(0, n_items); w < n_items && ok; w = sched_slot(n + 1, n_items), ++n) {
+    for (int w = slot(0); w < n_items && ok; w = slot(n + 1), ++n) {
       const AttnItem it = bwd_item(w, B, NH);
       const int kt = it.tile, nqi = nk - kt;
       const float* lse_bh = lse + static_cast<long long>(it.bh) * T;
@@ -805,10 +828,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       uint32_t g = 0;
       bool issued = false;  // S^T / dP^T of step g already issued
       int n = 0;
-      for (int w = sched_slot(0, n_items); w < n_items && ok; w = sched_slot(n + 1, n_items), ++n) {
+      for (int w = slot(0); w < n_items && ok; w = slot(n + 1), ++n) {
         const int nqi = nk - bwd_item(w, B, NH).tile;
         const int kb = n & 1;
-        const bool has_next = sched_slot(n + 1, n_items) < n_items;
+        const bool has_next = slot(n + 1) < n_items;
         const uint32_t k_addr = smem_u32(sK) + kb * S::KV_BYTES;
         for (int j = 0; j < nqi; ++j, ++g) {
           const int nst = stage + 1 == S::kStages ? 0 : stage + 1;
@@ -879,7 +902,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       uint32_t f = 0;
       bool ok = true;
       int n = 0;
-      for (int w = sched_slot(0, n_items); w < n_items && ok; w = sched_slot(++n, n_items)) {
+      for (int w = slot(0); w < n_items && ok; w = slot(++n)) {
         const AttnItem it = bwd_item(w, B, NH);
         for (int qt = it.tile; qt < nk; ++qt, ++f) {
           if (!mbar_wait(dqs_full, f & 1, status, abort_flag, 24)) { ok = false; break; }
@@ -989,7 +1012,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
       return true;
     };
-    for (int w = sched_slot(0, n_items), nw = 0; w < n_items && ok; w = sched_slot(++nw, n_items)) {
+    for (int w = slot(0), nw = 0; w < n_items && ok; w = slot(++nw)) {
       const AttnItem it = bwd_item(w, B, NH);
       const int kt = it.tile, nqi = nk - kt, k0 = kt * TILE;
       for (int j = 0; j < nqi; ++j, ++g) {
@@ -1078,6 +1101,39 @@ int set_smem(const void* k, size_t bytes) {
   return LLMK_OK;
 }
 
+// The last, partial round of the snake schedule (sched_slot_tail): ranks the
+// CTAs by the work the full rounds gave them, least first, ties by CTA index.
+// An item's work is its key-tile steps plus one for its set-up: forward pair
+// item p (2p+1 and 2p+2 key tiles), backward key tile kt (nq - kt query tiles).
+void attn_sched_tail(bool bwd, int n_items, int g, int nq, int bh_count, SchedTail& t) {
+  thread_local int key[5] = {-1, -1, -1, -1, -1};
+  thread_local SchedTail cached;
+  if (key[0] == static_cast<int>(bwd) && key[1] == n_items && key[2] == g && key[3] == nq && key[4] == bh_count) {
+    t = cached;
+    return;
+  }
+  const int np = (nq + 1) / 2, full = n_items / g, rem = n_items - full * g;
+  std::vector<long long> load(g, 0);
+  std::vector<int> order(g);
+  for (int c = 0; c < g; ++c) {
+    order[c] = c;
+    for (int k = 0; k < full; ++k) {
+      const int w = k * g + ((k & 1) ? g - 1 - c : c);
+      if (bwd) {
+        load[c] += nq - w / bh_count + 1;
+      } else {
+        const int p = np - 1 - w / bh_count;
+        load[c] += (2 * p + 1) + (2 * p + 1 < nq ? 2 * p + 2 : 0) + 1;
+      }
+    }
+  }
+  std::sort(order.begin(), order.end(), [&](int a, int b) { return load[a] != load[b] ? load[a] < load[b] : a < b; });
+  for (int c = 0; c < kMaxTailCtas; ++c) t.slot[c] = -1;
+  for (int r = 0; r < rem; ++r) t.slot[order[r]] = static_cast<int16_t>(r);
+  key[0] = static_cast<int>(bwd); key[1] = n_items; key[2] = g; key[3] = nq; key[4] = bh_count;
+  cached = t;
+}
+
 int check_shapes(int B, int T, int C3, int NH) {
   if (B <= 0 || T <= 0 || C3 <= 0 || NH <= 0 || C3 % 3) return fail(LLMK_ERR_INVALID_ARG, "attention: bad shape");
   const int C = C3 / 3;
@@ -1108,10 +1164,14 @@ int llmk_attention_forward(void* out, llmk_dtype out_dtype, float* lse, const vo
                         static_cast<uint64_t>(C3) * 2, static_cast<uint64_t>(T) * C3 * 2, HD, TILE, 1));
   auto kern = f16 ? attn_fwd_kernel<true> : attn_fwd_kernel<false>;
   LLMK_TRY(set_smem(reinterpret_cast<const void*>(kern), FwdSmem::BYTES));
-  const int np = ((T + TILE - 1) / TILE + 1) / 2;  // pairs of query tiles
-  const int grid = std::min(np * B * NH, num_sms());  // persistent: one CTA per SM
+  const int nq = (T + TILE - 1) / TILE;
+  const int np = (nq + 1) / 2;  // pairs of query tiles
+  // persistent: one CTA per SM
+  const int grid = std::min(std::min(np * B * NH, num_sms()), kMaxTailCtas);
+  SchedTail tail;
+  attn_sched_tail(false, np * B * NH, grid, nq, B * NH, tail);
   kern<<<grid, kFwdThreads, FwdSmem::BYTES, static_cast<cudaStream_t>(stream)>>>(
-      tm, out, out_dtype == LLMK_F32 ? 1 : 0, lse, B, T, NH, C, device_status_ptr());
+      tm, out, out_dtype == LLMK_F32 ? 1 : 0, lse, B, T, NH, C, device_status_ptr(), tail);
   count_launch();
   LLMK_CUDA(cudaGetLastError());
   return LLMK_OK;
@@ -1169,9 +1229,11 @@ int attention_backward_t(void* dqkv, const void* dout, const void* out, bool f32
   // persistent: one CTA per SM walking key-tile items in the snake-order
   // schedule, so an item's dK / dV drain and K / V load overlap the next
   // item's first query tile
-  const int grid = std::min(nk * B * NH, num_sms());
+  const int grid = std::min(std::min(nk * B * NH, num_sms()), kMaxTailCtas);
+  SchedTail tail;
+  attn_sched_tail(true, nk * B * NH, grid, nk, B * NH, tail);
   attn_bwd_kernel<kF16><<<grid, kBwdThreads, BwdSmem::BYTES, s>>>(tq, td, tdq, dqkv, f32 ? 1 : 0, dq, lse, Dv, B, T, NH, C,
-                                                                  device_status_ptr());
+                                                                  device_status_ptr(), tail);
   const long long n8 = static_cast<long long>(B) * T * C / 8;
   const int pg = static_cast<int>(std::min<long long>((n8 + 255) / 256, 148LL * 16));
   if (f32) attn_bwd_post_kernel<float, kF16><<<pg, 256, 0, s>>>(static_cast<float*>(dqkv), dq, B * T, C, 0.125f);
