@@ -15,14 +15,15 @@
 // (S = Q K^T into TMEM, O += P V in TMEM), warps 2..9 = softmax of the two
 // tiles (thread = query row): exp2 online softmax with lazy rescaling, P ->
 // TMEM (16-bit pairs, the P V MMA's A operand). The two tiles share each K/V load and
-// alternate on the tensor core, so one's softmax overlaps the other's MMAs.
+// take turns on the tensor core, so one's softmax overlaps the other's MMAs.
 //
 // Backward: persistent, one CTA per SM walking (128-key tile, head, batch)
-// items; each walks query tiles from the diagonal down. S^T = K Q^T and
-// dP^T = V dO^T land in TMEM; 8 softmax warps (2 per TMEM lane quarter, 64
-// query columns each) form P^T and dS^T = P^T (dP^T - D) in registers and then
-// in smem once the previous tile's gradient MMAs are done; dV += P^T dO and
-// dK += dS^T Q accumulate in TMEM, dQ_i = dS K lands in one of two TMEM
+// items; each walks query tiles from the diagonal down. S = Q K^T and
+// dP = dO V^T land in TMEM (lane = query); 8 softmax warps (2 per TMEM lane
+// quarter, 64 key columns each; thread = query row, so LSE and D are one value
+// a thread) form P and dS = P (dP - D) in registers and then in smem once the
+// previous tile's gradient MMAs are done; dV += P^T dO and dK += dS^T Q (P, dS
+// read as M-major A operands) accumulate in TMEM, dQ_i = dS K lands in one of two TMEM
 // buffers and is staged in smem and added to an fp32 workspace by TMA
 // reduce-adds (issued by a warp of their own) while the next query tile runs. D = rowsum(dO * O) and the
 // final dQ scaling run as small pre/post kernels.
@@ -562,7 +563,7 @@ struct BwdSmem {
   static constexpr int V_OFF = TILE_BYTES;
   static constexpr int KV_BYTES = 2 * TILE_BYTES;
   static constexpr int QD_OFF = 2 * KV_BYTES;                      // stages x (Q_i, dO_i)
-  static constexpr int PD_OFF = QD_OFF + kStages * 2 * TILE_BYTES;  // P^T, dS^T [128 keys x 128 q]
+  static constexpr int PD_OFF = QD_OFF + kStages * 2 * TILE_BYTES;  // P, dS [128 q x 128 keys]
   static constexpr int PD_BYTES = 4 * TILE_BYTES;
   static constexpr int DQ_OFF = PD_OFF + PD_BYTES;                 // dQ staging: 2 x [128 q x 32] fp32, 128B-swizzled
   static constexpr int LD_OFF = DQ_OFF + 2 * TILE_BYTES;           // stages x (LSE[128], D[128]) fp32
@@ -574,15 +575,15 @@ struct BwdSmem {
 // Backward CTA = 3 + kBwdSoftmaxWarps warps: warp 0 TMA, warp 1 tcgen05
 // issuer, warps 2.. the softmax-gradient warps, the last warp the dQ
 // reduce issuer. Softmax warp w reads TMEM lanes
-// 32*(w%4).. (key rows of S^T / dP^T / dK / dV, query rows of dQ) and owns
+// 32*(w%4).. (query rows of S / dP / dQ, key rows of dK / dV) and owns
 // column group (w-2)/4 of every tile it touches: kBwdSoftmaxWarps/4 warps
 // share each lane quarter and split its columns.
 //
 // A persistent CTA (one per SM) walks key-tile items in the snake-order
 // schedule (sched_slot_tail; most query tiles first). The query-tile steps g of a
-// CTA's items form one sequence. The softmax warps turn S^T / dP^T of step g into P^T /
-// dS^T in registers while the gradient MMAs of step g-1 run, write them to
-// the single smem P^T / dS^T buffer once those MMAs are done, and then stage
+// CTA's items form one sequence. The softmax warps turn S / dP of step g into P /
+// dS in registers while the gradient MMAs of step g-1 run, write them to
+// the single smem P / dS buffer once those MMAs are done, and then stage
 // dQ of step g-1 (TMEM, double-buffered by step parity) for the TMA
 // reduce-adds into the fp32 accumulator, which the last warp issues once every
 // softmax warp has staged its part: the softmax warps never wait for one
@@ -598,7 +599,7 @@ struct BwdSmem {
 constexpr int kBwdSoftmaxWarps = LLMK_BWD_SOFTMAX_WARPS;  // 8 or 16
 constexpr int kBwdDqWarp = 2 + kBwdSoftmaxWarps;            // the dQ reduce issuer
 constexpr int kBwdThreads = 32 * (kBwdDqWarp + 1);
-constexpr int kBwdCols = 4 * TILE / kBwdSoftmaxWarps;     // S^T columns per warp (64 or 32)
+constexpr int kBwdCols = 4 * TILE / kBwdSoftmaxWarps;     // S key columns per warp (64 or 32)
 constexpr int kBwdGradCols = HD * 4 / kBwdSoftmaxWarps;   // dQ / dK / dV columns per warp (32 or 16)
 static_assert(kBwdSoftmaxWarps == 8 || kBwdSoftmaxWarps == 16, "softmax warps");
 
@@ -612,47 +613,36 @@ __device__ __forceinline__ AttnItem bwd_item(int w, int B, int NH) {
   return it;
 }
 
-// P^T = exp2(S^T * scale*log2e - LSE*log2e) and dS^T = P^T (dP^T - D) for
-// one thread's key row `key` and kCols query columns tq0.., packed as pairs
-// of the 16-bit operand type into pk / dk. ld_lse / ld_d: the tile's LSE
-// (natural log) / D of those columns (smem, read as broadcast vectors).
-// kMask: the diagonal tile (query < key masked) or a tile reaching past T
+// P = exp2(S * scale*log2e - LSE*log2e) and dS = P (dP - D) for one
+// thread's query row tq and kCols key columns tk0.., packed as pairs of the
+// 16-bit operand type into pk / dk. nl2 = -LSE * log2e and d = D of the row.
+// kMask: the diagonal tile (key > query masked) or a tile reaching past T
 // (padded queries masked).
 template <bool kMask, int kCols, bool kF16>
-__device__ __forceinline__ void bwd_p_ds(const uint32_t* sv, const uint32_t* dv, const float* ld_lse,
-                                         const float* ld_d, int tq0, int key, int T, uint32_t* pk, uint32_t* dk) {
+__device__ __forceinline__ void bwd_p_ds(const uint32_t* sv, const uint32_t* dv, float nl2, float d, int tk0, int tq,
+                                         int T, uint32_t* pk, uint32_t* dk) {
   const float sl2 = 0.125f * kLog2e;
-  const uint64_t sl2x2 = f2_pack(sl2, sl2), nlog2e = f2_pack(-kLog2e, -kLog2e);
+  const uint64_t sl2x2 = f2_pack(sl2, sl2), nl2x2 = f2_pack(nl2, nl2), dd = f2_pack(d, d);
 #pragma unroll
-  for (int c = 0; c < kCols / 8; ++c) {
-    // (LSE, D) of 8 query columns as 4 pairs each, from the broadcast smem rows
-    uint64_t l2[4], dd[4];
-    *reinterpret_cast<uint4*>(l2) = reinterpret_cast<const uint4*>(ld_lse + c * 8)[0];
-    *reinterpret_cast<uint4*>(l2 + 2) = reinterpret_cast<const uint4*>(ld_lse + c * 8)[1];
-    *reinterpret_cast<uint4*>(dd) = reinterpret_cast<const uint4*>(ld_d + c * 8)[0];
-    *reinterpret_cast<uint4*>(dd + 2) = reinterpret_cast<const uint4*>(ld_d + c * 8)[1];
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const int i = c * 8 + 2 * k;
-      // x = S * scale * log2e - LSE * log2e, two columns at a time
-      const uint64_t x = f2_fma(f2_pack(__uint_as_float(sv[i]), __uint_as_float(sv[i + 1])), sl2x2,
-                                f2_mul(l2[k], nlog2e));
-      float x0, x1;
-      f2_unpack(x, x0, x1);
-      float p0 = ex2_approx(x0), p1 = ex2_approx(x1);
-      if (kMask) {  // causal (query before key) and padded queries
-        const int tq = tq0 + i;
-        if (tq < key || tq >= T) p0 = 0.f;
-        if (tq + 1 < key || tq + 1 >= T) p1 = 0.f;
-      }
-      // dS = P (dP - D)
-      const uint64_t pp = f2_pack(p0, p1);
-      const uint64_t t = f2_fma(dd[k], f2_pack(-1.f, -1.f), f2_pack(__uint_as_float(dv[i]), __uint_as_float(dv[i + 1])));
-      float d0, d1;
-      f2_unpack(f2_mul(pp, t), d0, d1);
-      pk[c * 4 + k] = pack16x2<kF16>(p0, p1);
-      dk[c * 4 + k] = pack16x2<kF16>(d0, d1);
+  for (int h = 0; h < kCols / 2; ++h) {
+    const int i = 2 * h;
+    // x = S * scale * log2e - LSE * log2e, two columns at a time
+    const uint64_t x = f2_fma(f2_pack(__uint_as_float(sv[i]), __uint_as_float(sv[i + 1])), sl2x2, nl2x2);
+    float x0, x1;
+    f2_unpack(x, x0, x1);
+    float p0 = ex2_approx(x0), p1 = ex2_approx(x1);
+    if (kMask) {  // causal (key after query) and padded queries
+      const int tk = tk0 + i;
+      if (tk > tq || tq >= T) p0 = 0.f;
+      if (tk + 1 > tq || tq >= T) p1 = 0.f;
     }
+    // dS = P (dP - D)
+    const uint64_t pp = f2_pack(p0, p1);
+    const uint64_t t = f2_fma(dd, f2_pack(-1.f, -1.f), f2_pack(__uint_as_float(dv[i]), __uint_as_float(dv[i + 1])));
+    float d0, d1;
+    f2_unpack(f2_mul(pp, t), d0, d1);
+    pk[h] = pack16x2<kF16>(p0, p1);
+    dk[h] = pack16x2<kF16>(d0, d1);
   }
 }
 
@@ -673,7 +663,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   uint8_t* smem = smem_bwd;
   uint8_t* sK = smem + S::K_OFF;
   uint8_t* sQD = smem + S::QD_OFF;
-  uint8_t* sPD = smem + S::PD_OFF;  // P^T, dS^T 2 tiles further
+  uint8_t* sPD = smem + S::PD_OFF;  // P, dS 2 tiles further
   float* sLD = reinterpret_cast<float*>(smem + S::LD_OFF);
   uint8_t* sDQ = smem + S::DQ_OFF;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::BAR_OFF);
@@ -681,9 +671,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   uint64_t* kv_empty = bars + 2;                  // [2] that item's last gradient MMAs done (buffer b free)
   uint64_t* qd_full = bars + 4;                   // [stages] Q_i, dO_i
   uint64_t* qd_empty = qd_full + S::kStages;      // [stages]
-  uint64_t* sdp_full = qd_empty + S::kStages;     // S^T and dP^T in TMEM
-  uint64_t* sdp_free = sdp_full + 1;              // S^T / dP^T read into registers (one arrival per warp)
-  uint64_t* ps_full = sdp_free + 1;               // [2] P^T, dS^T of a step of parity b in smem
+  uint64_t* sdp_full = qd_empty + S::kStages;     // S and dP in TMEM
+  uint64_t* sdp_free = sdp_full + 1;              // S / dP read into registers (one arrival per warp)
+  uint64_t* ps_full = sdp_free + 1;               // [2] P, dS of a step of parity b in smem
   uint64_t* grad_done = ps_full + 2;              // [2] gradient MMAs of step parity b done
   uint64_t* dq_free = grad_done + 2;              // [2] dQ TMEM buffer b read
   uint64_t* dkv_free = dq_free + 2;               // an item's dK / dV TMEM read
@@ -732,7 +722,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  // TMEM columns: S^T 0..127, dP^T 128..255, dV 256..319, dK 320..383,
+  // TMEM columns: S 0..127, dP 128..255, dV 256..319, dK 320..383,
   // dQ[0] 384..447, dQ[1] 448..511
 
   if (warp == 0) {
@@ -800,25 +790,26 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      // S^T = K Q^T and dP^T = V dO^T: M=128 keys, N=128 q, K=64 (all K-major).
+      // S = Q K^T and dP = dO V^T: M=128 q, N=128 keys, K=64 (all K-major).
       constexpr uint32_t kFmt = kF16 ? kFmtF16 : kFmtBF16;
       const uint32_t idesc_s = idesc_f32acc(128, 128, kFmt, false, false);
-      // dV += P^T dO, dK += dS^T Q: M=128 keys, N=64, K=128 q; B is [q][hd] = N-major.
-      const uint32_t idesc_kv = idesc_f32acc(128, HD, kFmt, false, true);
-      // dQ = dS K: M=128 q, N=64, K=128 keys; A = dS^T stored [keys][q] = M-major;
+      // dV += P^T dO, dK += dS^T Q: M=128 keys, N=64, K=128 q; A = P / dS stored
+      // [q][keys] = M-major; B is [q][hd] = N-major.
+      const uint32_t idesc_kv = idesc_f32acc(128, HD, kFmt, true, true);
+      // dQ = dS K: M=128 q, N=64, K=128 keys; A = dS stored [q][keys] = K-major;
       // B = K stored [keys][hd] = N-major.
-      const uint32_t idesc_q = idesc_f32acc(128, HD, kFmt, true, true);
+      const uint32_t idesc_q = idesc_f32acc(128, HD, kFmt, false, true);
       auto issue_sdp = [&](int st, int kb) {
         const uint32_t k_addr = smem_u32(sK) + kb * S::KV_BYTES, v_addr = k_addr + TILE_BYTES;
         const uint32_t q_addr = smem_u32(sQD + st * 2 * TILE_BYTES);
         const uint32_t do_addr = q_addr + TILE_BYTES;
 #pragma unroll
         for (int ks = 0; ks < HD / 16; ++ks)
-          mma_f16_ss(tmem + 0, sdesc_sw128(k_addr + ks * 32, 16, 1024), sdesc_sw128(q_addr + ks * 32, 16, 1024),
+          mma_f16_ss(tmem + 0, sdesc_sw128(q_addr + ks * 32, 16, 1024), sdesc_sw128(k_addr + ks * 32, 16, 1024),
                      idesc_s, ks > 0);
 #pragma unroll
         for (int ks = 0; ks < HD / 16; ++ks)
-          mma_f16_ss(tmem + 128, sdesc_sw128(v_addr + ks * 32, 16, 1024), sdesc_sw128(do_addr + ks * 32, 16, 1024),
+          mma_f16_ss(tmem + 128, sdesc_sw128(do_addr + ks * 32, 16, 1024), sdesc_sw128(v_addr + ks * 32, 16, 1024),
                      idesc_s, ks > 0);
         mma_commit(sdp_full);
       };
@@ -826,7 +817,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       uint32_t g = 0;
-      bool issued = false;  // S^T / dP^T of step g already issued
+      bool issued = false;  // S / dP of step g already issued
       int n = 0;
       for (int w = slot(0); w < n_items && ok; w = slot(n + 1), ++n) {
         const int nqi = nk - bwd_item(w, B, NH).tile;
@@ -838,7 +829,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           const uint32_t nph = stage + 1 == S::kStages ? phase ^ 1u : phase;
           const uint32_t pb = g & 1;
           if (!issued) {
-            // first step of an item: its K, V, and the S^T / dP^T TMEM of the previous step
+            // first step of an item: its K, V, and the S / dP TMEM of the previous step
             if ((j == 0 && !mbar_wait(kv_full + kb, (n >> 1) & 1, status, abort_flag, 9)) ||
                 !mbar_wait(qd_full + stage, phase, status, abort_flag, 10) ||
                 (g > 0 && !mbar_wait(sdp_free, (g - 1) & 1, status, abort_flag, 11))) { ok = false; break; }
@@ -861,7 +852,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             issue_sdp(nst, nkb);
             issued = true;
           }
-          // P^T / dS^T of this step in smem; dQ buffer pb read (step g-2); at an
+          // P / dS of this step in smem; dQ buffer pb read (step g-2); at an
           // item's first step, the previous item's dK / dV read
           if (!mbar_wait(ps_full + pb, (g >> 1) & 1, status, abort_flag, 12) ||
               (g >= 2 && !mbar_wait(dq_free + pb, ((g >> 1) & 1) ^ 1u, status, abort_flag, 13)) ||
@@ -870,19 +861,22 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           const uint32_t q_addr = smem_u32(sQD + stage * 2 * TILE_BYTES);
           const uint32_t do_addr = q_addr + TILE_BYTES;
           const uint32_t p_addr = smem_u32(sPD), ds_addr = p_addr + 2 * TILE_BYTES;
+          // dV, dK: A = P^T / dS^T as M-major from P / dS [q][keys] (key atoms 16 KB
+          // apart, q groups 1 KB apart), K-step = 16 q rows.
 #pragma unroll
           for (int ks = 0; ks < TILE / 16; ++ks) {
-            const uint32_t koff = (ks >> 2) * TILE_BYTES + (ks & 3) * 32;  // K (= q) offset in a [128 x 128] K-major tile
-            mma_f16_ss(tmem + 256, sdesc_sw128(p_addr + koff, 16, 1024),
+            mma_f16_ss(tmem + 256, sdesc_sw128(p_addr + ks * 2048, TILE_BYTES, 1024),
                        sdesc_sw128(do_addr + ks * 2048, TILE_BYTES, 1024), idesc_kv, (j > 0 || ks > 0));
-            mma_f16_ss(tmem + 320, sdesc_sw128(ds_addr + koff, 16, 1024),
+            mma_f16_ss(tmem + 320, sdesc_sw128(ds_addr + ks * 2048, TILE_BYTES, 1024),
                        sdesc_sw128(q_addr + ks * 2048, TILE_BYTES, 1024), idesc_kv, (j > 0 || ks > 0));
           }
-          // dQ = dS K: A = dS^T as M-major (q atoms 16 KB apart, key groups 1 KB apart), K-step = 16 keys.
+          // dQ = dS K: A = dS K-major (K = keys), K-step = 16 keys.
 #pragma unroll
-          for (int ks = 0; ks < TILE / 16; ++ks)
-            mma_f16_ss(tmem + 384 + pb * HD, sdesc_sw128(ds_addr + ks * 2048, TILE_BYTES, 1024),
+          for (int ks = 0; ks < TILE / 16; ++ks) {
+            const uint32_t koff = (ks >> 2) * TILE_BYTES + (ks & 3) * 32;  // K (= key) offset in a [128 x 128] K-major tile
+            mma_f16_ss(tmem + 384 + pb * HD, sdesc_sw128(ds_addr + koff, 16, 1024),
                        sdesc_sw128(k_addr + ks * 2048, TILE_BYTES, 1024), idesc_q, ks > 0);
+          }
           mma_commit(grad_done + pb);
           mma_commit(qd_empty + stage);
           if (j + 1 == nqi) mma_commit(kv_empty + kb);
@@ -919,7 +913,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   } else {
     const int q = warp & 3;
     const int cq = (warp - 2) >> 2;  // column quarter
-    const int r = q * 32 + lane;     // key row within the tile for S^T/dP^T/dK/dV; query row for dQ
+    const int r = q * 32 + lane;     // query row within the tile for S/dP/dQ; key row for dK/dV
     const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
     // dQ of step gg (TMEM buffer gg&1, lane = query row, columns cq*16..+16)
     // staged in smem (two 128B-swizzled [128 x 32] fp32 halves) by all the
@@ -1022,7 +1016,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                   mbar_wait(sdp_full, g & 1, status, abort_flag, 16);
         if (!__all_sync(0xffffffffu, wt)) { ok = false; break; }
         tc_fence_after();
-        // this warp's 32 columns of S^T and dP^T into registers, then release the TMEM
+        // this warp's key columns of S and dP into registers, then release the TMEM
         uint32_t sv[kBwdCols], dv[kBwdCols];
 #pragma unroll
         for (int h32 = 0; h32 < kBwdCols / 32; ++h32) {
@@ -1035,15 +1029,16 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(sdp_free);
-        // P^T / dS^T of this warp's query columns, packed in registers
-        const int tq0 = qt * TILE + cq * kBwdCols;
-        const float* ld = sLD + stage * 2 * TILE + cq * kBwdCols;
+        // P / dS of this warp's key columns, packed in registers
+        const float* ld = sLD + stage * 2 * TILE;
+        const float nl2 = ld[r] * -kLog2e, drow = ld[TILE + r];
+        const int tk0 = k0 + cq * kBwdCols, tq = qt * TILE + r;
         uint32_t pk[kBwdCols / 2], dk[kBwdCols / 2];
         if (qt == kt || qt * TILE + TILE > T)
-          bwd_p_ds<true, kBwdCols, kF16>(sv, dv, ld, ld + TILE, tq0, k0 + r, T, pk, dk);
+          bwd_p_ds<true, kBwdCols, kF16>(sv, dv, nl2, drow, tk0, tq, T, pk, dk);
         else
-          bwd_p_ds<false, kBwdCols, kF16>(sv, dv, ld, ld + TILE, tq0, k0 + r, T, pk, dk);
-        // the single P^T / dS^T buffer: the previous step's gradient MMAs have read it
+          bwd_p_ds<false, kBwdCols, kF16>(sv, dv, nl2, drow, tk0, tq, T, pk, dk);
+        // the single P / dS buffer: the previous step's gradient MMAs have read it
         if (have_prev) {
           const uint32_t gp = g - 1;
           bool gd = mbar_wait(grad_done + (gp & 1), (gp >> 1) & 1, status, abort_flag, 17);
