@@ -950,7 +950,10 @@ int launch_gemm(const void* A, long long lda, const void* B, long long ldb, int 
   const int group_m = (b_bytes > 32e6 && a_bytes <= 32e6) ? num_m : std::min(8, num_m);
   int units = 0;
   LLMK_TRY(persistent_units(kern, kPair, C::SMEM, C::kThreads, &units));
-  units = std::min(units, num_tiles);
+  // the fewest CTAs (pairs) that take as many rounds of tiles as all of them
+  // would: the rest of the SMs stay free for work on other streams
+  const int rounds = (num_tiles + units - 1) / units;
+  units = (num_tiles + rounds - 1) / rounds;
   unsigned int* st = device_status_ptr();
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (kPair) {
