@@ -864,8 +864,9 @@ __global__ void __launch_bounds__(Cfg<kTF32, kAMN, kBMN, kBN, kPair>::kThreads, 
   }
 }
 
-// Persistent grid: one CTA (or CTA pair) per SM that can hold one, at most
-// one per tile. Pairs need two SMs of one GPC, so their count comes from the
+// Persistent grid: at most one CTA (or CTA pair) per SM that can hold one
+// (launch_gemm then trims it to the fewest units that take as many rounds of
+// tiles). Pairs need two SMs of one GPC, so their count comes from the
 // occupancy calculator (cached per kernel and device).
 template <typename Kern>
 int persistent_units(Kern kern, bool pair, size_t smem, int threads, int* units) {
