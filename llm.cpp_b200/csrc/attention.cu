@@ -560,8 +560,7 @@ struct BwdSmem {
   // K, V of two items (by item parity: buffer b holds K at 2b tiles, V one
   // tile further), so the next item's K / V arrive while this item runs
   static constexpr int K_OFF = 0;
-  static constexpr int V_OFF = TILE_BYTES;
-  static constexpr int KV_BYTES = 2 * TILE_BYTES;
+  static constexpr int KV_BYTES = 2 * TILE_BYTES;  // K, then V at + TILE_BYTES
   static constexpr int QD_OFF = 2 * KV_BYTES;                      // stages x (Q_i, dO_i)
   static constexpr int PD_OFF = QD_OFF + kStages * 2 * TILE_BYTES;  // P, dS [128 q x 128 keys]
   static constexpr int PD_BYTES = 4 * TILE_BYTES;
